@@ -1,0 +1,103 @@
+// Shared device helpers for the B200 (sm_100a) kernels of chroma_b200.
+//
+// Numerics follow the reference's storage rules: every kernel computes in fp32; a value the reference keeps
+// in bf16 is rounded to nearest-even at the same points (chroma/_src/core/bfloat16.h:7-17,
+// chroma/_src/codegen/cuda/codegen.py:62-66 uses __float2bfloat16_rn for the same purpose).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace cb200 {
+
+// Error bits written by kernels into the per-program error word (the role of the index-error flag at
+// chroma/_src/codegen/cuda/runtime.h:18-32).
+enum : unsigned int { kErrIndex = 1u, kErrTimeout = 2u };
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Storage precision policy: Round<float> is the identity, Round<bf16> rounds to bf16 and back.
+template <typename T> struct Store;
+template <> struct Store<float> {
+    static __device__ __forceinline__ float round(float x) { return x; }
+    static __device__ __forceinline__ float load(const float* p) { return *p; }
+    static __device__ __forceinline__ void store(float* p, float v) { *p = v; }
+    static constexpr bool bf16 = false;
+};
+template <> struct Store<__nv_bfloat16> {
+    static __device__ __forceinline__ float round(float x) { return bf16_round(x); }
+    static __device__ __forceinline__ float load(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+    static __device__ __forceinline__ void store(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+    static constexpr bool bf16 = true;
+};
+
+// Loads four consecutive storage elements (16 B for fp32, 8 B for bf16) as floats. The pointer must be
+// aligned to the access size; every caller indexes rows whose length is a multiple of 4.
+__device__ __forceinline__ void load4(const float* p, float (&v)[4]) {
+    float4 q = __ldg(reinterpret_cast<const float4*>(p));
+    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
+    uint2 q = __ldg(reinterpret_cast<const uint2*>(p));
+    __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&q.x);
+    __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&q.y);
+    float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+    v[0] = fa.x; v[1] = fa.y; v[2] = fb.x; v[3] = fb.y;
+}
+// Streaming variant for weights read exactly once per launch: bypass L1 allocation.
+__device__ __forceinline__ void load4_stream(const float* p, float (&v)[4]) {
+    float4 q;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(q.x), "=f"(q.y), "=f"(q.z), "=f"(q.w) : "l"(p));
+    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+}
+__device__ __forceinline__ void load4_stream(const __nv_bfloat16* p, float (&v)[4]) {
+    uint32_t a, b;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(a), "=r"(b) : "l"(p));
+    __nv_bfloat162 pa = *reinterpret_cast<__nv_bfloat162*>(&a);
+    __nv_bfloat162 pb = *reinterpret_cast<__nv_bfloat162*>(&b);
+    float2 fa = __bfloat1622float2(pa), fb = __bfloat1622float2(pb);
+    v[0] = fa.x; v[1] = fa.y; v[2] = fb.x; v[3] = fb.y;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+// Sum within aligned groups of `width` lanes (width a power of two <= 32).
+__device__ __forceinline__ float group_sum(float v, int width) {
+    for (int o = width >> 1; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Bounds-checked row index with optional negative wrap-around (aten.index semantics), the device-side
+// counterpart of chroma::cuda::index (chroma/_src/codegen/cuda/runtime.h:18-32). An invalid value raises
+// the index bit and reads row 0 so the kernel can finish; the host turns the bit into IndexError.
+__device__ __forceinline__ int64_t checked_row(int64_t value, int64_t count, bool negative, unsigned int* error) {
+    if (value >= 0 && value < count) return value;
+    if (negative && value < 0 && value >= -count) return value + count;
+    atomicOr(error, kErrIndex);
+    return 0;
+}
+
+// Programmatic dependent launch (Hopper+): a kernel may start while its predecessor drains. Everything
+// before pdl_wait() must touch only data no earlier kernel writes (weights); pdl_trigger() lets the next
+// kernel in the stream begin launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// L2 prefetch of a byte range (weights a CTA will read after pdl_wait()).
+__device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes, int lane, int lanes) {
+    const char* c = static_cast<const char*>(p);
+    for (size_t off = size_t(lane) * 128; off < bytes; off += size_t(lanes) * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(c + off));
+}
+
+}  // namespace cb200

@@ -1,0 +1,983 @@
+// chroma_b200 runtime: the C ABI of include/chroma_b200.h.
+//
+// Replaces the reference's header-only CUDA runtime (chroma/_src/codegen/cuda/runtime.h:89-201) and the generated
+// per-graph launch list (chroma/_src/codegen/cuda/codegen.py:13-41, :87-111). Differences by design:
+//   * kernels are precompiled for sm_100a (no per-graph nvcc); a program is a descriptor + weights file;
+//   * one call's kernel sequence is captured once into a CUDA graph and replayed; kernels use programmatic
+//     dependent launch so each one's prologue (weight prefetch) overlaps its predecessor's tail;
+//   * device weights are shared between programs loaded from identical weight files (prefill/decode pairs);
+//   * KV-cached decoding can keep the cache in device memory (chroma_b200_decoder_*).
+// Error contract kept from the reference: an out-of-range index sets a device error word, the call finishes,
+// synchronises and reports CHROMA_B200_INDEX (IndexError); the program stays usable (runtime.h:147-173).
+
+#include "../../include/chroma_b200.h"
+#include "gptoss.cuh"
+#include "micro.cuh"
+
+#include <cstdio>
+#include <cstring>
+#include <algorithm>
+#include <fstream>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace cb200 {
+
+struct IndexError : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+struct ValueError : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+static void check(cudaError_t st, const char* what) {
+    if (st != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(st));
+}
+
+class DeviceGuard {
+public:
+    explicit DeviceGuard(int device) {
+        check(cudaGetDevice(&previous_), "cudaGetDevice");
+        if (previous_ != device) check(cudaSetDevice(device), "cudaSetDevice");
+        device_ = device;
+    }
+    ~DeviceGuard() {
+        if (previous_ != device_) cudaSetDevice(previous_);
+    }
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+
+private:
+    int previous_ = 0, device_ = 0;
+};
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    DevBuf() = default;
+    explicit DevBuf(size_t n) : bytes(n) { check(cudaMalloc(&p, n ? n : 1), "cudaMalloc"); }
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    DevBuf(DevBuf&& o) noexcept : p(o.p), bytes(o.bytes) { o.p = nullptr; }
+    DevBuf& operator=(DevBuf&& o) noexcept {
+        std::swap(p, o.p);
+        std::swap(bytes, o.bytes);
+        return *this;
+    }
+    template <typename T> T* as() const { return static_cast<T*>(p); }
+};
+
+struct PinnedBuf {
+    void* p = nullptr;
+    explicit PinnedBuf(size_t n) { check(cudaMallocHost(&p, n ? n : 1), "cudaMallocHost"); }
+    ~PinnedBuf() {
+        if (p) cudaFreeHost(p);
+    }
+    PinnedBuf(const PinnedBuf&) = delete;
+    PinnedBuf& operator=(const PinnedBuf&) = delete;
+};
+
+// ---------------------------------------------------------------------------------------------------------
+// Weights: read once per (device, file identity) and shared by every program that names the same file.
+struct Weights {
+    int device;
+    DevBuf buf;
+};
+
+static std::mutex g_weights_mu;
+static std::map<std::string, std::weak_ptr<Weights>> g_weights;
+
+static std::shared_ptr<Weights> load_weights(const char* path, size_t bytes, int device) {
+    std::string p(path);
+    const std::string base = p.substr(p.find_last_of('/') == std::string::npos ? 0 : p.find_last_of('/') + 1);
+    const std::string key = std::to_string(device) + ":" + base + ":" + std::to_string(bytes);
+    std::lock_guard<std::mutex> lock(g_weights_mu);
+    auto it = g_weights.find(key);
+    if (it != g_weights.end()) {
+        if (auto live = it->second.lock()) return live;
+    }
+    std::ifstream stream(p, std::ios::binary | std::ios::ate);
+    if (!stream || stream.tellg() != static_cast<std::streamoff>(bytes))
+        throw std::runtime_error("Missing weights file or incorrect byte size");
+    stream.seekg(0);
+    auto w = std::make_shared<Weights>();
+    w->device = device;
+    w->buf = DevBuf(bytes);
+    // Upload through a pinned bounce buffer in 64 MiB pieces.
+    const size_t piece = size_t(64) << 20;
+    PinnedBuf stage(std::min(bytes, piece));
+    for (size_t off = 0; off < bytes; off += piece) {
+        const size_t n = std::min(piece, bytes - off);
+        if (!stream.read(static_cast<char*>(stage.p), static_cast<std::streamsize>(n)))
+            throw std::runtime_error("Cannot read weights");
+        check(cudaMemcpy(w->buf.as<char>() + off, stage.p, n, cudaMemcpyHostToDevice), "Upload weights");
+    }
+    g_weights[key] = w;
+    return w;
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// Kernel launch with programmatic stream serialisation (PDL).
+template <typename... Params, typename... Args>
+static void launch(cudaStream_t s, dim3 grid, dim3 block, size_t smem, void (*kernel)(Params...), Args&&... args) {
+    if (smem > 48 * 1024)
+        check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)), "smem attribute");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    check(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), "kernel launch");
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// Small utility kernels.
+__global__ void k_positions(const int64_t* pos0, int B, int n, float* positions, int64_t* last, int count) {
+    pdl_wait();
+    pdl_trigger();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < B * n) positions[i] = float(pos0[i / n] + i % n);
+    if (i < B) last[i] = count - 1;
+}
+
+template <typename T>
+__global__ void k_commit(const T* new_k, const T* new_v, int L, int B, int n, int count, int ctx, int KV, int hd,
+                         const int64_t* pos0, T* cache_k, T* cache_v, int64_t* slots) {
+    pdl_wait();
+    pdl_trigger();
+    // One block per (layer, sequence, row < count); threads over KV*hd.
+    const int r = blockIdx.x % count;
+    const int b = (blockIdx.x / count) % B;
+    const int l = blockIdx.x / (count * B);
+    const int64_t t = pos0[b] + r;
+    const int slot = int(t % ctx);
+    const size_t row = size_t(KV) * hd;
+    const T* sk = new_k + (size_t(l) * B * n + size_t(b) * n + r) * row;
+    const T* sv = new_v + (size_t(l) * B * n + size_t(b) * n + r) * row;
+    T* dk = cache_k + ((size_t(b) * L + l) * ctx + slot) * row;
+    T* dv = cache_v + ((size_t(b) * L + l) * ctx + slot) * row;
+    for (size_t i = threadIdx.x; i < row; i += blockDim.x) {
+        dk[i] = sk[i];
+        dv[i] = sv[i];
+    }
+    if (l == 0 && threadIdx.x == 0) slots[size_t(b) * ctx + slot] = t;
+}
+
+// Greedy argmax over each row of logits (first index on ties, as numpy.argmax).
+template <typename T>
+__global__ void k_argmax(const T* logits, int V, int64_t* out) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    const int r = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    pdl_wait();
+    pdl_trigger();
+    float best = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        const float x = Store<T>::load(logits + size_t(r) * V + v);
+        if (x > best || (idx == 0x7fffffff)) { best = x; idx = v; }
+    }
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+    }
+    if (lane == 0) { bv[warp] = best; bi[warp] = idx; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < warps; ++w)
+            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) { best = bv[w]; idx = bi[w]; }
+        out[r] = idx;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------
+struct Model {
+    chroma_b200_desc desc{};
+    Dims dm{};
+    std::vector<int32_t> layer_window;
+    std::vector<int64_t> offsets;
+    std::shared_ptr<Weights> weights;
+    DevBuf inv_freq;
+    int device = 0;
+
+    const char* at(int i) const { return weights->buf.as<char>() + offsets.at(size_t(i)); }
+    template <typename T> LayerW<T> layer(int l) const {
+        const int b = 3 + 13 * l;
+        LayerW<T> w;
+        w.attn_norm = reinterpret_cast<const float*>(at(b + 0));
+        w.sinks = reinterpret_cast<const T*>(at(b + 1));
+        w.qkv_w = reinterpret_cast<const T*>(at(b + 2));
+        w.qkv_b = reinterpret_cast<const T*>(at(b + 3));
+        w.out_w = reinterpret_cast<const T*>(at(b + 4));
+        w.out_b = reinterpret_cast<const T*>(at(b + 5));
+        w.mlp_norm = reinterpret_cast<const float*>(at(b + 6));
+        w.gate_w = reinterpret_cast<const T*>(at(b + 7));
+        w.gate_b = reinterpret_cast<const T*>(at(b + 8));
+        w.w1 = reinterpret_cast<const T*>(at(b + 9));
+        w.b1 = reinterpret_cast<const T*>(at(b + 10));
+        w.w2 = reinterpret_cast<const T*>(at(b + 11));
+        w.b2 = reinterpret_cast<const T*>(at(b + 12));
+        return w;
+    }
+};
+
+static size_t storage_size(int storage) { return storage == CHROMA_B200_BF16 ? 2 : 4; }
+
+static void validate_desc(const chroma_b200_desc& d) {
+    auto need = [](bool ok, const char* what) {
+        if (!ok) throw ValueError(std::string("invalid program descriptor: ") + what);
+    };
+    need(d.storage == CHROMA_B200_FP32 || d.storage == CHROMA_B200_BF16, "storage");
+    need(d.offsets != nullptr && d.num_offsets > 0, "offsets");
+    if (d.kind == CHROMA_B200_MICRO) {
+        need(d.storage == CHROMA_B200_BF16, "micro storage");
+        need(d.rows > 0 && d.rows < (int64_t(1) << 31) && d.cols > 0 && d.cols % 8 == 0 && d.cols <= 8 * 512 * 8, "micro shape");
+        return;
+    }
+    need(d.kind == CHROMA_B200_GPTOSS_FORWARD || d.kind == CHROMA_B200_GPTOSS_CACHED || d.kind == CHROMA_B200_GPTOSS_LAST,
+         "kind");
+    need(d.layers > 0 && d.num_offsets == 3 + 13 * d.layers, "layer count / offsets");
+    need(d.hidden > 0 && d.hidden % 4 == 0, "hidden size (multiple of 4)");
+    need(d.heads > 0 && d.kv_heads > 0 && d.heads % d.kv_heads == 0 && d.heads / d.kv_heads <= 8, "heads (query groups of at most 8)");
+    need(d.head_dim > 0 && d.head_dim % 4 == 0 && d.head_dim <= 64, "head_dim (multiple of 4, <= 64)");
+    need(d.experts > 0 && d.experts <= 256 && d.top_k > 0 && d.top_k <= 8 && d.top_k <= d.experts, "experts");
+    need(d.intermediate > 0 && d.intermediate % 4 == 0, "intermediate size");
+    need(d.vocab > 0 && d.tokens > 0, "vocab / tokens");
+    need(d.kind != CHROMA_B200_GPTOSS_CACHED || d.context > 0, "context");
+    need(d.inv_freq != nullptr && d.layer_window != nullptr, "rope / window tables");
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// Arena planning: best fit over inclusive kernel-index lifetimes with a coalesced free list, the algorithm of the
+// reference's planner (chroma/_src/memory.py:12-50). Visiting order is by start, ties in insertion order.
+struct Alloc {
+    size_t size;
+    int start, end;
+    size_t offset;
+};
+
+static size_t plan_arena(std::vector<Alloc>& allocs) {
+    std::vector<size_t> order(allocs.size());
+    for (size_t i = 0; i < order.size(); ++i) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) { return allocs[a].start < allocs[b].start; });
+    std::vector<size_t> live;
+    std::vector<std::pair<size_t, size_t>> free_list;  // (offset, size)
+    size_t total = 0;
+    for (size_t idx : order) {
+        Alloc& a = allocs[idx];
+        std::vector<size_t> still;
+        for (size_t o : live) {
+            if (allocs[o].end < a.start) free_list.emplace_back(allocs[o].offset, allocs[o].size);
+            else still.push_back(o);
+        }
+        live.swap(still);
+        std::sort(free_list.begin(), free_list.end());
+        std::vector<std::pair<size_t, size_t>> merged;
+        for (const auto& f : free_list) {
+            if (!merged.empty() && merged.back().first + merged.back().second == f.first) merged.back().second += f.second;
+            else merged.push_back(f);
+        }
+        free_list.swap(merged);
+        long best = -1;
+        for (size_t i = 0; i < free_list.size(); ++i)
+            if (free_list[i].second >= a.size && (best < 0 || free_list[i].second < free_list[size_t(best)].second))
+                best = long(i);
+        if (best >= 0) {
+            const auto f = free_list[size_t(best)];
+            free_list.erase(free_list.begin() + best);
+            a.offset = f.first;
+            if (f.second > a.size) free_list.emplace_back(f.first + a.size, f.second - a.size);
+        } else {
+            a.offset = total;
+            total += a.size;
+        }
+        live.push_back(idx);
+    }
+    return total;
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// One configured execution of a GPT-OSS model: B sequences of n rows, with its own activation arena.
+struct GptIO {
+    const int64_t* tokens = nullptr;
+    const float* positions = nullptr;
+    const void* cache_k = nullptr;  // [B][L][ctx][KV][hd]
+    const void* cache_v = nullptr;
+    void* new_k = nullptr;          // [L][B*n][KV][hd]
+    void* new_v = nullptr;
+    const void* mask = nullptr;     // [n][ctx+n] (buffer mode, B == 1)
+    const void* window_mask = nullptr;
+    const int64_t* slots = nullptr; // [B][ctx] (slots mode)
+    const int64_t* pos0 = nullptr;  // [B]
+    const int64_t* rows = nullptr;  // [B] selected row per sequence, or nullptr for every row
+    void* logits = nullptr;
+    int64_t* argmax = nullptr;      // [rows] optional
+    int* routes = nullptr;          // [L][B*n][k] optional record of the routing
+};
+
+struct GptExec {
+    const Model* m = nullptr;
+    int B = 1, n = 1, ctx = 0, mask_mode = kMaskBuffer, window = 0, sms = 148;
+    DevBuf arena;
+    size_t arena_bytes = 0, unreused_bytes = 0;
+    float *x = nullptr, *x2 = nullptr, *tnorm = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *rw = nullptr,
+          *tf = nullptr;
+    int* ridx = nullptr;
+    void *scratch_k = nullptr, *scratch_v = nullptr;
+    GptIO io;
+    unsigned* err = nullptr;
+    int launches = 0;
+
+    // Temporaries with their kernel-index lifetimes (0 embedding; per layer l: 1+5l QKV, 2+5l attention,
+    // 3+5l out/router, 4+5l expert up, 5+5l expert down; 1+5L final norm; 2+5L vocab), in planning order.
+    void init(const Model& model, int batch, int rows_per_seq, int context, int mode, int win) {
+        m = &model;
+        B = batch;
+        n = rows_per_seq;
+        ctx = context;
+        mask_mode = mode;
+        window = win;
+        int dev = 0;
+        check(cudaGetDevice(&dev), "cudaGetDevice");
+        check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
+        const Dims& d = model.dm;
+        const int L = model.desc.layers;
+        const size_t N = size_t(B) * n;
+        const int last = 5 * (L - 1);
+        auto round = [](size_t b) { return (b + 255) / 256 * 256; };
+        std::vector<Alloc> a = {
+            {round(N * d.d * 4), 0, 1 + 5 * L, 0},           // x
+            {round(N * d.H * d.hd * 4), 1, 2 + last, 0},      // q
+            {round(N * d.H * d.hd * 4), 2, 3 + last, 0},      // attn
+            {round(N * d.d * 4), 3, 5 + last, 0},             // x2
+            {round(N * d.d * 4), 3, 4 + last, 0},             // tnorm
+            {round(N * d.k * 4), 3, 5 + last, 0},             // ridx
+            {round(N * d.k * 4), 3, 5 + last, 0},             // rw
+            {round(N * d.k * d.I * 4), 4, 5 + last, 0},       // act
+            {round(N * d.d * 4), 1 + 5 * L, 2 + 5 * L, 0},   // tf
+        };
+        const bool uncached = model.desc.kind != CHROMA_B200_GPTOSS_CACHED;
+        if (uncached) {
+            const size_t es = storage_size(model.desc.storage);
+            a.push_back({round(N * d.KV * d.hd * es), 1, 2 + last, 0});  // scratch_k
+            a.push_back({round(N * d.KV * d.hd * es), 1, 2 + last, 0});  // scratch_v
+        }
+        unreused_bytes = 0;
+        for (const auto& x_ : a) unreused_bytes += x_.size;
+        arena_bytes = plan_arena(a);
+        arena = DevBuf(arena_bytes);
+        char* base = arena.as<char>();
+        x = reinterpret_cast<float*>(base + a[0].offset);
+        q = reinterpret_cast<float*>(base + a[1].offset);
+        attn = reinterpret_cast<float*>(base + a[2].offset);
+        x2 = reinterpret_cast<float*>(base + a[3].offset);
+        tnorm = reinterpret_cast<float*>(base + a[4].offset);
+        ridx = reinterpret_cast<int*>(base + a[5].offset);
+        rw = reinterpret_cast<float*>(base + a[6].offset);
+        act = reinterpret_cast<float*>(base + a[7].offset);
+        tf = reinterpret_cast<float*>(base + a[8].offset);
+        if (uncached) {
+            scratch_k = base + a[9].offset;
+            scratch_v = base + a[10].offset;
+        }
+    }
+
+    template <typename T> void enqueue_t(cudaStream_t s) {
+        const Dims& dm = m->dm;
+        const int N = B * n;
+        const int L = m->desc.layers;
+        const size_t es = sizeof(T);
+        launches = 0;
+        launch(s, dim3(N), dim3(128), 0, k_embed<T>, io.tokens, N, reinterpret_cast<const T*>(m->at(0)), dm.V, dm.d,
+               x, err);
+        ++launches;
+        const int heads_total = dm.H + 2 * dm.KV;
+        const int hpc = 1;
+        const size_t smem_in = size_t(kAttnInTokens) * dm.d * 4 + size_t(kAttnInTokens) * hpc * dm.hd * 4 + kAttnInTokens * 4;
+        const int nkeys = ctx + n;
+        const size_t smem_attn = size_t(dm.G) * nkeys * 4;
+        const size_t smem_router = size_t(dm.H * dm.hd + dm.d + dm.E + 32) * 4;
+        const int ppc = 16, cpc = 16;
+        for (int l = 0; l < L; ++l) {
+            const LayerW<T> w = m->layer<T>(l);
+            T* nk;
+            T* nv;
+            const T* ck = nullptr;
+            const T* cv = nullptr;
+            if (m->desc.kind == CHROMA_B200_GPTOSS_CACHED) {
+                nk = static_cast<T*>(io.new_k) + size_t(l) * N * dm.KV * dm.hd;
+                nv = static_cast<T*>(io.new_v) + size_t(l) * N * dm.KV * dm.hd;
+                ck = static_cast<const T*>(io.cache_k) + size_t(l) * ctx * dm.KV * dm.hd;
+                cv = static_cast<const T*>(io.cache_v) + size_t(l) * ctx * dm.KV * dm.hd;
+            } else {
+                nk = static_cast<T*>(scratch_k);
+                nv = static_cast<T*>(scratch_v);
+                ck = nk;
+                cv = nv;
+            }
+            launch(s, dim3((heads_total + hpc - 1) / hpc, (N + kAttnInTokens - 1) / kAttnInTokens), dim3(256), smem_in,
+                   k_attn_in<T>, x, N, dm, hpc, w.attn_norm, w.qkv_w, w.qkv_b, io.positions,
+                   m->inv_freq.as<const float>(), q, nk, nv);
+            AttnArgs a;
+            a.n = n;
+            a.ctx = ctx;
+            a.B = B;
+            a.cache_seq_stride = size_t(L) * ctx * dm.KV * dm.hd;
+            a.mask_mode = mask_mode;
+            const bool windowed = m->layer_window[size_t(l)] != 0;
+            a.window = mask_mode == kMaskSlots ? (windowed ? window : ctx) : (windowed ? window : 0);
+            a.slots = io.slots;
+            a.pos0 = io.pos0;
+            const T* bias = static_cast<const T*>(windowed ? io.window_mask : io.mask);
+            launch(s, dim3(n, dm.KV, B), dim3(dm.G * 32), smem_attn, k_attention<T>, q, dm, a, ck, cv,
+                   static_cast<const T*>(nk), static_cast<const T*>(nv), bias, w.sinks, attn);
+            launch(s, dim3(N), dim3(256), smem_router, k_out_router<T>, attn, x, N, dm,
+                   w, x2, tnorm, ridx, rw, io.routes ? io.routes + size_t(l) * N * dm.k : nullptr);
+            launch(s, dim3(N * dm.k, (dm.I + ppc - 1) / ppc), dim3(256), size_t(dm.d) * 4, k_moe_up<T>,
+                   tnorm, N, dm, ridx, w.w1, w.b1, ppc, act, err);
+            launch(s, dim3(N, (dm.d + cpc - 1) / cpc), dim3(256), size_t(dm.k) * dm.I * 4, k_moe_down<T>,
+                   act, x2, N, dm, ridx, rw, w.w2,
+                   w.b2, cpc, x, err);
+            launches += 5;
+        }
+        const int nrows = io.rows ? B : N;
+        launch(s, dim3(nrows), dim3(256), 0, k_final_norm<T>, x, N, nrows, io.rows, n,
+               reinterpret_cast<const float*>(m->at(1)), dm, tf, err);
+        const int vgrid = std::max(1, std::min((dm.V + 31) / 32, sms * 4));
+        launch(s, dim3(vgrid), dim3(256), size_t(kVocabRows) * dm.d * 4, k_vocab<T, kVocabRows>, tf,
+               nrows, dm.d, dm.V, reinterpret_cast<const T*>(m->at(2)), static_cast<T*>(io.logits));
+        launches += 2;
+        if (io.argmax) {
+            launch(s, dim3(nrows), dim3(1024), 0, k_argmax<T>, static_cast<const T*>(io.logits), dm.V, io.argmax);
+            ++launches;
+        }
+        (void)es;
+    }
+
+    void enqueue(cudaStream_t s) {
+        if (m->desc.storage == CHROMA_B200_BF16) enqueue_t<__nv_bfloat16>(s);
+        else enqueue_t<float>(s);
+    }
+};
+
+// A captured CUDA graph of an enqueue function, rebuilt only when asked.
+struct Graph {
+    cudaGraphExec_t exec = nullptr;
+    bool failed = false;
+    ~Graph() {
+        if (exec) cudaGraphExecDestroy(exec);
+    }
+    template <typename F> void run(cudaStream_t s, F&& enqueue) {
+        if (!exec && !failed) {
+            cudaGraph_t g = nullptr;
+            check(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+            bool ok = true;
+            try {
+                enqueue(s);
+            } catch (...) {
+                ok = false;
+            }
+            const cudaError_t end = cudaStreamEndCapture(s, &g);
+            if (ok && end == cudaSuccess && g && cudaGraphInstantiate(&exec, g, 0) == cudaSuccess) {
+                cudaGraphDestroy(g);
+            } else {
+                if (g) cudaGraphDestroy(g);
+                exec = nullptr;
+                failed = true;
+                cudaGetLastError();
+            }
+        }
+        if (exec) check(cudaGraphLaunch(exec, s), "cudaGraphLaunch");
+        else enqueue(s);
+    }
+};
+
+}  // namespace cb200
+
+using namespace cb200;
+
+struct chroma_b200_program {
+    int device = 0;
+    std::string name;
+    cudaStream_t stream = nullptr;
+    std::shared_ptr<Model> model_ptr = std::make_shared<Model>();
+    Model& model = *model_ptr;
+    GptExec exec;
+    std::vector<DevBuf> in, out;
+    std::vector<size_t> in_bytes, out_bytes;
+    DevBuf err;
+    std::unique_ptr<PinnedBuf> err_host;
+    DevBuf positions, pos0, routes;
+    Graph graph;
+    int launches = 0;
+
+    ~chroma_b200_program() {
+        if (stream) {
+            int prev = 0;
+            cudaGetDevice(&prev);
+            cudaSetDevice(device);
+            cudaStreamSynchronize(stream);
+            cudaStreamDestroy(stream);
+            cudaSetDevice(prev);
+        }
+    }
+
+    void enqueue(cudaStream_t s) {
+        if (model.desc.kind == CHROMA_B200_MICRO) {
+            const auto& d = model.desc;
+            const int cols = int(d.cols);
+            // Chunks of 8 bf16 per thread; at most 512 threads and 8 chunks per row.
+            int chunks = 1;
+            while (chunks < 8 && (cols + 8 * chunks - 1) / (8 * chunks) > 256) chunks *= 2;
+            int threads = (cols / 8 + chunks - 1) / chunks;
+            threads = (threads + 31) / 32 * 32;
+            const auto* x = in[0].as<const __nv_bfloat16>();
+            const auto* g = in[1].as<const __nv_bfloat16>();
+            const auto* u = in[2].as<const __nv_bfloat16>();
+            const float* w = reinterpret_cast<const float*>(model.at(0));
+            auto* o = out[0].as<__nv_bfloat16>();
+            if (chunks == 1) launch(s, dim3(unsigned(d.rows)), dim3(threads), 0, k_micro<1>, x, g, u, w, o, d.rows, cols, d.eps);
+            else if (chunks == 2) launch(s, dim3(unsigned(d.rows)), dim3(threads), 0, k_micro<2>, x, g, u, w, o, d.rows, cols, d.eps);
+            else if (chunks == 4) launch(s, dim3(unsigned(d.rows)), dim3(threads), 0, k_micro<4>, x, g, u, w, o, d.rows, cols, d.eps);
+            else launch(s, dim3(unsigned(d.rows)), dim3(threads), 0, k_micro<8>, x, g, u, w, o, d.rows, cols, d.eps);
+            launches = 1;
+            return;
+        }
+        exec.enqueue(s);
+        launches = exec.launches;
+    }
+};
+
+struct chroma_b200_decoder {
+    std::shared_ptr<Model> models[2];  // shared with the programs, so either may be destroyed first
+    int device = 0, B = 1, ctx = 0, window = 0, L = 0, row = 0, V = 0, steps = 1;
+    size_t es = 4;
+    cudaStream_t stream = nullptr;
+    DevBuf cache_k, cache_v, slots, pos0, commit_pos, tokens, positions, last, logits, argmax, err;
+    std::unique_ptr<PinnedBuf> host_in, host_out;
+    GptExec ex[2];
+    DevBuf new_k[2], new_v[2];
+    Graph graph[2][2];
+
+    ~chroma_b200_decoder() {
+        if (stream) {
+            int prev = 0;
+            cudaGetDevice(&prev);
+            cudaSetDevice(device);
+            cudaStreamSynchronize(stream);
+            cudaStreamDestroy(stream);
+            cudaSetDevice(prev);
+        }
+    }
+};
+
+namespace {
+
+int fail(char* err, size_t n, int code, const char* msg) {
+    if (err && n) {
+        std::snprintf(err, n, "%s", msg);
+    }
+    return code;
+}
+
+template <typename F> int guarded(char* err, size_t n, F&& f) {
+    try {
+        f();
+        return CHROMA_B200_OK;
+    } catch (const IndexError& e) {
+        return fail(err, n, CHROMA_B200_INDEX, e.what());
+    } catch (const ValueError& e) {
+        return fail(err, n, CHROMA_B200_VALUE, e.what());
+    } catch (const std::exception& e) {
+        return fail(err, n, CHROMA_B200_RUNTIME, e.what());
+    } catch (...) {
+        return fail(err, n, CHROMA_B200_RUNTIME, "unknown native error");
+    }
+}
+
+void read_error_word(cudaStream_t s, DevBuf& err, unsigned* host) {
+    check(cudaMemcpyAsync(host, err.p, sizeof(unsigned), cudaMemcpyDeviceToHost, s), "Read index error");
+    check(cudaStreamSynchronize(s), "CUDA execution");
+    if (*host & kErrIndex) throw IndexError("Tensor index out of range");
+}
+
+}  // namespace
+
+extern "C" {
+
+int chroma_b200_create(const chroma_b200_desc* desc, const char* weights_path, chroma_b200_program** out, char* err,
+                       size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!desc || !weights_path || !out) throw ValueError("null argument");
+        validate_desc(*desc);
+        auto p = std::make_unique<chroma_b200_program>();
+        check(cudaGetDevice(&p->device), "cudaGetDevice");
+        cudaDeviceProp prop{};
+        check(cudaGetDeviceProperties(&prop, p->device), "cudaGetDeviceProperties");
+        if (prop.major != 10)
+            throw std::runtime_error(std::string("chroma_b200 kernels are built for sm_100a (B200); found ") + prop.name);
+        p->name = prop.name;
+        Model& m = p->model;
+        m.desc = *desc;
+        m.device = p->device;
+        m.offsets.assign(desc->offsets, desc->offsets + desc->num_offsets);
+        for (int64_t off : m.offsets)
+            if (off < 0 || off >= desc->weight_bytes || off % 16) throw ValueError("weight offset out of range or unaligned");
+        m.weights = load_weights(weights_path, size_t(desc->weight_bytes), p->device);
+        m.desc.offsets = nullptr;
+        m.desc.inv_freq = nullptr;
+        m.desc.layer_window = nullptr;
+        check(cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking), "cudaStreamCreateWithFlags");
+        p->err = DevBuf(sizeof(unsigned));
+        p->err_host = std::make_unique<PinnedBuf>(sizeof(unsigned));
+        check(cudaMemset(p->err.p, 0, sizeof(unsigned)), "cudaMemset");
+        const auto& d = *desc;
+        if (d.kind == CHROMA_B200_MICRO) {
+            const size_t bytes = size_t(d.rows) * size_t(d.cols) * 2;
+            for (int i = 0; i < 3; ++i) {
+                p->in.emplace_back(bytes);
+                p->in_bytes.push_back(bytes);
+            }
+            p->out.emplace_back(bytes);
+            p->out_bytes.push_back(bytes);
+        } else {
+            Dims& dm = m.dm;
+            dm.d = d.hidden;
+            dm.H = d.heads;
+            dm.KV = d.kv_heads;
+            dm.hd = d.head_dim;
+            dm.G = d.heads / d.kv_heads;
+            dm.E = d.experts;
+            dm.k = d.top_k;
+            dm.I = d.intermediate;
+            dm.V = d.vocab;
+            dm.eps = d.eps;
+            dm.sm_scale = d.sm_scale;
+            dm.alpha = d.swiglu_alpha;
+            dm.limit = d.swiglu_limit;
+            dm.conc = d.rope_concentration;
+            m.layer_window.assign(desc->layer_window, desc->layer_window + d.layers);
+            m.inv_freq = DevBuf(size_t(d.head_dim / 2) * 4);
+            check(cudaMemcpy(m.inv_freq.p, desc->inv_freq, size_t(d.head_dim / 2) * 4, cudaMemcpyHostToDevice), "rope table");
+            const size_t es = storage_size(d.storage);
+            const size_t n = size_t(d.tokens);
+            const size_t V = size_t(d.vocab);
+            const size_t cache = size_t(d.layers) * d.context * d.kv_heads * d.head_dim * es;
+            const size_t rows_kv = size_t(d.layers) * n * d.kv_heads * d.head_dim * es;
+            GptIO& io = p->exec.io;
+            if (d.kind == CHROMA_B200_GPTOSS_CACHED) {
+                const size_t mask = n * (d.context + n) * es;
+                const size_t sizes[7] = {n * 8, n * 4, cache, cache, mask, mask, 8};
+                for (size_t b : sizes) {
+                    p->in.emplace_back(b);
+                    p->in_bytes.push_back(b);
+                }
+                const size_t osz[3] = {V * es, rows_kv, rows_kv};
+                for (size_t b : osz) {
+                    p->out.emplace_back(b);
+                    p->out_bytes.push_back(b);
+                }
+                p->exec.init(m, 1, int(n), d.context, kMaskBuffer, d.window);
+                io.tokens = p->in[0].as<const int64_t>();
+                io.positions = p->in[1].as<const float>();
+                io.cache_k = p->in[2].p;
+                io.cache_v = p->in[3].p;
+                io.mask = p->in[4].p;
+                io.window_mask = p->in[5].p;
+                io.rows = p->in[6].as<const int64_t>();
+                io.logits = p->out[0].p;
+                io.new_k = p->out[1].p;
+                io.new_v = p->out[2].p;
+            } else {
+                p->in.emplace_back(n * 8);
+                p->in_bytes.push_back(n * 8);
+                const bool last = d.kind == CHROMA_B200_GPTOSS_LAST;
+                if (last) {
+                    p->in.emplace_back(8);
+                    p->in_bytes.push_back(8);
+                }
+                const size_t ob = (last ? 1 : n) * V * es;
+                p->out.emplace_back(ob);
+                p->out_bytes.push_back(ob);
+                p->exec.init(m, 1, int(n), 0, kMaskCausal, d.window);
+                p->positions = DevBuf(n * 4);
+                std::vector<float> pos(n);
+                for (size_t i = 0; i < n; ++i) pos[i] = float(i);
+                check(cudaMemcpy(p->positions.p, pos.data(), n * 4, cudaMemcpyHostToDevice), "positions");
+                io.tokens = p->in[0].as<const int64_t>();
+                io.positions = p->positions.as<const float>();
+                io.rows = last ? p->in[1].as<const int64_t>() : nullptr;
+                io.logits = p->out[0].p;
+            }
+            p->exec.err = p->err.as<unsigned>();
+            p->routes = DevBuf(size_t(d.layers) * n * d.top_k * 4);
+            check(cudaMemset(p->routes.p, 0xff, p->routes.bytes), "routes");
+            io.routes = p->routes.as<int>();
+        }
+        check(cudaDeviceSynchronize(), "create");
+        *out = p.release();
+    });
+}
+
+int chroma_b200_run(chroma_b200_program* p, const void* const* inputs, void* const* outputs, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!p) throw ValueError("null program");
+        DeviceGuard guard(p->device);
+        unsigned* eh = static_cast<unsigned*>(p->err_host->p);
+        try {
+            check(cudaMemsetAsync(p->err.p, 0, sizeof(unsigned), p->stream), "Reset index error");
+            for (size_t i = 0; i < p->in.size(); ++i)
+                check(cudaMemcpyAsync(p->in[i].p, inputs[i], p->in_bytes[i], cudaMemcpyHostToDevice, p->stream),
+                      "Upload input");
+            p->graph.run(p->stream, [&](cudaStream_t s) { p->enqueue(s); });
+            read_error_word(p->stream, p->err, eh);
+            for (size_t i = 0; i < p->out.size(); ++i)
+                check(cudaMemcpyAsync(outputs[i], p->out[i].p, p->out_bytes[i], cudaMemcpyDeviceToHost, p->stream),
+                      "Download output");
+            check(cudaStreamSynchronize(p->stream), "Download output");
+        } catch (...) {
+            // Host buffers must outlive every queued transfer (runtime.h:168-172).
+            cudaStreamSynchronize(p->stream);
+            throw;
+        }
+    });
+}
+
+int chroma_b200_buffers(chroma_b200_program* p, void** inputs, void** outputs, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!p) throw ValueError("null program");
+        for (size_t i = 0; i < p->in.size(); ++i)
+            if (inputs) inputs[i] = p->in[i].p;
+        for (size_t i = 0; i < p->out.size(); ++i)
+            if (outputs) outputs[i] = p->out[i].p;
+    });
+}
+
+int chroma_b200_run_device(chroma_b200_program* p, void* stream, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!p) throw ValueError("null program");
+        DeviceGuard guard(p->device);
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : p->stream;
+        p->graph.run(s, [&](cudaStream_t st) { p->enqueue(st); });
+    });
+}
+
+int chroma_b200_check(chroma_b200_program* p, void* stream, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!p) throw ValueError("null program");
+        DeviceGuard guard(p->device);
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : p->stream;
+        unsigned* eh = static_cast<unsigned*>(p->err_host->p);
+        check(cudaMemcpyAsync(eh, p->err.p, sizeof(unsigned), cudaMemcpyDeviceToHost, s), "Read index error");
+        check(cudaMemsetAsync(p->err.p, 0, sizeof(unsigned), s), "Reset index error");
+        check(cudaStreamSynchronize(s), "CUDA execution");
+        if (*eh & kErrIndex) throw IndexError("Tensor index out of range");
+    });
+}
+
+const char* chroma_b200_device(const chroma_b200_program* p) { return p ? p->name.c_str() : ""; }
+
+int32_t chroma_b200_launches(const chroma_b200_program* p) { return p ? p->launches : 0; }
+
+void chroma_b200_destroy(chroma_b200_program* p) { delete p; }
+
+int64_t chroma_b200_plan_arena(int32_t count, const int64_t* sizes, const int32_t* starts, const int32_t* ends,
+                               int64_t* offsets) {
+    if (count < 0 || (count > 0 && (!sizes || !starts || !ends || !offsets))) return -1;
+    std::vector<Alloc> a(static_cast<size_t>(count));
+    for (int32_t i = 0; i < count; ++i) a[size_t(i)] = {size_t(sizes[i]), starts[i], ends[i], 0};
+    const size_t total = plan_arena(a);
+    for (int32_t i = 0; i < count; ++i) offsets[i] = int64_t(a[size_t(i)].offset);
+    return int64_t(total);
+}
+
+int chroma_b200_routes(chroma_b200_program* p, int32_t* out, int64_t count, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!p || !out) throw ValueError("null argument");
+        if (!p->routes.p || size_t(count) * 4 != p->routes.bytes) throw ValueError("routes buffer size mismatch");
+        DeviceGuard guard(p->device);
+        check(cudaMemcpyAsync(out, p->routes.p, p->routes.bytes, cudaMemcpyDeviceToHost, p->stream), "routes");
+        check(cudaStreamSynchronize(p->stream), "routes");
+    });
+}
+
+int64_t chroma_b200_workspace_bytes(const chroma_b200_program* p) { return p ? int64_t(p->exec.arena_bytes) : 0; }
+
+// ---------------------------------------------------------------------------------------------------------
+int chroma_b200_decoder_create(chroma_b200_program* prefill, chroma_b200_program* decode, int32_t sliding_window,
+                               int32_t batch, chroma_b200_decoder** out, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!prefill || !decode || !out) throw ValueError("null argument");
+        const auto& pd = prefill->model.desc;
+        const auto& dd = decode->model.desc;
+        if (pd.kind != CHROMA_B200_GPTOSS_CACHED || dd.kind != CHROMA_B200_GPTOSS_CACHED || dd.tokens != 1 ||
+            pd.context != dd.context || pd.layers != dd.layers || pd.vocab != dd.vocab || pd.storage != dd.storage ||
+            pd.tokens < 1 || pd.tokens > pd.context)
+            throw ValueError("Decoder prefill and decode were not exported as a pair");
+        if (batch < 1) throw ValueError("batch must be positive");
+        if (sliding_window < 0) throw ValueError("sliding_window must be nonnegative");
+        DeviceGuard guard(decode->device);
+        auto d = std::make_unique<chroma_b200_decoder>();
+        d->models[0] = prefill->model_ptr;
+        d->models[1] = decode->model_ptr;
+        d->device = decode->device;
+        d->B = batch;
+        d->ctx = dd.context;
+        d->window = sliding_window > 0 ? std::min(sliding_window, dd.context) : dd.context;
+        d->L = dd.layers;
+        d->row = dd.kv_heads * dd.head_dim;
+        d->V = dd.vocab;
+        d->steps = pd.tokens;
+        d->es = storage_size(dd.storage);
+        check(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking), "cudaStreamCreateWithFlags");
+        const size_t cache = size_t(batch) * d->L * d->ctx * d->row * d->es;
+        d->cache_k = DevBuf(cache);
+        d->cache_v = DevBuf(cache);
+        check(cudaMemset(d->cache_k.p, 0, cache), "cache");
+        check(cudaMemset(d->cache_v.p, 0, cache), "cache");
+        d->slots = DevBuf(size_t(batch) * d->ctx * 8);
+        check(cudaMemset(d->slots.p, 0xff, size_t(batch) * d->ctx * 8), "slots");
+        d->pos0 = DevBuf(size_t(batch) * 8);
+        d->commit_pos = DevBuf(size_t(batch) * 8);
+        d->tokens = DevBuf(size_t(batch) * d->steps * 8);
+        d->positions = DevBuf(size_t(batch) * d->steps * 4);
+        d->last = DevBuf(size_t(batch) * 8);
+        d->logits = DevBuf(size_t(batch) * d->V * d->es);
+        d->argmax = DevBuf(size_t(batch) * 8);
+        d->err = DevBuf(sizeof(unsigned));
+        check(cudaMemset(d->err.p, 0, sizeof(unsigned)), "cudaMemset");
+        d->host_in = std::make_unique<PinnedBuf>(size_t(batch) * (d->steps + 1) * 8);
+        d->host_out = std::make_unique<PinnedBuf>(size_t(batch) * 8 + 16);
+        for (int i = 0; i < 2; ++i) {
+            const int n = d->models[i]->desc.tokens;
+            const size_t staged = size_t(d->L) * batch * n * d->row * d->es;
+            d->new_k[i] = DevBuf(staged);
+            d->new_v[i] = DevBuf(staged);
+            GptExec& e = d->ex[i];
+            e.init(*d->models[i], batch, n, d->ctx, kMaskSlots, d->window);
+            e.err = d->err.as<unsigned>();
+            e.io.tokens = d->tokens.as<const int64_t>();
+            e.io.positions = d->positions.as<const float>();
+            e.io.cache_k = d->cache_k.p;
+            e.io.cache_v = d->cache_v.p;
+            e.io.new_k = d->new_k[i].p;
+            e.io.new_v = d->new_v[i].p;
+            e.io.slots = d->slots.as<const int64_t>();
+            e.io.pos0 = d->pos0.as<const int64_t>();
+            e.io.rows = d->last.as<const int64_t>();
+            e.io.logits = d->logits.p;
+            e.io.argmax = nullptr;
+        }
+        check(cudaDeviceSynchronize(), "decoder create");
+        *out = d.release();
+    });
+}
+
+int chroma_b200_decoder_step(chroma_b200_decoder* d, int32_t use_decode, const int64_t* tokens, int32_t count,
+                             const int64_t* positions, void* logits, int64_t* argmax, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!d || !tokens || !positions) throw ValueError("null argument");
+        const int which = use_decode ? 1 : 0;
+        GptExec& e = d->ex[which];
+        const int n = e.n;
+        if (count < 1 || count > n) throw ValueError("count out of range for this program");
+        DeviceGuard guard(d->device);
+        cudaStream_t s = d->stream;
+        int64_t* hin = static_cast<int64_t*>(d->host_in->p);
+        std::memcpy(hin, tokens, size_t(d->B) * n * 8);
+        std::memcpy(hin + size_t(d->B) * n, positions, size_t(d->B) * 8);
+        try {
+            check(cudaMemsetAsync(d->err.p, 0, sizeof(unsigned), s), "Reset index error");
+            check(cudaMemcpyAsync(d->tokens.p, hin, size_t(d->B) * n * 8, cudaMemcpyHostToDevice, s), "Upload tokens");
+            check(cudaMemcpyAsync(d->pos0.p, hin + size_t(d->B) * n, size_t(d->B) * 8, cudaMemcpyHostToDevice, s),
+                  "Upload positions");
+            launch(s, dim3((d->B * n + 255) / 256), dim3(256), 0, k_positions, d->pos0.as<const int64_t>(), d->B, n,
+                   d->positions.as<float>(), d->last.as<int64_t>(), count);
+            // The argmax flag changes the kernel list, so each (program, argmax) pair has its own captured graph.
+            e.io.argmax = argmax ? d->argmax.as<int64_t>() : nullptr;
+            d->graph[which][argmax ? 1 : 0].run(s, [&](cudaStream_t st) { e.enqueue(st); });
+            unsigned* eh = static_cast<unsigned*>(d->host_out->p);
+            int64_t* am = reinterpret_cast<int64_t*>(static_cast<char*>(d->host_out->p) + 16);
+            check(cudaMemcpyAsync(eh, d->err.p, sizeof(unsigned), cudaMemcpyDeviceToHost, s), "Read index error");
+            if (argmax)
+                check(cudaMemcpyAsync(am, d->argmax.p, size_t(d->B) * 8, cudaMemcpyDeviceToHost, s), "Download argmax");
+            if (logits)
+                check(cudaMemcpyAsync(logits, d->logits.p, size_t(d->B) * d->V * d->es, cudaMemcpyDeviceToHost, s),
+                      "Download logits");
+            check(cudaStreamSynchronize(s), "CUDA execution");
+            if (*eh & kErrIndex) throw IndexError("Tensor index out of range");
+            if (argmax) std::memcpy(argmax, am, size_t(d->B) * 8);
+        } catch (...) {
+            cudaStreamSynchronize(s);
+            throw;
+        }
+    });
+}
+
+int chroma_b200_decoder_commit(chroma_b200_decoder* d, int32_t use_decode, int32_t count, const int64_t* positions,
+                               char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!d || !positions) throw ValueError("null argument");
+        const int which = use_decode ? 1 : 0;
+        const GptExec& e = d->ex[which];
+        if (count < 1 || count > e.n) throw ValueError("count out of range for this program");
+        DeviceGuard guard(d->device);
+        // Re-upload the chunk's positions: committing is idempotent and independent of later steps' pos0.
+        int64_t* hin = static_cast<int64_t*>(d->host_in->p);
+        std::memcpy(hin, positions, size_t(d->B) * 8);
+        check(cudaMemcpyAsync(d->commit_pos.p, hin, size_t(d->B) * 8, cudaMemcpyHostToDevice, d->stream), "commit positions");
+        const dim3 grid(unsigned(d->L * d->B * count));
+        const int threads = std::min(256, ((d->row + 31) / 32) * 32);
+        if (d->es == 2)
+            launch(d->stream, grid, dim3(threads), 0, k_commit<__nv_bfloat16>, d->new_k[which].as<const __nv_bfloat16>(),
+                   d->new_v[which].as<const __nv_bfloat16>(), d->L, d->B, e.n, count, d->ctx, d->row, 1,
+                   d->commit_pos.as<const int64_t>(), d->cache_k.as<__nv_bfloat16>(), d->cache_v.as<__nv_bfloat16>(),
+                   d->slots.as<int64_t>());
+        else
+            launch(d->stream, grid, dim3(threads), 0, k_commit<float>, d->new_k[which].as<const float>(),
+                   d->new_v[which].as<const float>(), d->L, d->B, e.n, count, d->ctx, d->row, 1,
+                   d->commit_pos.as<const int64_t>(), d->cache_k.as<float>(), d->cache_v.as<float>(), d->slots.as<int64_t>());
+        check(cudaStreamSynchronize(d->stream), "commit");
+    });
+}
+
+int chroma_b200_decoder_reset(chroma_b200_decoder* d, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!d) throw ValueError("null decoder");
+        DeviceGuard guard(d->device);
+        check(cudaMemsetAsync(d->slots.p, 0xff, size_t(d->B) * d->ctx * 8, d->stream), "reset");
+        check(cudaMemsetAsync(d->cache_k.p, 0, d->cache_k.bytes, d->stream), "reset");
+        check(cudaMemsetAsync(d->cache_v.p, 0, d->cache_v.bytes, d->stream), "reset");
+        check(cudaStreamSynchronize(d->stream), "reset");
+    });
+}
+
+int chroma_b200_decoder_read(chroma_b200_decoder* d, void* keys, void* values, int64_t* slots, char* err,
+                             size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!d) throw ValueError("null decoder");
+        DeviceGuard guard(d->device);
+        if (keys) check(cudaMemcpyAsync(keys, d->cache_k.p, d->cache_k.bytes, cudaMemcpyDeviceToHost, d->stream), "read");
+        if (values) check(cudaMemcpyAsync(values, d->cache_v.p, d->cache_v.bytes, cudaMemcpyDeviceToHost, d->stream), "read");
+        if (slots) check(cudaMemcpyAsync(slots, d->slots.p, d->slots.bytes, cudaMemcpyDeviceToHost, d->stream), "read");
+        check(cudaStreamSynchronize(d->stream), "read");
+    });
+}
+
+void chroma_b200_decoder_destroy(chroma_b200_decoder* d) { delete d; }
+
+}  // extern "C"

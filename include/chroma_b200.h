@@ -1,0 +1,129 @@
+/* chroma_b200: C ABI of the B200-native (sm_100a) backend for Chroma's compiled GPT-OSS-style programs.
+ *
+ * Every entry point takes plain pointers and sizes. Host buffers are caller-owned; all device memory is owned
+ * by the objects created here. Calls return a status code; on failure a NUL-terminated message is written to
+ * `err` (at most `err_len` bytes, may be NULL).
+ *
+ * The boundary replaces the native side of a compiled reference artefact:
+ *   - `create_model(const char* weights_file)` and `ModelProgram::run(const void* const* inputs,
+ *     void* const* outputs)` emitted by the CUDA generator (chroma/_src/codegen/cuda/codegen.py:13-41), and
+ *   - the runtime they drive, `chroma::cuda::Runner::{initialize, run}` (chroma/_src/codegen/cuda/runtime.h:116-173),
+ *   - exposed to Python as `Model(weights).run(inputs, outputs)` / `.device` (chroma/_src/core/bindings.h:35-75).
+ */
+#ifndef CHROMA_B200_H
+#define CHROMA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. They map to the exceptions the reference raises (runtime.h:63-73 and :160-162,
+ * bindings.h:17-33): INDEX -> IndexError, VALUE -> ValueError, RUNTIME -> RuntimeError. */
+#define CHROMA_B200_OK 0
+#define CHROMA_B200_INDEX 1
+#define CHROMA_B200_VALUE 2
+#define CHROMA_B200_RUNTIME 3
+
+/* Program kinds (what one `run` computes). */
+#define CHROMA_B200_GPTOSS_FORWARD 1 /* Transformer.forward: tokens[n] -> logits[n, V] (gpt_oss.py:304-310) */
+#define CHROMA_B200_GPTOSS_CACHED 2  /* CachedTransformer step: 7 inputs -> 3 outputs (cached.py:16-51) */
+#define CHROMA_B200_MICRO 3          /* rmsnorm(x)*w -> z=y*g -> z*sigmoid(z)*u + x, bf16 [rows, cols] */
+#define CHROMA_B200_GPTOSS_LAST 4    /* UncachedTransformer: tokens[n], position[1] -> logits[1, V] (cached.py:54-65) */
+
+#define CHROMA_B200_FP32 0
+#define CHROMA_B200_BF16 1
+
+/* Weight tensors of a GPT-OSS program, as byte offsets into the weights file, in this order:
+ *   [0] embedding [V, d]       [1] final norm scale [d] (fp32)   [2] unembedding [V, d]
+ *   then per layer l, at 3 + 13*l + i:
+ *   i=0 attn norm [d] (fp32)   1 sinks [H]   2 qkv.weight [(H+2KV)*hd, d]   3 qkv.bias   4 out.weight [d, H*hd]
+ *   5 out.bias [d]   6 mlp norm [d] (fp32)   7 gate.weight [E, d]   8 gate.bias [E]   9 mlp1_weight [E, 2I, d]
+ *   10 mlp1_bias [E, 2I]   11 mlp2_weight [E, d, I]   12 mlp2_bias [E, d]
+ * Tensors other than the norm scales are in the program's storage type. Offsets are 256-byte aligned.
+ * A MICRO program has a single tensor: [0] the fp32 norm weight [cols]. */
+typedef struct chroma_b200_desc {
+    int32_t kind;
+    int32_t storage;
+    int32_t layers, hidden, heads, kv_heads, head_dim, experts, top_k, intermediate, vocab;
+    int32_t tokens;      /* rows per call (n) */
+    int32_t context;     /* cache rows (CACHED) */
+    int32_t window;      /* sliding window of the layers that use one (0 = none) */
+    float eps, sm_scale, swiglu_alpha, swiglu_limit, rope_concentration;
+    int64_t rows, cols;  /* MICRO shape */
+    const float* inv_freq;        /* [head_dim / 2] RoPE inverse frequencies */
+    const int32_t* layer_window;  /* [layers]: 1 if the layer uses the window (mask) input */
+    const int64_t* offsets;       /* weight offsets, see above */
+    int32_t num_offsets;
+    int64_t weight_bytes;         /* exact size of the weights file */
+} chroma_b200_desc;
+
+typedef struct chroma_b200_program chroma_b200_program;
+typedef struct chroma_b200_decoder chroma_b200_decoder;
+
+/* Loads the weights once and allocates every device buffer a call needs on the CURRENT device
+ * (the reference binds a Program to the current device the same way, runtime.h:118).
+ * Replaces create_model()/Runner::initialize. */
+int chroma_b200_create(const chroma_b200_desc* desc, const char* weights_path, chroma_b200_program** out,
+                       char* err, size_t err_len);
+
+/* One call on host buffers: uploads inputs, runs, downloads outputs, synchronises. Input and output
+ * order and byte sizes are those of the program's manifest. Replaces ModelProgram::run / Runner::run. */
+int chroma_b200_run(chroma_b200_program* program, const void* const* inputs, void* const* outputs, char* err,
+                    size_t err_len);
+
+/* Device-resident execution for benchmarks and fused pipelines: device pointers of the program's own input
+ * and output buffers (valid until destroy), and one run on them, queued on `stream` (a cudaStream_t, 0 for the
+ * program's own stream). `chroma_b200_run_device` does not synchronise; it returns after queuing. */
+int chroma_b200_buffers(chroma_b200_program* program, void** inputs, void** outputs, char* err, size_t err_len);
+int chroma_b200_run_device(chroma_b200_program* program, void* stream, char* err, size_t err_len);
+/* Reads and clears the program's device error word after a run_device (synchronises `stream`). */
+int chroma_b200_check(chroma_b200_program* program, void* stream, char* err, size_t err_len);
+
+/* Device name of the program's GPU (bindings.h:39 `device`). */
+const char* chroma_b200_device(const chroma_b200_program* program);
+/* Number of kernels one run launches (for launch accounting). */
+int32_t chroma_b200_launches(const chroma_b200_program* program);
+void chroma_b200_destroy(chroma_b200_program* program);
+
+/* Activation arena planner used by every program: best fit over inclusive [start, end] kernel-index lifetimes with
+ * a coalesced free list, visiting allocations by start (the reference's plan_memory, chroma/_src/memory.py:12-50).
+ * Writes each allocation's byte offset and returns the arena size (-1 on bad arguments). Needs no GPU. */
+int64_t chroma_b200_plan_arena(int32_t count, const int64_t* sizes, const int32_t* starts, const int32_t* ends,
+                               int64_t* offsets);
+/* Routing of the last run of a GPT-OSS program: the selected experts [layers, tokens, top_k] in rank order (the
+ * indices of torch.topk(..., sorted=True) at gpt_oss.py:246), for parity checks. `count` is the element count. */
+int chroma_b200_routes(chroma_b200_program* program, int32_t* out, int64_t count, char* err, size_t err_len);
+/* Arena bytes of a program's executor (the manifest's workspace_bytes). */
+int64_t chroma_b200_workspace_bytes(const chroma_b200_program* program);
+
+/* Device-resident KV-cached decoding for a prefill/decode pair (the pair chroma.Decoder drives,
+ * chroma/_src/decoder.py:44-152), for `batch` independent sequences. The cache [batch, L, ctx, KV, hd] stays in
+ * device memory; masks are built on the device from each sequence's ring-slot positions with the semantics of
+ * decoder.py:115-127. */
+int chroma_b200_decoder_create(chroma_b200_program* prefill, chroma_b200_program* decode, int32_t sliding_window,
+                               int32_t batch, chroma_b200_decoder** out, char* err, size_t err_len);
+/* One chunk for every sequence: `tokens` [batch, steps] (steps = 1 for decode, the prefill width otherwise;
+ * entries past `count` are padding), `positions` [batch] absolute position of each sequence's first token.
+ * Writes the logits of row count-1 to `logits` [batch, V] (storage type) when non-NULL, and the greedy argmax
+ * (lowest index on ties) to `argmax` [batch] when non-NULL. New K/V rows are staged, not committed. */
+int chroma_b200_decoder_step(chroma_b200_decoder* decoder, int32_t use_decode, const int64_t* tokens, int32_t count,
+                             const int64_t* positions, void* logits, int64_t* argmax, char* err, size_t err_len);
+/* Writes rows [0, count) staged by the last step of the given program into ring slots (position % ctx) and
+ * records their positions; `positions` [batch] are that step's first positions. Idempotent until the same
+ * program steps again, so a host may commit lazily (decoder.py:130-137 commits only after a call succeeds). */
+int chroma_b200_decoder_commit(chroma_b200_decoder* decoder, int32_t use_decode, int32_t count,
+                               const int64_t* positions, char* err, size_t err_len);
+/* Empties every sequence's cache. */
+int chroma_b200_decoder_reset(chroma_b200_decoder* decoder, char* err, size_t err_len);
+/* Copies the committed cache and slot positions to host buffers ([batch, L, ctx, KV, hd] twice, [batch, ctx]). */
+int chroma_b200_decoder_read(chroma_b200_decoder* decoder, void* keys, void* values, int64_t* slots, char* err,
+                             size_t err_len);
+void chroma_b200_decoder_destroy(chroma_b200_decoder* decoder);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

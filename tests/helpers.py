@@ -1,0 +1,66 @@
+"""Shared test helpers: seeded models, oracle parameters, comparison utilities."""
+
+from __future__ import annotations
+
+import dataclasses
+import functools
+
+import numpy as np
+
+from oracle import gpt_oss as og
+
+
+@functools.lru_cache(maxsize=None)
+def dev_model():  # type: ignore[no-untyped-def]
+    from chroma_b200.models import make_dev_model
+
+    return make_dev_model(0)
+
+
+@functools.lru_cache(maxsize=None)
+def dev_oracle() -> tuple[og.Config, og.Params]:
+    from chroma_b200.models import dev
+
+    return og.Config.from_model_config(dev), og.Params.from_module(dev_model())
+
+
+def small_config(kind: str):  # type: ignore[no-untyped-def]
+    """The reference tests' small configurations (tests/test_cuda.py:29-43, tests/test_decoder.py:21-37)."""
+    from chroma_b200.models import dev
+
+    if kind == "cuda_small":
+        return dataclasses.replace(dev, num_hidden_layers=1, num_experts=2, experts_per_token=2, vocab_size=17,
+                                   hidden_size=8, intermediate_size=8, head_dim=4, num_attention_heads=2,
+                                   num_key_value_heads=1, sliding_window=3)
+    head_dim = int(kind.rsplit("_", 1)[1])
+    return dataclasses.replace(dev, num_hidden_layers=2, hidden_size=16, intermediate_size=16, vocab_size=31,
+                               num_experts=4, experts_per_token=2, num_attention_heads=4, num_key_value_heads=2,
+                               head_dim=head_dim, sliding_window=3, initial_context_length=4096,
+                               rope_scaling_factor=32.0 if head_dim == 64 else 1.0)
+
+
+def cuda_small_model(dtype):  # type: ignore[no-untyped-def]
+    """Seed 5, N(0, 0.1), cast before init (tests/test_cuda.py:29-43)."""
+    import torch
+
+    from chroma_b200.models import Transformer, init_weights
+
+    with torch.random.fork_rng(devices=[]):
+        torch.manual_seed(5)
+        model = Transformer(small_config("cuda_small")).to(dtype).eval()
+        return init_weights(model, std=0.1, zero_bias=False)
+
+
+def decoder_small_model(head_dim: int):  # type: ignore[no-untyped-def]
+    from chroma_b200.models import random_transformer
+
+    return random_transformer(small_config(f"decoder_small_{head_dim}"), seed=5, std=0.03)
+
+
+def assert_logits(actual: np.ndarray, expected: np.ndarray, *, rtol: float, atol: float) -> None:
+    np.testing.assert_allclose(np.asarray(actual, np.float32), np.asarray(expected, np.float32), rtol=rtol, atol=atol)
+
+
+def summary(logits: np.ndarray, cols: np.ndarray) -> dict[str, np.ndarray]:
+    logits = np.asarray(logits, np.float32).reshape(-1, logits.shape[-1])
+    return {"argmax": np.argmax(logits, -1), "sample": logits[:, cols], "rowsum": logits.astype(np.float64).sum(-1)}

@@ -1,0 +1,242 @@
+"""GPU parity of the GPT-OSS kernels against the reference's golden vectors and the oracle.
+
+Bars (from the backend's contract): argmax token ids and routing indices identical; fp32 logits within 1e-4
+relative (atol 1e-5 for near-zero logits); bf16 logits within 2e-2 relative (atol 1e-2).
+"""
+
+from __future__ import annotations
+
+import functools
+import os
+import subprocess
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import chroma_b200
+from chroma_b200 import models
+from oracle import gpt_oss as og
+from tests import helpers
+from tests.conftest import ROOT, golden
+
+pytestmark = pytest.mark.gpu
+FP32 = {"rtol": 1e-4, "atol": 1e-5}
+BF16 = {"rtol": 2e-2, "atol": 1e-2}
+_TMP = Path(tempfile.mkdtemp(prefix="chroma-b200-tests-"))
+
+
+@functools.lru_cache(maxsize=None)
+def dev_forward() -> chroma_b200.Program:
+    ep = torch.export.export(helpers.dev_model(), (torch.arange(8),))
+    return chroma_b200.compile(ep, _TMP / "dev_fwd8")
+
+
+@functools.lru_cache(maxsize=None)
+def dev_pair() -> tuple[Path, Path]:
+    model = helpers.dev_model()
+    chroma_b200.compile(models.export_cached(model, 256, 8), _TMP / "dev_prefill8").close()
+    chroma_b200.compile(models.export_cached(model, 256, 1), _TMP / "dev_decode").close()
+    return _TMP / "dev_prefill8", _TMP / "dev_decode"
+
+
+def dev_decoder() -> chroma_b200.Decoder:
+    prefill, decode = dev_pair()
+    return chroma_b200.Decoder(chroma_b200.Program(prefill), chroma_b200.Program(decode))
+
+
+def test_c1_forward_matches_reference(gpu: None) -> None:
+    g = golden("c1_fwd8")
+    program = dev_forward()
+    assert program.stats["backend"] == "cuda" and "B200" in program.device
+    for s, tokens in enumerate(g["tokens"]):
+        logits = program(tokens)
+        np.testing.assert_array_equal(np.argmax(logits, -1), g["argmax"][s])
+        np.testing.assert_allclose(logits[:, g["sample_cols"]], g["sample"][s], **FP32)
+        routes = program.native.routes()
+        np.testing.assert_array_equal(routes, g["routes"][s])
+
+
+def test_c1_routing_margins_are_reported(gpu: None) -> None:
+    # Bit-exact routing is only meaningful when the 4th/5th gate logits are separated by more than the
+    # accumulated rounding error; record the smallest margin the fixtures exercise.
+    g = golden("c1_fwd8")
+    cfg, p = helpers.dev_oracle()
+    margins = []
+    for tokens in g["tokens"]:
+        trace = og.Trace()
+        og.forward(cfg, p, tokens, trace)
+        for gate in trace.gates:
+            top = np.sort(gate, axis=-1)[:, ::-1]
+            margins.append(float(np.min(top[:, 3] - top[:, 4])))
+    assert min(margins) > 1e-5, min(margins)
+
+
+def test_c1_repeated_calls_out_reuse_and_index_errors(gpu: None) -> None:
+    program = dev_forward()
+    tokens = np.arange(8, dtype=np.int64)
+    first = program(tokens)
+    kept = first.copy()
+    program(tokens + 1)
+    np.testing.assert_array_equal(first, kept)
+    out = np.empty_like(first)
+    assert program(tokens, out=out) is out
+    np.testing.assert_array_equal(out, first)
+    for bad in (models.dev.vocab_size, -1, 2**40):
+        with pytest.raises(IndexError):
+            program(np.full(8, bad, dtype=np.int64))
+        np.testing.assert_array_equal(program(tokens), first)
+    for invalid in (np.arange(8, dtype=np.int32), np.arange(7, dtype=np.int64)):
+        with pytest.raises(ValueError):
+            program(invalid)
+    with pytest.raises(ValueError):
+        program()
+    readonly = np.empty_like(first)
+    readonly.setflags(write=False)
+    with pytest.raises(ValueError):
+        program(tokens, out=readonly)
+    noncontiguous = np.arange(16, dtype=np.int64)[::2]
+    np.testing.assert_allclose(program(noncontiguous), og.forward(*helpers.dev_oracle(), noncontiguous), **FP32)
+
+
+def test_c2_decoder_matches_reference(gpu: None) -> None:
+    g = golden("c2_decode")
+    with dev_decoder() as dec:
+        outs = [dec.append(g["prompt"])] + [dec.append([int(t)]) for t in g["forced"]]
+        assert dec.position == 8 + len(g["forced"])
+    for i, out in enumerate(outs):
+        assert out.shape == (1, models.dev.vocab_size)
+        assert int(np.argmax(out)) == int(g["step_argmax"][i][0])
+        np.testing.assert_allclose(out[:, g["sample_cols"]], g["step_sample"][i], **FP32)
+
+
+def test_c2_decoder_ring_wrap(gpu: None) -> None:
+    g = golden("c2_decode")
+    tokens = g["long_tokens"]
+    with dev_decoder() as dec:
+        ids = [int(np.argmax(dec.append(tokens[:8])))]
+        tail = []
+        for i, t in enumerate(tokens[8:]):
+            out = dec.append([int(t)])
+            ids.append(int(np.argmax(out)))
+            if i >= len(tokens) - 8 - 4:
+                tail.append(out)
+    np.testing.assert_array_equal(ids, g["long_argmax"])
+    for out, want in zip(tail, g["tail_sample"]):
+        np.testing.assert_allclose(out[:, g["sample_cols"]], want, **FP32)
+
+
+def test_c2_batch_decoder_matches_reference(gpu: None) -> None:
+    g = golden("c2_decode")
+    prefill, decode = dev_pair()
+    toks = g["batch_tokens"]
+    with chroma_b200.BatchDecoder(chroma_b200.Program(prefill), chroma_b200.Program(decode), len(toks)) as dec:
+        outs = [dec.append(toks[:, :8])] + [dec.append(toks[:, 8 + i : 9 + i]) for i in range(4)]
+        dec.reset()
+        ids = [dec.append(toks[:, :8], argmax=True)] + [dec.append(toks[:, 8 + i : 9 + i], argmax=True) for i in range(4)]
+    for step, (out, am) in enumerate(zip(outs, ids)):
+        np.testing.assert_array_equal(np.argmax(out, -1), g["batch_argmax"][:, step, 0])
+        np.testing.assert_array_equal(am, g["batch_argmax"][:, step, 0])
+        np.testing.assert_allclose(out[:, g["sample_cols"]], g["batch_sample"][:, step, 0], **FP32)
+
+
+def test_c2_program_with_host_masks_matches_device_path(gpu: None) -> None:
+    # The decode Program run directly on host buffers (the reference's seven-input protocol, masks built on the
+    # host) agrees with the device-resident decoder.
+    g = golden("c2_decode")
+    prefill, decode = dev_pair()
+    host = chroma_b200.Decoder(chroma_b200.Program(prefill), chroma_b200.Program(decode))
+    host._native.close()
+    host._native = None
+    host._buffers = [
+        ([np.empty(s["shape"], dtype=chroma_b200._src.native.dtype_of(s["dtype"])) for s in m.inputs],
+         [np.empty(s["shape"], dtype=chroma_b200._src.native.dtype_of(s["dtype"])) for s in m.outputs[1:]])
+        for m in host._models
+    ]
+    host._commit(host._empty())
+    with host:
+        outs = [host.append(g["prompt"])] + [host.append([int(t)]) for t in g["forced"][:4]]
+    for i, out in enumerate(outs):
+        assert int(np.argmax(out)) == int(g["step_argmax"][i][0])
+        np.testing.assert_allclose(out[:, g["sample_cols"]], g["step_sample"][i], **FP32)
+
+
+def test_decoder_errors_keep_state_and_recover(gpu: None) -> None:
+    with dev_decoder() as dec:
+        dec.append([1, 2, 3])
+        before = dec._state
+        for bad in ([-1], [models.dev.vocab_size], [2**40]):
+            with pytest.raises(IndexError):
+                dec.append(bad)
+            assert dec.position == 3 and dec._state is before
+        with pytest.raises(TypeError):
+            dec.append([1.5])
+        with pytest.raises(ValueError):
+            dec.append([])
+        a = dec.append([4])
+    with dev_decoder() as ref:
+        b = ref.append([1, 2, 3, 4])
+    np.testing.assert_allclose(a, b, **FP32)
+
+
+def test_small_models_fp32_and_bf16(gpu: None) -> None:
+    g = golden("small")
+    for dtype, tol in ((torch.float32, FP32), (torch.bfloat16, BF16)):
+        name = str(dtype).split(".")[1]
+        model = helpers.cuda_small_model(dtype)
+        tokens4 = g[f"{name}_full4_tokens"]
+        with chroma_b200.compile(torch.export.export(model, (torch.tensor(tokens4[0]),)), _TMP / f"small_{name}") as prog:
+            for tokens, want in zip(tokens4, g[f"{name}_full4"]):
+                np.testing.assert_allclose(np.asarray(prog(tokens), np.float32), want, **tol)
+            with pytest.raises(IndexError):
+                prog(np.full(4, 17, dtype=np.int64))
+        pre = chroma_b200.compile(models.export_cached(model, 5, 5), _TMP / f"small_{name}_pre")
+        dec_p = chroma_b200.compile(models.export_cached(model, 5, 1), _TMP / f"small_{name}_dec")
+        tokens = (np.arange(14) * 7 + 3) % 17
+        with chroma_b200.Decoder(pre, dec_p, sliding_window=3) as dec:
+            logs, pos = [], 0
+            for size in (2, 1, 4, 5, 2):
+                logs.append(np.asarray(dec.append(tokens[pos : pos + size]), np.float32))
+                pos += size
+            dec.reset()
+            assert dec.position == 0
+            logs.append(np.asarray(dec.append(tokens), np.float32))
+        np.testing.assert_allclose(np.concatenate(logs), g[f"{name}_decoder"], **tol)
+
+
+def test_small_decoders_window_yarn_wrap(gpu: None) -> None:
+    g = golden("small")
+    for head_dim in (8, 64):
+        model = helpers.decoder_small_model(head_dim)
+        pre = chroma_b200.compile(models.export_cached(model, 7, 7), _TMP / f"dec{head_dim}_pre")
+        dec_p = chroma_b200.compile(models.export_cached(model, 7, 1), _TMP / f"dec{head_dim}_dec")
+        tokens = (np.arange(23) * 7 + 3) % 31
+        with chroma_b200.Decoder(pre, dec_p, sliding_window=3) as dec:
+            logs, pos = [], 0
+            for size in (3, 1, 5, 7, 1, 6):
+                logs.append(dec.append(tokens[pos : pos + size]))
+                pos += size
+            dec.reset()
+            logs.append(dec.append(tokens))
+            dec.reset()
+            logs.append(dec.append(tokens[:3]))
+        np.testing.assert_allclose(np.concatenate(logs), g[f"dec{head_dim}_decoder"], **FP32)
+
+
+def test_torch_free_reload(gpu: None) -> None:
+    program = dev_forward()
+    np.save(_TMP / "c1_expected.npy", program(np.arange(8, dtype=np.int64)))
+    code = """
+import sys
+import numpy as np
+from chroma_b200 import Program
+assert 'torch' not in sys.modules
+with Program(sys.argv[1]) as model:
+    np.testing.assert_array_equal(model(np.arange(8, dtype=np.int64)), np.load(sys.argv[2]))
+assert 'torch' not in sys.modules
+"""
+    env = dict(os.environ, PYTHONPATH=str(ROOT))
+    subprocess.run([sys.executable, "-c", code, str(_TMP / "dev_fwd8"), str(_TMP / "c1_expected.npy")], check=True, env=env)
