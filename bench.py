@@ -1,0 +1,383 @@
+"""Benchmark: the dev model's KV-cached greedy decode step on B200 (config C2), plus the 8-token forward (C1).
+
+Headline metric: decode tokens/s at batch 1 per GPU with a 256-token fp32 KV cache (the reference publishes a
+3.27 ms cached decode step on an A100, docs/benchmarks.md:37, i.e. 305.8 tokens/s). One "step" = one decode step
+of every sequence: embedding, 12 layers (norm, QKV, RoPE, sink attention over the cache, out-projection, router,
+4 experts), final norm, the 201,088-way vocab projection, greedy argmax, KV commit and position advance.
+
+* ``value``: device-resident greedy decoding (``BatchDecoder.advance_device``: no host transfer inside the timed
+  region), CUDA events around each step on the launching stream, L2 flushed (256 MiB write) before every timed step.
+* ``e2e``: the public ``Decoder.append([token])`` API from host arrays, logits [1, V] returned to the host, per
+  step wall clock (the call synchronises), L2 flushed before every step.
+* ``batch64`` and ``fwd8``: the same two measurements for 64 sequences and for ``Program(tokens[8])``.
+* ``roofline``: the vocab-projection kernel (the dominant one) launched alone after an L2 flush, CUDA events.
+* ``cpu_baseline``: the reference's own compiled CPU program for this decode step (``oracle/_ref``), 1 thread.
+
+``--impl reference`` times the reference's CPU decode step instead (rank 0 only).
+Multi-GPU (torchrun): one replica per GPU (the dev model does not shard); value = all ranks' tokens / max time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+A100_DECODE_STEP_MS = 3.27  # reference, docs/benchmarks.md:37
+A100_FWD8_MS = 4.25  # reference, docs/benchmarks.md:23
+CONTEXT = 256
+PREFILL = 8
+
+
+def parse() -> argparse.Namespace:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------------------------------------
+class Clocks:
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc: subprocess.Popen | None = None
+
+    def __enter__(self) -> "Clocks":
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        time.sleep(0.2)
+        self.samples: list[list[str]] = []
+        if self.proc is not None:
+            self.proc.terminate()
+            out, _ = self.proc.communicate(timeout=10)
+            self.samples = [[x.strip() for x in line.split(",")] for line in out.splitlines() if line.count(",") >= 7]
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for s in self.samples for n, v in zip(names, s[4:8]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": data["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------------------------------------
+def cpu_reference_decode(seconds: float, steps: int | None = None) -> dict:
+    """The reference's compiled CPU decode step (oracle/_ref/c2_*), driven by the reference Decoder's host algorithm
+    (per-step masks, full-cache inputs, cache copy on commit). Falls back to the NumPy oracle port if the reference
+    programs were not built."""
+    from chroma_b200._src.decoder import Decoder
+
+    tokens = np.random.default_rng(7).integers(0, 201088, 4096)
+    try:
+        from oracle.refprogram import RefProgram, available
+
+        if not (available("c2_prefill8") and available("c2_decode")):
+            raise FileNotFoundError("oracle/_ref/c2_* not built")
+        dec = Decoder(RefProgram("c2_prefill8"), RefProgram("c2_decode"))
+        kind = "reference"
+        step = lambda t: dec.append([int(t)])  # noqa: E731
+        dec.append(tokens[:PREFILL])
+    except (FileNotFoundError, ImportError, OSError) as exc:
+        from oracle import gpt_oss as og
+        from tests.helpers import dev_oracle
+
+        cfg, p = dev_oracle()
+        odec = og.Decoder(cfg, p, CONTEXT, PREFILL)
+        odec.append(tokens[:PREFILL])
+        kind = f"port ({exc})"
+        step = lambda t: odec.append([int(t)])  # noqa: E731
+    step(tokens[PREFILL])  # warm-up
+    n, start = 0, time.perf_counter()
+    while True:
+        step(tokens[PREFILL + 1 + n % 2000])
+        n += 1
+        elapsed = time.perf_counter() - start
+        if (steps is not None and n >= steps) or (steps is None and elapsed >= seconds and n >= 8):
+            break
+    return {"value": n / elapsed, "unit": "tokens/s", "cores": 1, "kind": kind.split(" ")[0],
+            "ms_per_step": 1e3 * elapsed / n,
+            "sample": f"{n} cached decode steps (batch 1, 256-token cache, after an 8-token prefill), "
+                      f"single-threaded generated C++ (blas=False)" + ("" if kind == "reference" else f"; {kind}")}
+
+
+def reference_arm(args: argparse.Namespace) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cpu_reference_decode(0, steps=max(1, args.warmup))
+    res = cpu_reference_decode(0, steps=args.steps)
+    line = {
+        "impl": "reference", "metric": "dev decode tokens/s (KV cache 256, batch 1)", "value": res["value"],
+        "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded dev-model weights, seeded token ids)",
+        "config": {"workload": "C2 dev KV-cached decode, 256-token fp32 cache, batch 1", "model": "gpt-oss dev",
+                   "global_batch": 1, "seq_len": CONTEXT, "parallelism": "none (host CPU, 1 thread)"},
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------------------
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    import torch
+
+    import chroma_b200
+    from chroma_b200 import models
+    from chroma_b200._src.decoder import Decoder
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier() -> None:
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def flush() -> None:
+        flush_buf.fill_(1)
+
+    model = models.make_dev_model(0)
+    V = models.dev.vocab_size
+    tmp = Path(tempfile.mkdtemp(prefix=f"chroma-b200-bench-{rank}-"))
+    prefill = chroma_b200.compile_model(model, tmp / "prefill", steps=PREFILL, context=CONTEXT)
+    decode = chroma_b200.compile_model(model, tmp / "decode", steps=1, context=CONTEXT)
+    fwd8 = chroma_b200.compile_model(model, tmp / "fwd8", steps=8)
+    rng = np.random.default_rng(1234 + rank)
+    prompt = rng.integers(0, V, PREFILL)
+
+    def timed_device(bd: "chroma_b200.BatchDecoder", steps: int) -> list[float]:
+        times = []
+        for _ in range(steps):
+            flush()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            bd.advance_device(1, stream.cuda_stream)
+            e1.record(stream)
+            times.append((e0, e1))
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) for a, b in times]
+
+    # ---- headline: batch-1 device-resident greedy decode
+    bd1 = chroma_b200.BatchDecoder(prefill, decode, 1)
+    first = bd1.append(prompt[None, :], argmax=True)
+    bd1.generate(first, 1)
+    timed_device(bd1, args.warmup)
+    barrier()
+    with Clocks(local) as clocks:
+        step_ms = timed_device(bd1, args.steps)
+        barrier()
+    launches_per_step = bd1._native.step_launches
+    t_rank = sum(step_ms) / 1e3
+    t_max = max_over_ranks(t_rank)
+    value = world * args.steps / t_max
+
+    # ---- roofline: vocab kernel alone (L2 flushed before each launch)
+    vocab_ms = []
+    for i in range(args.warmup + 50):
+        flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        bd1._native.launch_vocab(stream.cuda_stream)
+        e1.record(stream)
+        if i >= args.warmup:
+            vocab_ms.append((e0, e1))
+    torch.cuda.synchronize()
+    vocab_ms = [a.elapsed_time(b) for a, b in vocab_ms]
+    d = models.dev.hidden_size
+    vocab_bytes = V * d * 4 + V * 4 + d * 4  # weights + one logits row + the normed row
+    vocab_t = statistics.mean(vocab_ms) / 1e3
+    pk = peaks()
+    achieved = vocab_bytes / vocab_t / 1e9
+    bd1.close()
+
+    # ---- e2e batch 1 through the public Decoder API
+    dec = Decoder(prefill, decode)
+    forced = rng.integers(0, V, args.warmup + args.steps)
+    dec.append(prompt)
+    for t in forced[: args.warmup]:
+        dec.append([int(t)])
+    barrier()
+    e2e_times = []
+    for t in forced[args.warmup :]:
+        flush()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        logits = dec.append([int(t)])
+        e2e_times.append(time.perf_counter() - t0)
+    e2e_max = max_over_ranks(sum(e2e_times))
+    e2e_value = world * args.steps / e2e_max
+    d2h = logits.nbytes + 4
+    dec._native.close()
+    dec._native = None
+
+    # ---- batch 64: device value and e2e through BatchDecoder.append(argmax=True)
+    B = 64
+    bsteps = max(1, args.steps // 4)
+    bd64 = chroma_b200.BatchDecoder(prefill, decode, B)
+    bprompt = rng.integers(0, V, (B, PREFILL))
+    firsts = bd64.append(bprompt, argmax=True)
+    bd64.generate(firsts, 1)
+    timed_device(bd64, args.warmup)
+    b_ms = timed_device(bd64, bsteps)
+    b_value = world * B * bsteps / max_over_ranks(sum(b_ms) / 1e3)
+    bd64.reset()
+    bforced = rng.integers(0, V, (B, args.warmup + bsteps))
+    bd64.append(bprompt, argmax=True)
+    for i in range(args.warmup):
+        bd64.append(bforced[:, i : i + 1], argmax=True)
+    be2e = []
+    for i in range(args.warmup, args.warmup + bsteps):
+        flush()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        bd64.append(bforced[:, i : i + 1], argmax=True)
+        be2e.append(time.perf_counter() - t0)
+    b_e2e = world * B * bsteps / max_over_ranks(sum(be2e))
+    bd64.close()
+
+    # ---- C1: 8-token forward, device and e2e
+    native = fwd8.native
+    ins, _ = native.buffers()
+    tokens8 = rng.integers(0, V, 8).astype(np.int64)
+    torch.cuda.synchronize()
+    fwd8(tokens8)
+    f_ms = []
+    for i in range(args.warmup + 50):
+        flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        native.run_device(stream.cuda_stream)
+        e1.record(stream)
+        if i >= args.warmup:
+            f_ms.append((e0, e1))
+    native.check(stream.cuda_stream)
+    f_ms = [a.elapsed_time(b) for a, b in f_ms]
+    out8 = np.empty((8, V), np.float32)
+    fe2e = []
+    for i in range(args.warmup + 50):
+        flush()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        fwd8(tokens8, out=out8)
+        if i >= args.warmup:
+            fe2e.append(time.perf_counter() - t0)
+    fwd_dev_ms = max_over_ranks(statistics.median(f_ms))
+    fwd_e2e_ms = max_over_ranks(1e3 * statistics.median(fe2e))
+
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu = cpu_reference_decode(args.cpu_seconds)
+    barrier()
+    if dist is not None:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    ms_per_step = 1e3 * t_max / args.steps
+    line = {
+        "metric": "dev decode tokens/s (KV cache 256, batch 1)",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": value / world / (1e3 / A100_DECODE_STEP_MS),
+        "dtype": "f32",
+        "data": "synthetic (seeded dev-model weights as scripts/export.py:16-29, seeded token ids)",
+        "config": {
+            "workload": "C2: dev GPT-OSS (12 layers, d=128, 59.1M params) KV-cached greedy decode step, "
+                        "256-token fp32 cache, 8-token prefill first, batch 1 per GPU",
+            "model": "gpt-oss dev", "global_batch": world, "seq_len": CONTEXT,
+            "parallelism": f"replicas x{world} (the dev model does not shard)",
+            "l2": "flushed (256 MiB write) before every timed step",
+        },
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": d2h,
+                "api": "chroma_b200.Decoder.append([token]) -> logits [1, 201088] on the host"},
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": {
+            "kernel": "k_vocab (unembedding GEMV, 201088 x 128 fp32, 1 row)", "bound": "hbm", "achieved": achieved,
+            "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
+            "algorithmic_bytes": vocab_bytes, "launch_us": vocab_t * 1e6,
+            "peak_source": f"{pk['source']} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
+            "timing": "launched alone after an L2 flush, CUDA events, mean of 50",
+        },
+        "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "clocks": clocks.summary(),
+        "batch64": {"value": b_value, "unit": "tokens/s", "ms_per_step": statistics.mean(b_ms),
+                    "e2e": {"value": b_e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * 16,
+                            "d2h_bytes_per_step": B * 8 + 4, "api": "BatchDecoder.append(tokens[64,1], argmax=True)"}},
+        "fwd8": {"device_ms": fwd_dev_ms, "e2e_ms": fwd_e2e_ms, "vs_a100_e2e": A100_FWD8_MS / fwd_e2e_ms,
+                 "h2d_bytes": 64, "d2h_bytes": 8 * V * 4, "api": "Program(tokens[8], out=logits)"},
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

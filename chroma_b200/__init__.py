@@ -21,4 +21,12 @@ def compile(input: Any, output: str | Path, *, blas: bool = True, backend: str =
     return compile_for_backend(input, output, blas=blas, backend=backend)
 
 
-__all__ = ["BatchDecoder", "Decoder", "Program", "compile"]
+def compile_model(model: Any, output: str | Path, *, steps: int, context: int | None = None, last: bool = False) -> Program:
+    """Compile a ``chroma_b200.models.Transformer`` straight from its parameters (no ``torch.export``): a forward
+    over ``steps`` tokens, or with ``context`` a KV-cached step of ``steps`` rows (the prefill/decode programs)."""
+    from chroma_b200._src.compiler import compile_model as _compile_model
+
+    return _compile_model(model, output, steps=steps, context=context, last=last)
+
+
+__all__ = ["BatchDecoder", "Decoder", "Program", "compile", "compile_model"]

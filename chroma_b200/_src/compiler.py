@@ -365,6 +365,73 @@ def _lower_micro(g: _Graph) -> Lowered:
                                                                "unreused_workspace_bytes": 0})
 
 
+def lower_model(model: Any, *, steps: int, context: int | None = None, last: bool = False) -> Lowered:
+    """A GPT-OSS program straight from a ``chroma_b200.models.Transformer`` (no export).
+
+    ``context=None``: ``Transformer.forward`` over ``steps`` tokens (``last=True``: the UncachedTransformer variant
+    returning one row); otherwise a CachedTransformer step of ``steps`` rows against a ``context``-row cache. The
+    plan is the one ``lower`` recognises from the corresponding export.
+    """
+    import math as _math
+
+    from chroma_b200.models import rope_tables
+
+    config = model.config
+    state = {k: v.detach() for k, v in model.state_dict().items()}
+    dtype = _DTYPE_NAMES[str(state["embedding.weight"].dtype)]
+    conc, inv_freq = rope_tables(config)
+
+    def T(name: str) -> np.ndarray:
+        return _torch_bytes(state[name], dtype)
+
+    def F(name: str) -> np.ndarray:
+        return _torch_bytes(state[name], "float32")
+
+    L = config.num_hidden_layers
+    tensors = [T("embedding.weight"), F("norm.scale"), T("unembedding.weight")]
+    for layer in range(L):
+        b = f"block.{layer}."
+        tensors += [F(b + "attn.norm.scale"), T(b + "attn.sinks"), T(b + "attn.qkv.weight"), T(b + "attn.qkv.bias"),
+                    T(b + "attn.out.weight"), T(b + "attn.out.bias"), F(b + "mlp.norm.scale"), T(b + "mlp.gate.weight"),
+                    T(b + "mlp.gate.bias"), T(b + "mlp.mlp1_weight"), T(b + "mlp.mlp1_bias"), T(b + "mlp.mlp2_weight"),
+                    T(b + "mlp.mlp2_bias")]
+    windowed = [1 if config.sliding_window > 0 and layer % 2 == 0 else 0 for layer in range(L)]
+    kind = nat.GPTOSS_CACHED if context is not None else (nat.GPTOSS_LAST if last else nat.GPTOSS_FORWARD)
+    desc = {
+        "kind": kind, "storage": nat.BF16 if dtype == "bfloat16" else nat.FP32, "layers": L,
+        "hidden": config.hidden_size, "heads": config.num_attention_heads, "kv_heads": config.num_key_value_heads,
+        "head_dim": config.head_dim, "experts": config.num_experts, "top_k": config.experts_per_token,
+        "intermediate": config.intermediate_size, "vocab": config.vocab_size, "tokens": steps,
+        "context": context or 0, "window": config.sliding_window if context is None else 0, "eps": 1e-5,
+        "sm_scale": 1.0 / _math.sqrt(config.head_dim), "swiglu_alpha": 1.702, "swiglu_limit": config.swiglu_limit,
+        "rope_concentration": float(conc), "rows": 0, "cols": 0,
+    }
+    cache = [config.num_hidden_layers, context or 0, config.num_key_value_heads, config.head_dim]
+    if context is not None:
+        inputs = [
+            {"name": "tokens", "shape": [steps], "dtype": "int64"},
+            {"name": "positions", "shape": [steps], "dtype": "float32"},
+            {"name": "keys", "shape": cache, "dtype": dtype},
+            {"name": "values", "shape": cache, "dtype": dtype},
+            {"name": "mask", "shape": [steps, context + steps], "dtype": dtype},
+            {"name": "window_mask", "shape": [steps, context + steps], "dtype": dtype},
+            {"name": "last", "shape": [1], "dtype": "int64"},
+        ]
+        rows = [config.num_hidden_layers, steps, config.num_key_value_heads, config.head_dim]
+        outputs = [
+            {"name": "logits", "shape": [1, config.vocab_size], "dtype": dtype},
+            {"name": "new_keys", "shape": rows, "dtype": dtype},
+            {"name": "new_values", "shape": rows, "dtype": dtype},
+        ]
+    else:
+        inputs = [{"name": "tokens", "shape": [steps], "dtype": "int64"}]
+        if last:
+            inputs.append({"name": "position", "shape": [1], "dtype": "int64"})
+        outputs = [{"name": "logits", "shape": [1 if last else steps, config.vocab_size], "dtype": dtype}]
+    plan = {"desc": desc, "inv_freq": inv_freq.float().numpy().tolist(), "layer_window": windowed}
+    return Lowered(plan, tensors, inputs, outputs, _gptoss_stats(desc))
+
+
 def lower(program: Any) -> Lowered:
     """prepare + recognise. Raises NotImplementedError for graphs outside the supported families."""
     g = _Graph(prepare(program))
@@ -452,6 +519,12 @@ def write_artifact(lowered: Lowered, output: str | os.PathLike[str]) -> Path:
         (output / name).unlink(missing_ok=True)
     shutil.rmtree(output / "__pycache__", ignore_errors=True)
     return output
+
+
+def compile_model(model: Any, output: str | os.PathLike[str], *, steps: int, context: int | None = None,
+                  last: bool = False) -> Program:
+    """Write and load the artefact of a GPT-OSS model without exporting it (see ``lower_model``)."""
+    return Program(write_artifact(lower_model(model, steps=steps, context=context, last=last), output))
 
 
 def compile_for_backend(program: Any, output: str | os.PathLike[str], *, blas: bool = True, backend: str = "cuda") -> Program:

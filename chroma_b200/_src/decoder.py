@@ -113,6 +113,22 @@ class NativeDecoder:
             argmax.ctypes.data_as(i64) if argmax is not None else None,
         )
 
+    def advance(self, tokens: np.ndarray | None, positions: np.ndarray | None, steps: int, stream: int = 0,
+                ids: np.ndarray | None = None) -> None:
+        i64 = nat.ctypes.POINTER(nat.ctypes.c_int64)
+        t = np.ascontiguousarray(tokens, np.int64) if tokens is not None else None
+        p = np.ascontiguousarray(positions, np.int64) if positions is not None else None
+        nat.call("chroma_b200_decoder_advance", self.handle, t.ctypes.data_as(i64) if t is not None else None,
+                 p.ctypes.data_as(i64) if p is not None else None, int(steps), nat._VP(stream),
+                 ids.ctypes.data_as(i64) if ids is not None else None)
+
+    def launch_vocab(self, stream: int = 0) -> None:
+        nat.call("chroma_b200_decoder_launch_vocab", self.handle, nat._VP(stream))
+
+    @property
+    def step_launches(self) -> int:
+        return int(nat.lib().chroma_b200_decoder_step_launches(self.handle))
+
     def commit(self, which: int, count: int, positions: np.ndarray) -> None:
         positions = np.ascontiguousarray(positions, dtype=np.int64)
         nat.call("chroma_b200_decoder_commit", self.handle, int(which), int(count),
@@ -380,6 +396,24 @@ class BatchDecoder:
                 self._position = first + count
                 offset += count
             return out
+
+    def generate(self, tokens: np.ndarray, steps: int) -> np.ndarray:
+        """Greedy decoding on the device: consume ``tokens`` [batch] (one per sequence), then feed each argmax back,
+        ``steps`` times. Returns the generated ids [batch, steps]; ids[:, 0] follows ``tokens``."""
+        tokens = np.asarray(tokens, np.int64).reshape(self.batch)
+        with self._lock:
+            self._flush()
+            ids = np.empty((steps, self.batch), np.int64)
+            self._native.advance(tokens, self._position, steps, 0, ids)
+            self._position = self._position + steps
+            return ids.T.copy()
+
+    def advance_device(self, steps: int, stream: int) -> None:
+        """Continue greedy decoding from the device state left by ``generate`` without any host transfer; queued on
+        ``stream`` (a cudaStream_t) and not synchronised. For benchmarks."""
+        with self._lock:
+            self._native.advance(None, None, steps, stream, None)
+            self._position = self._position + steps
 
     def close(self) -> None:
         with self._lock:

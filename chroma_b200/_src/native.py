@@ -82,6 +82,9 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "chroma_b200_decoder_reset": (ctypes.c_int, [_VP, _CP, _SZ]),
     "chroma_b200_decoder_read": (ctypes.c_int, [_VP, _VP, _VP, _I64P, _CP, _SZ]),
     "chroma_b200_decoder_destroy": (None, [_VP]),
+    "chroma_b200_decoder_advance": (ctypes.c_int, [_VP, _I64P, _I64P, _I32, _VP, _I64P, _CP, _SZ]),
+    "chroma_b200_decoder_step_launches": (ctypes.c_int32, [_VP]),
+    "chroma_b200_decoder_launch_vocab": (ctypes.c_int, [_VP, _VP, _CP, _SZ]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -175,6 +175,22 @@ __global__ void k_commit(const T* new_k, const T* new_v, int L, int B, int n, in
     if (l == 0 && threadIdx.x == 0) slots[size_t(b) * ctx + slot] = t;
 }
 
+// After a device-only greedy step: feed each sequence's argmax back as its next token, advance its position and
+// append the id to the generation record.
+__global__ void k_advance(const int64_t* argmax, int B, int64_t* tokens, int64_t* pos0, int64_t* record, int* counter,
+                          int capacity) {
+    pdl_wait();
+    pdl_trigger();
+    const int step = *counter;
+    for (int b = threadIdx.x; b < B; b += blockDim.x) {
+        tokens[b] = argmax[b];
+        pos0[b] += 1;
+        if (step < capacity) record[size_t(step) * B + b] = argmax[b];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *counter = step + 1;
+}
+
 // Greedy argmax over each row of logits (first index on ties, as numpy.argmax).
 template <typename T>
 __global__ void k_argmax(const T* logits, int V, int64_t* out) {
@@ -457,9 +473,7 @@ struct GptExec {
         const int nrows = io.rows ? B : N;
         launch(s, dim3(nrows), dim3(256), 0, k_final_norm<T>, x, N, nrows, io.rows, n,
                reinterpret_cast<const float*>(m->at(1)), dm, tf, err);
-        const int vgrid = std::max(1, std::min((dm.V + 31) / 32, sms * 4));
-        launch(s, dim3(vgrid), dim3(256), size_t(kVocabRows) * dm.d * 4, k_vocab<T, kVocabRows>, tf,
-               nrows, dm.d, dm.V, reinterpret_cast<const T*>(m->at(2)), static_cast<T*>(io.logits));
+        enqueue_vocab_t<T>(s);
         launches += 2;
         if (io.argmax) {
             launch(s, dim3(nrows), dim3(1024), 0, k_argmax<T>, static_cast<const T*>(io.logits), dm.V, io.argmax);
@@ -468,9 +482,22 @@ struct GptExec {
         (void)es;
     }
 
+    // The vocab projection alone (reads the final-norm rows left by the last run).
+    template <typename T> void enqueue_vocab_t(cudaStream_t s) {
+        const Dims& dm = m->dm;
+        const int nrows = io.rows ? B : B * n;
+        const int vgrid = std::max(1, std::min((dm.V + 31) / 32, sms * 4));
+        launch(s, dim3(vgrid), dim3(256), size_t(kVocabRows) * dm.d * 4, k_vocab<T, kVocabRows>, tf, nrows, dm.d, dm.V,
+               reinterpret_cast<const T*>(m->at(2)), static_cast<T*>(io.logits));
+    }
+
     void enqueue(cudaStream_t s) {
         if (m->desc.storage == CHROMA_B200_BF16) enqueue_t<__nv_bfloat16>(s);
         else enqueue_t<float>(s);
+    }
+    void enqueue_vocab(cudaStream_t s) {
+        if (m->desc.storage == CHROMA_B200_BF16) enqueue_vocab_t<__nv_bfloat16>(s);
+        else enqueue_vocab_t<float>(s);
     }
 };
 
@@ -572,6 +599,9 @@ struct chroma_b200_decoder {
     GptExec ex[2];
     DevBuf new_k[2], new_v[2];
     Graph graph[2][2];
+    Graph advance_graph;
+    DevBuf record, counter;
+    int capacity = 0;
 
     ~chroma_b200_decoder() {
         if (stream) {
@@ -952,6 +982,77 @@ int chroma_b200_decoder_commit(chroma_b200_decoder* d, int32_t use_decode, int32
                    d->new_v[which].as<const float>(), d->L, d->B, e.n, count, d->ctx, d->row, 1,
                    d->commit_pos.as<const int64_t>(), d->cache_k.as<float>(), d->cache_v.as<float>(), d->slots.as<int64_t>());
         check(cudaStreamSynchronize(d->stream), "commit");
+    });
+}
+
+int chroma_b200_decoder_advance(chroma_b200_decoder* d, const int64_t* tokens, const int64_t* positions, int32_t steps,
+                                void* stream, int64_t* ids, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!d) throw ValueError("null decoder");
+        if (steps < 1) throw ValueError("steps must be positive");
+        if ((tokens == nullptr) != (positions == nullptr)) throw ValueError("tokens and positions go together");
+        DeviceGuard guard(d->device);
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : d->stream;
+        if (tokens) {
+            int64_t* hin = static_cast<int64_t*>(d->host_in->p);
+            check(cudaStreamSynchronize(s), "advance");
+            std::memcpy(hin, tokens, size_t(d->B) * 8);
+            std::memcpy(hin + d->B, positions, size_t(d->B) * 8);
+            check(cudaMemcpyAsync(d->tokens.p, hin, size_t(d->B) * 8, cudaMemcpyHostToDevice, s), "advance tokens");
+            check(cudaMemcpyAsync(d->pos0.p, hin + d->B, size_t(d->B) * 8, cudaMemcpyHostToDevice, s), "advance positions");
+        }
+        if (!d->record.p || d->capacity < steps) {
+            check(cudaStreamSynchronize(s), "advance");
+            d->capacity = std::max(steps, 1024);
+            d->record = DevBuf(size_t(d->capacity) * d->B * 8);
+            d->counter = DevBuf(sizeof(int));
+            d->advance_graph = Graph();
+        }
+        check(cudaMemsetAsync(d->counter.p, 0, sizeof(int), s), "advance counter");
+        GptExec& e = d->ex[1];
+        for (int i = 0; i < steps; ++i) {
+            d->advance_graph.run(s, [&](cudaStream_t st) {
+                launch(st, dim3((d->B + 255) / 256), dim3(256), 0, k_positions, d->pos0.as<const int64_t>(), d->B, 1,
+                       d->positions.as<float>(), d->last.as<int64_t>(), 1);
+                e.io.argmax = d->argmax.as<int64_t>();
+                e.enqueue(st);
+                const dim3 grid(unsigned(d->L * d->B));
+                const int threads = std::min(256, ((d->row + 31) / 32) * 32);
+                if (d->es == 2)
+                    launch(st, grid, dim3(threads), 0, k_commit<__nv_bfloat16>, d->new_k[1].as<const __nv_bfloat16>(),
+                           d->new_v[1].as<const __nv_bfloat16>(), d->L, d->B, 1, 1, d->ctx, d->row, 1,
+                           d->pos0.as<const int64_t>(), d->cache_k.as<__nv_bfloat16>(), d->cache_v.as<__nv_bfloat16>(),
+                           d->slots.as<int64_t>());
+                else
+                    launch(st, grid, dim3(threads), 0, k_commit<float>, d->new_k[1].as<const float>(),
+                           d->new_v[1].as<const float>(), d->L, d->B, 1, 1, d->ctx, d->row, 1,
+                           d->pos0.as<const int64_t>(), d->cache_k.as<float>(), d->cache_v.as<float>(),
+                           d->slots.as<int64_t>());
+                launch(st, dim3(1), dim3(std::min(1024, ((d->B + 31) / 32) * 32)), 0, k_advance,
+                       d->argmax.as<const int64_t>(), d->B, d->tokens.as<int64_t>(), d->pos0.as<int64_t>(),
+                       d->record.as<int64_t>(), d->counter.as<int>(), d->capacity);
+            });
+        }
+        if (ids) {
+            unsigned* eh = static_cast<unsigned*>(d->host_out->p);
+            check(cudaMemcpyAsync(ids, d->record.p, size_t(steps) * d->B * 8, cudaMemcpyDeviceToHost, s), "advance ids");
+            check(cudaMemcpyAsync(eh, d->err.p, sizeof(unsigned), cudaMemcpyDeviceToHost, s), "Read index error");
+            check(cudaStreamSynchronize(s), "advance");
+            if (*eh & kErrIndex) throw IndexError("Tensor index out of range");
+        }
+    });
+}
+
+int32_t chroma_b200_decoder_step_launches(const chroma_b200_decoder* d) {
+    // positions + decode program (embed, 5 per layer, final norm, vocab, argmax) + commit + advance
+    return d ? 1 + (1 + 5 * d->L + 3) + 2 : 0;
+}
+
+int chroma_b200_decoder_launch_vocab(chroma_b200_decoder* d, void* stream, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!d) throw ValueError("null decoder");
+        DeviceGuard guard(d->device);
+        d->ex[1].enqueue_vocab(stream ? static_cast<cudaStream_t>(stream) : d->stream);
     });
 }
 

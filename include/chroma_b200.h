@@ -116,6 +116,18 @@ int chroma_b200_decoder_step(chroma_b200_decoder* decoder, int32_t use_decode, c
  * program steps again, so a host may commit lazily (decoder.py:130-137 commits only after a call succeeds). */
 int chroma_b200_decoder_commit(chroma_b200_decoder* decoder, int32_t use_decode, int32_t count,
                                const int64_t* positions, char* err, size_t err_len);
+/* Greedy generation entirely on the device: `steps` decode steps, each decoding every sequence's current token,
+ * committing its K/V row, advancing its position and feeding its argmax back as the next token. With `tokens` and
+ * `positions` ([batch] each) the first step consumes those; with NULL it continues from the device state a
+ * previous advance left. Rows staged by a host step must be committed first. Queued on `stream` (0: the
+ * decoder's own); when `ids` is non-NULL the generated ids [steps, batch] are copied there and the stream is
+ * synchronised. */
+int chroma_b200_decoder_advance(chroma_b200_decoder* decoder, const int64_t* tokens, const int64_t* positions,
+                                int32_t steps, void* stream, int64_t* ids, char* err, size_t err_len);
+/* Kernels launched by one `advance` step (launch accounting). */
+int32_t chroma_b200_decoder_step_launches(const chroma_b200_decoder* decoder);
+/* Queues the decode program's vocab-projection kernel alone on `stream` (for per-kernel event timing). */
+int chroma_b200_decoder_launch_vocab(chroma_b200_decoder* decoder, void* stream, char* err, size_t err_len);
 /* Empties every sequence's cache. */
 int chroma_b200_decoder_reset(chroma_b200_decoder* decoder, char* err, size_t err_len);
 /* Copies the committed cache and slot positions to host buffers ([batch, L, ctx, KV, hd] twice, [batch, ctx]). */

@@ -223,7 +223,26 @@ def build(name: str, *, force: bool = False) -> Path:
     program.close()
     (target / "build.json").write_text(json.dumps({"name": name, "seconds": time.time() - start}) + "\n")
     print(f"built {name} in {time.time() - start:.1f}s -> {target}", flush=True)
+    dedupe()
     return target
+
+
+def dedupe() -> None:
+    """Keep one copy of identical weight files (the prefill/decode pair of one model share theirs).
+
+    The reference names weight files by content hash (chroma/_src/build.py:61), so equal names mean equal bytes.
+    A program whose file was removed records the directory that holds it in ``shared_weights.json``;
+    ``oracle/refprogram.py`` follows that record.
+    """
+    seen: dict[str, Path] = {}
+    for directory in sorted(p for p in ROOT.iterdir() if (p / "model.json").exists()):
+        weights = json.loads((directory / "model.json").read_text())["weights"]
+        if weights in seen:
+            if (directory / weights).exists():
+                (directory / weights).unlink()
+            (directory / "shared_weights.json").write_text(json.dumps({"directory": seen[weights].name}) + "\n")
+        elif (directory / weights).exists():
+            seen[weights] = directory
 
 
 def names() -> list[str]:

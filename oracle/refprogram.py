@@ -46,15 +46,23 @@ class RefProgram:
         self.inputs = manifest["inputs"]
         self.outputs = manifest["outputs"]
         self.stats = manifest["stats"]
-        self.model = module.Model(str(self.directory / manifest["weights"]))
+        weights = self.directory / manifest["weights"]
+        shared = self.directory / "shared_weights.json"
+        if not weights.exists() and shared.exists():
+            weights = self.directory.parent / json.loads(shared.read_text())["directory"] / manifest["weights"]
+        self.model = module.Model(str(weights))
+        self.device = "CPU"
 
-    def __call__(self, *inputs: np.ndarray) -> tuple[np.ndarray, ...]:
+    def __call__(self, *inputs: np.ndarray, out: list[np.ndarray] | None = None):  # type: ignore[no-untyped-def]
         from ml_dtypes import bfloat16  # noqa: F401  (registers the dtype name)
 
         arrays = [np.require(a, requirements=["C", "A"]) for a in inputs]
-        outs = [np.empty(s["shape"], dtype=s["dtype"]) for s in self.outputs]
+        outs = list(out) if out is not None else [np.empty(s["shape"], dtype=s["dtype"]) for s in self.outputs]
         self.model.run(arrays, outs)
-        return tuple(outs)
+        return outs[0] if len(outs) == 1 else tuple(outs)
+
+    def close(self) -> None:
+        self.model = None
 
 
 def available(name: str) -> bool:

@@ -165,17 +165,33 @@ def test_c2_program_with_host_masks_matches_device_path(gpu: None) -> None:
 
 
 def test_decoder_errors_keep_state_and_recover(gpu: None) -> None:
+    # A failed append leaves the committed state as it was (decoder.py:130-137). A failing call may first apply
+    # the previous step's staged rows, which replaces the state object but not its content.
     with dev_decoder() as dec:
         dec.append([1, 2, 3])
         before = dec._state
         for bad in ([-1], [models.dev.vocab_size], [2**40]):
             with pytest.raises(IndexError):
                 dec.append(bad)
-            assert dec.position == 3 and dec._state is before
+            assert dec.position == before.position == 3
+            np.testing.assert_array_equal(dec._state.slots, before.slots)
         with pytest.raises(TypeError):
             dec.append([1.5])
         with pytest.raises(ValueError):
             dec.append([])
+        # KeyboardInterrupt after the native call returns: nothing is committed (tests/test_decoder.py:122-131).
+        state = dec._state
+        step = dec._native.step
+
+        def interrupted(*args, **kwargs):  # type: ignore[no-untyped-def]
+            step(*args, **kwargs)
+            raise KeyboardInterrupt
+
+        dec._native.step = interrupted
+        with pytest.raises(KeyboardInterrupt):
+            dec.append([4])
+        dec._native.step = step
+        assert dec._state is state and dec.position == 3
         a = dec.append([4])
     with dev_decoder() as ref:
         b = ref.append([1, 2, 3, 4])
