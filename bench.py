@@ -195,7 +195,10 @@ def main() -> None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    stream = torch.cuda.current_stream()
+    # A dedicated stream: its handle is non-zero, so the native calls queue on it (0 would select the objects' own
+    # streams) and the CUDA events below bracket exactly the queued work.
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
 
     def flush() -> None:
@@ -238,7 +241,8 @@ def main() -> None:
 
     # ---- roofline: vocab kernel alone (L2 flushed before each launch)
     vocab_ms = []
-    for i in range(args.warmup + 50):
+    reps = max(3, min(50, args.steps))
+    for i in range(args.warmup + reps):
         flush()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -307,7 +311,7 @@ def main() -> None:
     torch.cuda.synchronize()
     fwd8(tokens8)
     f_ms = []
-    for i in range(args.warmup + 50):
+    for i in range(args.warmup + reps):
         flush()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -319,7 +323,7 @@ def main() -> None:
     f_ms = [a.elapsed_time(b) for a, b in f_ms]
     out8 = np.empty((8, V), np.float32)
     fe2e = []
-    for i in range(args.warmup + 50):
+    for i in range(args.warmup + reps):
         flush()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
@@ -366,7 +370,7 @@ def main() -> None:
             "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
             "algorithmic_bytes": vocab_bytes, "launch_us": vocab_t * 1e6,
             "peak_source": f"{pk['source']} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
-            "timing": "launched alone after an L2 flush, CUDA events, mean of 50",
+            "timing": f"launched alone after an L2 flush, CUDA events, mean of {reps}",
         },
         "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "clocks": clocks.summary(),

@@ -58,22 +58,24 @@ def plan_memory(allocations: dict[str, Allocation]) -> int:
 def gptoss_buffers(desc: dict, batch: int = 1) -> list[tuple[str, int, int, int]]:
     """(name, bytes, start, end) of one GPT-OSS call's temporaries, in the order the native executor plans them.
 
-    Kernel indices: 0 embedding; per layer l: 1+5l QKV, 2+5l attention, 3+5l out/router, 4+5l expert up,
+    Kernel indices: 0 embedding; per layer l: 1+5l QKV, 2+5l attention, 3+5l out, 4+5l router + expert up,
     5+5l expert down; then 1+5L final norm and 2+5L vocab. Per-layer buffers are reused by every layer.
     """
     L, d, H, hd, KV, k, I = (desc[x] for x in ("layers", "hidden", "heads", "head_dim", "kv_heads", "top_k", "intermediate"))
     N = batch * desc["tokens"]
     es = 2 if desc["storage"] == 1 else 4
     last = 5 * (L - 1)
+    chunks = -(-(desc.get("context", 0) + desc["tokens"]) // 256)
+    G = H // KV
     out = [
         ("x", N * d * 4, 0, 1 + 5 * L),
         ("q", N * H * hd * 4, 1, 2 + last),
         ("attn", N * H * hd * 4, 2, 3 + last),
         ("x2", N * d * 4, 3, 5 + last),
-        ("tnorm", N * d * 4, 3, 4 + last),
-        ("ridx", N * k * 4, 3, 5 + last),
-        ("rw", N * k * 4, 3, 5 + last),
+        ("ridx", N * k * 4, 4, 5 + last),
+        ("rw", N * k * 4, 4, 5 + last),
         ("act", N * k * I * 4, 4, 5 + last),
+        ("partial", N * KV * G * chunks * (hd + 2) * 4, 2, 2 + last),
         ("tf", N * d * 4, 1 + 5 * L, 2 + 5 * L),
     ]
     if desc["kind"] != 2:  # uncached programs keep the layer's new K/V rows in the arena

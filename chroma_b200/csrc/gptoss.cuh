@@ -1,16 +1,23 @@
-// GPT-OSS-style transformer kernels (fp32 or bf16 storage) for token counts up to a few hundred per launch.
+// GPT-OSS-style transformer kernels (fp32 or bf16 storage) for token counts up to a few hundred per launch
+// (decode steps, prefill chunks, short forwards).
 //
 // One fused kernel per stage of the block, replacing the reference's chain of generated one-thread-per-element
 // kernels plus cuBLAS calls (chroma/_src/codegen/gpu.py:165-424, chroma/_src/codegen/cuda/codegen.py:87-140):
 //
-//   k_embed         embedding gather with bounds check                         (gpt_oss.py:304-306)
-//   k_attn_in       RMSNorm -> QKV linear (+bias) -> RoPE -> q, new K/V rows   (gpt_oss.py:189-202)
-//   k_attention     scores*scale + mask, sink column, softmax, P.V            (gpt_oss.py:133-151, cached.py:36-47)
-//   k_out_router    out linear + residual -> RMSNorm -> gate -> top-k -> softmax (gpt_oss.py:204-209, 243-247)
-//   k_moe_up        selected-expert mlp1 GEMV (+bias) -> interleaved SwiGLU   (gpt_oss.py:251-254, 212-219)
-//   k_moe_down      selected-expert mlp2 GEMV (+bias) -> weighted combine -> residual (gpt_oss.py:257-265)
-//   k_final_norm    final RMSNorm of the rows whose logits are wanted         (gpt_oss.py:309, cached.py:50)
-//   k_vocab         unembedding GEMV, the 201,088-way vocab projection        (gpt_oss.py:310)
+//   k_embed         embedding gather with bounds check                          (gpt_oss.py:304-306)
+//   k_attn_in       RMSNorm -> QKV linear (+bias) -> RoPE -> q, new K/V rows    (gpt_oss.py:189-202)
+//   k_attention     scores*scale + mask, sink column, softmax, P.V, split over key chunks
+//                                                                                (gpt_oss.py:133-151, cached.py:36-47)
+//   k_out           out linear (+bias) + residual                               (gpt_oss.py:204-209)
+//   k_moe_up        RMSNorm -> gate -> top-k -> softmax, then the selected expert's mlp1 (+bias) -> SwiGLU
+//                                                                                (gpt_oss.py:243-254, 212-219)
+//   k_moe_down      selected experts' mlp2 (+bias) -> weighted combine -> residual (gpt_oss.py:257-265)
+//   k_final_norm    final RMSNorm of the rows whose logits are wanted            (gpt_oss.py:309, cached.py:50)
+//   k_vocab         unembedding GEMV with a fused greedy argmax                  (gpt_oss.py:310)
+//
+// Decode-sized work is latency-bound, so every GEMV is written for memory-level parallelism: a warp owns a few
+// weight rows, each lane issues all of its 16-byte loads for those rows before any arithmetic, and the first chunk
+// of weights is loaded BEFORE the programmatic-dependent-launch wait, overlapping the previous kernel's tail.
 //
 // Activations live in fp32 buffers; for bf16 programs every value is rounded to bf16 wherever the exported graph
 // rounds it (after each linear, einsum, residual add and SwiGLU step), so results track the reference's CPU program.
@@ -43,42 +50,94 @@ template <typename T> struct LayerW {
 
 enum MaskMode : int { kMaskBuffer = 0, kMaskCausal = 1, kMaskSlots = 2 };
 
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kTileTokens = 8;  // activation rows per CTA tile in the GEMV kernels
+constexpr int kMJ = 4;          // float4 chunks per lane per row in one fragment: 512 elements per chunk pass
+constexpr int kChunk = 128 * kMJ;
+
 // ------------------------------------------------------------------------------------------------------
-// Block-wide RMS of rows held in shared memory: one warp per row. inv[r] = 1 / sqrt(sum(x^2)/d + eps),
-// the fused norm of chroma/_src/codegen/cpu/kernels.h:101-115.
-__device__ __forceinline__ void rows_inv_rms(const float* xs, int rows, int d, float eps, float* inv) {
+// Register fragment of up to MR weight rows: lane l holds elements c0 + 4*l + 128*j (j < kMJ) of each row.
+template <int MR> struct Frag {
+    float v[MR][kMJ][4];
+};
+
+template <typename T, int MR>
+__device__ __forceinline__ void frag_load(Frag<MR>& f, const T* const (&rows)[MR], int nr, int d, int c0) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int r = 0; r < MR; ++r)
+#pragma unroll
+        for (int j = 0; j < kMJ; ++j) {
+            const int c = c0 + lane * 4 + 128 * j;
+            if (r < nr && c < d) {
+                load4(rows[r] + c, f.v[r][j]);
+            } else {
+                f.v[r][j][0] = f.v[r][j][1] = f.v[r][j][2] = f.v[r][j][3] = 0.f;
+            }
+        }
+}
+
+// acc[r][t] += frag row r . xs row t over the fragment's chunk (xs: fp32 rows of stride d in shared memory).
+template <int MR, int TT>
+__device__ __forceinline__ void frag_fma(const Frag<MR>& f, const float* xs, int d, int tt, int c0, float (&acc)[MR][TT]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < kMJ; ++j) {
+        const int c = c0 + lane * 4 + 128 * j;
+        if (c < d) {
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+                if (t < tt) {
+                    const float4 x = *reinterpret_cast<const float4*>(xs + t * d + c);
+#pragma unroll
+                    for (int r = 0; r < MR; ++r) {
+                        acc[r][t] = fmaf(f.v[r][j][0], x.x, acc[r][t]);
+                        acc[r][t] = fmaf(f.v[r][j][1], x.y, acc[r][t]);
+                        acc[r][t] = fmaf(f.v[r][j][2], x.z, acc[r][t]);
+                        acc[r][t] = fmaf(f.v[r][j][3], x.w, acc[r][t]);
+                    }
+                }
+            }
+        }
+    }
+}
+
+// Full dot products of MR rows with tt activation rows; `f` must already hold the chunk at c0 = 0.
+template <typename T, int MR, int TT>
+__device__ __forceinline__ void warp_gemv(Frag<MR>& f, const T* const (&rows)[MR], int nr, const float* xs, int d, int tt,
+                                          float (&acc)[MR][TT]) {
+#pragma unroll
+    for (int r = 0; r < MR; ++r)
+#pragma unroll
+        for (int t = 0; t < TT; ++t) acc[r][t] = 0.f;
+    for (int c0 = 0;;) {
+        frag_fma<MR, TT>(f, xs, d, tt, c0, acc);
+        c0 += kChunk;
+        if (c0 >= d) break;
+        frag_load<T, MR>(f, rows, nr, d, c0);
+    }
+#pragma unroll
+    for (int r = 0; r < MR; ++r)
+#pragma unroll
+        for (int t = 0; t < TT; ++t) acc[r][t] = warp_sum(acc[r][t]);
+}
+
+// Normalise `tt` rows staged in shared memory in place: x * (1/sqrt(mean(x^2) + eps)) * w, rounded to storage
+// (the fused norm of chroma/_src/codegen/cpu/kernels.h:101-115). `inv` is [tt] scratch.
+template <typename T>
+__device__ __forceinline__ void rows_rmsnorm(float* xs, int tt, int d, float eps, const float* __restrict__ w, float* inv) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
-    for (int r = warp; r < rows; r += warps) {
+    for (int r = warp; r < tt; r += warps) {
         float s = 0.f;
         for (int c = lane; c < d; c += 32) s = fmaf(xs[r * d + c], xs[r * d + c], s);
         s = warp_sum(s);
         if (lane == 0) inv[r] = 1.0f / sqrtf(s / float(d) + eps);
     }
-}
-
-// Dot product of one weight row (length d, storage T, 16/8-byte aligned) with `tt` fp32 rows in shared
-// memory (row stride d), accumulated by the whole warp; result valid in every lane.
-template <typename T, int MAXT>
-__device__ __forceinline__ void warp_row_dots(const T* wrow, const float* xs, int d, int tt, float (&acc)[MAXT]) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int t = 0; t < MAXT; ++t) acc[t] = 0.f;
-    for (int c = lane * 4; c < d; c += 128) {
-        float w4[4];
-        load4(wrow + c, w4);
-#pragma unroll
-        for (int t = 0; t < MAXT; ++t) {
-            if (t < tt) {
-                const float4 xv = *reinterpret_cast<const float4*>(xs + t * d + c);
-                acc[t] = fmaf(w4[0], xv.x, acc[t]);
-                acc[t] = fmaf(w4[1], xv.y, acc[t]);
-                acc[t] = fmaf(w4[2], xv.z, acc[t]);
-                acc[t] = fmaf(w4[3], xv.w, acc[t]);
-            }
-        }
-    }
-#pragma unroll
-    for (int t = 0; t < MAXT; ++t) acc[t] = warp_sum(acc[t]);
+    __syncthreads();
+    for (int i = threadIdx.x; i < tt * d; i += blockDim.x)
+        xs[i] = Store<T>::round(__fmul_rn(__fmul_rn(xs[i], inv[i / d]), w[i % d]));
+    __syncthreads();
 }
 
 // ------------------------------------------------------------------------------------------------------
@@ -94,53 +153,56 @@ __global__ void k_embed(const int64_t* tokens, int ntok, const T* emb, int V, in
 }
 
 // ------------------------------------------------------------------------------------------------------
-// grid = (ceil(heads_total / hpc), ceil(ntok / TT)); block = 256. Each CTA owns `hpc` whole heads of the fused
-// QKV projection (so RoPE pairs stay local) for up to TT tokens.
-constexpr int kAttnInTokens = 8;
-
+// grid = (heads_total, ceil(ntok / kTileTokens)); block = kThreads. A CTA owns one head of the fused QKV projection
+// (so both halves of each RoPE pair are local); each warp owns 2 of its rows at a time.
 template <typename T>
-__global__ void __launch_bounds__(256) k_attn_in(const float* __restrict__ x, int ntok, Dims dm, int hpc,
-                                                 const float* __restrict__ norm_w, const T* __restrict__ W,
-                                                 const T* __restrict__ bias, const float* __restrict__ positions,
-                                                 const float* __restrict__ inv_freq, float* __restrict__ q_out,
-                                                 T* __restrict__ k_out, T* __restrict__ v_out) {
+__global__ void __launch_bounds__(kThreads) k_attn_in(const float* __restrict__ x, int ntok, Dims dm,
+                                                      const float* __restrict__ norm_w, const T* __restrict__ W,
+                                                      const T* __restrict__ bias, const float* __restrict__ positions,
+                                                      const float* __restrict__ inv_freq, float* __restrict__ q_out,
+                                                      T* __restrict__ k_out, T* __restrict__ v_out) {
     extern __shared__ float smem[];
-    constexpr int TT = kAttnInTokens;
+    constexpr int TT = kTileTokens, MR = 2;
     const int d = dm.d, hd = dm.hd;
-    const int heads_total = dm.H + 2 * dm.KV;
-    const int head0 = blockIdx.x * hpc;
-    const int nheads = min(hpc, heads_total - head0);
-    const int cols = nheads * hd;
+    const int head = blockIdx.x;
     const int t0 = blockIdx.y * TT;
     const int tt = min(TT, ntok - t0);
-    float* xs = smem;                 // [TT][d]
-    float* out = xs + TT * d;         // [TT][hpc*hd]
-    float* inv = out + TT * hpc * hd; // [TT]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    float* xs = smem;            // [TT][d]
+    float* out = xs + TT * d;    // [TT][hd]
+    float* inv = out + TT * hd;  // [TT]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    prefetch_l2(W + size_t(head0) * hd * d, size_t(cols) * d * sizeof(T), threadIdx.x, blockDim.x);
+    const int r0 = warp * MR;
+    const T* rows[MR];
+#pragma unroll
+    for (int r = 0; r < MR; ++r) rows[r] = W + size_t(head * hd + min(r0 + r, hd - 1)) * d;
+    Frag<MR> f;
+    frag_load<T, MR>(f, rows, max(0, min(MR, hd - r0)), d, 0);
     pdl_wait();
     pdl_trigger();
 
     for (int i = threadIdx.x; i < tt * d; i += blockDim.x) xs[i] = x[size_t(t0) * d + i];
     __syncthreads();
-    rows_inv_rms(xs, tt, d, dm.eps, inv);
-    __syncthreads();
-    for (int i = threadIdx.x; i < tt * d; i += blockDim.x) {
-        const int r = i / d, c = i % d;
-        xs[i] = Store<T>::round(__fmul_rn(__fmul_rn(xs[i], inv[r]), norm_w[c]));
-    }
-    __syncthreads();
+    rows_rmsnorm<T>(xs, tt, d, dm.eps, norm_w, inv);
 
-    for (int c = warp; c < cols; c += warps) {
-        const int col = head0 * hd + c;
-        float acc[TT];
-        warp_row_dots<T, TT>(W + size_t(col) * d, xs, d, tt, acc);
-        if (lane == 0) {
-            const float b = Store<T>::load(bias + col);
+    for (int rb = r0; rb < hd; rb += kWarps * MR) {
+        const int nr = min(MR, hd - rb);
+        if (rb != r0) {
 #pragma unroll
-            for (int t = 0; t < TT; ++t)
-                if (t < tt) out[t * (hpc * hd) + c] = Store<T>::round(__fadd_rn(acc[t], b));
+            for (int r = 0; r < MR; ++r) rows[r] = W + size_t(head * hd + min(rb + r, hd - 1)) * d;
+            frag_load<T, MR>(f, rows, nr, d, 0);
+        }
+        float acc[MR][TT];
+        warp_gemv<T, MR, TT>(f, rows, nr, xs, d, tt, acc);
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < MR; ++r) {
+                if (r >= nr) break;
+                const float b = Store<T>::load(bias + head * hd + rb + r);
+#pragma unroll
+                for (int t = 0; t < TT; ++t)
+                    if (t < tt) out[t * hd + rb + r] = Store<T>::round(__fadd_rn(acc[r][t], b));
+            }
         }
     }
     __syncthreads();
@@ -148,16 +210,13 @@ __global__ void __launch_bounds__(256) k_attn_in(const float* __restrict__ x, in
     // RoPE on q and k heads (gpt_oss.py:44-54): o1 = x1*cos - x2*sin, o2 = x2*cos + x1*sin, cos/sin rounded to
     // storage first; v heads pass through.
     const int half = hd / 2;
-    for (int i = threadIdx.x; i < tt * nheads * half; i += blockDim.x) {
-        const int t = i / (nheads * half);
-        const int rem = i % (nheads * half);
-        const int lh = rem / half, j = rem % half;
-        const int gh = head0 + lh;
-        const float lo = out[t * (hpc * hd) + lh * hd + j];
-        const float hi = out[t * (hpc * hd) + lh * hd + j + half];
+    for (int i = threadIdx.x; i < tt * half; i += blockDim.x) {
+        const int t = i / half, j = i % half;
+        const float lo = out[t * hd + j];
+        const float hi = out[t * hd + j + half];
         const int tok = t0 + t;
         float o1 = lo, o2 = hi;
-        if (gh < dm.H + dm.KV) {
+        if (head < dm.H + dm.KV) {
             const float angle = __fmul_rn(positions[tok], inv_freq[j]);
             float s, c;
             sincosf(angle, &s, &c);
@@ -166,132 +225,249 @@ __global__ void __launch_bounds__(256) k_attn_in(const float* __restrict__ x, in
             o1 = Store<T>::round(__fsub_rn(Store<T>::round(__fmul_rn(lo, c)), Store<T>::round(__fmul_rn(hi, s))));
             o2 = Store<T>::round(__fadd_rn(Store<T>::round(__fmul_rn(hi, c)), Store<T>::round(__fmul_rn(lo, s))));
         }
-        if (gh < dm.H) {
-            float* qrow = q_out + size_t(tok) * dm.H * hd + size_t(gh) * hd;
+        if (head < dm.H) {
+            float* qrow = q_out + size_t(tok) * dm.H * hd + size_t(head) * hd;
             qrow[j] = o1;
             qrow[j + half] = o2;
-        } else if (gh < dm.H + dm.KV) {
-            T* krow = k_out + size_t(tok) * dm.KV * hd + size_t(gh - dm.H) * hd;
-            Store<T>::store(krow + j, o1);
-            Store<T>::store(krow + j + half, o2);
         } else {
-            T* vrow = v_out + size_t(tok) * dm.KV * hd + size_t(gh - dm.H - dm.KV) * hd;
-            Store<T>::store(vrow + j, o1);
-            Store<T>::store(vrow + j + half, o2);
+            T* dst = head < dm.H + dm.KV ? k_out + size_t(tok) * dm.KV * hd + size_t(head - dm.H) * hd
+                                         : v_out + size_t(tok) * dm.KV * hd + size_t(head - dm.H - dm.KV) * hd;
+            Store<T>::store(dst + j, o1);
+            Store<T>::store(dst + j + half, o2);
         }
     }
 }
 
 // ------------------------------------------------------------------------------------------------------
-// Sink-augmented attention, one CTA per (query row, kv head, sequence), one warp per query head of the group.
-// Keys are the `ctx` cache rows followed by the sequence's `n` new rows. Scores are kept in shared memory so the
-// probabilities can be rounded like the reference's softmax output before P.V.
+// Sink-augmented attention over key chunks. grid = (query row, kv head, sequence * chunks); block = kThreads.
+// Each CTA stages one chunk of K and V rows in shared memory (cache rows before the PDL wait: no kernel of the
+// running step writes them), scores it for the G query heads of its kv head (one warp each), and either finishes
+// the softmax directly (single chunk: probabilities rounded like the reference's softmax output) or writes an
+// (m, l, o) partial that the last CTA of the row merges with the sink logit (split-KV, flash-decoding style).
+constexpr int kKeyChunk = 256;
+
 struct AttnArgs {
-    int n, ctx, B;
+    int n, ctx, B, chunks;
     size_t cache_seq_stride;  // elements between sequences in the cache (layer offset already applied)
     int mask_mode;
     int window;               // mask window for kMaskCausal / kMaskSlots (0 = none)
     const int64_t* slots;     // [B][ctx] absolute positions of cache rows (-1 empty)
     const int64_t* pos0;      // [B] absolute position of each sequence's first new row
+    float* partial;           // [B*n][KV][G][chunks][hd + 2] split-KV partials
+    unsigned* counters;       // [B*n][KV] arrival counters, left at zero
 };
 
 template <typename T>
-__global__ void __launch_bounds__(256) k_attention(const float* __restrict__ q, Dims dm, AttnArgs a,
-                                                    const T* __restrict__ cache_k, const T* __restrict__ cache_v,
-                                                    const T* __restrict__ new_k, const T* __restrict__ new_v,
-                                                    const T* __restrict__ bias, const T* __restrict__ sinks,
-                                                    float* __restrict__ out) {
-    extern __shared__ float scores[];
-    const int i = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+__global__ void __launch_bounds__(kThreads) k_attention(const float* __restrict__ q, Dims dm, AttnArgs a,
+                                                        const T* __restrict__ cache_k, const T* __restrict__ cache_v,
+                                                        const T* __restrict__ new_k, const T* __restrict__ new_v,
+                                                        const T* __restrict__ bias, const T* __restrict__ sinks,
+                                                        float* __restrict__ out) {
+    extern __shared__ float sm[];
+    const int i = blockIdx.x, kvh = blockIdx.y;
+    const int b = blockIdx.z / a.chunks, chunk = blockIdx.z % a.chunks;
+    const int hd = dm.hd, G = dm.G, stride = hd + 1;
+    const int nkeys = a.ctx + a.n;
+    const int j0 = chunk * kKeyChunk;
+    const int nk = min(kKeyChunk, nkeys - j0);
+    float* Ks = sm;                          // [kKeyChunk][hd+1]
+    float* Vs = Ks + kKeyChunk * stride;     // [kKeyChunk][hd+1]
+    float* sc = Vs + kKeyChunk * stride;     // [G][kKeyChunk]
+    float* qs = sc + G * kKeyChunk;          // [G][hd]
+    __shared__ unsigned last_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int hd = dm.hd, nkeys = a.ctx + a.n;
-    const int hq = kvh * dm.G + warp;
     const size_t tok = size_t(b) * a.n + i;
-    float* sc = scores + size_t(warp) * nkeys;
-
-    pdl_wait();
-    pdl_trigger();
-
-    float qv[64];
-    const float* qrow = q + tok * dm.H * hd + size_t(hq) * hd;
-#pragma unroll
-    for (int e = 0; e < 64; ++e)
-        if (e < hd) qv[e] = qrow[e];
+    const size_t kstride = size_t(dm.KV) * hd;
+    const int q4 = hd / 4;
 
     const T* ck = cache_k + b * a.cache_seq_stride + size_t(kvh) * hd;
     const T* cv = cache_v + b * a.cache_seq_stride + size_t(kvh) * hd;
-    const T* nk = new_k + (size_t(b) * a.n * dm.KV + kvh) * hd;
-    const T* nv = new_v + (size_t(b) * a.n * dm.KV + kvh) * hd;
-    const size_t kstride = size_t(dm.KV) * hd;
+    const T* nkp = new_k + (size_t(b) * a.n * dm.KV + kvh) * hd;
+    const T* nvp = new_v + (size_t(b) * a.n * dm.KV + kvh) * hd;
+    // Cache rows of this chunk.
+    for (int e = threadIdx.x; e < nk * q4; e += blockDim.x) {
+        const int jj = e / q4, c = (e % q4) * 4, j = j0 + jj;
+        if (j < a.ctx) {
+            float kv[4], vv[4];
+            load4(ck + size_t(j) * kstride + c, kv);
+            load4(cv + size_t(j) * kstride + c, vv);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                Ks[jj * stride + c + u] = kv[u];
+                Vs[jj * stride + c + u] = vv[u];
+            }
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+    for (int e = threadIdx.x; e < nk * q4; e += blockDim.x) {
+        const int jj = e / q4, c = (e % q4) * 4, j = j0 + jj;
+        if (j >= a.ctx) {
+            float kv[4], vv[4];
+            load4(nkp + size_t(j - a.ctx) * kstride + c, kv);
+            load4(nvp + size_t(j - a.ctx) * kstride + c, vv);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                Ks[jj * stride + c + u] = kv[u];
+                Vs[jj * stride + c + u] = vv[u];
+            }
+        }
+    }
+    for (int e = threadIdx.x; e < G * hd; e += blockDim.x)
+        qs[e] = q[tok * dm.H * hd + size_t(kvh) * G * hd + e];
+    __syncthreads();
 
     int64_t t_i = 0;
     if (a.mask_mode == kMaskSlots) t_i = a.pos0[b] + i;
-
-    float mx = -INFINITY;
-    for (int j = lane; j < nkeys; j += 32) {
-        const T* krow = j < a.ctx ? ck + size_t(j) * kstride : nk + size_t(j - a.ctx) * kstride;
-        float dot = 0.f;
-#pragma unroll
-        for (int e = 0; e < 64; e += 4) {
-            if (e < hd) {
-                float k4[4];
-                load4(krow + e, k4);
-                dot = fmaf(qv[e], k4[0], dot);
-                dot = fmaf(qv[e + 1], k4[1], dot);
-                dot = fmaf(qv[e + 2], k4[2], dot);
-                dot = fmaf(qv[e + 3], k4[3], dot);
-            }
-        }
-        float s = Store<T>::round(__fmul_rn(Store<T>::round(dot), dm.sm_scale));
-        if (a.mask_mode == kMaskBuffer) {
-            s = Store<T>::round(__fadd_rn(s, Store<T>::load(bias + size_t(i) * nkeys + j)));
-        } else {
-            bool visible;
-            if (a.mask_mode == kMaskCausal) {
-                visible = (j - a.ctx) <= i && (a.window <= 0 || i - (j - a.ctx) < a.window);
-            } else {
-                const int64_t t_j = j < a.ctx ? a.slots[size_t(b) * a.ctx + j] : a.pos0[b] + (j - a.ctx);
-                const bool valid = j >= a.ctx || t_j >= 0;
-                visible = valid && t_j <= t_i && (a.window <= 0 || t_j > t_i - a.window);
-            }
-            if (!visible) s = -INFINITY;
-        }
-        sc[j] = s;
-        mx = fmaxf(mx, s);
-    }
-    const float sink = Store<T>::load(sinks + hq);
-    mx = fmaxf(warp_max(mx), sink);
-    float l = 0.f;
-    for (int j = lane; j < nkeys; j += 32) {
-        const float e = expf(sc[j] - mx);
-        sc[j] = e;
-        l += e;
-    }
-    l = warp_sum(l) + expf(sink - mx);
-    const float rl = l;
-    __syncwarp();
-    for (int j = lane; j < nkeys; j += 32) sc[j] = Store<T>::round(sc[j] / rl);
-    __syncwarp();
-
-    // P.V: lanes split into `groups` key groups of `dl` dims each.
     const int dl = hd < 32 ? hd : 32;
     const int groups = 32 / dl;
     const int g = lane / dl, dd = lane % dl;
-    float acc[2] = {0.f, 0.f};
-    for (int j = g; j < nkeys; j += groups) {
-        const T* vrow = j < a.ctx ? cv + size_t(j) * kstride : nv + size_t(j - a.ctx) * kstride;
-        const float p = sc[j];
-        acc[0] = fmaf(p, Store<T>::load(vrow + dd), acc[0]);
-        if (hd > 32) acc[1] = fmaf(p, Store<T>::load(vrow + dd + 32), acc[1]);
+
+    for (int m = warp; m < G; m += kWarps) {
+        const int hq = kvh * G + m;
+        const float* qv = qs + m * hd;
+        float* s_row = sc + m * kKeyChunk;
+        float mx = -INFINITY;
+        for (int jj = lane; jj < nk; jj += 32) {
+            const int j = j0 + jj;
+            const float* kr = Ks + jj * stride;
+            float dot = 0.f;
+            for (int e = 0; e < hd; ++e) dot = fmaf(qv[e], kr[e], dot);
+            float s = Store<T>::round(__fmul_rn(Store<T>::round(dot), dm.sm_scale));
+            if (a.mask_mode == kMaskBuffer) {
+                s = Store<T>::round(__fadd_rn(s, Store<T>::load(bias + size_t(i) * nkeys + j)));
+            } else {
+                bool visible;
+                if (a.mask_mode == kMaskCausal) {
+                    visible = (j - a.ctx) <= i && (a.window <= 0 || i - (j - a.ctx) < a.window);
+                } else {
+                    const int64_t t_j = j < a.ctx ? a.slots[size_t(b) * a.ctx + j] : a.pos0[b] + (j - a.ctx);
+                    const bool valid = j >= a.ctx || t_j >= 0;
+                    visible = valid && t_j <= t_i && (a.window <= 0 || t_j > t_i - a.window);
+                }
+                if (!visible) s = -INFINITY;
+            }
+            s_row[jj] = s;
+            mx = fmaxf(mx, s);
+        }
+        mx = warp_max(mx);
+        const float sink = Store<T>::load(sinks + hq);
+        const bool single = a.chunks == 1;
+        // Single chunk: normalise against max(m, sink) now; otherwise keep chunk-local (m, l) for the merge.
+        const float ref = single ? fmaxf(mx, sink) : mx;
+        float l = 0.f;
+        for (int jj = lane; jj < nk; jj += 32) {
+            const float p = ref == -INFINITY ? 0.f : expf(s_row[jj] - ref);
+            s_row[jj] = p;
+            l += p;
+        }
+        l = warp_sum(l);
+        if (single) {
+            l += expf(sink - ref);
+            __syncwarp();
+            for (int jj = lane; jj < nk; jj += 32) s_row[jj] = Store<T>::round(s_row[jj] / l);
+        }
+        __syncwarp();
+        float acc[2] = {0.f, 0.f};
+        for (int jj = g; jj < nk; jj += groups) {
+            const float p = s_row[jj];
+            acc[0] = fmaf(p, Vs[jj * stride + dd], acc[0]);
+            if (hd > 32) acc[1] = fmaf(p, Vs[jj * stride + dd + 32], acc[1]);
+        }
+        for (int o = dl; o < 32; o <<= 1) {
+            acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], o);
+            acc[1] += __shfl_xor_sync(0xffffffffu, acc[1], o);
+        }
+        if (single) {
+            float* orow = out + tok * dm.H * hd + size_t(hq) * hd;
+            if (g == 0) {
+                orow[dd] = Store<T>::round(acc[0]);
+                if (hd > 32) orow[dd + 32] = Store<T>::round(acc[1]);
+            }
+        } else {
+            float* part = a.partial + (((tok * dm.KV + kvh) * G + m) * a.chunks + chunk) * (hd + 2);
+            if (g == 0) {
+                part[2 + dd] = acc[0];
+                if (hd > 32) part[2 + dd + 32] = acc[1];
+            }
+            if (lane == 0) {
+                part[0] = mx;
+                part[1] = l;
+            }
+        }
     }
-    for (int o = dl; o < 32; o <<= 1) {
-        acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], o);
-        acc[1] += __shfl_xor_sync(0xffffffffu, acc[1], o);
+    if (a.chunks == 1) return;
+    // Split-KV merge: the last CTA of this (row, kv head) combines every chunk's partial with the sink.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(a.counters + tok * dm.KV + kvh, 1u);
+        last_flag = prev == unsigned(a.chunks - 1);
     }
-    float* orow = out + tok * dm.H * hd + size_t(hq) * hd;
-    if (g == 0) {
-        orow[dd] = Store<T>::round(acc[0]);
-        if (hd > 32) orow[dd + 32] = Store<T>::round(acc[1]);
+    __syncthreads();
+    if (!last_flag) return;
+    __threadfence();
+    for (int m = warp; m < G; m += kWarps) {
+        const int hq = kvh * G + m;
+        const float* part = a.partial + ((tok * dm.KV + kvh) * G + m) * a.chunks * (hd + 2);
+        const float sink = Store<T>::load(sinks + hq);
+        float M = sink;
+        for (int c = 0; c < a.chunks; ++c) M = fmaxf(M, part[c * (hd + 2)]);
+        float L = expf(sink - M);
+        for (int c = 0; c < a.chunks; ++c) {
+            const float mc = part[c * (hd + 2)];
+            if (mc != -INFINITY) L += part[c * (hd + 2) + 1] * expf(mc - M);
+        }
+        float* orow = out + tok * dm.H * hd + size_t(hq) * hd;
+        for (int e = lane; e < hd; e += 32) {
+            float o = 0.f;
+            for (int c = 0; c < a.chunks; ++c) {
+                const float mc = part[c * (hd + 2)];
+                if (mc != -INFINITY) o += part[c * (hd + 2) + 2 + e] * expf(mc - M);
+            }
+            orow[e] = Store<T>::round(o / L);
+        }
+    }
+    if (threadIdx.x == 0) a.counters[tok * dm.KV + kvh] = 0u;
+}
+
+// ------------------------------------------------------------------------------------------------------
+// grid = (ceil(d / (kWarps*2)), ceil(ntok / kTileTokens)); block = kThreads. Out-projection + bias + residual.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) k_out(const float* __restrict__ attn, const float* __restrict__ x, int ntok,
+                                                  Dims dm, const T* __restrict__ Wo, const T* __restrict__ bo,
+                                                  float* __restrict__ x2) {
+    extern __shared__ float as[];  // [TT][K]
+    constexpr int TT = kTileTokens, MR = 2;
+    const int K = dm.H * dm.hd, d = dm.d;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = blockIdx.x * kWarps * MR + warp * MR;
+    const int t0 = blockIdx.y * TT, tt = min(TT, ntok - t0);
+    const int nr = max(0, min(MR, d - r0));
+    const T* rows[MR];
+#pragma unroll
+    for (int r = 0; r < MR; ++r) rows[r] = Wo + size_t(min(r0 + r, d - 1)) * K;
+    Frag<MR> f;
+    frag_load<T, MR>(f, rows, nr, K, 0);
+    pdl_wait();
+    pdl_trigger();
+    for (int e = threadIdx.x; e < tt * K; e += blockDim.x) as[e] = attn[size_t(t0) * K + e];
+    __syncthreads();
+    if (nr == 0) return;
+    float acc[MR][TT];
+    warp_gemv<T, MR, TT>(f, rows, nr, as, K, tt, acc);
+    if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < MR; ++r) {
+            if (r >= nr) break;
+            const float b = Store<T>::load(bo + r0 + r);
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+                if (t >= tt) break;
+                const size_t o = size_t(t0 + t) * d + r0 + r;
+                x2[o] = Store<T>::round(__fadd_rn(x[o], Store<T>::round(__fadd_rn(acc[r][t], b))));
+            }
+        }
     }
 }
 
@@ -299,7 +475,7 @@ __global__ void __launch_bounds__(256) k_attention(const float* __restrict__ q, 
 // Warp-wide top-k over `n` logits in shared memory: NaN ranks highest, ties go to the lowest index, output
 // sorted (the ranking of chroma/_src/codegen/gpu.py:300-337). Then softmax over the k values (kernels.h:125-151).
 template <typename T>
-__device__ void warp_topk_softmax(const float* g, int n, int k, int* idx_out, float* w_out, int* trace) {
+__device__ void warp_topk_softmax(const float* g, int n, int k, int* idx_out, float* w_out) {
     const int lane = threadIdx.x & 31;
     unsigned taken = 0;  // bit per owned slot (lane + 32*s), n <= 256
     float vals[8];
@@ -341,163 +517,159 @@ __device__ void warp_topk_softmax(const float* g, int n, int k, int* idx_out, fl
         for (int r = 0; r < k; ++r) {
             idx_out[r] = ids[r];
             w_out[r] = Store<T>::round(e[r] / s);
-            if (trace) trace[r] = ids[r];
         }
     }
 }
 
-// grid = ntok; block = 256. Out-projection + residual, then the MLP block's norm, gate and routing. `routes`
-// (optional) records this layer's selected experts for inspection.
-template <typename T>
-__global__ void __launch_bounds__(256) k_out_router(const float* __restrict__ attn, const float* __restrict__ x,
-                                                    int ntok, Dims dm, LayerW<T> w, float* __restrict__ x2,
-                                                    float* __restrict__ tnorm, int* __restrict__ ridx,
-                                                    float* __restrict__ rw, int* __restrict__ routes) {
-    extern __shared__ float smem[];
-    const int K = dm.H * dm.hd, d = dm.d;
-    float* as = smem;       // [K]
-    float* xr = as + K;     // [d]
-    float* gl = xr + d;     // [E]
-    float* red = gl + dm.E; // [32]
-    const int t = blockIdx.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
-    prefetch_l2(w.out_w, size_t(d) * K * sizeof(T), threadIdx.x, blockDim.x);
-    pdl_wait();
-    pdl_trigger();
+// grid = (ntok * k, ceil(I / kPairsPerCta)); block = kThreads. Every CTA recomputes its token's router (norm, gate,
+// top-k, softmax: a few KB of L2-resident weights) so no separate router launch is needed; the (slot 0, block 0) CTA
+// publishes the routing for k_moe_down and for inspection. Then each warp computes 2 (glu, linear) row pairs of the
+// CTA's expert and applies the clamped SwiGLU (gpt_oss.py:212-219) with the reference's rounding points.
+constexpr int kPairsPerCta = kWarps * 2;
 
-    for (int c = threadIdx.x; c < K; c += blockDim.x) as[c] = attn[size_t(t) * K + c];
-    __syncthreads();
-    for (int c = warp; c < d; c += warps) {
-        float acc[1];
-        warp_row_dots<T, 1>(w.out_w + size_t(c) * K, as, K, 1, acc);
-        if (lane == 0) {
-            const float o = Store<T>::round(__fadd_rn(acc[0], Store<T>::load(w.out_b + c)));
-            const float v = Store<T>::round(__fadd_rn(x[size_t(t) * d + c], o));
-            xr[c] = v;
-            x2[size_t(t) * d + c] = v;
-        }
-    }
-    __syncthreads();
-    float s = 0.f;
-    for (int c = threadIdx.x; c < d; c += blockDim.x) s = fmaf(xr[c], xr[c], s);
-    s = warp_sum(s);
-    if (lane == 0) red[warp] = s;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float tot = 0.f;
-        for (int i = 0; i < warps; ++i) tot += red[i];
-        red[0] = 1.0f / sqrtf(tot / float(d) + dm.eps);
-    }
-    __syncthreads();
-    const float inv = red[0];
-    for (int c = threadIdx.x; c < d; c += blockDim.x) {
-        const float v = Store<T>::round(__fmul_rn(__fmul_rn(xr[c], inv), w.mlp_norm[c]));
-        xr[c] = v;
-        tnorm[size_t(t) * d + c] = v;
-    }
-    __syncthreads();
-    for (int e = warp; e < dm.E; e += warps) {
-        float acc[1];
-        warp_row_dots<T, 1>(w.gate_w + size_t(e) * d, xr, d, 1, acc);
-        if (lane == 0) gl[e] = Store<T>::round(__fadd_rn(acc[0], Store<T>::load(w.gate_b + e)));
-    }
-    __syncthreads();
-    if (warp == 0)
-        warp_topk_softmax<T>(gl, dm.E, dm.k, ridx + size_t(t) * dm.k, rw + size_t(t) * dm.k,
-                             routes ? routes + size_t(t) * dm.k : nullptr);
-}
-
-// ------------------------------------------------------------------------------------------------------
-// grid = (ntok * k, ceil(I / pairs_per_cta)); block = 256. Each warp computes one (glu, linear) row pair of the
-// selected expert's mlp1 and applies the clamped SwiGLU (gpt_oss.py:212-219) with the reference's rounding points.
 template <typename T>
-__global__ void __launch_bounds__(256) k_moe_up(const float* __restrict__ tnorm, int ntok, Dims dm,
-                                                const int* __restrict__ ridx, const T* __restrict__ w1,
-                                                const T* __restrict__ b1, int pairs_per_cta,
-                                                float* __restrict__ act, unsigned* err) {
-    extern __shared__ float xs[];  // [d]
-    const int te = blockIdx.x;  // token * k + slot
-    const int t = te / dm.k;
+__global__ void __launch_bounds__(kThreads) k_moe_up(const float* __restrict__ x2, int ntok, Dims dm, LayerW<T> w,
+                                                     int* __restrict__ ridx, float* __restrict__ rw,
+                                                     int* __restrict__ routes, float* __restrict__ act, unsigned* err) {
+    extern __shared__ float sm[];
     const int d = dm.d;
-    const int p0 = blockIdx.y * pairs_per_cta;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    float* xs = sm;            // [d]
+    float* gl = xs + d;        // [E]
+    float* misc = gl + dm.E;   // [1 + 8 + 8]: inv, indices, weights
+    int* sidx = reinterpret_cast<int*>(misc + 1);
+    float* sw = misc + 9;
+    const int te = blockIdx.x;  // token * k + slot
+    const int t = te / dm.k, slot = te % dm.k;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();
     pdl_trigger();
-    const int e = int(checked_row(ridx[te], dm.E, true, err));
-    const T* W = w1 + size_t(e) * 2 * dm.I * d;
-    const T* B = b1 + size_t(e) * 2 * dm.I;
-    for (int c = threadIdx.x; c < d; c += blockDim.x) xs[c] = tnorm[size_t(t) * d + c];
+    for (int c = threadIdx.x; c < d; c += blockDim.x) xs[c] = x2[size_t(t) * d + c];
     __syncthreads();
-    const int p_end = min(dm.I, p0 + pairs_per_cta);
-    for (int p = p0 + warp; p < p_end; p += warps) {
-        float ag[1], al[1];
-        warp_row_dots<T, 1>(W + size_t(2 * p) * d, xs, d, 1, ag);
-        warp_row_dots<T, 1>(W + size_t(2 * p + 1) * d, xs, d, 1, al);
+    rows_rmsnorm<T>(xs, 1, d, dm.eps, w.mlp_norm, misc);
+    // Gate: rows e of gate_w, two per warp at a time.
+    for (int e0 = warp * 2; e0 < dm.E; e0 += kWarps * 2) {
+        const T* rows[2] = {w.gate_w + size_t(e0) * d, w.gate_w + size_t(min(e0 + 1, dm.E - 1)) * d};
+        const int nr = min(2, dm.E - e0);
+        Frag<2> f;
+        frag_load<T, 2>(f, rows, nr, d, 0);
+        float acc[2][1];
+        warp_gemv<T, 2, 1>(f, rows, nr, xs, d, 1, acc);
         if (lane == 0) {
-            // einsum output (rounded), then + mlp1_bias (rounded) (gpt_oss.py:253).
-            const float hg = Store<T>::round(__fadd_rn(Store<T>::round(ag[0]), Store<T>::load(B + 2 * p)));
-            const float hl = Store<T>::round(__fadd_rn(Store<T>::round(al[0]), Store<T>::load(B + 2 * p + 1)));
-            const float glu = fminf(hg, dm.limit);
-            const float lin = fminf(fmaxf(hl, -dm.limit), dm.limit);
-            const float z = Store<T>::round(__fmul_rn(glu, dm.alpha));
-            const float sg = Store<T>::round(1.0f / (1.0f + expf(-z)));
-            const float og = Store<T>::round(__fmul_rn(glu, sg));
-            const float l1 = Store<T>::round(__fadd_rn(lin, 1.0f));
-            act[size_t(te) * dm.I + p] = Store<T>::round(__fmul_rn(og, l1));
+            gl[e0] = Store<T>::round(__fadd_rn(acc[0][0], Store<T>::load(w.gate_b + e0)));
+            if (nr > 1) gl[e0 + 1] = Store<T>::round(__fadd_rn(acc[1][0], Store<T>::load(w.gate_b + e0 + 1)));
         }
+    }
+    __syncthreads();
+    if (warp == 0) warp_topk_softmax<T>(gl, dm.E, dm.k, sidx, sw);
+    __syncthreads();
+    if (slot == 0 && blockIdx.y == 0 && threadIdx.x < dm.k) {
+        ridx[size_t(t) * dm.k + threadIdx.x] = sidx[threadIdx.x];
+        rw[size_t(t) * dm.k + threadIdx.x] = sw[threadIdx.x];
+        if (routes) routes[size_t(t) * dm.k + threadIdx.x] = sidx[threadIdx.x];
+    }
+    const int e = int(checked_row(sidx[slot], dm.E, true, err));
+    const T* W = w.w1 + size_t(e) * 2 * dm.I * d;
+    const T* B = w.b1 + size_t(e) * 2 * dm.I;
+    const int p = blockIdx.y * kPairsPerCta + warp * 2;  // this warp's first pair
+    if (p >= dm.I) return;
+    const int np = min(2, dm.I - p);
+    const int p1 = min(p + 1, dm.I - 1);
+    const T* rows[4] = {W + size_t(2 * p) * d, W + size_t(2 * p + 1) * d, W + size_t(2 * p1) * d, W + size_t(2 * p1 + 1) * d};
+    Frag<4> f;
+    frag_load<T, 4>(f, rows, 2 * np, d, 0);
+    float acc[4][1];
+    warp_gemv<T, 4, 1>(f, rows, 2 * np, xs, d, 1, acc);
+    if (lane < np) {
+        const int pp = p + lane;
+        const float ag = lane == 0 ? acc[0][0] : acc[2][0];
+        const float al = lane == 0 ? acc[1][0] : acc[3][0];
+        // einsum output (rounded), then + mlp1_bias (rounded) (gpt_oss.py:253).
+        const float hg = Store<T>::round(__fadd_rn(Store<T>::round(ag), Store<T>::load(B + 2 * pp)));
+        const float hl = Store<T>::round(__fadd_rn(Store<T>::round(al), Store<T>::load(B + 2 * pp + 1)));
+        const float glu = fminf(hg, dm.limit);
+        const float lin = fminf(fmaxf(hl, -dm.limit), dm.limit);
+        const float z = Store<T>::round(__fmul_rn(glu, dm.alpha));
+        const float sg = Store<T>::round(1.0f / (1.0f + expf(-z)));
+        const float og = Store<T>::round(__fmul_rn(glu, sg));
+        const float l1 = Store<T>::round(__fadd_rn(lin, 1.0f));
+        act[size_t(te) * dm.I + pp] = Store<T>::round(__fmul_rn(og, l1));
     }
 }
 
-// grid = (ntok, ceil(d / cols_per_cta)); block = 256. mlp2 of every selected expert for a slice of output
-// columns, + bias, weighted sum over the k experts in slot order, + residual.
+// grid = (ntok, ceil(d / kWarps)); block = kThreads. One output column per warp: mlp2 row of each selected expert
+// (+ bias), weighted sum over the k experts in slot order, + residual. The k rows are loaded together.
 template <typename T>
-__global__ void __launch_bounds__(256) k_moe_down(const float* __restrict__ act, const float* __restrict__ x2,
-                                                  int ntok, Dims dm, const int* __restrict__ ridx,
-                                                  const float* __restrict__ rw, const T* __restrict__ w2,
-                                                  const T* __restrict__ b2, int cols_per_cta,
-                                                  float* __restrict__ x_out, unsigned* err) {
+__global__ void __launch_bounds__(kThreads) k_moe_down(const float* __restrict__ act, const float* __restrict__ x2,
+                                                       int ntok, Dims dm, const int* __restrict__ ridx,
+                                                       const float* __restrict__ rw, const T* __restrict__ w2,
+                                                       const T* __restrict__ b2, float* __restrict__ x_out,
+                                                       unsigned* err) {
     extern __shared__ float as[];  // [k][I]
     const int t = blockIdx.x;
-    const int c0 = blockIdx.y * cols_per_cta;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.y * kWarps + warp;
     pdl_wait();
     pdl_trigger();
     for (int i = threadIdx.x; i < dm.k * dm.I; i += blockDim.x) as[i] = act[size_t(t) * dm.k * dm.I + i];
     __syncthreads();
-    const int c_end = min(dm.d, c0 + cols_per_cta);
-    for (int c = c0 + warp; c < c_end; c += warps) {
-        float comb = 0.f;
-        for (int s = 0; s < dm.k; ++s) {
-            const int e = int(checked_row(ridx[size_t(t) * dm.k + s], dm.E, true, err));
-            float acc[1];
-            warp_row_dots<T, 1>(w2 + (size_t(e) * dm.d + c) * dm.I, as + s * dm.I, dm.I, 1, acc);
-            const float y = Store<T>::round(__fadd_rn(Store<T>::round(acc[0]), Store<T>::load(b2 + size_t(e) * dm.d + c)));
-            comb = __fadd_rn(comb, __fmul_rn(y, rw[size_t(t) * dm.k + s]));
+    if (c >= dm.d) return;
+    float comb = 0.f;
+    for (int s0 = 0; s0 < dm.k; s0 += 4) {
+        const int ns = min(4, dm.k - s0);
+        int e[4];
+        const T* rows[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            e[u] = int(checked_row(ridx[size_t(t) * dm.k + min(s0 + u, dm.k - 1)], dm.E, true, err));
+            rows[u] = w2 + (size_t(e[u]) * dm.d + c) * dm.I;
         }
-        if (lane == 0) {
-            const float cm = Store<T>::round(comb);
-            x_out[size_t(t) * dm.d + c] = Store<T>::round(__fadd_rn(x2[size_t(t) * dm.d + c], cm));
+        // All (up to 4) rows in flight at once; each is then dotted with its own expert's activation row.
+        float part[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c0 = 0; c0 < dm.I; c0 += kChunk) {
+            Frag<4> f;
+            frag_load<T, 4>(f, rows, ns, dm.I, c0);
+#pragma unroll
+            for (int j = 0; j < kMJ; ++j) {
+                const int cc = c0 + lane * 4 + 128 * j;
+                if (cc >= dm.I) break;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    if (u >= ns) break;
+                    const float4 xv = *reinterpret_cast<const float4*>(as + (s0 + u) * dm.I + cc);
+                    part[u] = fmaf(f.v[u][j][0], xv.x, part[u]);
+                    part[u] = fmaf(f.v[u][j][1], xv.y, part[u]);
+                    part[u] = fmaf(f.v[u][j][2], xv.z, part[u]);
+                    part[u] = fmaf(f.v[u][j][3], xv.w, part[u]);
+                }
+            }
         }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) part[u] = warp_sum(part[u]);
+        for (int u = 0; u < ns; ++u) {
+            const float y = Store<T>::round(__fadd_rn(Store<T>::round(part[u]), Store<T>::load(b2 + size_t(e[u]) * dm.d + c)));
+            comb = __fadd_rn(comb, __fmul_rn(y, rw[size_t(t) * dm.k + s0 + u]));
+        }
+    }
+    if (lane == 0) {
+        const float cm = Store<T>::round(comb);
+        x_out[size_t(t) * dm.d + c] = Store<T>::round(__fadd_rn(x2[size_t(t) * dm.d + c], cm));
     }
 }
 
 // ------------------------------------------------------------------------------------------------------
-// Final RMSNorm of selected rows: rows[r] = index of the r-th wanted row (negative wraps, aten.index semantics).
+// Final RMSNorm of selected rows: rows[s] = row within sequence s (negative wraps, aten.index semantics), or every
+// row when rows == nullptr. Also clears the argmax keys the vocab kernel accumulates into.
 template <typename T>
-__global__ void k_final_norm(const float* __restrict__ x, int ntok, int nrows, const int64_t* __restrict__ rows,
-                             int rows_per_seq, const float* __restrict__ norm_w, Dims dm, float* __restrict__ out,
-                             unsigned* err) {
+__global__ void k_final_norm(const float* __restrict__ x, int nrows, const int64_t* __restrict__ rows, int rows_per_seq,
+                             const float* __restrict__ norm_w, Dims dm, float* __restrict__ out,
+                             unsigned long long* __restrict__ keys, unsigned* err) {
     __shared__ float red[32];
     const int r = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
     pdl_wait();
     pdl_trigger();
     int64_t src = r;
-    if (rows != nullptr) {
-        // One selected row per sequence; rows[] holds the row index within each sequence.
-        const int seq = r;
-        src = int64_t(seq) * rows_per_seq + checked_row(rows[seq], rows_per_seq, true, err);
-    }
+    if (rows != nullptr) src = int64_t(r) * rows_per_seq + checked_row(rows[r], rows_per_seq, true, err);
     const float* xr = x + size_t(src) * dm.d;
     float s = 0.f;
     for (int c = threadIdx.x; c < dm.d; c += blockDim.x) s = fmaf(xr[c], xr[c], s);
@@ -508,6 +680,7 @@ __global__ void k_final_norm(const float* __restrict__ x, int ntok, int nrows, c
         float tot = 0.f;
         for (int i = 0; i < warps; ++i) tot += red[i];
         red[0] = 1.0f / sqrtf(tot / float(dm.d) + dm.eps);
+        if (keys) keys[r] = 0ull;
     }
     __syncthreads();
     const float inv = red[0];
@@ -515,18 +688,35 @@ __global__ void k_final_norm(const float* __restrict__ x, int ntok, int nrows, c
         out[size_t(r) * dm.d + c] = Store<T>::round(__fmul_rn(__fmul_rn(xr[c], inv), norm_w[c]));
 }
 
-// Vocab projection: logits[r][v] = sum_c xs[r][c] * W[v][c], rows R <= 8 per pass. Each warp covers 4 vocab rows per
-// step with 8 lanes per row; the grid strides over blocks of rows. Weights stream once (no L1 allocation).
+// Orderable 64-bit argmax key: larger value wins, then the lower index (numpy.argmax: first occurrence).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    unsigned u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    if (isnan(v)) u = 0xffffffffu;
+    return (static_cast<unsigned long long>(u) << 32) | (0xffffffffu - static_cast<unsigned>(idx));
+}
+
+__host__ __device__ inline int64_t argmax_index(unsigned long long key) {
+    return int64_t(0xffffffffu - static_cast<unsigned>(key & 0xffffffffull));
+}
+
+// Vocab projection: logits[r][v] = sum_c xs[r][c] * W[v][c] for up to R rows per pass. 8 lanes per vocab row, 4 rows
+// per warp step, 2 steps unrolled: every lane issues its 16-byte streaming loads for 8 rows (d=128: 8 loads) before
+// any FMA. With `keys`, each row's greedy argmax is reduced in-block and merged with one 64-bit atomicMax per block.
 constexpr int kVocabRows = 8;
 
 template <typename T, int R>
-__global__ void __launch_bounds__(256) k_vocab(const float* __restrict__ xin, int nrows, int d, int V,
-                                               const T* __restrict__ W, T* __restrict__ logits) {
+__global__ void __launch_bounds__(kThreads) k_vocab(const float* __restrict__ xin, int nrows, int d, int V,
+                                                    const T* __restrict__ W, T* __restrict__ logits,
+                                                    unsigned long long* __restrict__ keys) {
     extern __shared__ float xs[];  // [R][d]
+    __shared__ unsigned long long best_s[kWarps][R];
+    constexpr int U = 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int sub = lane & 7, grp = lane >> 3;
-    const int warps_total = gridDim.x * (blockDim.x >> 5);
-    const int gw = blockIdx.x * (blockDim.x >> 5) + warp;
+    const int warps_total = gridDim.x * kWarps;
+    const int gw = blockIdx.x * kWarps + warp;
+    const int jn = (d + 31) / 32;  // float4 per lane per row
     pdl_wait();
     pdl_trigger();
     for (int r0 = 0; r0 < nrows; r0 += R) {
@@ -534,34 +724,71 @@ __global__ void __launch_bounds__(256) k_vocab(const float* __restrict__ xin, in
         __syncthreads();
         for (int i = threadIdx.x; i < rr * d; i += blockDim.x) xs[i] = xin[size_t(r0) * d + i];
         __syncthreads();
-        for (int v0 = gw * 4; v0 < V; v0 += warps_total * 4) {
-            const int v = v0 + grp;
-            float acc[R];
+        unsigned long long best[R];
 #pragma unroll
-            for (int r = 0; r < R; ++r) acc[r] = 0.f;
-            if (v < V) {
-                const T* wrow = W + size_t(v) * d;
-                for (int c = sub * 4; c < d; c += 32) {
-                    float w4[4];
-                    load4_stream(wrow + c, w4);
+        for (int r = 0; r < R; ++r) best[r] = 0ull;
+        for (int v0 = gw * 4 * U; v0 < V; v0 += warps_total * 4 * U) {
+            float acc[U][R];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int r = 0; r < R; ++r) acc[u][r] = 0.f;
+            for (int jb = 0; jb < jn; jb += 4) {
+                float w[U][4][4];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int v = v0 + u * 4 + grp;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int c = (jb + j) * 32 + sub * 4;
+                        if (v < V && jb + j < jn && c < d) load4_stream(W + size_t(v) * d + c, w[u][j]);
+                        else w[u][j][0] = w[u][j][1] = w[u][j][2] = w[u][j][3] = 0.f;
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (jb + j >= jn) break;
+                    const int c = (jb + j) * 32 + sub * 4;
+                    if (c >= d) continue;
 #pragma unroll
                     for (int r = 0; r < R; ++r) {
-                        if (r < rr) {
-                            const float4 xv = *reinterpret_cast<const float4*>(xs + r * d + c);
-                            acc[r] = fmaf(w4[0], xv.x, acc[r]);
-                            acc[r] = fmaf(w4[1], xv.y, acc[r]);
-                            acc[r] = fmaf(w4[2], xv.z, acc[r]);
-                            acc[r] = fmaf(w4[3], xv.w, acc[r]);
+                        if (r >= rr) break;
+                        const float4 x = *reinterpret_cast<const float4*>(xs + r * d + c);
+#pragma unroll
+                        for (int u = 0; u < U; ++u) {
+                            acc[u][r] = fmaf(w[u][j][0], x.x, acc[u][r]);
+                            acc[u][r] = fmaf(w[u][j][1], x.y, acc[u][r]);
+                            acc[u][r] = fmaf(w[u][j][2], x.z, acc[u][r]);
+                            acc[u][r] = fmaf(w[u][j][3], x.w, acc[u][r]);
                         }
                     }
                 }
             }
 #pragma unroll
-            for (int r = 0; r < R; ++r) acc[r] = group_sum(acc[r], 8);
-            if (sub == 0 && v < V) {
+            for (int u = 0; u < U; ++u) {
+                const int v = v0 + u * 4 + grp;
 #pragma unroll
-                for (int r = 0; r < R; ++r)
-                    if (r < rr) Store<T>::store(logits + size_t(r0 + r) * V + v, acc[r]);
+                for (int r = 0; r < R; ++r) {
+                    const float val = Store<T>::round(group_sum(acc[u][r], 8));
+                    if (sub == 0 && v < V && r < rr) {
+                        if (logits) Store<T>::store(logits + size_t(r0 + r) * V + v, val);
+                        best[r] = max(best[r], argmax_key(val, v));
+                    }
+                }
+            }
+        }
+        if (keys) {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                unsigned long long b = best[r];
+                for (int o = 16; o; o >>= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
+                if (lane == 0) best_s[warp][r] = b;
+            }
+            __syncthreads();
+            if (threadIdx.x < rr) {
+                unsigned long long b = 0ull;
+                for (int w = 0; w < kWarps; ++w) b = max(b, best_s[w][threadIdx.x]);
+                atomicMax(keys + r0 + threadIdx.x, b);
             }
         }
     }

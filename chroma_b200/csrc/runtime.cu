@@ -177,47 +177,19 @@ __global__ void k_commit(const T* new_k, const T* new_v, int L, int B, int n, in
 
 // After a device-only greedy step: feed each sequence's argmax back as its next token, advance its position and
 // append the id to the generation record.
-__global__ void k_advance(const int64_t* argmax, int B, int64_t* tokens, int64_t* pos0, int64_t* record, int* counter,
-                          int capacity) {
+__global__ void k_advance(const unsigned long long* keys, int B, int64_t* tokens, int64_t* pos0, int64_t* record,
+                          int* counter, int capacity) {
     pdl_wait();
     pdl_trigger();
     const int step = *counter;
     for (int b = threadIdx.x; b < B; b += blockDim.x) {
-        tokens[b] = argmax[b];
+        const int64_t id = argmax_index(keys[b]);
+        tokens[b] = id;
         pos0[b] += 1;
-        if (step < capacity) record[size_t(step) * B + b] = argmax[b];
+        if (step < capacity) record[size_t(step) * B + b] = id;
     }
     __syncthreads();
     if (threadIdx.x == 0) *counter = step + 1;
-}
-
-// Greedy argmax over each row of logits (first index on ties, as numpy.argmax).
-template <typename T>
-__global__ void k_argmax(const T* logits, int V, int64_t* out) {
-    __shared__ float bv[32];
-    __shared__ int bi[32];
-    const int r = blockIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
-    pdl_wait();
-    pdl_trigger();
-    float best = -INFINITY;
-    int idx = 0x7fffffff;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) {
-        const float x = Store<T>::load(logits + size_t(r) * V + v);
-        if (x > best || (idx == 0x7fffffff)) { best = x; idx = v; }
-    }
-    for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
-    }
-    if (lane == 0) { bv[warp] = best; bi[warp] = idx; }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < warps; ++w)
-            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) { best = bv[w]; idx = bi[w]; }
-        out[r] = idx;
-    }
 }
 
 // ---------------------------------------------------------------------------------------------------------
@@ -341,25 +313,25 @@ struct GptIO {
     const int64_t* pos0 = nullptr;  // [B]
     const int64_t* rows = nullptr;  // [B] selected row per sequence, or nullptr for every row
     void* logits = nullptr;
-    int64_t* argmax = nullptr;      // [rows] optional
+    unsigned long long* keys = nullptr;  // [rows] optional fused-argmax keys
     int* routes = nullptr;          // [L][B*n][k] optional record of the routing
 };
 
 struct GptExec {
     const Model* m = nullptr;
-    int B = 1, n = 1, ctx = 0, mask_mode = kMaskBuffer, window = 0, sms = 148;
-    DevBuf arena;
+    int B = 1, n = 1, ctx = 0, mask_mode = kMaskBuffer, window = 0, sms = 148, chunks = 1;
+    DevBuf arena, counters;
     size_t arena_bytes = 0, unreused_bytes = 0;
-    float *x = nullptr, *x2 = nullptr, *tnorm = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *rw = nullptr,
-          *tf = nullptr;
+    float *x = nullptr, *x2 = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *rw = nullptr, *tf = nullptr,
+          *partial = nullptr;
     int* ridx = nullptr;
     void *scratch_k = nullptr, *scratch_v = nullptr;
     GptIO io;
     unsigned* err = nullptr;
     int launches = 0;
 
-    // Temporaries with their kernel-index lifetimes (0 embedding; per layer l: 1+5l QKV, 2+5l attention,
-    // 3+5l out/router, 4+5l expert up, 5+5l expert down; 1+5L final norm; 2+5L vocab), in planning order.
+    // Temporaries with their kernel-index lifetimes (0 embedding; per layer l: 1+5l QKV, 2+5l attention, 3+5l out,
+    // 4+5l router + expert up, 5+5l expert down; 1+5L final norm; 2+5L vocab), in planning order.
     void init(const Model& model, int batch, int rows_per_seq, int context, int mode, int win) {
         m = &model;
         B = batch;
@@ -374,17 +346,18 @@ struct GptExec {
         const int L = model.desc.layers;
         const size_t N = size_t(B) * n;
         const int last = 5 * (L - 1);
+        chunks = (ctx + n + kKeyChunk - 1) / kKeyChunk;
         auto round = [](size_t b) { return (b + 255) / 256 * 256; };
         std::vector<Alloc> a = {
-            {round(N * d.d * 4), 0, 1 + 5 * L, 0},           // x
-            {round(N * d.H * d.hd * 4), 1, 2 + last, 0},      // q
-            {round(N * d.H * d.hd * 4), 2, 3 + last, 0},      // attn
-            {round(N * d.d * 4), 3, 5 + last, 0},             // x2
-            {round(N * d.d * 4), 3, 4 + last, 0},             // tnorm
-            {round(N * d.k * 4), 3, 5 + last, 0},             // ridx
-            {round(N * d.k * 4), 3, 5 + last, 0},             // rw
-            {round(N * d.k * d.I * 4), 4, 5 + last, 0},       // act
-            {round(N * d.d * 4), 1 + 5 * L, 2 + 5 * L, 0},   // tf
+            {round(N * d.d * 4), 0, 1 + 5 * L, 0},                                  // x
+            {round(N * d.H * d.hd * 4), 1, 2 + last, 0},                             // q
+            {round(N * d.H * d.hd * 4), 2, 3 + last, 0},                             // attn
+            {round(N * d.d * 4), 3, 5 + last, 0},                                    // x2
+            {round(N * d.k * 4), 4, 5 + last, 0},                                    // ridx
+            {round(N * d.k * 4), 4, 5 + last, 0},                                    // rw
+            {round(N * d.k * d.I * 4), 4, 5 + last, 0},                              // act
+            {round(N * d.KV * d.G * size_t(chunks) * (d.hd + 2) * 4), 2, 2 + last, 0},  // partial
+            {round(N * d.d * 4), 1 + 5 * L, 2 + 5 * L, 0},                          // tf
         };
         const bool uncached = model.desc.kind != CHROMA_B200_GPTOSS_CACHED;
         if (uncached) {
@@ -401,33 +374,33 @@ struct GptExec {
         q = reinterpret_cast<float*>(base + a[1].offset);
         attn = reinterpret_cast<float*>(base + a[2].offset);
         x2 = reinterpret_cast<float*>(base + a[3].offset);
-        tnorm = reinterpret_cast<float*>(base + a[4].offset);
-        ridx = reinterpret_cast<int*>(base + a[5].offset);
-        rw = reinterpret_cast<float*>(base + a[6].offset);
-        act = reinterpret_cast<float*>(base + a[7].offset);
+        ridx = reinterpret_cast<int*>(base + a[4].offset);
+        rw = reinterpret_cast<float*>(base + a[5].offset);
+        act = reinterpret_cast<float*>(base + a[6].offset);
+        partial = reinterpret_cast<float*>(base + a[7].offset);
         tf = reinterpret_cast<float*>(base + a[8].offset);
         if (uncached) {
             scratch_k = base + a[9].offset;
             scratch_v = base + a[10].offset;
         }
+        counters = DevBuf(N * d.KV * sizeof(unsigned));
+        check(cudaMemset(counters.p, 0, counters.bytes), "attention counters");
     }
 
     template <typename T> void enqueue_t(cudaStream_t s) {
         const Dims& dm = m->dm;
         const int N = B * n;
         const int L = m->desc.layers;
-        const size_t es = sizeof(T);
         launches = 0;
-        launch(s, dim3(N), dim3(128), 0, k_embed<T>, io.tokens, N, reinterpret_cast<const T*>(m->at(0)), dm.V, dm.d,
-               x, err);
+        launch(s, dim3(N), dim3(128), 0, k_embed<T>, io.tokens, N, reinterpret_cast<const T*>(m->at(0)), dm.V, dm.d, x,
+               err);
         ++launches;
         const int heads_total = dm.H + 2 * dm.KV;
-        const int hpc = 1;
-        const size_t smem_in = size_t(kAttnInTokens) * dm.d * 4 + size_t(kAttnInTokens) * hpc * dm.hd * 4 + kAttnInTokens * 4;
-        const int nkeys = ctx + n;
-        const size_t smem_attn = size_t(dm.G) * nkeys * 4;
-        const size_t smem_router = size_t(dm.H * dm.hd + dm.d + dm.E + 32) * 4;
-        const int ppc = 16, cpc = 16;
+        const int tiles = (N + kTileTokens - 1) / kTileTokens;
+        const size_t smem_in = size_t(kTileTokens) * (dm.d + dm.hd + 1) * 4;
+        const size_t smem_attn = (size_t(2) * kKeyChunk * (dm.hd + 1) + size_t(dm.G) * kKeyChunk + size_t(dm.G) * dm.hd) * 4;
+        const size_t smem_out = size_t(kTileTokens) * dm.H * dm.hd * 4;
+        const size_t smem_up = size_t(dm.d + dm.E + 17) * 4;
         for (int l = 0; l < L; ++l) {
             const LayerW<T> w = m->layer<T>(l);
             T* nk;
@@ -445,41 +418,37 @@ struct GptExec {
                 ck = nk;
                 cv = nv;
             }
-            launch(s, dim3((heads_total + hpc - 1) / hpc, (N + kAttnInTokens - 1) / kAttnInTokens), dim3(256), smem_in,
-                   k_attn_in<T>, x, N, dm, hpc, w.attn_norm, w.qkv_w, w.qkv_b, io.positions,
-                   m->inv_freq.as<const float>(), q, nk, nv);
+            launch(s, dim3(heads_total, tiles), dim3(kThreads), smem_in, k_attn_in<T>, x, N, dm, w.attn_norm, w.qkv_w,
+                   w.qkv_b, io.positions, m->inv_freq.as<const float>(), q, nk, nv);
             AttnArgs a;
             a.n = n;
             a.ctx = ctx;
             a.B = B;
+            a.chunks = chunks;
             a.cache_seq_stride = size_t(L) * ctx * dm.KV * dm.hd;
             a.mask_mode = mask_mode;
             const bool windowed = m->layer_window[size_t(l)] != 0;
             a.window = mask_mode == kMaskSlots ? (windowed ? window : ctx) : (windowed ? window : 0);
             a.slots = io.slots;
             a.pos0 = io.pos0;
+            a.partial = partial;
+            a.counters = counters.as<unsigned>();
             const T* bias = static_cast<const T*>(windowed ? io.window_mask : io.mask);
-            launch(s, dim3(n, dm.KV, B), dim3(dm.G * 32), smem_attn, k_attention<T>, q, dm, a, ck, cv,
+            launch(s, dim3(n, dm.KV, B * chunks), dim3(kThreads), smem_attn, k_attention<T>, q, dm, a, ck, cv,
                    static_cast<const T*>(nk), static_cast<const T*>(nv), bias, w.sinks, attn);
-            launch(s, dim3(N), dim3(256), smem_router, k_out_router<T>, attn, x, N, dm,
-                   w, x2, tnorm, ridx, rw, io.routes ? io.routes + size_t(l) * N * dm.k : nullptr);
-            launch(s, dim3(N * dm.k, (dm.I + ppc - 1) / ppc), dim3(256), size_t(dm.d) * 4, k_moe_up<T>,
-                   tnorm, N, dm, ridx, w.w1, w.b1, ppc, act, err);
-            launch(s, dim3(N, (dm.d + cpc - 1) / cpc), dim3(256), size_t(dm.k) * dm.I * 4, k_moe_down<T>,
-                   act, x2, N, dm, ridx, rw, w.w2,
-                   w.b2, cpc, x, err);
+            launch(s, dim3((dm.d + 2 * kWarps - 1) / (2 * kWarps), tiles), dim3(kThreads), smem_out, k_out<T>, attn, x, N,
+                   dm, w.out_w, w.out_b, x2);
+            launch(s, dim3(N * dm.k, (dm.I + kPairsPerCta - 1) / kPairsPerCta), dim3(kThreads), smem_up, k_moe_up<T>, x2,
+                   N, dm, w, ridx, rw, io.routes ? io.routes + size_t(l) * N * dm.k : nullptr, act, err);
+            launch(s, dim3(N, (dm.d + kWarps - 1) / kWarps), dim3(kThreads), size_t(dm.k) * dm.I * 4, k_moe_down<T>, act,
+                   x2, N, dm, ridx, rw, w.w2, w.b2, x, err);
             launches += 5;
         }
         const int nrows = io.rows ? B : N;
-        launch(s, dim3(nrows), dim3(256), 0, k_final_norm<T>, x, N, nrows, io.rows, n,
-               reinterpret_cast<const float*>(m->at(1)), dm, tf, err);
+        launch(s, dim3(nrows), dim3(256), 0, k_final_norm<T>, x, nrows, io.rows, n,
+               reinterpret_cast<const float*>(m->at(1)), dm, tf, io.keys, err);
         enqueue_vocab_t<T>(s);
         launches += 2;
-        if (io.argmax) {
-            launch(s, dim3(nrows), dim3(1024), 0, k_argmax<T>, static_cast<const T*>(io.logits), dm.V, io.argmax);
-            ++launches;
-        }
-        (void)es;
     }
 
     // The vocab projection alone (reads the final-norm rows left by the last run).
@@ -487,8 +456,8 @@ struct GptExec {
         const Dims& dm = m->dm;
         const int nrows = io.rows ? B : B * n;
         const int vgrid = std::max(1, std::min((dm.V + 31) / 32, sms * 4));
-        launch(s, dim3(vgrid), dim3(256), size_t(kVocabRows) * dm.d * 4, k_vocab<T, kVocabRows>, tf, nrows, dm.d, dm.V,
-               reinterpret_cast<const T*>(m->at(2)), static_cast<T*>(io.logits));
+        launch(s, dim3(vgrid), dim3(kThreads), size_t(kVocabRows) * dm.d * 4, k_vocab<T, kVocabRows>, tf, nrows, dm.d, dm.V,
+               reinterpret_cast<const T*>(m->at(2)), static_cast<T*>(io.logits), io.keys);
     }
 
     void enqueue(cudaStream_t s) {
@@ -594,7 +563,7 @@ struct chroma_b200_decoder {
     int device = 0, B = 1, ctx = 0, window = 0, L = 0, row = 0, V = 0, steps = 1;
     size_t es = 4;
     cudaStream_t stream = nullptr;
-    DevBuf cache_k, cache_v, slots, pos0, commit_pos, tokens, positions, last, logits, argmax, err;
+    DevBuf cache_k, cache_v, slots, pos0, commit_pos, tokens, positions, last, logits, keys, err;
     std::unique_ptr<PinnedBuf> host_in, host_out;
     GptExec ex[2];
     DevBuf new_k[2], new_v[2];
@@ -887,7 +856,7 @@ int chroma_b200_decoder_create(chroma_b200_program* prefill, chroma_b200_program
         d->positions = DevBuf(size_t(batch) * d->steps * 4);
         d->last = DevBuf(size_t(batch) * 8);
         d->logits = DevBuf(size_t(batch) * d->V * d->es);
-        d->argmax = DevBuf(size_t(batch) * 8);
+        d->keys = DevBuf(size_t(batch) * 8);
         d->err = DevBuf(sizeof(unsigned));
         check(cudaMemset(d->err.p, 0, sizeof(unsigned)), "cudaMemset");
         d->host_in = std::make_unique<PinnedBuf>(size_t(batch) * (d->steps + 1) * 8);
@@ -910,7 +879,7 @@ int chroma_b200_decoder_create(chroma_b200_program* prefill, chroma_b200_program
             e.io.pos0 = d->pos0.as<const int64_t>();
             e.io.rows = d->last.as<const int64_t>();
             e.io.logits = d->logits.p;
-            e.io.argmax = nullptr;
+            e.io.keys = nullptr;
         }
         check(cudaDeviceSynchronize(), "decoder create");
         *out = d.release();
@@ -937,20 +906,21 @@ int chroma_b200_decoder_step(chroma_b200_decoder* d, int32_t use_decode, const i
                   "Upload positions");
             launch(s, dim3((d->B * n + 255) / 256), dim3(256), 0, k_positions, d->pos0.as<const int64_t>(), d->B, n,
                    d->positions.as<float>(), d->last.as<int64_t>(), count);
-            // The argmax flag changes the kernel list, so each (program, argmax) pair has its own captured graph.
-            e.io.argmax = argmax ? d->argmax.as<int64_t>() : nullptr;
+            // The argmax flag changes the kernel arguments, so each (program, argmax) pair has its own captured graph.
+            e.io.keys = argmax ? d->keys.as<unsigned long long>() : nullptr;
             d->graph[which][argmax ? 1 : 0].run(s, [&](cudaStream_t st) { e.enqueue(st); });
             unsigned* eh = static_cast<unsigned*>(d->host_out->p);
             int64_t* am = reinterpret_cast<int64_t*>(static_cast<char*>(d->host_out->p) + 16);
             check(cudaMemcpyAsync(eh, d->err.p, sizeof(unsigned), cudaMemcpyDeviceToHost, s), "Read index error");
             if (argmax)
-                check(cudaMemcpyAsync(am, d->argmax.p, size_t(d->B) * 8, cudaMemcpyDeviceToHost, s), "Download argmax");
+                check(cudaMemcpyAsync(am, d->keys.p, size_t(d->B) * 8, cudaMemcpyDeviceToHost, s), "Download argmax");
             if (logits)
                 check(cudaMemcpyAsync(logits, d->logits.p, size_t(d->B) * d->V * d->es, cudaMemcpyDeviceToHost, s),
                       "Download logits");
             check(cudaStreamSynchronize(s), "CUDA execution");
             if (*eh & kErrIndex) throw IndexError("Tensor index out of range");
-            if (argmax) std::memcpy(argmax, am, size_t(d->B) * 8);
+            if (argmax)
+                for (int b = 0; b < d->B; ++b) argmax[b] = argmax_index(static_cast<unsigned long long>(am[b]));
         } catch (...) {
             cudaStreamSynchronize(s);
             throw;
@@ -1014,7 +984,7 @@ int chroma_b200_decoder_advance(chroma_b200_decoder* d, const int64_t* tokens, c
             d->advance_graph.run(s, [&](cudaStream_t st) {
                 launch(st, dim3((d->B + 255) / 256), dim3(256), 0, k_positions, d->pos0.as<const int64_t>(), d->B, 1,
                        d->positions.as<float>(), d->last.as<int64_t>(), 1);
-                e.io.argmax = d->argmax.as<int64_t>();
+                e.io.keys = d->keys.as<unsigned long long>();
                 e.enqueue(st);
                 const dim3 grid(unsigned(d->L * d->B));
                 const int threads = std::min(256, ((d->row + 31) / 32) * 32);
@@ -1029,7 +999,7 @@ int chroma_b200_decoder_advance(chroma_b200_decoder* d, const int64_t* tokens, c
                            d->pos0.as<const int64_t>(), d->cache_k.as<float>(), d->cache_v.as<float>(),
                            d->slots.as<int64_t>());
                 launch(st, dim3(1), dim3(std::min(1024, ((d->B + 31) / 32) * 32)), 0, k_advance,
-                       d->argmax.as<const int64_t>(), d->B, d->tokens.as<int64_t>(), d->pos0.as<int64_t>(),
+                       d->keys.as<const unsigned long long>(), d->B, d->tokens.as<int64_t>(), d->pos0.as<int64_t>(),
                        d->record.as<int64_t>(), d->counter.as<int>(), d->capacity);
             });
         }
@@ -1044,8 +1014,8 @@ int chroma_b200_decoder_advance(chroma_b200_decoder* d, const int64_t* tokens, c
 }
 
 int32_t chroma_b200_decoder_step_launches(const chroma_b200_decoder* d) {
-    // positions + decode program (embed, 5 per layer, final norm, vocab, argmax) + commit + advance
-    return d ? 1 + (1 + 5 * d->L + 3) + 2 : 0;
+    // positions + decode program (embed, 5 per layer, final norm, vocab with fused argmax) + commit + advance
+    return d ? 1 + (1 + 5 * d->L + 2) + 2 : 0;
 }
 
 int chroma_b200_decoder_launch_vocab(chroma_b200_decoder* d, void* stream, char* err, size_t err_len) {
