@@ -814,6 +814,70 @@ int chroma_b200_routes(chroma_b200_program* p, int32_t* out, int64_t count, char
     });
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// Vocab projection + greedy argmax that allocates nothing. For callers that cannot call cudaMalloc: code running
+// inside a stream capture another framework owns, allocator-free embedded runtimes, or hosts that hand this library
+// pre-sized device buffers and forbid it from touching the allocator. The only scratch (one 64-bit argmax key per
+// row) lives in the static array below, kStaticArgmaxRows entries, which every GPU that loads this library holds
+// until exit.
+constexpr int kStaticArgmaxRows = 256;
+static __device__ __align__(256) unsigned long long g_static_argmax_keys[kStaticArgmaxRows];
+
+__global__ void k_clear_keys(unsigned long long* keys, int rows) {
+    pdl_wait();
+    pdl_trigger();
+    for (int i = threadIdx.x; i < rows; i += blockDim.x) keys[i] = 0ull;
+}
+
+__global__ void k_keys_to_ids(const unsigned long long* keys, int rows, int64_t* ids) {
+    pdl_wait();
+    pdl_trigger();
+    for (int i = threadIdx.x; i < rows; i += blockDim.x) ids[i] = argmax_index(keys[i]);
+}
+
+// Device address of the static scratch, looked up once per device (with that device current). In host code the
+// array's name is only a host-side stand-in, never a device address.
+constexpr int kMaxDevices = 64;
+static std::mutex g_static_mu;
+static unsigned long long* g_static_keys[kMaxDevices] = {};
+
+static unsigned long long* static_keys(int device) {
+    if (device < 0 || device >= kMaxDevices) throw std::runtime_error("device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_keys[device]) {
+        unsigned long long* ptr = nullptr;
+        check(cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_static_argmax_keys), "cudaGetSymbolAddress");
+        g_static_keys[device] = ptr;
+    }
+    return g_static_keys[device];
+}
+
+int chroma_b200_vocab_argmax_static(const chroma_b200_program* p, const float* x, int32_t rows, void* logits,
+                                    int64_t* ids, void* stream, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!p || !x || !ids) throw ValueError("null argument");
+        const auto& d = p->model.desc;
+        if (d.kind == CHROMA_B200_MICRO) throw ValueError("not a GPT-OSS program");
+        if (rows < 1 || rows > kStaticArgmaxRows)
+            throw ValueError("rows must be in [1, " + std::to_string(kStaticArgmaxRows) +
+                             "]: the static argmax scratch holds that many rows");
+        DeviceGuard guard(p->device);
+        unsigned long long* keys = static_keys(p->device);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        const Dims& dm = p->model.dm;
+        launch(s, dim3(1), dim3(256), 0, k_clear_keys, keys, int(rows));
+        const int vgrid = std::max(1, std::min((dm.V + 31) / 32, p->exec.sms * 4));
+        const size_t smem = size_t(kVocabRows) * dm.d * 4;
+        if (d.storage == CHROMA_B200_BF16)
+            launch(s, dim3(vgrid), dim3(kThreads), smem, k_vocab<__nv_bfloat16, kVocabRows>, x, int(rows), dm.d, dm.V,
+                   reinterpret_cast<const __nv_bfloat16*>(p->model.at(2)), static_cast<__nv_bfloat16*>(logits), keys);
+        else
+            launch(s, dim3(vgrid), dim3(kThreads), smem, k_vocab<float, kVocabRows>, x, int(rows), dm.d, dm.V,
+                   reinterpret_cast<const float*>(p->model.at(2)), static_cast<float*>(logits), keys);
+        launch(s, dim3(1), dim3(256), 0, k_keys_to_ids, keys, int(rows), ids);
+    });
+}
+
 int64_t chroma_b200_workspace_bytes(const chroma_b200_program* p) { return p ? int64_t(p->exec.arena_bytes) : 0; }
 
 // ---------------------------------------------------------------------------------------------------------

@@ -96,6 +96,16 @@ int64_t chroma_b200_plan_arena(int32_t count, const int64_t* sizes, const int32_
 /* Routing of the last run of a GPT-OSS program: the selected experts [layers, tokens, top_k] in rank order (the
  * indices of torch.topk(..., sorted=True) at gpt_oss.py:246), for parity checks. `count` is the element count. */
 int chroma_b200_routes(chroma_b200_program* program, int32_t* out, int64_t count, char* err, size_t err_len);
+/* Vocab projection with greedy argmax that allocates nothing (no counterpart in the reference). For callers that
+ * cannot call cudaMalloc, such as code running inside another framework's stream capture or an allocator-free host:
+ * `x` [rows, hidden] fp32 final-normed rows and `ids` [rows] int64 (and `logits` [rows, vocab] in the program's
+ * storage type, or NULL) are caller-owned device buffers; the program supplies the unembedding weights it already
+ * holds. Scratch is a static device array of 256 rows (2 KiB) held by every GPU that loads the library: rows > 256
+ * is a CHROMA_B200_VALUE error. The first call on a device looks up that array's device address, so make it before
+ * any stream capture. Calls share the array: calls that overlap on the GPU race. Queued on `stream` (a cudaStream_t;
+ * 0 is the legacy default stream), not synchronised. */
+int chroma_b200_vocab_argmax_static(const chroma_b200_program* program, const float* x, int32_t rows, void* logits,
+                                    int64_t* ids, void* stream, char* err, size_t err_len);
 /* Arena bytes of a program's executor (the manifest's workspace_bytes). */
 int64_t chroma_b200_workspace_bytes(const chroma_b200_program* program);
 

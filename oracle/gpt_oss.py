@@ -295,6 +295,12 @@ def embed(p: Params, tokens: np.ndarray, vocab: int) -> np.ndarray:
 def forward(cfg: Config, p: Params, tokens: np.ndarray, trace: Trace | None = None) -> np.ndarray:
     """Transformer.forward (gpt_oss.py:304-310): logits [n, V] for a causal pass over ``tokens``."""
     num = Numerics(p.bf16)
+    return linear(num, final_rows(cfg, p, tokens, trace), p["unembedding.weight"], None)
+
+
+def final_rows(cfg: Config, p: Params, tokens: np.ndarray, trace: Trace | None = None) -> np.ndarray:
+    """The final-normed hidden rows [n, d] that Transformer.forward projects onto the vocabulary."""
+    num = Numerics(p.bf16)
     x = embed(p, tokens, cfg.vocab)
     n = x.shape[0]
     positions = np.arange(n, dtype=F32)
@@ -310,8 +316,7 @@ def forward(cfg: Config, p: Params, tokens: np.ndarray, trace: Trace | None = No
         a = f"block.{layer}.attn."
         x = num.r(x + linear(num, attn, p[a + "out.weight"], p[a + "out.bias"]))
         x = _mlp(num, cfg, p, layer, x, trace)
-    t = num.r(rmsnorm(x, p["norm.scale"], 1e-5))
-    return linear(num, t, p["unembedding.weight"], None)
+    return num.r(rmsnorm(x, p["norm.scale"], 1e-5))
 
 
 def cached_step(cfg: Config, p: Params, tokens, positions, keys, values, mask, window_mask, last,  # type: ignore[no-untyped-def]
