@@ -521,6 +521,19 @@ def write_artifact(lowered: Lowered, output: str | os.PathLike[str]) -> Path:
     return output
 
 
+def lower_micro(weight: np.ndarray, rows: int, cols: int, eps: float = 1e-5) -> Lowered:
+    """The fused RMSNorm + gated-SiLU + residual row program for bf16 [rows, cols] inputs x, g, u (no export)."""
+    desc = {"kind": nat.MICRO, "storage": nat.BF16, "rows": rows, "cols": cols, "eps": float(eps),
+            "layers": 0, "hidden": 0, "heads": 0, "kv_heads": 0, "head_dim": 0, "experts": 0, "top_k": 0,
+            "intermediate": 0, "vocab": 0, "tokens": 0, "context": 0, "window": 0, "sm_scale": 0.0,
+            "swiglu_alpha": 0.0, "swiglu_limit": 0.0, "rope_concentration": 0.0}
+    spec = {"shape": [rows, cols], "dtype": "bfloat16"}
+    inputs = [{"name": n, **spec} for n in ("x", "g", "u")]
+    outputs = [{"name": "out", **spec}]
+    return Lowered({"desc": desc}, [np.asarray(weight, np.float32)], inputs, outputs,
+                   {"kernels": 1, "workspace_bytes": 0, "unreused_workspace_bytes": 0})
+
+
 def compile_model(model: Any, output: str | os.PathLike[str], *, steps: int, context: int | None = None,
                   last: bool = False) -> Program:
     """Write and load the artefact of a GPT-OSS model without exporting it (see ``lower_model``)."""

@@ -65,7 +65,8 @@ def gptoss_buffers(desc: dict, batch: int = 1) -> list[tuple[str, int, int, int]
     N = batch * desc["tokens"]
     es = 2 if desc["storage"] == 1 else 4
     last = 5 * (L - 1)
-    chunks = -(-(desc.get("context", 0) + desc["tokens"]) // 256)
+    key_chunk = 512 if hd <= 32 else 256
+    chunks = -(-(desc.get("context", 0) + desc["tokens"]) // key_chunk)
     G = H // KV
     out = [
         ("x", N * d * 4, 0, 1 + 5 * L),

@@ -45,16 +45,17 @@ __device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
     float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
     v[0] = fa.x; v[1] = fa.y; v[2] = fb.x; v[3] = fb.y;
 }
-// Streaming variant for weights read exactly once per launch: bypass L1 allocation.
+// Streaming variant for weights read exactly once per launch: bypass L1 allocation. Not volatile, so the
+// compiler may batch several of these ahead of their uses (the data is read-only for the kernel's lifetime).
 __device__ __forceinline__ void load4_stream(const float* p, float (&v)[4]) {
     float4 q;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
-                 : "=f"(q.x), "=f"(q.y), "=f"(q.z), "=f"(q.w) : "l"(p));
+    asm("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+        : "=f"(q.x), "=f"(q.y), "=f"(q.z), "=f"(q.w) : "l"(p));
     v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
 }
 __device__ __forceinline__ void load4_stream(const __nv_bfloat16* p, float (&v)[4]) {
     uint32_t a, b;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(a), "=r"(b) : "l"(p));
+    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(a), "=r"(b) : "l"(p));
     __nv_bfloat162 pa = *reinterpret_cast<__nv_bfloat162*>(&a);
     __nv_bfloat162 pb = *reinterpret_cast<__nv_bfloat162*>(&b);
     float2 fa = __bfloat1622float2(pa), fb = __bfloat1622float2(pb);

@@ -24,6 +24,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace cb200 {
 
@@ -244,10 +245,8 @@ __global__ void __launch_bounds__(kThreads) k_attn_in(const float* __restrict__ 
 // running step writes them), scores it for the G query heads of its kv head (one warp each), and either finishes
 // the softmax directly (single chunk: probabilities rounded like the reference's softmax output) or writes an
 // (m, l, o) partial that the last CTA of the row merges with the sink logit (split-KV, flash-decoding style).
-constexpr int kKeyChunk = 256;
-
 struct AttnArgs {
-    int n, ctx, B, chunks;
+    int n, ctx, B, chunks, key_chunk;  // key_chunk: keys per CTA (512 for head_dim <= 32, else 256)
     size_t cache_seq_stride;  // elements between sequences in the cache (layer offset already applied)
     int mask_mode;
     int window;               // mask window for kMaskCausal / kMaskSlots (0 = none)
@@ -268,12 +267,13 @@ __global__ void __launch_bounds__(kThreads) k_attention(const float* __restrict_
     const int b = blockIdx.z / a.chunks, chunk = blockIdx.z % a.chunks;
     const int hd = dm.hd, G = dm.G, stride = hd + 1;
     const int nkeys = a.ctx + a.n;
-    const int j0 = chunk * kKeyChunk;
-    const int nk = min(kKeyChunk, nkeys - j0);
-    float* Ks = sm;                          // [kKeyChunk][hd+1]
-    float* Vs = Ks + kKeyChunk * stride;     // [kKeyChunk][hd+1]
-    float* sc = Vs + kKeyChunk * stride;     // [G][kKeyChunk]
-    float* qs = sc + G * kKeyChunk;          // [G][hd]
+    const int KC = a.key_chunk;
+    const int j0 = chunk * KC;
+    const int nk = min(KC, nkeys - j0);
+    float* Ks = sm;                   // [KC][hd+1]
+    float* Vs = Ks + KC * stride;     // [KC][hd+1]
+    float* sc = Vs + KC * stride;     // [G][KC]
+    float* qs = sc + G * KC;          // [G][hd]
     __shared__ unsigned last_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t tok = size_t(b) * a.n + i;
@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kThreads) k_attention(const float* __restrict_
     for (int m = warp; m < G; m += kWarps) {
         const int hq = kvh * G + m;
         const float* qv = qs + m * hd;
-        float* s_row = sc + m * kKeyChunk;
+        float* s_row = sc + m * KC;
         float mx = -INFINITY;
         for (int jj = lane; jj < nk; jj += 32) {
             const int j = j0 + jj;
@@ -701,8 +701,8 @@ __host__ __device__ inline int64_t argmax_index(unsigned long long key) {
 }
 
 // Vocab projection: logits[r][v] = sum_c xs[r][c] * W[v][c] for up to R rows per pass. 8 lanes per vocab row, 4 rows
-// per warp step, 2 steps unrolled: every lane issues its 16-byte streaming loads for 8 rows (d=128: 8 loads) before
-// any FMA. With `keys`, each row's greedy argmax is reduced in-block and merged with one 64-bit atomicMax per block.
+// per warp step, U steps unrolled (4 for a single activation row, 2 otherwise): every lane issues its 16-byte
+// streaming loads for 4*U vocab rows before any FMA. With `keys`, each row's greedy argmax is reduced in-block and merged with one 64-bit atomicMax per block.
 constexpr int kVocabRows = 8;
 
 template <typename T, int R>
@@ -711,7 +711,7 @@ __global__ void __launch_bounds__(kThreads) k_vocab(const float* __restrict__ xi
                                                     unsigned long long* __restrict__ keys) {
     extern __shared__ float xs[];  // [R][d]
     __shared__ unsigned long long best_s[kWarps][R];
-    constexpr int U = 2;
+    constexpr int U = R == 1 ? 4 : 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int sub = lane & 7, grp = lane >> 3;
     const int warps_total = gridDim.x * kWarps;
@@ -791,6 +791,133 @@ __global__ void __launch_bounds__(kThreads) k_vocab(const float* __restrict__ xi
                 atomicMax(keys + r0 + threadIdx.x, b);
             }
         }
+    }
+}
+
+// Vocab projection streamed through shared memory by the TMA engine (rows of at most 2 KiB: the dev model's
+// 512-byte fp32 rows). One CTA per SM: warp kWarps (the producer) bulk-copies contiguous blocks of `rb` vocab rows
+// (32 KiB) into a kVocabStages-deep ring, signalling a "full" mbarrier per stage; the kWarps consumer warps compute
+// 4 rows at a time (8 lanes per row, 16-byte shared-memory reads) and release the stage on its "empty" mbarrier.
+// The first blocks are requested before the PDL wait: the weights never depend on the previous kernel. All waits
+// are bounded (tma.cuh): a stuck pipeline raises kErrTimeout instead of hanging.
+constexpr int kVocabStages = 4;
+constexpr int kVocabStageBytes = 32 * 1024;
+
+template <typename T, int R>
+__global__ void __launch_bounds__(kThreads + 32) k_vocab_tma(const float* __restrict__ xin, int nrows, int d, int V,
+                                                             const T* __restrict__ W, T* __restrict__ logits,
+                                                             unsigned long long* __restrict__ keys, int rb,
+                                                             unsigned* err) {
+    extern __shared__ __align__(128) unsigned char vsm[];
+    T* stage_buf = reinterpret_cast<T*>(vsm);                                        // [kVocabStages][rb*d]
+    float* xs = reinterpret_cast<float*>(vsm + size_t(kVocabStages) * kVocabStageBytes);  // [R][d]
+    __shared__ uint64_t full[kVocabStages], empty[kVocabStages];
+    __shared__ unsigned long long best_s[kWarps][R];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nblocks = (V + rb - 1) / rb;
+    const int mine = blockIdx.x < nblocks ? (nblocks - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+    const size_t stage_elems = size_t(rb) * d;
+    auto block_rows = [&](int k) { return min(rb, V - (int(blockIdx.x) + k * int(gridDim.x)) * rb); };
+    auto issue = [&](int k) {
+        const int s = k % kVocabStages;
+        const int blk = int(blockIdx.x) + k * int(gridDim.x);
+        const unsigned bytes = unsigned(block_rows(k)) * unsigned(d) * unsigned(sizeof(T));
+        mbar_arrive_expect_tx(&full[s], bytes);
+        bulk_load(stage_buf + s * stage_elems, W + size_t(blk) * rb * d, bytes, &full[s]);
+    };
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kVocabStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (warp == kWarps && lane == 0)
+        for (int k = 0; k < min(kVocabStages, mine); ++k) issue(k);
+    pdl_wait();
+    pdl_trigger();
+    for (int i = threadIdx.x; i < nrows * d; i += blockDim.x) xs[i] = xin[i];
+    __syncthreads();  // the last CTA-wide barrier: after it, producer and consumers never wait on each other's barriers
+
+    if (warp == kWarps) {
+        // Producer: refill each stage once all consumer warps have released it.
+        if (lane == 0) {
+            for (int k = kVocabStages; k < mine; ++k) {
+                const int s = k % kVocabStages;
+                if (!mbar_wait(&empty[s], unsigned((k / kVocabStages - 1) & 1), err)) break;
+                issue(k);
+            }
+        }
+        return;
+    }
+    const int sub = lane & 7, grp = lane >> 3;
+    unsigned long long best[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) best[r] = 0ull;
+    bool ok = true;
+    for (int k = 0; k < mine && ok; ++k) {
+        const int s = k % kVocabStages;
+        ok = mbar_wait(&full[s], unsigned((k / kVocabStages) & 1), err);
+        if (!ok) break;
+        const T* blk = stage_buf + s * stage_elems;
+        const int rows_in = block_rows(k);
+        const int v_base = (int(blockIdx.x) + k * int(gridDim.x)) * rb;
+        for (int r0 = warp * 4; r0 < rows_in; r0 += kWarps * 4) {
+            const int row = r0 + grp;
+            float acc[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) acc[r] = 0.f;
+            if (row < rows_in) {
+                for (int c = sub * 4; c < d; c += 32) {
+                    float w4[4];
+                    if constexpr (Store<T>::bf16) {
+                        const uint2 q = *reinterpret_cast<const uint2*>(blk + size_t(row) * d + c);
+                        const float2 fa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.x));
+                        const float2 fb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.y));
+                        w4[0] = fa.x; w4[1] = fa.y; w4[2] = fb.x; w4[3] = fb.y;
+                    } else {
+                        const float4 q = *reinterpret_cast<const float4*>(blk + size_t(row) * d + c);
+                        w4[0] = q.x; w4[1] = q.y; w4[2] = q.z; w4[3] = q.w;
+                    }
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        if (r >= nrows) break;
+                        const float4 x = *reinterpret_cast<const float4*>(xs + r * d + c);
+                        acc[r] = fmaf(w4[0], x.x, acc[r]);
+                        acc[r] = fmaf(w4[1], x.y, acc[r]);
+                        acc[r] = fmaf(w4[2], x.z, acc[r]);
+                        acc[r] = fmaf(w4[3], x.w, acc[r]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                if (r >= nrows) break;
+                const float val = Store<T>::round(group_sum(acc[r], 8));
+                if (sub == 0 && row < rows_in) {
+                    const int v = v_base + row;
+                    if (logits) Store<T>::store(logits + size_t(r) * V + v, val);
+                    best[r] = max(best[r], argmax_key(val, v));
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (keys) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            unsigned long long b = best[r];
+            for (int o = 16; o; o >>= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
+            if (lane == 0) best_s[warp][r] = b;
+        }
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kThreads) : "memory");  // consumer warps only
+    if (keys && threadIdx.x < nrows) {
+        unsigned long long b = 0ull;
+        for (int w = 0; w < kWarps; ++w) b = max(b, best_s[w][threadIdx.x]);
+        atomicMax(keys + threadIdx.x, b);
     }
 }
 

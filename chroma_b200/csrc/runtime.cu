@@ -15,6 +15,7 @@
 #include "micro.cuh"
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <algorithm>
 #include <fstream>
@@ -192,6 +193,55 @@ __global__ void k_advance(const unsigned long long* keys, int B, int64_t* tokens
     if (threadIdx.x == 0) *counter = step + 1;
 }
 
+// Vocab GEMV launch: the row-count template is the smallest that covers `rows` (a decode step has one row), and the
+// grid is exactly the CTAs that fit on the GPU at once (one wave of a grid-stride loop).
+template <typename T, int R>
+static void launch_vocab_r(cudaStream_t s, const Dims& dm, int sms, const float* x, int rows, const T* W, T* logits,
+                           unsigned long long* keys) {
+    const size_t smem = size_t(R) * dm.d * 4;
+    int per_sm = 0;
+    check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_vocab<T, R>, kThreads, smem), "vocab occupancy");
+    const int vgrid = std::max(1, std::min((dm.V + 31) / 32, sms * std::max(1, per_sm)));
+    launch(s, dim3(vgrid), dim3(kThreads), smem, k_vocab<T, R>, x, rows, dm.d, dm.V, W, logits, keys);
+}
+
+template <typename T, int R>
+static void launch_vocab_tma(cudaStream_t s, const Dims& dm, int sms, const float* x, int rows, const T* W, T* logits,
+                             unsigned long long* keys, unsigned* err) {
+    const int row_bytes = dm.d * int(sizeof(T));
+    const int rb = kVocabStageBytes / row_bytes;
+    const size_t smem = size_t(kVocabStages) * kVocabStageBytes + size_t(R) * dm.d * 4;
+    const int nblocks = (dm.V + rb - 1) / rb;
+    launch(s, dim3(std::min(nblocks, sms)), dim3(kThreads + 32), smem, k_vocab_tma<T, R>, x, rows, dm.d, dm.V, W, logits,
+           keys, rb, err);
+}
+
+// Rows of at most 2 KiB that tile 32 KiB stages exactly go through the TMA-pipelined kernel; others (large hidden
+// sizes) through the register-fragment kernel.
+static bool vocab_tma_ok(const Dims& dm, size_t es) {
+    const size_t row = size_t(dm.d) * es;
+    return row % 16 == 0 && row <= 2048 && kVocabStageBytes % row == 0;
+}
+
+template <typename T>
+static void launch_vocab(cudaStream_t s, const Dims& dm, int sms, const float* x, int rows, const T* W, T* logits,
+                         unsigned long long* keys, unsigned* err) {
+    // The TMA ring measured slower than the register-fragment kernel for the dev vocab (26.7 vs 21.6 us per launch,
+    // same 103 MB of DRAM reads), so it is only selected when CHROMA_B200_VOCAB_TMA is set.
+    static const bool use_tma = std::getenv("CHROMA_B200_VOCAB_TMA") != nullptr;
+    if (use_tma && vocab_tma_ok(dm, sizeof(T)) && rows <= kVocabRows) {
+        if (rows == 1) launch_vocab_tma<T, 1>(s, dm, sms, x, rows, W, logits, keys, err);
+        else if (rows <= 2) launch_vocab_tma<T, 2>(s, dm, sms, x, rows, W, logits, keys, err);
+        else if (rows <= 4) launch_vocab_tma<T, 4>(s, dm, sms, x, rows, W, logits, keys, err);
+        else launch_vocab_tma<T, kVocabRows>(s, dm, sms, x, rows, W, logits, keys, err);
+        return;
+    }
+    if (rows == 1) launch_vocab_r<T, 1>(s, dm, sms, x, rows, W, logits, keys);
+    else if (rows <= 2) launch_vocab_r<T, 2>(s, dm, sms, x, rows, W, logits, keys);
+    else if (rows <= 4) launch_vocab_r<T, 4>(s, dm, sms, x, rows, W, logits, keys);
+    else launch_vocab_r<T, kVocabRows>(s, dm, sms, x, rows, W, logits, keys);
+}
+
 // ---------------------------------------------------------------------------------------------------------
 struct Model {
     chroma_b200_desc desc{};
@@ -319,7 +369,7 @@ struct GptIO {
 
 struct GptExec {
     const Model* m = nullptr;
-    int B = 1, n = 1, ctx = 0, mask_mode = kMaskBuffer, window = 0, sms = 148, chunks = 1;
+    int B = 1, n = 1, ctx = 0, mask_mode = kMaskBuffer, window = 0, sms = 148, chunks = 1, key_chunk = 256;
     DevBuf arena, counters;
     size_t arena_bytes = 0, unreused_bytes = 0;
     float *x = nullptr, *x2 = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *rw = nullptr, *tf = nullptr,
@@ -346,7 +396,8 @@ struct GptExec {
         const int L = model.desc.layers;
         const size_t N = size_t(B) * n;
         const int last = 5 * (L - 1);
-        chunks = (ctx + n + kKeyChunk - 1) / kKeyChunk;
+        key_chunk = d.hd <= 32 ? 512 : 256;
+        chunks = (ctx + n + key_chunk - 1) / key_chunk;
         auto round = [](size_t b) { return (b + 255) / 256 * 256; };
         std::vector<Alloc> a = {
             {round(N * d.d * 4), 0, 1 + 5 * L, 0},                                  // x
@@ -398,7 +449,7 @@ struct GptExec {
         const int heads_total = dm.H + 2 * dm.KV;
         const int tiles = (N + kTileTokens - 1) / kTileTokens;
         const size_t smem_in = size_t(kTileTokens) * (dm.d + dm.hd + 1) * 4;
-        const size_t smem_attn = (size_t(2) * kKeyChunk * (dm.hd + 1) + size_t(dm.G) * kKeyChunk + size_t(dm.G) * dm.hd) * 4;
+        const size_t smem_attn = (size_t(2) * key_chunk * (dm.hd + 1) + size_t(dm.G) * key_chunk + size_t(dm.G) * dm.hd) * 4;
         const size_t smem_out = size_t(kTileTokens) * dm.H * dm.hd * 4;
         const size_t smem_up = size_t(dm.d + dm.E + 17) * 4;
         for (int l = 0; l < L; ++l) {
@@ -425,6 +476,7 @@ struct GptExec {
             a.ctx = ctx;
             a.B = B;
             a.chunks = chunks;
+            a.key_chunk = key_chunk;
             a.cache_seq_stride = size_t(L) * ctx * dm.KV * dm.hd;
             a.mask_mode = mask_mode;
             const bool windowed = m->layer_window[size_t(l)] != 0;
@@ -453,11 +505,8 @@ struct GptExec {
 
     // The vocab projection alone (reads the final-norm rows left by the last run).
     template <typename T> void enqueue_vocab_t(cudaStream_t s) {
-        const Dims& dm = m->dm;
-        const int nrows = io.rows ? B : B * n;
-        const int vgrid = std::max(1, std::min((dm.V + 31) / 32, sms * 4));
-        launch(s, dim3(vgrid), dim3(kThreads), size_t(kVocabRows) * dm.d * 4, k_vocab<T, kVocabRows>, tf, nrows, dm.d, dm.V,
-               reinterpret_cast<const T*>(m->at(2)), static_cast<T*>(io.logits), io.keys);
+        launch_vocab<T>(s, m->dm, sms, tf, io.rows ? B : B * n, reinterpret_cast<const T*>(m->at(2)),
+                        static_cast<T*>(io.logits), io.keys, err);
     }
 
     void enqueue(cudaStream_t s) {
@@ -866,14 +915,13 @@ int chroma_b200_vocab_argmax_static(const chroma_b200_program* p, const float* x
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         const Dims& dm = p->model.dm;
         launch(s, dim3(1), dim3(256), 0, k_clear_keys, keys, int(rows));
-        const int vgrid = std::max(1, std::min((dm.V + 31) / 32, p->exec.sms * 4));
-        const size_t smem = size_t(kVocabRows) * dm.d * 4;
         if (d.storage == CHROMA_B200_BF16)
-            launch(s, dim3(vgrid), dim3(kThreads), smem, k_vocab<__nv_bfloat16, kVocabRows>, x, int(rows), dm.d, dm.V,
-                   reinterpret_cast<const __nv_bfloat16*>(p->model.at(2)), static_cast<__nv_bfloat16*>(logits), keys);
+            launch_vocab<__nv_bfloat16>(s, dm, p->exec.sms, x, int(rows),
+                                        reinterpret_cast<const __nv_bfloat16*>(p->model.at(2)),
+                                        static_cast<__nv_bfloat16*>(logits), keys, p->err.as<unsigned>());
         else
-            launch(s, dim3(vgrid), dim3(kThreads), smem, k_vocab<float, kVocabRows>, x, int(rows), dm.d, dm.V,
-                   reinterpret_cast<const float*>(p->model.at(2)), static_cast<float*>(logits), keys);
+            launch_vocab<float>(s, dm, p->exec.sms, x, int(rows), reinterpret_cast<const float*>(p->model.at(2)),
+                                static_cast<float*>(logits), keys, p->err.as<unsigned>());
         launch(s, dim3(1), dim3(256), 0, k_keys_to_ids, keys, int(rows), ids);
     });
 }
