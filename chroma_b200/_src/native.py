@@ -77,6 +77,8 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "chroma_b200_workspace_bytes": (ctypes.c_int64, [_VP]),
     "chroma_b200_routes": (ctypes.c_int, [_VP, ctypes.POINTER(ctypes.c_int32), ctypes.c_int64, _CP, _SZ]),
     "chroma_b200_vocab_argmax_static": (ctypes.c_int, [_VP, _VP, _I32, _VP, _I64P, _VP, _CP, _SZ]),
+    "chroma_b200_gemm_bf16": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, _I32, _I32, _I32, _I32, ctypes.c_float,
+                                             ctypes.c_float, _I32, _VP, _VP, _VP, _VP, _CP, _SZ]),
     "chroma_b200_decoder_create": (ctypes.c_int, [_VP, _VP, _I32, _I32, ctypes.POINTER(_VP), _CP, _SZ]),
     "chroma_b200_decoder_step": (ctypes.c_int, [_VP, _I32, _I64P, _I32, _I64P, _VP, _I64P, _CP, _SZ]),
     "chroma_b200_decoder_commit": (ctypes.c_int, [_VP, _I32, _I32, _I64P, _CP, _SZ]),

@@ -1,0 +1,240 @@
+// bf16 GEMM on the sm_100a tensor cores: C[M, N] = A[M, K] . B[N, K]^T with fp32 accumulation in TMEM.
+//
+// Replaces the reference's cuBLAS SGEMM / scalar bf16 linear (chroma/_src/codegen/cuda/runtime.h:175-181,
+// chroma/_src/codegen/gpu.py:263-273) and its per-(token, expert) einsum loops (gpu.py:390-424) for the GPT-OSS-20B/
+// 120B-shaped programs. One kernel serves dense projections and grouped (per-expert) problems:
+//
+//   * persistent CTAs, one per SM, walk a static sequence of 128 x BN output tiles (no atomics);
+//   * warp 0 (one thread) streams A and B tiles with TMA (128-byte swizzle) into a kGemmStages-deep ring;
+//   * warp 1 allocates BN TMEM columns and (one thread) issues tcgen05.mma (M=128, N=BN, K=16) per 64-wide K block,
+//     releasing each ring stage with tcgen05.commit and signalling the epilogue when a tile's accumulation is done;
+//   * warps 2-5 read the accumulator (each warp its 32-lane TMEM quadrant = 32 tile rows) with tcgen05.ld and apply
+//     the fused epilogue (bias, rounding, residual add, SwiGLU), then hand TMEM back.
+//
+// Grouped problems (MoE experts): rows [offsets[g], offsets[g+1]) of A multiply B rows [g*N, (g+1)*N); tiles never
+// straddle groups (rows past a group's end are masked in the epilogue). All waits are bounded (tma.cuh).
+#pragma once
+
+#include "tcgen05.cuh"
+
+namespace cb200 {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmStages = 4;
+constexpr int kGemmThreads = 192;
+constexpr int kGemmMaxGroups = 256;
+
+enum GemmEpi : int {
+    kEpiStore = 0,    // C = round(acc + bias)
+    kEpiResidual = 1, // C = round(R[row] + round(acc + bias))            (linear + residual, gpt_oss.py:209)
+    kEpiSwiglu = 2,   // C[row, p] = swiglu(round(round(acc)+b) pairs)    (mlp1 + SwiGLU, gpt_oss.py:253-254)
+    kEpiExpert = 3,   // C = round(round(acc) + bias[g])                   (mlp2 einsum + bias, gpt_oss.py:259-260)
+};
+
+struct GemmArgs {
+    int M, N, K;
+    int epi;
+    const __nv_bfloat16* bias;      // [groups][N] (group stride N), or nullptr
+    const __nv_bfloat16* residual;  // [M][ldr] for kEpiResidual
+    int ldr;
+    __nv_bfloat16* C;               // [M][ldc]
+    int ldc;
+    float alpha, limit;             // SwiGLU slope and clamp
+    int groups;                     // 1 for a dense GEMM
+    const int* offsets;             // [groups + 1] row offsets of each group in A (device), or nullptr (dense)
+    const int* tile_starts;         // [groups + 1] prefix sums of 128-row tiles per group (device), or nullptr
+};
+
+__device__ __forceinline__ float round_bf16(float x) { return bf16_round(x); }
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_constant__ CUtensorMap map_a,
+                                                               const __grid_constant__ CUtensorMap map_b, GemmArgs g,
+                                                               unsigned* err) {
+    constexpr int A_BYTES = kGemmBM * kGemmBK * 2;
+    constexpr int B_BYTES = BN * kGemmBK * 2;
+    constexpr int STAGE = A_BYTES + B_BYTES;
+    extern __shared__ uint8_t gsm_raw[];
+    uint8_t* gsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t full[kGemmStages], empty[kGemmStages], tmem_full, tmem_empty;
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int abort_flag;  // set by any role whose bounded wait gave up
+    __shared__ int s_tiles[kGemmMaxGroups + 1];
+    __shared__ int s_offsets[kGemmMaxGroups + 1];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntiles_n = (g.N + BN - 1) / BN;
+    const int kblocks = (g.K + kGemmBK - 1) / kGemmBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kGemmStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&tmem_full, 1);
+        mbar_init(&tmem_empty, 4);
+        abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&map_a);
+        prefetch_tensormap(&map_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_base, BN);
+        tmem_relinquish();
+    }
+    // Weights and activations of this GEMM are produced by earlier kernels: wait before reading the offsets.
+    pdl_wait();
+    pdl_trigger();
+    for (int i = threadIdx.x; i <= g.groups; i += blockDim.x) {
+        s_offsets[i] = g.offsets ? g.offsets[i] : (i == 0 ? 0 : g.M);
+        s_tiles[i] = g.tile_starts ? g.tile_starts[i] : (i == 0 ? 0 : (g.M + kGemmBM - 1) / kGemmBM);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const int total_m = s_tiles[g.groups];
+    const int total = total_m * ntiles_n;
+    const uint32_t tmem = tmem_base;
+
+    // Tile t -> (group, first row, row end, n0). Consecutive tiles share an m-tile (A reuse) and sweep the group's B.
+    auto tile_of = [&](int t, int& grp, int& row0, int& row_end, int& n0) {
+        const int mt = t / ntiles_n;
+        n0 = (t % ntiles_n) * BN;
+        int lo = 0, hi = g.groups - 1;
+        while (lo < hi) {  // last group with s_tiles[grp] <= mt
+            const int mid = (lo + hi + 1) >> 1;
+            if (s_tiles[mid] <= mt) lo = mid;
+            else hi = mid - 1;
+        }
+        grp = lo;
+        row0 = s_offsets[grp] + (mt - s_tiles[grp]) * kGemmBM;
+        row_end = min(row0 + kGemmBM, s_offsets[grp + 1]);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int it = 0;
+            for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x) {
+                int grp, row0, row_end, n0;
+                tile_of(t, grp, row0, row_end, n0);
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kGemmStages;
+                    if (!mbar_wait(&empty[s], unsigned(((it / kGemmStages) & 1) ^ 1), err)) { abort_flag = 1; break; }
+                    uint8_t* sa = gsm + size_t(s) * STAGE;
+                    mbar_arrive_expect_tx(&full[s], STAGE);
+                    tma_load_2d(sa, &map_a, kb * kGemmBK, row0, &full[s]);
+                    tma_load_2d(sa + A_BYTES, &map_b, kb * kGemmBK, grp * g.N + n0, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16(kGemmBM, BN);
+            int it = 0, tile_it = 0;
+            for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++tile_it) {
+                if (!mbar_wait(&tmem_empty, unsigned((tile_it & 1) ^ 1), err)) { abort_flag = 1; break; }
+                tc_fence_after();
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kGemmStages;
+                    if (!mbar_wait(&full[s], unsigned((it / kGemmStages) & 1), err)) { abort_flag = 1; break; }
+                    tc_fence_after();
+                    const uint8_t* sa = gsm + size_t(s) * STAGE;
+                    const uint64_t da = umma_desc_sw128(sa);
+                    const uint64_t db = umma_desc_sw128(sa + A_BYTES);
+#pragma unroll
+                    for (int k = 0; k < kGemmBK / 16; ++k)  // advance 16 elements = 32 bytes = 2 in the >>4 field
+                        umma_bf16(tmem, da + 2 * k, db + 2 * k, idesc, kb > 0 || k > 0);
+                    umma_commit(&empty[s]);
+                }
+                if (abort_flag) break;
+                umma_commit(&tmem_full);
+            }
+        }
+    } else {
+        // Epilogue warps 2..5: TMEM quadrant q = warp % 4 holds tile rows [32q, 32q + 32).
+        const int q = warp & 3;
+        int tile_it = 0;
+        for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++tile_it) {
+            if (!mbar_wait(&tmem_full, unsigned(tile_it & 1), err)) { abort_flag = 1; break; }
+            tc_fence_after();
+            int grp, row0, row_end, n0;
+            tile_of(t, grp, row0, row_end, n0);
+            const int row = row0 + q * 32 + lane;
+            const bool live = row < row_end;
+            const __nv_bfloat16* bias = g.bias ? g.bias + size_t(grp) * g.N : nullptr;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                float v[32];
+                tmem_load32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c * 32), v);
+                const int col0 = n0 + c * 32;
+                if (!live || col0 >= g.N) continue;
+                const int ncols = min(32, g.N - col0);
+                if (g.epi == kEpiSwiglu) {
+                    // Interleaved pairs (glu = even column, linear = odd column) -> one output column per pair.
+                    __nv_bfloat16* out = g.C + size_t(row) * g.ldc + col0 / 2;
+#pragma unroll
+                    for (int p = 0; p < 16; ++p) {
+                        if (2 * p + 1 >= ncols) break;
+                        const float bg = bias ? __bfloat162float(bias[col0 + 2 * p]) : 0.f;
+                        const float bl = bias ? __bfloat162float(bias[col0 + 2 * p + 1]) : 0.f;
+                        const float hg = round_bf16(round_bf16(v[2 * p]) + bg);
+                        const float hl = round_bf16(round_bf16(v[2 * p + 1]) + bl);
+                        const float glu = fminf(hg, g.limit);
+                        const float lin = fminf(fmaxf(hl, -g.limit), g.limit);
+                        const float z = round_bf16(glu * g.alpha);
+                        const float sg = round_bf16(1.0f / (1.0f + expf(-z)));
+                        const float og = round_bf16(glu * sg);
+                        const float l1 = round_bf16(lin + 1.0f);
+                        out[p] = __float2bfloat16_rn(og * l1);
+                    }
+                } else {
+                    __nv_bfloat16* out = g.C + size_t(row) * g.ldc + col0;
+                    const __nv_bfloat16* res = g.epi == kEpiResidual ? g.residual + size_t(row) * g.ldr + col0 : nullptr;
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        if (j >= ncols) break;
+                        float r[2];
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const float b = bias ? __bfloat162float(bias[col0 + j + h]) : 0.f;
+                            float y = g.epi == kEpiExpert ? round_bf16(round_bf16(v[j + h]) + b) : round_bf16(v[j + h] + b);
+                            if (res) y = round_bf16(__bfloat162float(res[j + h]) + y);
+                            r[h] = y;
+                        }
+                        if (j + 1 < ncols) {
+                            *reinterpret_cast<__nv_bfloat162*>(out + j) = __floats2bfloat162_rn(r[0], r[1]);
+                        } else {
+                            out[j] = __float2bfloat16_rn(r[0]);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BN);
+    }
+}
+
+// Prefix sums of 128-row tiles per group from row offsets: tile_starts[g] = sum_{h<g} ceil(count_h / 128).
+__global__ void k_gemm_tile_starts(const int* offsets, int groups, int* tile_starts) {
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        int acc = 0;
+        for (int i = 0; i < groups; ++i) {
+            tile_starts[i] = acc;
+            acc += (offsets[i + 1] - offsets[i] + kGemmBM - 1) / kGemmBM;
+        }
+        tile_starts[groups] = acc;
+    }
+}
+
+}  // namespace cb200

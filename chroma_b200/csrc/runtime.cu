@@ -11,6 +11,7 @@
 // synchronises and reports CHROMA_B200_INDEX (IndexError); the program stays usable (runtime.h:147-173).
 
 #include "../../include/chroma_b200.h"
+#include "gemm.cuh"
 #include "gptoss.cuh"
 #include "micro.cuh"
 
@@ -141,6 +142,62 @@ static void launch(cudaStream_t s, dim3 grid, dim3 block, size_t smem, void (*ke
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     check(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), "kernel launch");
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// TMA tensor maps. cuTensorMapEncodeTiled is a driver entry point, fetched at run time (no link against libcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        check(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q), "cuTensorMapEncodeTiled");
+        if (!p || q != cudaDriverEntryPointSuccess) throw std::runtime_error("cuTensorMapEncodeTiled unavailable");
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// Row-major bf16 matrix [rows][cols] read in boxes of box_rows x 64 columns with the 128-byte swizzle.
+static CUtensorMap bf16_tile_map(const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    if (reinterpret_cast<uintptr_t>(base) % 16 || (cols * 2) % 16)
+        throw ValueError("TMA operands need 16-byte aligned bases and rows");
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {uint32_t(kGemmBK), box_rows};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUresult r = encode_tiled()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                                      elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+    return map;
+}
+
+// C = A . B^T on the tensor cores. Dense when groups == 1 and offsets == nullptr; grouped otherwise (offsets and
+// tile_scratch are device arrays of groups + 1 ints; tile_scratch receives the per-group tile prefix sums).
+static void gemm_bf16(cudaStream_t s, const void* A, const void* B, GemmArgs g, int rows_a, int rows_b, void* tile_scratch,
+                      int sms, unsigned* err) {
+    if (g.groups < 1 || g.groups > kGemmMaxGroups) throw ValueError("GEMM group count out of range");
+    if (g.K % 8) throw ValueError("GEMM K must be a multiple of 8");
+    if (g.epi == kEpiSwiglu && g.N % 32) throw ValueError("SwiGLU epilogue needs N a multiple of 32");
+    const bool narrow = g.N <= 32;
+    const CUtensorMap ma = bf16_tile_map(A, uint64_t(rows_a), uint64_t(g.K), kGemmBM);
+    const CUtensorMap mb = bf16_tile_map(B, uint64_t(rows_b), uint64_t(g.K), narrow ? 32 : 256);
+    if (g.offsets) {
+        if (!tile_scratch) throw ValueError("grouped GEMM needs tile scratch");
+        launch(s, dim3(1), dim3(32), 0, k_gemm_tile_starts, g.offsets, g.groups, static_cast<int*>(tile_scratch));
+        g.tile_starts = static_cast<const int*>(tile_scratch);
+    }
+    const int bn = narrow ? 32 : 256;
+    const int tiles = g.offsets ? sms : ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + bn - 1) / bn);
+    const dim3 grid(unsigned(std::max(1, std::min(tiles, sms))));
+    const size_t smem = size_t(kGemmStages) * (kGemmBM + bn) * kGemmBK * 2 + 1024;
+    if (narrow) launch(s, grid, dim3(kGemmThreads), smem, k_gemm_bf16<32>, ma, mb, g, err);
+    else launch(s, grid, dim3(kGemmThreads), smem, k_gemm_bf16<256>, ma, mb, g, err);
 }
 
 // ---------------------------------------------------------------------------------------------------------
@@ -923,6 +980,36 @@ int chroma_b200_vocab_argmax_static(const chroma_b200_program* p, const float* x
             launch_vocab<float>(s, dm, p->exec.sms, x, int(rows), reinterpret_cast<const float*>(p->model.at(2)),
                                 static_cast<float*>(logits), keys, p->err.as<unsigned>());
         launch(s, dim3(1), dim3(256), 0, k_keys_to_ids, keys, int(rows), ids);
+    });
+}
+
+int chroma_b200_gemm_bf16(const void* a, const void* b, const void* bias, const void* residual, void* c, int32_t m,
+                          int32_t n, int32_t k, int32_t epilogue, float swiglu_alpha, float swiglu_limit, int32_t groups,
+                          const int32_t* offsets, void* tile_scratch, unsigned int* error_word, void* stream, char* err,
+                          size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!a || !b || !c || !error_word) throw ValueError("null argument");
+        if (m < 1 || n < 1 || k < 1) throw ValueError("GEMM sizes must be positive");
+        if (epilogue < kEpiStore || epilogue > kEpiExpert) throw ValueError("unknown GEMM epilogue");
+        if (epilogue == kEpiResidual && !residual) throw ValueError("residual epilogue needs the residual matrix");
+        int dev = 0, sms = 148;
+        check(cudaGetDevice(&dev), "cudaGetDevice");
+        check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
+        GemmArgs g{};
+        g.M = m;
+        g.N = n;
+        g.K = k;
+        g.epi = epilogue;
+        g.bias = static_cast<const __nv_bfloat16*>(bias);
+        g.residual = static_cast<const __nv_bfloat16*>(residual);
+        g.ldr = n;
+        g.C = static_cast<__nv_bfloat16*>(c);
+        g.ldc = epilogue == kEpiSwiglu ? n / 2 : n;
+        g.alpha = swiglu_alpha;
+        g.limit = swiglu_limit;
+        g.groups = groups;
+        g.offsets = offsets;
+        gemm_bf16(static_cast<cudaStream_t>(stream), a, b, g, m, groups * n, tile_scratch, sms, error_word);
     });
 }
 

@@ -1,0 +1,98 @@
+// 5th-generation tensor core (tcgen05) primitives for sm_100a: TMEM allocation, UMMA descriptors, MMA issue and
+// commit, TMEM -> register loads, and TMA tiled loads through a CUtensorMap. Written against the PTX ISA for
+// sm_100a; every wait is bounded (tma.cuh).
+#pragma once
+
+#include <cuda.h>
+
+#include "tma.cuh"
+
+namespace cb200 {
+
+// ---- TMEM ---------------------------------------------------------------------------------------------------------
+// Allocate `cols` TMEM columns (a power of two >= 32); the base address is written to shared memory. Warp-wide.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)), "r"(cols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// ---- UMMA descriptors -----------------------------------------------------------------------------------------------
+// Shared-memory matrix descriptor for a K-major operand tile stored with the 128-byte swizzle: rows of 64 bf16
+// (128 B), 8-row swizzle atoms of 1024 B. Fields: start address >> 4 [0,14), leading byte offset >> 4 [16,30)
+// (unused for swizzled K-major), stride byte offset >> 4 [32,46) = 1024 B between 8-row groups, version 1 [46,48),
+// layout type 2 = SWIZZLE_128B [61,64).
+__device__ __forceinline__ uint64_t umma_desc_sw128(const void* smem_tile) {
+    const uint64_t addr = smem_addr(smem_tile);
+    uint64_t d = 0;
+    d |= (addr >> 4) & 0x3FFFull;
+    d |= uint64_t(1) << 16;             // LBO (16 B), ignored for this layout
+    d |= uint64_t(1024 >> 4) << 32;     // SBO
+    d |= uint64_t(1) << 46;             // descriptor version for sm_100
+    d |= uint64_t(2) << 61;             // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor for kind::f16 with bf16 A and B (both K-major), fp32 accumulation, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
+    return (1u << 4)                     // D format: f32
+           | (1u << 7)                   // A format: bf16
+           | (1u << 10)                  // B format: bf16
+           | (uint32_t(N >> 3) << 17)    // N >> 3
+           | (uint32_t(M >> 4) << 24);   // M >> 4
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by a single thread.
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(uint32_t(accumulate))
+        : "memory");
+}
+
+// Arrive on `bar` once every previously issued tcgen05.mma of this thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// 32 lanes x 32 columns of 32-bit TMEM data: thread i of the warp receives lane (base lane + i), 32 columns.
+__device__ __forceinline__ void tmem_load32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- TMA tiled loads --------------------------------------------------------------------------------------------------
+// 2-D tiled load of box {c0 (innermost), c1} from the tensor map into shared memory, completing on `bar`.
+// The innermost coordinate must be a multiple of 8 elements for bf16 (16 bytes); callers pass multiples of 64.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+}  // namespace cb200

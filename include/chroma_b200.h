@@ -106,6 +106,22 @@ int chroma_b200_routes(chroma_b200_program* program, int32_t* out, int64_t count
  * 0 is the legacy default stream), not synchronised. */
 int chroma_b200_vocab_argmax_static(const chroma_b200_program* program, const float* x, int32_t rows, void* logits,
                                     int64_t* ids, void* stream, char* err, size_t err_len);
+/* GEMM epilogues of chroma_b200_gemm_bf16. */
+#define CHROMA_B200_EPI_STORE 0    /* C = bf16(A.B^T + bias) (nn.Linear, chroma/_src/codegen/cpu/kernels.h:63-74) */
+#define CHROMA_B200_EPI_RESIDUAL 1 /* C = bf16(R + bf16(A.B^T + bias)): linear + residual (gpt_oss.py:209) */
+#define CHROMA_B200_EPI_SWIGLU 2   /* C[:, p] = SwiGLU of column pair (2p, 2p+1) (gpt_oss.py:212-219, 253-254) */
+#define CHROMA_B200_EPI_EXPERT 3   /* C = bf16(bf16(A.B^T) + bias[group]): expert einsum + bias (gpt_oss.py:259-260) */
+
+/* bf16 tensor-core GEMM on device buffers, C = A[m, k] . B^T with B stored [groups * n, k] row-major (nn.Linear
+ * layout), fp32 accumulation, fused epilogue. Dense when `offsets` is NULL (groups = 1). Grouped (MoE experts) when
+ * `offsets` [groups + 1] (device, int32) gives each group's row range in A: rows of group g use B rows
+ * [g*n, (g+1)*n) and bias row g; `tile_scratch` then needs groups + 1 int32 of device memory. C has n columns
+ * (n / 2 for the SwiGLU epilogue). Replaces the cuBLAS SGEMM of Runner::linear (runtime.h:175-181) and the generated
+ * per-expert einsum loops (gpu.py:390-424). Queued on `stream`; a stuck pipeline sets bit 2 of `error_word`. */
+int chroma_b200_gemm_bf16(const void* a, const void* b, const void* bias, const void* residual, void* c, int32_t m,
+                          int32_t n, int32_t k, int32_t epilogue, float swiglu_alpha, float swiglu_limit, int32_t groups,
+                          const int32_t* offsets, void* tile_scratch, unsigned int* error_word, void* stream, char* err,
+                          size_t err_len);
 /* Arena bytes of a program's executor (the manifest's workspace_bytes). */
 int64_t chroma_b200_workspace_bytes(const chroma_b200_program* program);
 

@@ -11,7 +11,7 @@ from tests.conftest import ROOT
 
 def declared() -> set[str]:
     text = (ROOT / "include" / "chroma_b200.h").read_text()
-    return set(re.findall(r"\b(chroma_b200_[a-z_]+)\s*\(", text))
+    return set(re.findall(r"\b(chroma_b200_[a-z0-9_]+)\s*\(", text))
 
 
 def test_header_declarations_are_exported_and_bound() -> None:
