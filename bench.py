@@ -49,6 +49,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--skip-c4", action="store_true", help="skip the GPT-OSS-20B-shaped prefill measurement")
     return ap.parse_args()
 
 
@@ -161,6 +162,71 @@ def reference_arm(args: argparse.Namespace) -> None:
 
 
 # ---------------------------------------------------------------------------------------------------------
+def prefill_flops(cfg, batch: int, n: int) -> float:  # type: ignore[no-untyped-def]
+    """Algorithmic FLOPs of one batched prefill chunk (GEMMs + causal attention + the last-row vocab projection)."""
+    d, H, KV, hd, E, k, I = (cfg.hidden_size, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim,
+                             cfg.num_experts, cfg.experts_per_token, cfg.intermediate_size)
+    N = batch * n
+    gemm = 2 * N * ((H + 2 * KV) * hd * d + d * H * hd + E * d + k * (2 * I * d + d * I))
+    attention = batch * H * (n * (n + 1) / 2) * hd * 2 * 2
+    return cfg.num_hidden_layers * (gemm + attention) + 2 * batch * cfg.vocab_size * d
+
+
+def bench_c4(args: argparse.Namespace, rng: np.random.Generator, max_over_ranks) -> dict:  # type: ignore[no-untyped-def]
+    """GPT-OSS-20B-shaped prefill of 4 x 2048 tokens (config C4) on this GPU: bf16 weights N(0, 0.02) generated in
+    device memory, the batched prefill program through BatchDecoder (tokens in from the host, greedy ids out)."""
+    import torch
+
+    import chroma_b200
+    from chroma_b200 import models
+    from chroma_b200._src.compiler import synthetic_gptoss
+    from chroma_b200._src.native import Native
+
+    cfg = models.gpt_oss_20b
+    batch, n = 4, 2048
+    plan_p, regions = synthetic_gptoss(cfg, steps=n, context=n)
+    plan_d, _ = synthetic_gptoss(cfg, steps=1, context=n)
+    wbuf = torch.empty(plan_p["desc"]["weight_bytes"], dtype=torch.uint8, device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(20)
+    for _, off, numel, is_norm in regions:
+        if is_norm:
+            wbuf[off : off + numel * 4].view(torch.float32).fill_(1.0)
+        else:
+            wbuf[off : off + numel * 2].view(torch.bfloat16).normal_(0.0, 0.02, generator=gen)
+    torch.cuda.synchronize()
+    pre = chroma_b200.Program.from_native(Native(plan_p, device_weights=wbuf.data_ptr()))
+    dec = chroma_b200.Program.from_native(Native(plan_d, device_weights=wbuf.data_ptr()))
+    bd = chroma_b200.BatchDecoder(pre, dec, batch)
+    tokens = rng.integers(0, cfg.vocab_size, (batch, n))
+    reps = max(2, min(5, args.steps // 40))
+    for _ in range(max(1, min(3, args.warmup))):
+        bd.reset()
+        bd.append(tokens, argmax=True)
+    times = []
+    for _ in range(reps):
+        bd.reset()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ids = bd.append(tokens, argmax=True)
+        times.append(time.perf_counter() - t0)
+    t = max_over_ranks(statistics.median(times))
+    flops = prefill_flops(cfg, batch, n)
+    peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops_sustained"] if (ROOT / "MEASURED_PEAKS.json").exists() else 1400.0
+    bd.close()
+    del pre, dec, wbuf
+    torch.cuda.empty_cache()
+    return {
+        "workload": "C4: GPT-OSS-20B-shaped prefill (24 layers, d=2880, 64/8 heads, 32 experts top-4, bf16 N(0,0.02)), "
+                    "4 x 2048 tokens, 1 GPU, all experts local",
+        "tokens_per_s": batch * n / t, "ms": t * 1e3, "reps": reps,
+        "e2e": {"api": "BatchDecoder.append(tokens[4, 2048], argmax=True)", "h2d_bytes": batch * n * 8 + batch * 16,
+                "d2h_bytes": batch * 8 + 4},
+        "algorithmic_tflop": flops / 1e12, "achieved_tflops": flops / t / 1e12,
+        "frac_of_bf16_sustained": flops / t / 1e12 / peak, "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained",
+        "argmax_head": [int(v) for v in ids[:2]],
+    }
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
@@ -364,6 +430,8 @@ def main() -> None:
     micro.close()
     del mout
 
+    c4 = bench_c4(args, rng, max_over_ranks) if not args.skip_c4 else None
+
     cpu = None
     if rank == 0 and world == 1:
         cpu = cpu_reference_decode(args.cpu_seconds)
@@ -411,6 +479,7 @@ def main() -> None:
         "micro": {"workload": "C3 fused RMSNorm*w -> z=y*g -> z*sigmoid(z)*u + x, bf16 [16384, 4096]",
                   "device_us": micro_t * 1e6, "algorithmic_bytes": micro_bytes,
                   "achieved_gbs": micro_bytes / micro_t / 1e9, "frac": micro_bytes / micro_t / 1e9 / pk["hbm_gbs"]},
+        "c4_prefill": c4,
         "fwd8": {"device_ms": fwd_dev_ms, "e2e_ms": fwd_e2e_ms, "vs_a100_e2e": A100_FWD8_MS / fwd_e2e_ms,
                  "h2d_bytes": 64, "d2h_bytes": 8 * V * 4, "api": "Program(tokens[8], out=logits)"},
     }

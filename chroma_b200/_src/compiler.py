@@ -39,7 +39,7 @@ from typing import Any
 import numpy as np
 
 from chroma_b200._src import native as nat
-from chroma_b200._src.memory import gptoss_arena
+from chroma_b200._src.memory import gptoss_arena, is_large
 from chroma_b200._src.program import Program, signature
 
 # ATen targets the reference accepts (chroma/_src/lowering.py:34-86); the same names, as an interface table.
@@ -307,8 +307,9 @@ def _gptoss_stats(desc: dict[str, Any]) -> dict[str, Any]:
     """Kernel count of one call and its activation arena (planned like the native executor does)."""
     L = desc["layers"]
     workspace, unreused = gptoss_arena(desc)
-    return {"kernels": 1 + 5 * L + 2, "workspace_bytes": workspace, "unreused_workspace_bytes": unreused,
-            "expert_contractions": 2 * L, "matrix_contractions": 4 * L + 1}
+    kernels = 1 + 13 * L + 2 if is_large(desc) else 1 + 5 * L + 2
+    return {"kernels": kernels, "workspace_bytes": workspace, "unreused_workspace_bytes": unreused,
+            "expert_contractions": 2 * L, "matrix_contractions": 4 * L + 1, "tensor_core_path": is_large(desc)}
 
 
 def _lower_micro(g: _Graph) -> Lowered:
@@ -363,6 +364,90 @@ def _lower_micro(g: _Graph) -> Lowered:
     outputs = [_spec(out.name, out.meta["val"])]
     return Lowered({"desc": desc}, [weight], inputs, outputs, {"kernels": 1, "workspace_bytes": 0,
                                                                "unreused_workspace_bytes": 0})
+
+
+def gptoss_layout(config: Any) -> list[tuple[str, tuple[int, ...], bool]]:
+    """(name, shape, is_fp32_norm) of every weight tensor in packing order (include/chroma_b200.h layout)."""
+    d, V, L = config.hidden_size, config.vocab_size, config.num_hidden_layers
+    H, KV, hd = config.num_attention_heads, config.num_key_value_heads, config.head_dim
+    E, I = config.num_experts, config.intermediate_size
+    out = [("embedding.weight", (V, d), False), ("norm.scale", (d,), True), ("unembedding.weight", (V, d), False)]
+    for layer in range(L):
+        b = f"block.{layer}."
+        out += [
+            (b + "attn.norm.scale", (d,), True), (b + "attn.sinks", (H,), False),
+            (b + "attn.qkv.weight", ((H + 2 * KV) * hd, d), False), (b + "attn.qkv.bias", ((H + 2 * KV) * hd,), False),
+            (b + "attn.out.weight", (d, H * hd), False), (b + "attn.out.bias", (d,), False),
+            (b + "mlp.norm.scale", (d,), True), (b + "mlp.gate.weight", (E, d), False), (b + "mlp.gate.bias", (E,), False),
+            (b + "mlp.mlp1_weight", (E, 2 * I, d), False), (b + "mlp.mlp1_bias", (E, 2 * I), False),
+            (b + "mlp.mlp2_weight", (E, d, I), False), (b + "mlp.mlp2_bias", (E, d), False),
+        ]
+    return out
+
+
+def _gptoss_specs(config: Any, dtype: str, steps: int, context: int | None, last: bool) -> tuple[list, list]:
+    V = config.vocab_size
+    if context is not None:
+        cache = [config.num_hidden_layers, context, config.num_key_value_heads, config.head_dim]
+        rows = [config.num_hidden_layers, steps, config.num_key_value_heads, config.head_dim]
+        inputs = [
+            {"name": "tokens", "shape": [steps], "dtype": "int64"},
+            {"name": "positions", "shape": [steps], "dtype": "float32"},
+            {"name": "keys", "shape": cache, "dtype": dtype},
+            {"name": "values", "shape": cache, "dtype": dtype},
+            {"name": "mask", "shape": [steps, context + steps], "dtype": dtype},
+            {"name": "window_mask", "shape": [steps, context + steps], "dtype": dtype},
+            {"name": "last", "shape": [1], "dtype": "int64"},
+        ]
+        outputs = [{"name": "logits", "shape": [1, V], "dtype": dtype}, {"name": "new_keys", "shape": rows, "dtype": dtype},
+                   {"name": "new_values", "shape": rows, "dtype": dtype}]
+    else:
+        inputs = [{"name": "tokens", "shape": [steps], "dtype": "int64"}]
+        if last:
+            inputs.append({"name": "position", "shape": [1], "dtype": "int64"})
+        outputs = [{"name": "logits", "shape": [1 if last else steps, V], "dtype": dtype}]
+    return inputs, outputs
+
+
+def _gptoss_desc(config: Any, dtype: str, steps: int, context: int | None, last: bool) -> dict[str, Any]:
+    import math as _math
+
+    kind = nat.GPTOSS_CACHED if context is not None else (nat.GPTOSS_LAST if last else nat.GPTOSS_FORWARD)
+    return {
+        "kind": kind, "storage": nat.BF16 if dtype == "bfloat16" else nat.FP32, "layers": config.num_hidden_layers,
+        "hidden": config.hidden_size, "heads": config.num_attention_heads, "kv_heads": config.num_key_value_heads,
+        "head_dim": config.head_dim, "experts": config.num_experts, "top_k": config.experts_per_token,
+        "intermediate": config.intermediate_size, "vocab": config.vocab_size, "tokens": steps,
+        "context": context or 0, "window": config.sliding_window if context is None else 0, "eps": 1e-5,
+        "sm_scale": 1.0 / _math.sqrt(config.head_dim), "swiglu_alpha": 1.702, "swiglu_limit": config.swiglu_limit,
+        "rope_concentration": 0.0, "rows": 0, "cols": 0,
+    }
+
+
+def synthetic_gptoss(config: Any, *, steps: int, context: int | None = None, dtype: str = "bfloat16",
+                     last: bool = False) -> tuple[dict[str, Any], list[tuple[str, int, int, bool]]]:
+    """The plan of a GPT-OSS program whose weights will be written straight into device memory (no host copy): returns
+    (plan, regions) with regions = (name, byte offset, element count, is_fp32_norm) in packing order. Use with
+    ``Native(plan, device_weights=ptr)`` over a buffer of ``plan["desc"]["weight_bytes"]`` bytes."""
+    from chroma_b200.models import rope_tables
+
+    es = 2 if dtype == "bfloat16" else 4
+    regions, total = [], 0
+    for name, shape, is_norm in gptoss_layout(config):
+        total = (total + ALIGN - 1) // ALIGN * ALIGN
+        numel = math.prod(shape)
+        regions.append((name, total, numel, is_norm))
+        total += numel * (4 if is_norm else es)
+    total = (total + ALIGN - 1) // ALIGN * ALIGN
+    conc, inv_freq = rope_tables(config)
+    desc = _gptoss_desc(config, dtype, steps, context, last)
+    desc["rope_concentration"] = float(conc)
+    desc["weight_bytes"] = total
+    inputs, outputs = _gptoss_specs(config, dtype, steps, context, last)
+    windowed = [1 if config.sliding_window > 0 and layer % 2 == 0 else 0 for layer in range(config.num_hidden_layers)]
+    plan = {"desc": desc, "inv_freq": inv_freq.float().numpy().tolist(), "layer_window": windowed,
+            "offsets": [r[1] for r in regions], "inputs": inputs, "outputs": outputs}
+    return plan, regions
 
 
 def lower_model(model: Any, *, steps: int, context: int | None = None, last: bool = False) -> Lowered:

@@ -84,8 +84,31 @@ def gptoss_buffers(desc: dict, batch: int = 1) -> list[tuple[str, int, int, int]
     return out
 
 
+def is_large(desc: dict) -> bool:
+    """The large-width bf16 path (tensor-core GEMMs, flash attention): hidden >= 1024, head_dim 64."""
+    return (desc["storage"] == 1 and desc["hidden"] >= 1024 and desc["hidden"] % 64 == 0 and desc["head_dim"] == 64
+            and desc["intermediate"] % 64 == 0 and desc["experts"] <= 256)
+
+
+def large_arena(desc: dict, batch: int = 1, selected_rows: bool = True) -> int:
+    """Arena bytes of the large-width executor (every buffer lives for the whole call)."""
+    d, H, hd, KV, k, I, E = (desc[x] for x in ("hidden", "heads", "head_dim", "kv_heads", "top_k", "intermediate", "experts"))
+    N = batch * desc["tokens"]
+    P = N * k
+    rows = batch if selected_rows else N
+    chunks = -(-(desc.get("context", 0) + desc["tokens"]) // 256)
+    heads = (H + 2 * KV) * hd
+    sizes = [N * d * 2, N * d * 2, N * heads * 2, N * H * hd * 2, N * H * hd * 2, N * E * 2, P * d * 2, P * I * 2,
+             P * d * 2, rows * d * 2, N * KV * hd * 2, N * KV * hd * 2, P * 4, rows * d * 4,
+             N * KV * (H // KV) * chunks * (hd + 2) * 4, P * 4, P * 4, E * 4, E * 4, (E + 1) * 4, (E + 1) * 4]
+    return sum(-(-s // 1024) * 1024 for s in sizes)
+
+
 def gptoss_arena(desc: dict, batch: int = 1) -> tuple[int, int]:
     """(planned arena bytes, bytes without reuse) for a GPT-OSS executor."""
+    if is_large(desc):
+        total = large_arena(desc, batch, desc["kind"] != 1)
+        return total, total
     allocations = {
         name: Allocation((size + 255) // 256 * 256, start, end) for name, size, start, end in gptoss_buffers(desc, batch)
     }

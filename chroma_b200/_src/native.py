@@ -66,6 +66,7 @@ class Desc(ctypes.Structure):
 _VP, _CP, _SZ, _I32, _I64P = ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int32, ctypes.POINTER(ctypes.c_int64)
 SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "chroma_b200_create": (ctypes.c_int, [ctypes.POINTER(Desc), _CP, ctypes.POINTER(_VP), _CP, _SZ]),
+    "chroma_b200_create_device": (ctypes.c_int, [ctypes.POINTER(Desc), _VP, ctypes.POINTER(_VP), _CP, _SZ]),
     "chroma_b200_run": (ctypes.c_int, [_VP, ctypes.POINTER(_VP), ctypes.POINTER(_VP), _CP, _SZ]),
     "chroma_b200_buffers": (ctypes.c_int, [_VP, ctypes.POINTER(_VP), ctypes.POINTER(_VP), _CP, _SZ]),
     "chroma_b200_run_device": (ctypes.c_int, [_VP, _VP, _CP, _SZ]),
@@ -153,12 +154,15 @@ def dtype_of(name: str) -> np.dtype:
 class Native:
     """Owns one ``chroma_b200_program``."""
 
-    def __init__(self, plan: dict[str, Any], weights_path: str) -> None:
+    def __init__(self, plan: dict[str, Any], weights_path: str | None = None, *, device_weights: int | None = None) -> None:
         self.plan = plan
         self._keep: list[Any] = []
         desc = self._desc(plan)
         handle = _VP()
-        call("chroma_b200_create", ctypes.byref(desc), str(weights_path).encode(), ctypes.byref(handle))
+        if device_weights is not None:
+            call("chroma_b200_create_device", ctypes.byref(desc), _VP(device_weights), ctypes.byref(handle))
+        else:
+            call("chroma_b200_create", ctypes.byref(desc), str(weights_path).encode(), ctypes.byref(handle))
         self.handle = handle
         self.inputs = plan["inputs"]
         self.outputs = plan["outputs"]

@@ -53,6 +53,29 @@ class Program:
         self._directory = Path(directory).resolve()
         self._device = native.device
 
+    @classmethod
+    def from_native(cls, native: Any, stats: dict[str, Any] | None = None) -> "Program":
+        """A Program over an already created native program (e.g. one whose weights live in device memory)."""
+        self = cls.__new__(cls)
+        self._lock = threading.Lock()
+
+        class _Model:
+            def __init__(self, n: Any) -> None:
+                self.native = n
+                self.device = n.device
+
+            def run(self, inputs: list[Any], outputs: list[Any]) -> None:
+                self.native.run(inputs, outputs)
+
+        self._model = _Model(native)
+        self._inputs = native.inputs
+        self._outputs = native.outputs
+        self._stats = stats or {}
+        self._plan = native.plan
+        self._directory = None
+        self._device = native.device
+        return self
+
     @staticmethod
     def _load(directory: str | Path) -> tuple[dict[str, Any], Any]:
         directory = Path(directory).resolve()

@@ -1,0 +1,260 @@
+// Flash attention for prefill chunks (head_dim 64, bf16), the reference's sink attention
+// (chroma/models/gpt_oss.py:133-151, chroma/models/cached.py:36-47) without materialising the score matrix:
+//
+//   out[i] = sum_j softmax_j([s_i0 .. s_ij .., sink]) v_j,  s_ij = q_i . k_j / sqrt(64) (masked to -inf)
+//
+// One CTA = 64 query rows of one head of one sequence, 4 warps x 16 rows. Keys come in 64-row tiles, first the ring
+// cache (visible when its slot's position is <= the query's and inside the window; tiles with no live slot are
+// skipped) then the chunk's own rows (causal, windowed). S = Q K^T and O += P V run on mma.sync m16n8k16 (bf16 in,
+// fp32 accumulate); the online softmax keeps a running max and sum per row; the sink logit joins the final
+// normalisation. K/V tiles are double-buffered with cp.async into XOR-swizzled shared memory read by ldmatrix.
+#pragma once
+
+#include "tma.cuh"
+
+namespace cb200 {
+
+constexpr int kFaRows = 64;  // query rows per CTA
+constexpr int kFaKeys = 64;  // keys per tile
+constexpr int kFaDim = 64;   // head_dim
+
+struct FlashArgs {
+    int n, ctx, B, H, KV, G;
+    size_t cache_seq_stride;  // elements between sequences in the cache (layer offset applied)
+    int window;               // 0 = none
+    float scale_log2;         // sm_scale * log2(e)
+    const int64_t* slots;     // [B][ctx] ring-slot positions (-1 empty), or nullptr when ctx == 0
+    const int64_t* pos0;      // [B] position of each sequence's first new row (nullptr: 0)
+};
+
+__device__ __forceinline__ uint32_t fa_swz(int row, int col) {  // element offset in a [64][64] bf16 tile
+    return uint32_t(row * 64 + (((col >> 3) ^ (row & 7)) << 3) + (col & 7));
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_addr(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_addr(p)));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// grid = (ceil(n / 64), H, B); block = 128.
+__global__ void __launch_bounds__(128) k_flash_prefill(const __nv_bfloat16* __restrict__ q, FlashArgs a,
+                                                       const __nv_bfloat16* __restrict__ cache_k,
+                                                       const __nv_bfloat16* __restrict__ cache_v,
+                                                       const __nv_bfloat16* __restrict__ new_k,
+                                                       const __nv_bfloat16* __restrict__ new_v,
+                                                       const __nv_bfloat16* __restrict__ sinks,
+                                                       __nv_bfloat16* __restrict__ out) {
+    __shared__ __align__(128) __nv_bfloat16 Qs[kFaRows * kFaDim];
+    __shared__ __align__(128) __nv_bfloat16 Ks[2][kFaKeys * kFaDim];
+    __shared__ __align__(128) __nv_bfloat16 Vs[2][kFaKeys * kFaDim];
+    __shared__ int64_t tslot[2][kFaKeys];
+    const int qb = gridDim.x - 1 - blockIdx.x;  // heavy (late) query blocks first
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int kvh = h / a.G;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int i0 = qb * kFaRows;
+    const int64_t p0 = a.pos0 ? a.pos0[b] : 0;
+    const size_t row_stride = size_t(a.KV) * kFaDim;  // elements between consecutive key rows
+    const __nv_bfloat16* ck = cache_k + b * a.cache_seq_stride + size_t(kvh) * kFaDim;
+    const __nv_bfloat16* cv = cache_v + b * a.cache_seq_stride + size_t(kvh) * kFaDim;
+    const __nv_bfloat16* nk = new_k + (size_t(b) * a.n * a.KV + kvh) * kFaDim;
+    const __nv_bfloat16* nv = new_v + (size_t(b) * a.n * a.KV + kvh) * kFaDim;
+
+    pdl_wait();
+    pdl_trigger();
+    // Q tile -> shared memory (rows past n are zero).
+    for (int e = threadIdx.x; e < kFaRows * 8; e += blockDim.x) {
+        const int r = e >> 3, c = (e & 7) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (i0 + r < a.n) v = *reinterpret_cast<const uint4*>(q + ((size_t(b) * a.n + i0 + r) * a.H + h) * kFaDim + c);
+        *reinterpret_cast<uint4*>(Qs + fa_swz(r, c)) = v;
+    }
+    // Key tiles: cache tiles [0, ctx) then the chunk's own rows [0, n) (only up to the block's last query row).
+    const int cache_tiles = (a.ctx + kFaKeys - 1) / kFaKeys;
+    const int own_tiles = (min(a.n, i0 + kFaRows) + kFaKeys - 1) / kFaKeys;
+    const int tiles = cache_tiles + own_tiles;
+    auto load_tile = [&](int tile, int buf) {
+        const bool cached = tile < cache_tiles;
+        const int j0 = (cached ? tile : tile - cache_tiles) * kFaKeys;
+        const int limit = cached ? a.ctx : a.n;
+        const __nv_bfloat16* kb = cached ? ck : nk;
+        const __nv_bfloat16* vb = cached ? cv : nv;
+        for (int e = threadIdx.x; e < kFaKeys * 8; e += blockDim.x) {
+            const int r = e >> 3, c = (e & 7) * 8;
+            if (j0 + r < limit) {
+                cp_async16(Ks[buf] + fa_swz(r, c), kb + size_t(j0 + r) * row_stride + c);
+                cp_async16(Vs[buf] + fa_swz(r, c), vb + size_t(j0 + r) * row_stride + c);
+            } else {
+                *reinterpret_cast<uint4*>(Ks[buf] + fa_swz(r, c)) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4*>(Vs[buf] + fa_swz(r, c)) = make_uint4(0, 0, 0, 0);
+            }
+        }
+        if (threadIdx.x < kFaKeys) {
+            const int j = j0 + threadIdx.x;
+            // Absolute position of each key (-1: not a key).
+            tslot[buf][threadIdx.x] = j < limit ? (cached ? a.slots[size_t(b) * a.ctx + j] : p0 + j) : -1;
+        }
+        cp_async_commit();
+    };
+    if (tiles > 0) load_tile(0, 0);
+
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    const int r_lo = warp * 16 + g;  // this thread's two query rows within the block: r_lo, r_lo + 8
+    const int64_t ti[2] = {p0 + i0 + r_lo, p0 + i0 + r_lo + 8};
+    uint32_t qf[4][4];
+
+    for (int tile = 0; tile < tiles; ++tile) {
+        const int buf = tile & 1;
+        if (tile + 1 < tiles) {
+            load_tile(tile + 1, buf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        if (tile == 0) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const int row = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+                const int col = kk * 16 + 8 * (lane >> 4);
+                ldsm_x4(qf[kk], Qs + fa_swz(row, col));
+            }
+        }
+        // Skip tiles with no visible key for any row of this block (empty ring slots, or beyond the window).
+        bool any = false;
+        if (threadIdx.x < kFaKeys) {
+            const int64_t tj = tslot[buf][threadIdx.x];
+            const int64_t first = p0 + i0, last = p0 + min(i0 + kFaRows, a.n) - 1;
+            any = tj >= 0 && tj <= last && (a.window <= 0 || tj > first - a.window);
+        }
+        if (__syncthreads_or(any)) {
+            float s[8][4];
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+                for (int nt = 0; nt < 8; nt += 2) {
+                    uint32_t kf[4];
+                    const int key = nt * 8 + (lane & 7) + 8 * (lane >> 4);
+                    const int col = kk * 16 + 8 * ((lane >> 3) & 1);
+                    ldsm_x4(kf, Ks[buf] + fa_swz(key, col));
+                    mma_bf16(s[nt], qf[kk], kf[0], kf[1]);
+                    mma_bf16(s[nt + 1], qf[kk], kf[2], kf[3]);
+                }
+            }
+            // Mask and online softmax (log2 domain).
+            float mx[2] = {m_run[0], m_run[1]};
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int rr = e >> 1;  // 0: row r_lo, 1: row r_lo + 8
+                    const int64_t tj = tslot[buf][nt * 8 + 2 * t4 + (e & 1)];
+                    const bool vis = tj >= 0 && tj <= ti[rr] && (a.window <= 0 || tj > ti[rr] - a.window) &&
+                                     (i0 + r_lo + 8 * rr) < a.n;
+                    s[nt][e] = vis ? s[nt][e] * a.scale_log2 : -INFINITY;
+                    mx[rr] = fmaxf(mx[rr], s[nt][e]);
+                }
+            }
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 1));
+                mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 2));
+            }
+            float corr[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) corr[rr] = mx[rr] == -INFINITY ? 1.f : exp2f(m_run[rr] - mx[rr]);
+            uint32_t pf[4][4];
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) {
+                float p[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int rr = e >> 1;
+                    p[e] = mx[rr] == -INFINITY ? 0.f : exp2f(s[nt][e] - mx[rr]);
+                    rs[rr] += p[e];
+                }
+                const int ks = nt >> 1, hi = nt & 1;
+                pf[ks][hi * 2 + 0] = pack_bf16(p[0], p[1]);
+                pf[ks][hi * 2 + 1] = pack_bf16(p[2], p[3]);
+            }
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                l_run[rr] = l_run[rr] * corr[rr] + rs[rr];
+                m_run[rr] = mx[rr];
+            }
+#pragma unroll
+            for (int nd = 0; nd < 8; ++nd) {
+                o[nd][0] *= corr[0];
+                o[nd][1] *= corr[0];
+                o[nd][2] *= corr[1];
+                o[nd][3] *= corr[1];
+            }
+            // A-fragment order of P for k-step ks: {rows g / keys 2t, rows g+8 / keys 2t, rows g / keys 2t+8, ...}.
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                const uint32_t af[4] = {pf[ks][0], pf[ks][1], pf[ks][2], pf[ks][3]};
+#pragma unroll
+                for (int nd = 0; nd < 8; nd += 2) {
+                    uint32_t vf[4];
+                    const int key = ks * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+                    const int col = nd * 8 + 8 * (lane >> 4);
+                    ldsm_x4_t(vf, Vs[buf] + fa_swz(key, col));
+                    mma_bf16(o[nd], af, vf[0], vf[1]);
+                    mma_bf16(o[nd + 1], af, vf[2], vf[3]);
+                }
+            }
+        }
+        __syncthreads();
+    }
+    // Row sums across the quad, the sink logit, normalise and store.
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        l_run[rr] += __shfl_xor_sync(0xffffffffu, l_run[rr], 1);
+        l_run[rr] += __shfl_xor_sync(0xffffffffu, l_run[rr], 2);
+    }
+    const float sink = __bfloat162float(sinks[h]) * 1.4426950408889634f;
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        const int i = i0 + r_lo + 8 * rr;
+        if (i >= a.n) continue;
+        const float mf = fmaxf(m_run[rr], sink);
+        const float c = m_run[rr] == -INFINITY ? 0.f : exp2f(m_run[rr] - mf);
+        const float inv = 1.0f / (l_run[rr] * c + exp2f(sink - mf));
+        __nv_bfloat16* orow = out + ((size_t(b) * a.n + i) * a.H + h) * kFaDim;
+#pragma unroll
+        for (int nd = 0; nd < 8; ++nd) {
+            const float v0 = o[nd][2 * rr] * c * inv, v1 = o[nd][2 * rr + 1] * c * inv;
+            *reinterpret_cast<__nv_bfloat162*>(orow + nd * 8 + 2 * t4) = __floats2bfloat162_rn(v0, v1);
+        }
+    }
+}
+
+}  // namespace cb200

@@ -256,12 +256,12 @@ struct AttnArgs {
     unsigned* counters;       // [B*n][KV] arrival counters, left at zero
 };
 
-template <typename T>
-__global__ void __launch_bounds__(kThreads) k_attention(const float* __restrict__ q, Dims dm, AttnArgs a,
+template <typename T, typename TQ = float>
+__global__ void __launch_bounds__(kThreads) k_attention(const TQ* __restrict__ q, Dims dm, AttnArgs a,
                                                         const T* __restrict__ cache_k, const T* __restrict__ cache_v,
                                                         const T* __restrict__ new_k, const T* __restrict__ new_v,
                                                         const T* __restrict__ bias, const T* __restrict__ sinks,
-                                                        float* __restrict__ out) {
+                                                        TQ* __restrict__ out) {
     extern __shared__ float sm[];
     const int i = blockIdx.x, kvh = blockIdx.y;
     const int b = blockIdx.z / a.chunks, chunk = blockIdx.z % a.chunks;
@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(kThreads) k_attention(const float* __restrict_
         }
     }
     for (int e = threadIdx.x; e < G * hd; e += blockDim.x)
-        qs[e] = q[tok * dm.H * hd + size_t(kvh) * G * hd + e];
+        qs[e] = Store<TQ>::load(q + tok * dm.H * hd + size_t(kvh) * G * hd + e);
     __syncthreads();
 
     int64_t t_i = 0;
@@ -379,10 +379,10 @@ __global__ void __launch_bounds__(kThreads) k_attention(const float* __restrict_
             acc[1] += __shfl_xor_sync(0xffffffffu, acc[1], o);
         }
         if (single) {
-            float* orow = out + tok * dm.H * hd + size_t(hq) * hd;
+            TQ* orow = out + tok * dm.H * hd + size_t(hq) * hd;
             if (g == 0) {
-                orow[dd] = Store<T>::round(acc[0]);
-                if (hd > 32) orow[dd + 32] = Store<T>::round(acc[1]);
+                Store<TQ>::store(orow + dd, Store<T>::round(acc[0]));
+                if (hd > 32) Store<TQ>::store(orow + dd + 32, Store<T>::round(acc[1]));
             }
         } else {
             float* part = a.partial + (((tok * dm.KV + kvh) * G + m) * a.chunks + chunk) * (hd + 2);
@@ -418,14 +418,14 @@ __global__ void __launch_bounds__(kThreads) k_attention(const float* __restrict_
             const float mc = part[c * (hd + 2)];
             if (mc != -INFINITY) L += part[c * (hd + 2) + 1] * expf(mc - M);
         }
-        float* orow = out + tok * dm.H * hd + size_t(hq) * hd;
+        TQ* orow = out + tok * dm.H * hd + size_t(hq) * hd;
         for (int e = lane; e < hd; e += 32) {
             float o = 0.f;
             for (int c = 0; c < a.chunks; ++c) {
                 const float mc = part[c * (hd + 2)];
                 if (mc != -INFINITY) o += part[c * (hd + 2) + 2 + e] * expf(mc - M);
             }
-            orow[e] = Store<T>::round(o / L);
+            Store<TQ>::store(orow + e, Store<T>::round(o / L));
         }
     }
     if (threadIdx.x == 0) a.counters[tok * dm.KV + kvh] = 0u;

@@ -11,8 +11,10 @@
 // synchronises and reports CHROMA_B200_INDEX (IndexError); the program stays usable (runtime.h:147-173).
 
 #include "../../include/chroma_b200.h"
+#include "flash.cuh"
 #include "gemm.cuh"
 #include "gptoss.cuh"
+#include "large.cuh"
 #include "micro.cuh"
 
 #include <cstdio>
@@ -90,7 +92,8 @@ struct PinnedBuf {
 // Weights: read once per (device, file identity) and shared by every program that names the same file.
 struct Weights {
     int device;
-    DevBuf buf;
+    DevBuf buf;           // owned copy of a weights file
+    const char* ptr = nullptr;  // device address of the weights (owned buffer or caller-owned memory)
 };
 
 static std::mutex g_weights_mu;
@@ -121,6 +124,7 @@ static std::shared_ptr<Weights> load_weights(const char* path, size_t bytes, int
             throw std::runtime_error("Cannot read weights");
         check(cudaMemcpy(w->buf.as<char>() + off, stage.p, n, cudaMemcpyHostToDevice), "Upload weights");
     }
+    w->ptr = w->buf.as<const char>();
     g_weights[key] = w;
     return w;
 }
@@ -309,7 +313,7 @@ struct Model {
     DevBuf inv_freq;
     int device = 0;
 
-    const char* at(int i) const { return weights->buf.as<char>() + offsets.at(size_t(i)); }
+    const char* at(int i) const { return weights->ptr + offsets.at(size_t(i)); }
     template <typename T> LayerW<T> layer(int l) const {
         const int b = 3 + 13 * l;
         LayerW<T> w;
@@ -424,6 +428,204 @@ struct GptIO {
     int* routes = nullptr;          // [L][B*n][k] optional record of the routing
 };
 
+// The large-width bf16 path (hidden >= 1024, head_dim 64): tensor-core GEMMs, flash attention for prefill chunks,
+// expert grouping for the MoE. Used for the GPT-OSS-20B/120B shapes.
+static bool is_large(const chroma_b200_desc& d) {
+    return d.storage == CHROMA_B200_BF16 && d.hidden >= 1024 && d.hidden % 64 == 0 && d.head_dim == 64 &&
+           d.intermediate % 64 == 0 && d.experts <= kGemmMaxGroups;
+}
+
+struct LargeExec {
+    const Model* m = nullptr;
+    int B = 1, n = 1, ctx = 0, mask_mode = kMaskBuffer, window = 0, sms = 148, chunks = 1, key_chunk = 256, rows = 1;
+    DevBuf arena, counters;
+    bf16 *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *glog = nullptr, *grouped = nullptr,
+         *act = nullptr, *y = nullptr, *tf16 = nullptr, *scratch_k = nullptr, *scratch_v = nullptr;
+    float *rw = nullptr, *tf32 = nullptr, *partial = nullptr;
+    int *ridx = nullptr, *perm = nullptr, *counts = nullptr, *cursor = nullptr, *offsets = nullptr, *tiles = nullptr;
+    size_t arena_bytes = 0;
+    int launches = 0;
+
+    void init(const Model& model, int batch, int rows_per_seq, int context, int mode, int win, bool selected_rows) {
+        m = &model;
+        B = batch;
+        n = rows_per_seq;
+        ctx = context;
+        mask_mode = mode;
+        window = win;
+        int dev = 0;
+        check(cudaGetDevice(&dev), "cudaGetDevice");
+        check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
+        const Dims& d = model.dm;
+        const size_t N = size_t(B) * n, P = N * d.k;
+        rows = selected_rows ? B : int(N);
+        key_chunk = 256;
+        chunks = (ctx + n + key_chunk - 1) / key_chunk;
+        const size_t heads = size_t(d.H + 2 * d.KV) * d.hd;
+        std::vector<size_t> sizes = {
+            N * d.d * 2, N * d.d * 2, N * heads * 2, N * d.H * d.hd * 2, N * d.H * d.hd * 2, N * d.E * 2,
+            P * d.d * 2, P * d.I * 2, P * d.d * 2, size_t(rows) * d.d * 2, N * d.KV * d.hd * 2, N * d.KV * d.hd * 2,
+            P * 4, size_t(rows) * d.d * 4, N * d.KV * d.G * size_t(chunks) * (d.hd + 2) * 4,
+            P * 4, P * 4, size_t(d.E) * 4, size_t(d.E) * 4, size_t(d.E + 1) * 4, size_t(d.E + 1) * 4,
+        };
+        std::vector<size_t> off(sizes.size());
+        arena_bytes = 0;
+        for (size_t i = 0; i < sizes.size(); ++i) {
+            off[i] = arena_bytes;
+            arena_bytes += (sizes[i] + 1023) / 1024 * 1024;
+        }
+        arena = DevBuf(arena_bytes);
+        check(cudaMemset(arena.p, 0, arena_bytes), "arena");
+        char* base = arena.as<char>();
+        auto at = [&](int i) { return static_cast<void*>(base + off[size_t(i)]); };
+        x = static_cast<bf16*>(at(0));
+        xn = static_cast<bf16*>(at(1));
+        qkv = static_cast<bf16*>(at(2));
+        q = static_cast<bf16*>(at(3));
+        attn = static_cast<bf16*>(at(4));
+        glog = static_cast<bf16*>(at(5));
+        grouped = static_cast<bf16*>(at(6));
+        act = static_cast<bf16*>(at(7));
+        y = static_cast<bf16*>(at(8));
+        tf16 = static_cast<bf16*>(at(9));
+        scratch_k = static_cast<bf16*>(at(10));
+        scratch_v = static_cast<bf16*>(at(11));
+        rw = static_cast<float*>(at(12));
+        tf32 = static_cast<float*>(at(13));
+        partial = static_cast<float*>(at(14));
+        ridx = static_cast<int*>(at(15));
+        perm = static_cast<int*>(at(16));
+        counts = static_cast<int*>(at(17));
+        cursor = static_cast<int*>(at(18));
+        offsets = static_cast<int*>(at(19));
+        tiles = static_cast<int*>(at(20));
+        counters = DevBuf(N * d.KV * sizeof(unsigned));
+        check(cudaMemset(counters.p, 0, counters.bytes), "attention counters");
+    }
+
+    void gemm(cudaStream_t s, const bf16* A, int M, const bf16* W, int N, int K, int epi, const bf16* bias, bf16* C,
+              int ldc, const bf16* residual, int groups, const int* offs, unsigned* err) {
+        GemmArgs g{};
+        g.M = M;
+        g.N = N;
+        g.K = K;
+        g.epi = epi;
+        g.bias = bias;
+        g.residual = residual;
+        g.ldr = N;
+        g.C = C;
+        g.ldc = ldc;
+        g.alpha = m->dm.alpha;
+        g.limit = m->dm.limit;
+        g.groups = groups;
+        g.offsets = offs;
+        gemm_bf16(s, A, W, g, M, groups * N, tiles, sms, err);
+        launches += offs ? 2 : 1;
+    }
+
+    void enqueue(cudaStream_t s, const GptIO& io, unsigned* err) {
+        const Dims& dm = m->dm;
+        const int N = B * n, P = N * dm.k, L = m->desc.layers;
+        const int heads = (dm.H + 2 * dm.KV) * dm.hd;
+        launches = 0;
+        launch(s, dim3(N), dim3(128), 0, k_embed_bf16, io.tokens, N, reinterpret_cast<const bf16*>(m->at(0)), dm.V, dm.d,
+               x, err);
+        ++launches;
+        const bool flash = n >= 16 && mask_mode != kMaskBuffer;
+        for (int l = 0; l < L; ++l) {
+            const LayerW<bf16> w = m->layer<bf16>(l);
+            bf16* nk;
+            bf16* nv;
+            const bf16* ck;
+            const bf16* cv;
+            if (m->desc.kind == CHROMA_B200_GPTOSS_CACHED) {
+                nk = static_cast<bf16*>(io.new_k) + size_t(l) * N * dm.KV * dm.hd;
+                nv = static_cast<bf16*>(io.new_v) + size_t(l) * N * dm.KV * dm.hd;
+                ck = static_cast<const bf16*>(io.cache_k) + size_t(l) * ctx * dm.KV * dm.hd;
+                cv = static_cast<const bf16*>(io.cache_v) + size_t(l) * ctx * dm.KV * dm.hd;
+            } else {
+                nk = scratch_k;
+                nv = scratch_v;
+                ck = nk;
+                cv = nv;
+            }
+            launch(s, dim3(N), dim3(256), 0, k_rms_bf16, x, dm.d, dm.eps, w.attn_norm, xn);
+            gemm(s, xn, N, w.qkv_w, heads, dm.d, kEpiStore, w.qkv_b, qkv, heads, nullptr, 1, nullptr, err);
+            launch(s, dim3(N), dim3(256), 0, k_rope_split, qkv, dm.H, dm.KV, dm.hd, io.positions,
+                   m->inv_freq.as<const float>(), dm.conc, q, nk, nv);
+            const bool windowed = m->layer_window[size_t(l)] != 0;
+            const int win = mask_mode == kMaskSlots ? (windowed ? window : ctx) : (windowed ? window : 0);
+            if (flash) {
+                FlashArgs fa;
+                fa.n = n;
+                fa.ctx = ctx;
+                fa.B = B;
+                fa.H = dm.H;
+                fa.KV = dm.KV;
+                fa.G = dm.G;
+                fa.cache_seq_stride = size_t(L) * ctx * dm.KV * dm.hd;
+                fa.window = win;
+                fa.scale_log2 = dm.sm_scale * 1.4426950408889634f;
+                fa.slots = mask_mode == kMaskSlots ? io.slots : nullptr;
+                fa.pos0 = mask_mode == kMaskSlots ? io.pos0 : nullptr;
+                if (mask_mode != kMaskSlots) fa.ctx = 0;
+                launch(s, dim3((n + kFaRows - 1) / kFaRows, dm.H, B), dim3(128), 0, k_flash_prefill, q, fa, ck, cv,
+                       static_cast<const bf16*>(nk), static_cast<const bf16*>(nv), w.sinks, attn);
+            } else {
+                AttnArgs a;
+                a.n = n;
+                a.ctx = ctx;
+                a.B = B;
+                a.chunks = chunks;
+                a.key_chunk = key_chunk;
+                a.cache_seq_stride = size_t(L) * ctx * dm.KV * dm.hd;
+                a.mask_mode = mask_mode;
+                a.window = win;
+                a.slots = io.slots;
+                a.pos0 = io.pos0;
+                a.partial = partial;
+                a.counters = counters.as<unsigned>();
+                const bf16* bias = static_cast<const bf16*>(windowed ? io.window_mask : io.mask);
+                const size_t smem = (size_t(2) * key_chunk * (dm.hd + 1) + size_t(dm.G) * key_chunk + size_t(dm.G) * dm.hd) * 4;
+                launch(s, dim3(n, dm.KV, B * chunks), dim3(kThreads), smem, k_attention<bf16, bf16>, q, dm, a, ck, cv,
+                       static_cast<const bf16*>(nk), static_cast<const bf16*>(nv), bias, w.sinks, attn);
+            }
+            gemm(s, attn, N, w.out_w, dm.d, dm.H * dm.hd, kEpiResidual, w.out_b, x, dm.d, x, 1, nullptr, err);
+            launch(s, dim3(N), dim3(256), 0, k_rms_bf16, x, dm.d, dm.eps, w.mlp_norm, xn);
+            gemm(s, xn, N, w.gate_w, dm.E, dm.d, kEpiStore, w.gate_b, glog, dm.E, nullptr, 1, nullptr, err);
+            launch(s, dim3((N + 7) / 8), dim3(256), 0, k_router, glog, N, dm.E, dm.k, ridx, rw,
+                   io.routes ? io.routes + size_t(l) * N * dm.k : nullptr);
+            launch(s, dim3((P + 255) / 256), dim3(256), 0, k_route_count, ridx, P, counts);
+            launch(s, dim3(1), dim3(32), 0, k_route_offsets, counts, dm.E, offsets, cursor);
+            launch(s, dim3((P + 7) / 8), dim3(256), 0, k_route_scatter, ridx, P, dm.k, dm.d, xn, cursor, perm, grouped);
+            gemm(s, grouped, P, w.w1, 2 * dm.I, dm.d, kEpiSwiglu, w.b1, act, dm.I, nullptr, dm.E, offsets, err);
+            gemm(s, act, P, w.w2, dm.d, dm.I, kEpiExpert, w.b2, y, dm.d, nullptr, dm.E, offsets, err);
+            launch(s, dim3(N), dim3(256), 0, k_moe_combine, y, perm, rw, dm.k, dm.d, x);
+            launches += 11;
+        }
+        launch(s, dim3(rows), dim3(256), 0, k_norm_rows, x, rows, io.rows, n, reinterpret_cast<const float*>(m->at(1)),
+               dm.d, dm.eps, tf32, tf16, io.keys, err);
+        ++launches;
+        enqueue_vocab(s, io, err);
+    }
+
+    void enqueue_vocab(cudaStream_t s, const GptIO& io, unsigned* err) {
+        const Dims& dm = m->dm;
+        const bf16* W = reinterpret_cast<const bf16*>(m->at(2));
+        if (rows < 16) {
+            launch_vocab<bf16>(s, dm, sms, tf32, rows, W, static_cast<bf16*>(io.logits), io.keys, err);
+            ++launches;
+        } else {
+            gemm(s, tf16, rows, W, dm.V, dm.d, kEpiStore, nullptr, static_cast<bf16*>(io.logits), dm.V, nullptr, 1, nullptr,
+                 err);
+            if (io.keys) {
+                launch(s, dim3(rows), dim3(1024), 0, k_argmax_rows, static_cast<const bf16*>(io.logits), dm.V, io.keys);
+                ++launches;
+            }
+        }
+    }
+};
+
 struct GptExec {
     const Model* m = nullptr;
     int B = 1, n = 1, ctx = 0, mask_mode = kMaskBuffer, window = 0, sms = 148, chunks = 1, key_chunk = 256;
@@ -439,13 +641,22 @@ struct GptExec {
 
     // Temporaries with their kernel-index lifetimes (0 embedding; per layer l: 1+5l QKV, 2+5l attention, 3+5l out,
     // 4+5l router + expert up, 5+5l expert down; 1+5L final norm; 2+5L vocab), in planning order.
-    void init(const Model& model, int batch, int rows_per_seq, int context, int mode, int win) {
+    bool large_path = false;
+    LargeExec large;
+
+    void init(const Model& model, int batch, int rows_per_seq, int context, int mode, int win, bool selected_rows) {
         m = &model;
         B = batch;
         n = rows_per_seq;
         ctx = context;
         mask_mode = mode;
         window = win;
+        if (is_large(model.desc)) {
+            large_path = true;
+            large.init(model, batch, rows_per_seq, context, mode, win, selected_rows);
+            arena_bytes = unreused_bytes = large.arena_bytes;
+            return;
+        }
         int dev = 0;
         check(cudaGetDevice(&dev), "cudaGetDevice");
         check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
@@ -567,11 +778,18 @@ struct GptExec {
     }
 
     void enqueue(cudaStream_t s) {
-        if (m->desc.storage == CHROMA_B200_BF16) enqueue_t<__nv_bfloat16>(s);
-        else enqueue_t<float>(s);
+        if (large_path) {
+            large.enqueue(s, io, err);
+            launches = large.launches;
+        } else if (m->desc.storage == CHROMA_B200_BF16) {
+            enqueue_t<__nv_bfloat16>(s);
+        } else {
+            enqueue_t<float>(s);
+        }
     }
     void enqueue_vocab(cudaStream_t s) {
-        if (m->desc.storage == CHROMA_B200_BF16) enqueue_vocab_t<__nv_bfloat16>(s);
+        if (large_path) large.enqueue_vocab(s, io, err);
+        else if (m->desc.storage == CHROMA_B200_BF16) enqueue_vocab_t<__nv_bfloat16>(s);
         else enqueue_vocab_t<float>(s);
     }
 };
@@ -724,10 +942,30 @@ void read_error_word(cudaStream_t s, DevBuf& err, unsigned* host) {
 
 extern "C" {
 
+static void create_program(const chroma_b200_desc* desc, const char* weights_path, const void* device_weights,
+                           chroma_b200_program** out);
+
 int chroma_b200_create(const chroma_b200_desc* desc, const char* weights_path, chroma_b200_program** out, char* err,
                        size_t err_len) {
     return guarded(err, err_len, [&] {
         if (!desc || !weights_path || !out) throw ValueError("null argument");
+        create_program(desc, weights_path, nullptr, out);
+    });
+}
+
+int chroma_b200_create_device(const chroma_b200_desc* desc, const void* device_weights, chroma_b200_program** out,
+                              char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!desc || !device_weights || !out) throw ValueError("null argument");
+        create_program(desc, nullptr, device_weights, out);
+    });
+}
+
+}  // extern "C"
+
+static void create_program(const chroma_b200_desc* desc, const char* weights_path, const void* device_weights,
+                           chroma_b200_program** out) {
+    {
         validate_desc(*desc);
         auto p = std::make_unique<chroma_b200_program>();
         check(cudaGetDevice(&p->device), "cudaGetDevice");
@@ -742,7 +980,13 @@ int chroma_b200_create(const chroma_b200_desc* desc, const char* weights_path, c
         m.offsets.assign(desc->offsets, desc->offsets + desc->num_offsets);
         for (int64_t off : m.offsets)
             if (off < 0 || off >= desc->weight_bytes || off % 16) throw ValueError("weight offset out of range or unaligned");
-        m.weights = load_weights(weights_path, size_t(desc->weight_bytes), p->device);
+        if (weights_path) {
+            m.weights = load_weights(weights_path, size_t(desc->weight_bytes), p->device);
+        } else {
+            m.weights = std::make_shared<Weights>();
+            m.weights->device = p->device;
+            m.weights->ptr = static_cast<const char*>(device_weights);
+        }
         m.desc.offsets = nullptr;
         m.desc.inv_freq = nullptr;
         m.desc.layer_window = nullptr;
@@ -796,7 +1040,7 @@ int chroma_b200_create(const chroma_b200_desc* desc, const char* weights_path, c
                     p->out.emplace_back(b);
                     p->out_bytes.push_back(b);
                 }
-                p->exec.init(m, 1, int(n), d.context, kMaskBuffer, d.window);
+                p->exec.init(m, 1, int(n), d.context, kMaskBuffer, d.window, true);
                 io.tokens = p->in[0].as<const int64_t>();
                 io.positions = p->in[1].as<const float>();
                 io.cache_k = p->in[2].p;
@@ -818,7 +1062,7 @@ int chroma_b200_create(const chroma_b200_desc* desc, const char* weights_path, c
                 const size_t ob = (last ? 1 : n) * V * es;
                 p->out.emplace_back(ob);
                 p->out_bytes.push_back(ob);
-                p->exec.init(m, 1, int(n), 0, kMaskCausal, d.window);
+                p->exec.init(m, 1, int(n), 0, kMaskCausal, d.window, last);
                 p->positions = DevBuf(n * 4);
                 std::vector<float> pos(n);
                 for (size_t i = 0; i < n; ++i) pos[i] = float(i);
@@ -835,8 +1079,10 @@ int chroma_b200_create(const chroma_b200_desc* desc, const char* weights_path, c
         }
         check(cudaDeviceSynchronize(), "create");
         *out = p.release();
-    });
+    }
 }
+
+extern "C" {
 
 int chroma_b200_run(chroma_b200_program* p, const void* const* inputs, void* const* outputs, char* err, size_t err_len) {
     return guarded(err, err_len, [&] {
@@ -1066,7 +1312,7 @@ int chroma_b200_decoder_create(chroma_b200_program* prefill, chroma_b200_program
             d->new_k[i] = DevBuf(staged);
             d->new_v[i] = DevBuf(staged);
             GptExec& e = d->ex[i];
-            e.init(*d->models[i], batch, n, d->ctx, kMaskSlots, d->window);
+            e.init(*d->models[i], batch, n, d->ctx, kMaskSlots, d->window, true);
             e.err = d->err.as<unsigned>();
             e.io.tokens = d->tokens.as<const int64_t>();
             e.io.positions = d->positions.as<const float>();

@@ -69,6 +69,12 @@ typedef struct chroma_b200_decoder chroma_b200_decoder;
 int chroma_b200_create(const chroma_b200_desc* desc, const char* weights_path, chroma_b200_program** out,
                        char* err, size_t err_len);
 
+/* Same as chroma_b200_create, with the weights already in device memory of the current device, laid out as the
+ * weights file would be (`desc->offsets`). They are not copied: the caller keeps them alive until destroy. For
+ * weights generated on the device (benchmarks) or shared with another runtime. No reference counterpart. */
+int chroma_b200_create_device(const chroma_b200_desc* desc, const void* device_weights, chroma_b200_program** out,
+                              char* err, size_t err_len);
+
 /* One call on host buffers: uploads inputs, runs, downloads outputs, synchronises. Input and output
  * order and byte sizes are those of the program's manifest. Replaces ModelProgram::run / Runner::run. */
 int chroma_b200_run(chroma_b200_program* program, const void* const* inputs, void* const* outputs, char* err,

@@ -86,6 +86,11 @@ def small_config(kind: str):  # type: ignore[no-untyped-def]
             experts_per_token=2, num_attention_heads=4, num_key_value_heads=2, head_dim=head_dim, sliding_window=3,
             initial_context_length=4096, rope_scaling_factor=32.0 if head_dim == 64 else 1.0,
         )
+    if kind == "c4_slice":  # one layer of the GPT-OSS-20B-shaped benchmark model (full widths and vocabulary)
+        return dataclasses.replace(
+            dev, num_hidden_layers=1, hidden_size=2880, intermediate_size=2880, num_attention_heads=64,
+            num_key_value_heads=8, head_dim=64, num_experts=32, experts_per_token=4,
+        )
     if kind == "yarn_small":  # tests/test_runtime.py:209-228
         return dataclasses.replace(
             dev, num_hidden_layers=2, hidden_size=16, head_dim=64, num_attention_heads=4, num_key_value_heads=2,
@@ -161,6 +166,12 @@ class RoutingProbe:
         return Probe().eval()
 
 
+def c4_tokens():  # type: ignore[no-untyped-def]
+    import torch
+
+    return torch.from_numpy(__import__("numpy").random.default_rng(11).integers(0, 201088, 16))
+
+
 def _programs() -> dict[str, Callable[[], object]]:
     """name -> thunk returning an ExportedProgram (built lazily; the reference must be importable)."""
 
@@ -201,6 +212,11 @@ def _programs() -> dict[str, Callable[[], object]]:
         programs[f"small_{dtype_name}_full4"] = lambda small=small: export(small(), import_torch().arange(4) * 3 % 17)
         programs[f"small_{dtype_name}_prefill5"] = lambda small=small: cached(small(), 5, 5)
         programs[f"small_{dtype_name}_decode"] = lambda small=small: cached(small(), 5, 1)
+    def c4_slice():  # type: ignore[no-untyped-def]
+        return random_transformer(small_config("c4_slice"), seed=11, std=0.02, dtype=import_torch().bfloat16)
+
+    programs["c4_slice_fwd16"] = lambda: export(c4_slice(), c4_tokens())
+    programs["c4_slice_route16"] = lambda: export(RoutingProbe.build(c4_slice()), c4_tokens())
     for head_dim in (8, 64):
         def decoder_small(head_dim=head_dim):  # type: ignore[no-untyped-def]
             return random_transformer(small_config(f"decoder_small_{head_dim}"), seed=5, std=0.03)

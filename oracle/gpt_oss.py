@@ -266,10 +266,11 @@ def _mlp(num: Numerics, cfg: Config, p: Params, layer: int, x: np.ndarray, trace
     w1, b1 = p[m + "mlp1_weight"], p[m + "mlp1_bias"]
     w2, b2 = p[m + "mlp2_weight"], p[m + "mlp2_bias"]
     n = x.shape[0]
+    # Per-(token, expert) GEMVs (kernels.h:76-99), evaluated one expert at a time.
     h = np.empty((n, cfg.top_k, 2 * cfg.intermediate), F32)
-    for b in range(n):
-        for e in range(cfg.top_k):
-            h[b, e] = matmul_t(t[b], w1[chosen[b, e]])
+    for e in np.unique(chosen):
+        bs, ss = np.nonzero(chosen == e)
+        h[bs, ss] = matmul_t(t[bs], w1[e])
     h = num.r(num.r(h) + b1[chosen])
     limit = F32(cfg.swiglu_limit)
     glu = np.minimum(h[..., ::2], limit)
@@ -277,9 +278,9 @@ def _mlp(num: Numerics, cfg: Config, p: Params, layer: int, x: np.ndarray, trace
     act = num.r(glu * num.r(sigmoid(num.r(glu * F32(1.702)))))
     act = num.r(act * num.r(lin + num.scalar(1.0)))
     y = np.empty((n, cfg.top_k, cfg.hidden), F32)
-    for b in range(n):
-        for e in range(cfg.top_k):
-            y[b, e] = matmul_t(act[b, e], w2[chosen[b, e]])
+    for e in np.unique(chosen):
+        bs, ss = np.nonzero(chosen == e)
+        y[bs, ss] = matmul_t(act[bs, ss], w2[e])
     y = num.r(num.r(y) + b2[chosen])
     combined = num.r(np.einsum("bec,be->bc", y.astype(np.float64), weights.astype(np.float64)).astype(F32))
     return num.r(x + combined)

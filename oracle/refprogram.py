@@ -64,6 +64,12 @@ class RefProgram:
     def close(self) -> None:
         self.model = None
 
+    def __enter__(self) -> "RefProgram":
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        self.close()
+
 
 def available(name: str) -> bool:
     return (ROOT / name / "model.json").exists()

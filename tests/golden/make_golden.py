@@ -60,7 +60,39 @@ def c1_token_sets() -> np.ndarray:
                      np.random.default_rng(0).integers(0, V, 8)])
 
 
+def c4_slice() -> None:
+    """One layer of the 20B-shaped model at full widths (d=2880, 64/8 heads, 32 experts, 201,088 vocab), bf16."""
+    from oracle import build_ref, refimport
+
+    refimport.install()
+
+    build_ref.build("c4_slice_fwd16")
+    model = build_ref.random_transformer(build_ref.small_config("c4_slice"), seed=11, std=0.02,
+                                         dtype=__import__("torch").bfloat16)
+    tokens = build_ref.c4_tokens().numpy()
+    from oracle.refprogram import RefProgram
+
+    # RefProgram follows the shared-weights record oracle/build_ref.py leaves after deduplicating weight files.
+    logits = np.asarray(RefProgram("c4_slice_fwd16")(tokens), np.float32)
+    build_ref.build("c4_slice_route16")
+    _, routes = RefProgram("c4_slice_route16")(tokens)
+    # The oracle's bf16 gate logits identify exact ties at the top-k boundary, where the reference's choice is
+    # unspecified (nth_element, chroma/_src/codegen/cpu/kernels.h:153-185; docs/runtime.md "Tied top-k values").
+    from oracle import gpt_oss as og
+
+    trace = og.Trace()
+    og.forward(og.Config.from_model_config(build_ref.small_config("c4_slice")), og.Params.from_module(model), tokens, trace)
+    np.savez_compressed(HERE / "c4_slice.npz", tokens=tokens, sample_cols=SAMPLE, weights_digest=np.array(digest(model)),
+                        routes=routes, oracle_gates=np.stack(trace.gates), **summary(logits))
+    print("c4 slice done", flush=True)
+
+
 def main() -> None:
+    import sys as _sys
+
+    if "--c4" in _sys.argv:
+        c4_slice()
+        return
     from oracle import build_ref, refimport
 
     refimport.install()
@@ -76,20 +108,22 @@ def main() -> None:
 
     # ---- C1: dev forward, 8 tokens, five token sets, with per-layer routing.
     sets = c1_token_sets()
-    with chroma.Program(R / "c1_fwd8") as fwd, chroma.Program(R / "c1_route8") as route:
-        outs, routes = [], []
-        for tokens in sets:
-            outs.append(summary(fwd(tokens)))
-            logits2, r = route(tokens)
-            routes.append(r)
-            assert np.array_equal(np.argmax(logits2, -1), outs[-1]["argmax"])
+    from oracle.refprogram import RefProgram
+
+    fwd, route = RefProgram("c1_fwd8"), RefProgram("c1_route8")
+    outs, routes = [], []
+    for tokens in sets:
+        outs.append(summary(fwd(tokens)))
+        logits2, r = route(tokens)
+        routes.append(r)
+        assert np.array_equal(np.argmax(logits2, -1), outs[-1]["argmax"])
     np.savez_compressed(HERE / "c1_fwd8.npz", tokens=sets, routes=np.stack(routes), sample_cols=SAMPLE,
                         weights_digest=np.array(dev_digest), **stack(outs, ""))
     print("c1 done", flush=True)
 
     # ---- C2: dev decode through the reference Decoder (prefill chunk 8, context 256).
     def decoder():  # type: ignore[no-untyped-def]
-        return chroma.Decoder(chroma.Program(R / "c2_prefill8"), chroma.Program(R / "c2_decode"))
+        return chroma.Decoder(RefProgram("c2_prefill8"), RefProgram("c2_decode"))
 
     rng = np.random.default_rng(1)
     prompt = rng.integers(0, V, 8)

@@ -102,3 +102,27 @@ def test_bf16_rounding_known_answers() -> None:
     x = np.array([1 + 2**-8, 1 + 3 * 2**-8, -1 - 2**-8, -1 - 3 * 2**-8, np.inf, -np.inf, 0.0, -0.0], np.float32)
     np.testing.assert_array_equal(og.bf16_round(x), np.array([1, 1 + 2**-6, -1, -1 - 2**-6, np.inf, -np.inf, 0, -0.0], np.float32))
     assert og.bf16_bits(np.array([np.nan], np.float32))[0] == 0x7FC0
+
+
+def test_c4_slice_forward_logits_and_routing() -> None:
+    """The oracle at GPT-OSS-20B widths (one layer, bf16) against the reference's compiled CPU program."""
+    import dataclasses
+
+    from chroma_b200 import models
+
+    g = golden("c4_slice")
+    config = dataclasses.replace(models.gpt_oss_20b, num_hidden_layers=1)
+    model = models.random_transformer(config, seed=11, std=0.02, dtype=torch.bfloat16)
+    from tests.golden.make_golden import digest
+
+    assert digest(model) == str(g["weights_digest"])
+    trace = og.Trace()
+    logits = og.forward(og.Config.from_model_config(config), og.Params.from_module(model), g["tokens"], trace)
+    ours = np.stack(trace.routes)
+    ok = helpers.routes_match(ours, g["routes"], g["oracle_gates"], 4)
+    assert ok.all(), np.argwhere(~ok)
+    # Tokens routed identically must also agree on logits; a tie broken differently changes that token's expert.
+    same = np.all(ours == g["routes"], axis=-1).all(axis=0)
+    assert same.sum() >= 14
+    np.testing.assert_array_equal(np.argmax(logits, -1)[same], g["argmax"][same])
+    np.testing.assert_allclose(logits[same][:, g["sample_cols"]], g["sample"][same], rtol=2e-2, atol=2e-2)
