@@ -50,6 +50,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-c4", action="store_true", help="skip the GPT-OSS-20B-shaped prefill measurement")
+    ap.add_argument("--c4-only", action="store_true", help="run only the GPT-OSS-20B-shaped prefill measurement")
     return ap.parse_args()
 
 
@@ -265,6 +266,13 @@ def main() -> None:
     # streams) and the CUDA events below bracket exactly the queued work.
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
+    if args.c4_only:
+        c4 = bench_c4(args, np.random.default_rng(0), max_over_ranks)
+        if rank == 0:
+            print(json.dumps({"c4_prefill": c4}), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
     flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     flush_read = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
 

@@ -6,10 +6,12 @@
 //
 //   * persistent CTAs, one per SM, walk a static sequence of 128 x BN output tiles (no atomics);
 //   * warp 0 (one thread) streams A and B tiles with TMA (128-byte swizzle) into a kGemmStages-deep ring;
-//   * warp 1 allocates BN TMEM columns and (one thread) issues tcgen05.mma (M=128, N=BN, K=16) per 64-wide K block,
-//     releasing each ring stage with tcgen05.commit and signalling the epilogue when a tile's accumulation is done;
-//   * warps 2-5 read the accumulator (each warp its 32-lane TMEM quadrant = 32 tile rows) with tcgen05.ld and apply
-//     the fused epilogue (bias, rounding, residual add, SwiGLU), then hand TMEM back.
+//   * warp 1 allocates two BN-column TMEM accumulators and (one thread) issues tcgen05.mma (M=128, N=BN, K=16) per
+//     64-wide K block, releasing each ring stage with tcgen05.commit and signalling the epilogue when a tile's
+//     accumulation is done; tile i+1 accumulates into the other buffer while tile i is drained;
+//   * warps 2-5 read the accumulator (each warp its 32-lane TMEM quadrant = 32 tile rows) with tcgen05.ld, apply the
+//     fused epilogue (bias, rounding, residual add, SwiGLU) and store 16-byte row segments coalesced through a small
+//     shared-memory stage, then hand the accumulator back.
 //
 // Grouped problems (MoE experts): rows [offsets[g], offsets[g+1]) of A multiply B rows [g*N, (g+1)*N); tiles never
 // straddle groups (rows past a group's end are masked in the epilogue). All waits are bounded (tma.cuh).
@@ -48,6 +50,140 @@ struct GemmArgs {
 
 __device__ __forceinline__ float round_bf16(float x) { return bf16_round(x); }
 
+// Epilogue staging: each epilogue warp owns 32 rows x 64 bytes of shared memory. 16-byte chunk c of row r sits at
+// chunk c ^ ((r >> 1) & 3), so a row-per-thread write and an 8-rows-per-instruction coalesced read are both free of
+// bank conflicts.
+constexpr int kGemmStageBytes = 32 * 64;
+__device__ __forceinline__ int stage_off(int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float swiglu_pair(float acc_g, float acc_l, float bg, float bl, float alpha, float limit) {
+    const float hg = round_bf16(round_bf16(acc_g) + bg);
+    const float hl = round_bf16(round_bf16(acc_l) + bl);
+    const float glu = fminf(hg, limit);
+    const float lin = fminf(fmaxf(hl, -limit), limit);
+    const float z = round_bf16(glu * alpha);
+    const float sg = round_bf16(1.0f / (1.0f + expf(-z)));
+    const float og = round_bf16(glu * sg);
+    const float l1 = round_bf16(lin + 1.0f);
+    return og * l1;
+}
+
+// Row-per-thread packed bf16 words -> stage -> coalesced 16-byte stores of rows [row_base, row_end).
+// CHUNKS = 16-byte chunks per row (4 = 32 columns, 2 = 16 SwiGLU outputs).
+template <int CHUNKS>
+__device__ __forceinline__ void stage_store(const GemmArgs& g, const uint32_t (&w)[16], int row_base, int row_end,
+                                            int out_col, uint8_t* stage) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c)
+        *reinterpret_cast<uint4*>(stage + stage_off(lane, c)) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int pass = 0; pass < CHUNKS; ++pass) {
+        const int r = pass * (32 / CHUNKS) + lane / CHUNKS, c = lane % CHUNKS;
+        if (row_base + r < row_end)
+            *reinterpret_cast<uint4*>(g.C + size_t(row_base + r) * g.ldc + out_col + 8 * c) =
+                *reinterpret_cast<const uint4*>(stage + stage_off(r, c));
+    }
+    __syncwarp();
+}
+
+// One 32-row x 32-column accumulator chunk of an epilogue warp: `v` holds row (row_base + lane), columns
+// [col0, col0 + 32). Fast path (vec): 16-byte residual loads and output stores, coalesced through `stage`.
+__device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& g, const float (&v)[32], const __nv_bfloat16* bias,
+                                                    int row_base, int row_end, int col0, bool vec, uint8_t* stage) {
+    const int lane = threadIdx.x & 31;
+    const int row = row_base + lane;
+    if (vec && col0 + 32 <= g.N) {
+        float b[32];
+        if (bias) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint4 w = __ldg(reinterpret_cast<const uint4*>(bias + col0) + c);
+                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 f = __bfloat1622float2(h[j]);
+                    b[8 * c + 2 * j] = f.x;
+                    b[8 * c + 2 * j + 1] = f.y;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) b[j] = 0.f;
+        }
+        uint32_t w[16];
+        if (g.epi == kEpiSwiglu) {
+#pragma unroll
+            for (int p = 0; p < 8; ++p)
+                w[p] = pack_bf16x2(swiglu_pair(v[4 * p], v[4 * p + 1], b[4 * p], b[4 * p + 1], g.alpha, g.limit),
+                                   swiglu_pair(v[4 * p + 2], v[4 * p + 3], b[4 * p + 2], b[4 * p + 3], g.alpha, g.limit));
+            stage_store<2>(g, w, row_base, row_end, col0 / 2, stage);
+        } else {
+            float y[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                y[j] = g.epi == kEpiExpert ? round_bf16(round_bf16(v[j]) + b[j]) : round_bf16(v[j] + b[j]);
+            if (g.epi == kEpiResidual) {
+                // Coalesced residual rows -> stage -> one row per thread.
+#pragma unroll
+                for (int pass = 0; pass < 4; ++pass) {
+                    const int r = pass * 8 + (lane >> 2), c = lane & 3;
+                    if (row_base + r < row_end)
+                        *reinterpret_cast<uint4*>(stage + stage_off(r, c)) = *reinterpret_cast<const uint4*>(
+                            g.residual + size_t(row_base + r) * g.ldr + col0 + 8 * c);
+                }
+                __syncwarp();
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint4 rw = *reinterpret_cast<const uint4*>(stage + stage_off(lane, c));
+                    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&rw);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = __bfloat1622float2(h[j]);
+                        y[8 * c + 2 * j] = round_bf16(f.x + y[8 * c + 2 * j]);
+                        y[8 * c + 2 * j + 1] = round_bf16(f.y + y[8 * c + 2 * j + 1]);
+                    }
+                }
+                __syncwarp();
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(y[2 * j], y[2 * j + 1]);
+            stage_store<4>(g, w, row_base, row_end, col0, stage);
+        }
+        return;
+    }
+    // General path: ragged last columns or unaligned operands, one element at a time.
+    if (row >= row_end) return;
+    const int ncols = min(32, g.N - col0);
+    if (g.epi == kEpiSwiglu) {
+        __nv_bfloat16* out = g.C + size_t(row) * g.ldc + col0 / 2;
+#pragma unroll
+        for (int p = 0; p < 16; ++p) {
+            if (2 * p + 1 >= ncols) break;
+            const float bg = bias ? __bfloat162float(bias[col0 + 2 * p]) : 0.f;
+            const float bl = bias ? __bfloat162float(bias[col0 + 2 * p + 1]) : 0.f;
+            out[p] = __float2bfloat16_rn(swiglu_pair(v[2 * p], v[2 * p + 1], bg, bl, g.alpha, g.limit));
+        }
+        return;
+    }
+    __nv_bfloat16* out = g.C + size_t(row) * g.ldc + col0;
+    const __nv_bfloat16* res = g.epi == kEpiResidual ? g.residual + size_t(row) * g.ldr + col0 : nullptr;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        if (j >= ncols) break;
+        const float b = bias ? __bfloat162float(bias[col0 + j]) : 0.f;
+        float y = g.epi == kEpiExpert ? round_bf16(round_bf16(v[j]) + b) : round_bf16(v[j] + b);
+        if (res) y = round_bf16(__bfloat162float(res[j]) + y);
+        out[j] = __float2bfloat16_rn(y);
+    }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_constant__ CUtensorMap map_a,
                                                                const __grid_constant__ CUtensorMap map_b, GemmArgs g,
@@ -55,9 +191,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
     constexpr int A_BYTES = kGemmBM * kGemmBK * 2;
     constexpr int B_BYTES = BN * kGemmBK * 2;
     constexpr int STAGE = A_BYTES + B_BYTES;
+    constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators: the epilogue drains one while the MMA fills the other
     extern __shared__ uint8_t gsm_raw[];
     uint8_t* gsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t full[kGemmStages], empty[kGemmStages], tmem_full, tmem_empty;
+    __shared__ uint64_t full[kGemmStages], empty[kGemmStages], tmem_full[2], tmem_empty[2];
     __shared__ uint32_t tmem_base;
     __shared__ volatile int abort_flag;  // set by any role whose bounded wait gave up
     __shared__ int s_tiles[kGemmMaxGroups + 1];
@@ -72,15 +209,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(&tmem_full, 1);
-        mbar_init(&tmem_empty, 4);
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tmem_full[a], 1);
+            mbar_init(&tmem_empty[a], 4);
+        }
         abort_flag = 0;
         fence_barrier_init();
         prefetch_tensormap(&map_a);
         prefetch_tensormap(&map_b);
     }
     if (warp == 1) {
-        tmem_alloc(&tmem_base, BN);
+        tmem_alloc(&tmem_base, TMEM_COLS);
         tmem_relinquish();
     }
     // Weights and activations of this GEMM are produced by earlier kernels: wait before reading the offsets.
@@ -133,8 +272,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
             constexpr uint32_t idesc = umma_idesc_bf16(kGemmBM, BN);
             int it = 0, tile_it = 0;
             for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++tile_it) {
-                if (!mbar_wait(&tmem_empty, unsigned((tile_it & 1) ^ 1), err)) { abort_flag = 1; break; }
+                const int acc = tile_it & 1;
+                if (!mbar_wait(&tmem_empty[acc], unsigned(((tile_it >> 1) & 1) ^ 1), err)) { abort_flag = 1; break; }
                 tc_fence_after();
+                const uint32_t d = tmem + uint32_t(acc * BN);
                 for (int kb = 0; kb < kblocks; ++kb, ++it) {
                     const int s = it % kGemmStages;
                     if (!mbar_wait(&full[s], unsigned((it / kGemmStages) & 1), err)) { abort_flag = 1; break; }
@@ -144,82 +285,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
                     const uint64_t db = umma_desc_sw128(sa + A_BYTES);
 #pragma unroll
                     for (int k = 0; k < kGemmBK / 16; ++k)  // advance 16 elements = 32 bytes = 2 in the >>4 field
-                        umma_bf16(tmem, da + 2 * k, db + 2 * k, idesc, kb > 0 || k > 0);
+                        umma_bf16(d, da + 2 * k, db + 2 * k, idesc, kb > 0 || k > 0);
                     umma_commit(&empty[s]);
                 }
                 if (abort_flag) break;
-                umma_commit(&tmem_full);
+                umma_commit(&tmem_full[acc]);
             }
         }
     } else {
         // Epilogue warps 2..5: TMEM quadrant q = warp % 4 holds tile rows [32q, 32q + 32).
         const int q = warp & 3;
+        uint8_t* stage = gsm + size_t(kGemmStages) * STAGE + size_t(q) * kGemmStageBytes;
+        const bool vec = ((reinterpret_cast<uintptr_t>(g.C) | reinterpret_cast<uintptr_t>(g.residual) |
+                           reinterpret_cast<uintptr_t>(g.bias)) & 15) == 0 &&
+                         g.ldc % 8 == 0 && g.N % 8 == 0 && (g.epi != kEpiResidual || g.ldr % 8 == 0);
         int tile_it = 0;
         for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++tile_it) {
-            if (!mbar_wait(&tmem_full, unsigned(tile_it & 1), err)) { abort_flag = 1; break; }
+            const int acc = tile_it & 1;
+            if (!mbar_wait(&tmem_full[acc], unsigned((tile_it >> 1) & 1), err)) { abort_flag = 1; break; }
             tc_fence_after();
             int grp, row0, row_end, n0;
             tile_of(t, grp, row0, row_end, n0);
-            const int row = row0 + q * 32 + lane;
-            const bool live = row < row_end;
             const __nv_bfloat16* bias = g.bias ? g.bias + size_t(grp) * g.N : nullptr;
+            const uint32_t taddr = tmem + uint32_t(acc * BN) + (uint32_t(q * 32) << 16);
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 float v[32];
-                tmem_load32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c * 32), v);
+                tmem_load32(taddr + uint32_t(c * 32), v);
                 const int col0 = n0 + c * 32;
-                if (!live || col0 >= g.N) continue;
-                const int ncols = min(32, g.N - col0);
-                if (g.epi == kEpiSwiglu) {
-                    // Interleaved pairs (glu = even column, linear = odd column) -> one output column per pair.
-                    __nv_bfloat16* out = g.C + size_t(row) * g.ldc + col0 / 2;
-#pragma unroll
-                    for (int p = 0; p < 16; ++p) {
-                        if (2 * p + 1 >= ncols) break;
-                        const float bg = bias ? __bfloat162float(bias[col0 + 2 * p]) : 0.f;
-                        const float bl = bias ? __bfloat162float(bias[col0 + 2 * p + 1]) : 0.f;
-                        const float hg = round_bf16(round_bf16(v[2 * p]) + bg);
-                        const float hl = round_bf16(round_bf16(v[2 * p + 1]) + bl);
-                        const float glu = fminf(hg, g.limit);
-                        const float lin = fminf(fmaxf(hl, -g.limit), g.limit);
-                        const float z = round_bf16(glu * g.alpha);
-                        const float sg = round_bf16(1.0f / (1.0f + expf(-z)));
-                        const float og = round_bf16(glu * sg);
-                        const float l1 = round_bf16(lin + 1.0f);
-                        out[p] = __float2bfloat16_rn(og * l1);
-                    }
-                } else {
-                    __nv_bfloat16* out = g.C + size_t(row) * g.ldc + col0;
-                    const __nv_bfloat16* res = g.epi == kEpiResidual ? g.residual + size_t(row) * g.ldr + col0 : nullptr;
-#pragma unroll
-                    for (int j = 0; j < 32; j += 2) {
-                        if (j >= ncols) break;
-                        float r[2];
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const float b = bias ? __bfloat162float(bias[col0 + j + h]) : 0.f;
-                            float y = g.epi == kEpiExpert ? round_bf16(round_bf16(v[j + h]) + b) : round_bf16(v[j + h] + b);
-                            if (res) y = round_bf16(__bfloat162float(res[j + h]) + y);
-                            r[h] = y;
-                        }
-                        if (j + 1 < ncols) {
-                            *reinterpret_cast<__nv_bfloat162*>(out + j) = __floats2bfloat162_rn(r[0], r[1]);
-                        } else {
-                            out[j] = __float2bfloat16_rn(r[0]);
-                        }
-                    }
-                }
+                if (col0 >= g.N) continue;
+                gemm_epilogue_chunk(g, v, bias, row0 + q * 32, row_end, col0, vec, stage);
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tmem_empty);
+            if (lane == 0) mbar_arrive(&tmem_empty[acc]);
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, BN);
+        tmem_dealloc(tmem, TMEM_COLS);
     }
 }
 

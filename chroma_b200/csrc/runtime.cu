@@ -199,7 +199,7 @@ static void gemm_bf16(cudaStream_t s, const void* A, const void* B, GemmArgs g, 
     const int bn = narrow ? 32 : 256;
     const int tiles = g.offsets ? sms : ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + bn - 1) / bn);
     const dim3 grid(unsigned(std::max(1, std::min(tiles, sms))));
-    const size_t smem = size_t(kGemmStages) * (kGemmBM + bn) * kGemmBK * 2 + 1024;
+    const size_t smem = size_t(kGemmStages) * (kGemmBM + bn) * kGemmBK * 2 + 4 * kGemmStageBytes + 1024;
     if (narrow) launch(s, grid, dim3(kGemmThreads), smem, k_gemm_bf16<32>, ma, mb, g, err);
     else launch(s, grid, dim3(kGemmThreads), smem, k_gemm_bf16<256>, ma, mb, g, err);
 }
