@@ -20,6 +20,7 @@ Multi-GPU (torchrun): one replica per GPU (the dev model does not shard); value 
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -51,6 +52,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-c4", action="store_true", help="skip the GPT-OSS-20B-shaped prefill measurement")
     ap.add_argument("--c4-only", action="store_true", help="run only the GPT-OSS-20B-shaped prefill measurement")
+    ap.add_argument("--c4-layers", type=int, default=0, help="layers of the C4 model (0: all 24; fewer for profiling)")
     return ap.parse_args()
 
 
@@ -184,6 +186,8 @@ def bench_c4(args: argparse.Namespace, rng: np.random.Generator, max_over_ranks)
     from chroma_b200._src.native import Native
 
     cfg = models.gpt_oss_20b
+    if args.c4_layers:
+        cfg = dataclasses.replace(cfg, num_hidden_layers=args.c4_layers)
     batch, n = 4, 2048
     plan_p, regions = synthetic_gptoss(cfg, steps=n, context=n)
     plan_d, _ = synthetic_gptoss(cfg, steps=1, context=n)

@@ -3,9 +3,9 @@
 //
 //   out[i] = sum_j softmax_j([s_i0 .. s_ij .., sink]) v_j,  s_ij = q_i . k_j / sqrt(64) (masked to -inf)
 //
-// One CTA = 64 query rows of one head of one sequence, 4 warps x 16 rows. Keys come in 64-row tiles, first the ring
+// One CTA = 128 query rows of one head of one sequence, 8 warps x 16 rows. Keys come in 64-row tiles, first the ring
 // cache (visible when its slot's position is <= the query's and inside the window; tiles with no live slot are
-// skipped) then the chunk's own rows (causal, windowed). S = Q K^T and O += P V run on mma.sync m16n8k16 (bf16 in,
+// never loaded) then the chunk's own rows (causal, windowed). S = Q K^T and O += P V run on mma.sync m16n8k16 (bf16 in,
 // fp32 accumulate); the online softmax keeps a running max and sum per row; the sink logit joins the final
 // normalisation. K/V tiles are double-buffered with cp.async into XOR-swizzled shared memory read by ldmatrix.
 #pragma once
@@ -14,7 +14,7 @@
 
 namespace cb200 {
 
-constexpr int kFaRows = 64;  // query rows per CTA
+constexpr int kFaRows = 128;  // query rows per CTA (8 warps x 16)
 constexpr int kFaKeys = 64;  // keys per tile
 constexpr int kFaDim = 64;   // head_dim
 
@@ -53,38 +53,65 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], 
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// 2^x on the special-function unit (ex2.approx, flush-to-zero): 2^-inf = 0.
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// grid = (ceil(n / 64), H, B); block = 128.
-__global__ void __launch_bounds__(128) k_flash_prefill(const __nv_bfloat16* __restrict__ q, FlashArgs a,
-                                                       const __nv_bfloat16* __restrict__ cache_k,
-                                                       const __nv_bfloat16* __restrict__ cache_v,
-                                                       const __nv_bfloat16* __restrict__ new_k,
-                                                       const __nv_bfloat16* __restrict__ new_v,
-                                                       const __nv_bfloat16* __restrict__ sinks,
-                                                       __nv_bfloat16* __restrict__ out) {
-    __shared__ __align__(128) __nv_bfloat16 Qs[kFaRows * kFaDim];
-    __shared__ __align__(128) __nv_bfloat16 Ks[2][kFaKeys * kFaDim];
-    __shared__ __align__(128) __nv_bfloat16 Vs[2][kFaKeys * kFaDim];
-    __shared__ int64_t tslot[2][kFaKeys];
+// Shared memory of one CTA (dynamic): Q tile, double-buffered K and V tiles, key positions, the list of live cache
+// tiles and its bitmask.
+constexpr int kFaThreads = 32 * (kFaRows / 16);
+constexpr int kFaMaxCacheTiles = 1024;  // ring contexts up to 65,536 positions
+constexpr size_t kFaSmemBytes = size_t(kFaRows) * kFaDim * 2 + 4 * size_t(kFaKeys) * kFaDim * 2 +
+                                2 * kFaKeys * sizeof(int64_t) + kFaMaxCacheTiles * sizeof(uint16_t) +
+                                (kFaMaxCacheTiles / 32) * sizeof(uint32_t);
+
+// grid = (ceil(n / kFaRows), H, B); block = kFaThreads; dynamic shared memory kFaSmemBytes.
+//
+// Only tiles holding a key some row of the block can see are loaded: cache tiles are screened against the ring-slot
+// positions first (a fresh sequence has none), and the chunk's own tiles start at the window's edge. Tiles whose
+// every key is visible to every row (below the diagonal, inside the window) skip the per-element mask.
+__global__ void __launch_bounds__(kFaThreads, 2) k_flash_prefill(const __nv_bfloat16* __restrict__ q, FlashArgs a,
+                                                                 const __nv_bfloat16* __restrict__ cache_k,
+                                                                 const __nv_bfloat16* __restrict__ cache_v,
+                                                                 const __nv_bfloat16* __restrict__ new_k,
+                                                                 const __nv_bfloat16* __restrict__ new_v,
+                                                                 const __nv_bfloat16* __restrict__ sinks,
+                                                                 __nv_bfloat16* __restrict__ out) {
+    extern __shared__ __align__(128) uint8_t fa_smem[];
+    __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(fa_smem);
+    __nv_bfloat16* Ks0 = Qs + kFaRows * kFaDim;
+    __nv_bfloat16* Vs0 = Ks0 + 2 * kFaKeys * kFaDim;
+    int64_t* tslot0 = reinterpret_cast<int64_t*>(Vs0 + 2 * kFaKeys * kFaDim);
+    uint16_t* live_list = reinterpret_cast<uint16_t*>(tslot0 + 2 * kFaKeys);
+    uint32_t* live_bits = reinterpret_cast<uint32_t*>(live_list + kFaMaxCacheTiles);
+    __shared__ int s_nlive;
+
     const int qb = gridDim.x - 1 - blockIdx.x;  // heavy (late) query blocks first
     const int h = blockIdx.y, b = blockIdx.z;
     const int kvh = h / a.G;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t4 = lane & 3;
     const int i0 = qb * kFaRows;
-    const int64_t p0 = a.pos0 ? a.pos0[b] : 0;
+    const int i_last = min(i0 + kFaRows, a.n) - 1;  // last real query row of the block
     const size_t row_stride = size_t(a.KV) * kFaDim;  // elements between consecutive key rows
     const __nv_bfloat16* ck = cache_k + b * a.cache_seq_stride + size_t(kvh) * kFaDim;
     const __nv_bfloat16* cv = cache_v + b * a.cache_seq_stride + size_t(kvh) * kFaDim;
     const __nv_bfloat16* nk = new_k + (size_t(b) * a.n * a.KV + kvh) * kFaDim;
     const __nv_bfloat16* nv = new_v + (size_t(b) * a.n * a.KV + kvh) * kFaDim;
 
+    const int cache_tiles = (a.ctx + kFaKeys - 1) / kFaKeys;
+    for (int w = threadIdx.x; w < (cache_tiles + 31) / 32; w += blockDim.x) live_bits[w] = 0;
     pdl_wait();
     pdl_trigger();
+    const int64_t p0 = a.pos0 ? a.pos0[b] : 0;
+    const int64_t first = p0 + i0, last = p0 + i_last;
     // Q tile -> shared memory (rows past n are zero).
     for (int e = threadIdx.x; e < kFaRows * 8; e += blockDim.x) {
         const int r = e >> 3, c = (e & 7) * 8;
@@ -92,30 +119,61 @@ __global__ void __launch_bounds__(128) k_flash_prefill(const __nv_bfloat16* __re
         if (i0 + r < a.n) v = *reinterpret_cast<const uint4*>(q + ((size_t(b) * a.n + i0 + r) * a.H + h) * kFaDim + c);
         *reinterpret_cast<uint4*>(Qs + fa_swz(r, c)) = v;
     }
-    // Key tiles: cache tiles [0, ctx) then the chunk's own rows [0, n) (only up to the block's last query row).
-    const int cache_tiles = (a.ctx + kFaKeys - 1) / kFaKeys;
-    const int own_tiles = (min(a.n, i0 + kFaRows) + kFaKeys - 1) / kFaKeys;
-    const int tiles = cache_tiles + own_tiles;
+    // Screen the ring: a cache tile is live when one of its slots holds a position some row of the block can see.
+    __syncthreads();
+    for (int j = threadIdx.x; j < a.ctx; j += blockDim.x) {
+        const int64_t tj = a.slots[size_t(b) * a.ctx + j];
+        if (tj >= 0 && tj <= last && (a.window <= 0 || tj > first - a.window))
+            atomicOr(&live_bits[(j / kFaKeys) >> 5], 1u << ((j / kFaKeys) & 31));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int nl = 0;
+        for (int w = 0; w < (cache_tiles + 31) / 32; ++w) {
+            uint32_t bits = live_bits[w];
+            while (bits) {
+                const int bit = __ffs(bits) - 1;
+                bits &= bits - 1;
+                live_list[nl++] = uint16_t(w * 32 + bit);
+            }
+        }
+        s_nlive = nl;
+    }
+    __syncthreads();
+    const int nlive = s_nlive;
+    // The chunk's own tiles: from the window's edge (row i sees own key j iff j <= i and j > i - window) to the
+    // tile holding the block's last row.
+    const int own_lo = a.window > 0 ? max(0, i0 - a.window + 1) / kFaKeys : 0;
+    const int own_hi = (i_last + kFaKeys) / kFaKeys;
+    const int tiles = nlive + max(0, own_hi - own_lo);
+
+    // Tile index -> (cached?, first key row).
+    auto tile_key0 = [&](int tile, bool& cached) {
+        cached = tile < nlive;
+        return (cached ? int(live_list[tile]) : own_lo + tile - nlive) * kFaKeys;
+    };
     auto load_tile = [&](int tile, int buf) {
-        const bool cached = tile < cache_tiles;
-        const int j0 = (cached ? tile : tile - cache_tiles) * kFaKeys;
+        bool cached;
+        const int j0 = tile_key0(tile, cached);
         const int limit = cached ? a.ctx : a.n;
         const __nv_bfloat16* kb = cached ? ck : nk;
         const __nv_bfloat16* vb = cached ? cv : nv;
+        __nv_bfloat16* Kd = Ks0 + buf * kFaKeys * kFaDim;
+        __nv_bfloat16* Vd = Vs0 + buf * kFaKeys * kFaDim;
         for (int e = threadIdx.x; e < kFaKeys * 8; e += blockDim.x) {
             const int r = e >> 3, c = (e & 7) * 8;
             if (j0 + r < limit) {
-                cp_async16(Ks[buf] + fa_swz(r, c), kb + size_t(j0 + r) * row_stride + c);
-                cp_async16(Vs[buf] + fa_swz(r, c), vb + size_t(j0 + r) * row_stride + c);
+                cp_async16(Kd + fa_swz(r, c), kb + size_t(j0 + r) * row_stride + c);
+                cp_async16(Vd + fa_swz(r, c), vb + size_t(j0 + r) * row_stride + c);
             } else {
-                *reinterpret_cast<uint4*>(Ks[buf] + fa_swz(r, c)) = make_uint4(0, 0, 0, 0);
-                *reinterpret_cast<uint4*>(Vs[buf] + fa_swz(r, c)) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4*>(Kd + fa_swz(r, c)) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4*>(Vd + fa_swz(r, c)) = make_uint4(0, 0, 0, 0);
             }
         }
         if (threadIdx.x < kFaKeys) {
             const int j = j0 + threadIdx.x;
             // Absolute position of each key (-1: not a key).
-            tslot[buf][threadIdx.x] = j < limit ? (cached ? a.slots[size_t(b) * a.ctx + j] : p0 + j) : -1;
+            tslot0[buf * kFaKeys + threadIdx.x] = j < limit ? (cached ? a.slots[size_t(b) * a.ctx + j] : p0 + j) : -1;
         }
         cp_async_commit();
     };
@@ -126,7 +184,8 @@ __global__ void __launch_bounds__(128) k_flash_prefill(const __nv_bfloat16* __re
     for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
     const int r_lo = warp * 16 + g;  // this thread's two query rows within the block: r_lo, r_lo + 8
-    const int64_t ti[2] = {p0 + i0 + r_lo, p0 + i0 + r_lo + 8};
+    const int64_t t_lo = p0 + i0 + r_lo;  // position of row r_lo (row r_lo + 8: t_lo + 8)
+    const bool row_ok[2] = {i0 + r_lo < a.n, i0 + r_lo + 8 < a.n};
     uint32_t qf[4][4];
 
     for (int tile = 0; tile < tiles; ++tile) {
@@ -146,70 +205,80 @@ __global__ void __launch_bounds__(128) k_flash_prefill(const __nv_bfloat16* __re
                 ldsm_x4(qf[kk], Qs + fa_swz(row, col));
             }
         }
-        // Skip tiles with no visible key for any row of this block (empty ring slots, or beyond the window).
-        bool any = false;
-        if (threadIdx.x < kFaKeys) {
-            const int64_t tj = tslot[buf][threadIdx.x];
-            const int64_t first = p0 + i0, last = p0 + min(i0 + kFaRows, a.n) - 1;
-            any = tj >= 0 && tj <= last && (a.window <= 0 || tj > first - a.window);
-        }
-        if (__syncthreads_or(any)) {
-            float s[8][4];
+        const __nv_bfloat16* Kb = Ks0 + buf * kFaKeys * kFaDim;
+        const __nv_bfloat16* Vb = Vs0 + buf * kFaKeys * kFaDim;
+        const int64_t* ts = tslot0 + buf * kFaKeys;
+        bool cached;
+        const int j0 = tile_key0(tile, cached);
+        // Every key of an own tile is visible to every row when the tile ends at or before the first row and starts
+        // inside the last row's window.
+        const bool masked = cached || j0 + kFaKeys - 1 > i0 || (a.window > 0 && j0 <= i_last - a.window);
+
+        float s[8][4];
 #pragma unroll
-            for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+        for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
+        for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-                for (int nt = 0; nt < 8; nt += 2) {
-                    uint32_t kf[4];
-                    const int key = nt * 8 + (lane & 7) + 8 * (lane >> 4);
-                    const int col = kk * 16 + 8 * ((lane >> 3) & 1);
-                    ldsm_x4(kf, Ks[buf] + fa_swz(key, col));
-                    mma_bf16(s[nt], qf[kk], kf[0], kf[1]);
-                    mma_bf16(s[nt + 1], qf[kk], kf[2], kf[3]);
-                }
+            for (int nt = 0; nt < 8; nt += 2) {
+                uint32_t kf[4];
+                const int key = nt * 8 + (lane & 7) + 8 * (lane >> 4);
+                const int col = kk * 16 + 8 * ((lane >> 3) & 1);
+                ldsm_x4(kf, Kb + fa_swz(key, col));
+                mma_bf16(s[nt], qf[kk], kf[0], kf[1]);
+                mma_bf16(s[nt + 1], qf[kk], kf[2], kf[3]);
             }
-            // Mask and online softmax (log2 domain).
-            float mx[2] = {m_run[0], m_run[1]};
+        }
+        // Mask, then the online softmax in the log2 domain: the running max m_run is kept scaled, so each
+        // probability is one FMA and one ex2: p = 2^(s * scale - m).
+        float mx[2] = {-INFINITY, -INFINITY};
+        if (masked) {
 #pragma unroll
             for (int nt = 0; nt < 8; ++nt) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int rr = e >> 1;  // 0: row r_lo, 1: row r_lo + 8
-                    const int64_t tj = tslot[buf][nt * 8 + 2 * t4 + (e & 1)];
-                    const bool vis = tj >= 0 && tj <= ti[rr] && (a.window <= 0 || tj > ti[rr] - a.window) &&
-                                     (i0 + r_lo + 8 * rr) < a.n;
-                    s[nt][e] = vis ? s[nt][e] * a.scale_log2 : -INFINITY;
+                    const int64_t tj = ts[nt * 8 + 2 * t4 + (e & 1)];
+                    const int64_t t_i = t_lo + 8 * rr;
+                    const bool vis = tj >= 0 && tj <= t_i && (a.window <= 0 || tj > t_i - a.window) && row_ok[rr];
+                    s[nt][e] = vis ? s[nt][e] : -INFINITY;
                     mx[rr] = fmaxf(mx[rr], s[nt][e]);
                 }
             }
-#pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-                mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 1));
-                mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 2));
-            }
-            float corr[2], rs[2] = {0.f, 0.f};
-#pragma unroll
-            for (int rr = 0; rr < 2; ++rr) corr[rr] = mx[rr] == -INFINITY ? 1.f : exp2f(m_run[rr] - mx[rr]);
-            uint32_t pf[4][4];
+        } else {
 #pragma unroll
             for (int nt = 0; nt < 8; ++nt) {
-                float p[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int rr = e >> 1;
-                    p[e] = mx[rr] == -INFINITY ? 0.f : exp2f(s[nt][e] - mx[rr]);
-                    rs[rr] += p[e];
-                }
-                const int ks = nt >> 1, hi = nt & 1;
-                pf[ks][hi * 2 + 0] = pack_bf16(p[0], p[1]);
-                pf[ks][hi * 2 + 1] = pack_bf16(p[2], p[3]);
+                mx[0] = fmaxf(mx[0], fmaxf(s[nt][0], s[nt][1]));
+                mx[1] = fmaxf(mx[1], fmaxf(s[nt][2], s[nt][3]));
             }
+        }
+        float corr[2], neg[2], rs[2] = {0.f, 0.f};
 #pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-                l_run[rr] = l_run[rr] * corr[rr] + rs[rr];
-                m_run[rr] = mx[rr];
+        for (int rr = 0; rr < 2; ++rr) {
+            mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 1));
+            mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 2));
+            const float m_new = fmaxf(m_run[rr], mx[rr] * a.scale_log2);
+            const bool none = m_new == -INFINITY;  // no visible key for this row yet
+            corr[rr] = none ? 1.f : fast_exp2(m_run[rr] - m_new);
+            neg[rr] = none ? 0.f : -m_new;
+            m_run[rr] = m_new;
+        }
+        uint32_t pf[4][4];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            float p[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                p[e] = fast_exp2(fmaf(s[nt][e], a.scale_log2, neg[e >> 1]));
+                rs[e >> 1] += p[e];
             }
+            const int ks = nt >> 1, hi = nt & 1;
+            pf[ks][hi * 2 + 0] = pack_bf16(p[0], p[1]);
+            pf[ks][hi * 2 + 1] = pack_bf16(p[2], p[3]);
+        }
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) l_run[rr] = l_run[rr] * corr[rr] + rs[rr];
+        if (__any_sync(0xffffffffu, corr[0] != 1.f || corr[1] != 1.f)) {
 #pragma unroll
             for (int nd = 0; nd < 8; ++nd) {
                 o[nd][0] *= corr[0];
@@ -217,19 +286,19 @@ __global__ void __launch_bounds__(128) k_flash_prefill(const __nv_bfloat16* __re
                 o[nd][2] *= corr[1];
                 o[nd][3] *= corr[1];
             }
-            // A-fragment order of P for k-step ks: {rows g / keys 2t, rows g+8 / keys 2t, rows g / keys 2t+8, ...}.
+        }
+        // A-fragment order of P for k-step ks: {rows g / keys 2t, rows g+8 / keys 2t, rows g / keys 2t+8, ...}.
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-                const uint32_t af[4] = {pf[ks][0], pf[ks][1], pf[ks][2], pf[ks][3]};
+        for (int ks = 0; ks < 4; ++ks) {
+            const uint32_t af[4] = {pf[ks][0], pf[ks][1], pf[ks][2], pf[ks][3]};
 #pragma unroll
-                for (int nd = 0; nd < 8; nd += 2) {
-                    uint32_t vf[4];
-                    const int key = ks * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
-                    const int col = nd * 8 + 8 * (lane >> 4);
-                    ldsm_x4_t(vf, Vs[buf] + fa_swz(key, col));
-                    mma_bf16(o[nd], af, vf[0], vf[1]);
-                    mma_bf16(o[nd + 1], af, vf[2], vf[3]);
-                }
+            for (int nd = 0; nd < 8; nd += 2) {
+                uint32_t vf[4];
+                const int key = ks * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+                const int col = nd * 8 + 8 * (lane >> 4);
+                ldsm_x4_t(vf, Vb + fa_swz(key, col));
+                mma_bf16(o[nd], af, vf[0], vf[1]);
+                mma_bf16(o[nd + 1], af, vf[2], vf[3]);
             }
         }
         __syncthreads();

@@ -531,7 +531,9 @@ struct LargeExec {
         launch(s, dim3(N), dim3(128), 0, k_embed_bf16, io.tokens, N, reinterpret_cast<const bf16*>(m->at(0)), dm.V, dm.d,
                x, err);
         ++launches;
-        const bool flash = n >= 16 && mask_mode != kMaskBuffer;
+        // CHROMA_B200_NO_FLASH selects the split-KV SIMT attention for every chunk (a cross-check of the two kernels).
+        static const bool no_flash = std::getenv("CHROMA_B200_NO_FLASH") != nullptr;
+        const bool flash = !no_flash && n >= 16 && mask_mode != kMaskBuffer && ctx <= kFaMaxCacheTiles * kFaKeys;
         for (int l = 0; l < L; ++l) {
             const LayerW<bf16> w = m->layer<bf16>(l);
             bf16* nk;
@@ -569,7 +571,7 @@ struct LargeExec {
                 fa.slots = mask_mode == kMaskSlots ? io.slots : nullptr;
                 fa.pos0 = mask_mode == kMaskSlots ? io.pos0 : nullptr;
                 if (mask_mode != kMaskSlots) fa.ctx = 0;
-                launch(s, dim3((n + kFaRows - 1) / kFaRows, dm.H, B), dim3(128), 0, k_flash_prefill, q, fa, ck, cv,
+                launch(s, dim3((n + kFaRows - 1) / kFaRows, dm.H, B), dim3(kFaThreads), kFaSmemBytes, k_flash_prefill, q, fa, ck, cv,
                        static_cast<const bf16*>(nk), static_cast<const bf16*>(nv), w.sinks, attn);
             } else {
                 AttnArgs a;

@@ -368,7 +368,7 @@ class Decoder:
         self.slots = np.full(context, -1, np.int64)
         self.position = 0
 
-    def append(self, tokens) -> np.ndarray:  # type: ignore[no-untyped-def]
+    def append(self, tokens, trace: Trace | None = None) -> np.ndarray:  # type: ignore[no-untyped-def]
         ids = np.asarray(tokens, dtype=np.int64)
         offset = 0
         logits = None
@@ -388,7 +388,7 @@ class Decoder:
             token_ids = np.zeros(steps, np.int64)
             token_ids[:count] = ids[offset : offset + count]
             logits, nk, nv = cached_step(self.cfg, self.p, token_ids, times.astype(F32), self.keys, self.values,
-                                         masks[0], masks[1], np.array([count - 1]))
+                                         masks[0], masks[1], np.array([count - 1]), trace)
             rows = times[:count] % self.context
             self.keys[:, rows] = nk[:, :count]
             self.values[:, rows] = nv[:, :count]

@@ -90,3 +90,17 @@ def assert_bf16_logits(got: np.ndarray, want: np.ndarray, rel: float = 2e-2, ele
     assert worst <= rel, f"max |diff| / row scale = {worst:.4g} > {rel}"
     close = np.abs(got - want) <= rel + rel * np.abs(want)
     assert close.mean() >= elementwise_share, f"only {close.mean():.4%} of elements within {rel} rel/abs"
+
+
+def near_tie(gates: np.ndarray, k: int, rel: float = 1 / 64) -> np.ndarray:
+    """Rows whose k-th and (k+1)-th largest gate logits are within ``rel`` (relative) of each other.
+
+    Routing on such rows depends on the last bits of the gate logits, which follow the accumulation order of every
+    GEMM before the router; an implementation that sums in another order than the reference's sequential fp32 loops
+    (chroma/_src/codegen/cpu/kernels.h:63-74) may pick the other expert there. Comparisons skip or relax those rows.
+    """
+    g = np.sort(np.asarray(gates, np.float32).reshape(-1, np.asarray(gates).shape[-1]), axis=-1)[:, ::-1]
+    if g.shape[-1] <= k:
+        return np.zeros(g.shape[0], bool)
+    gap = np.abs(g[:, k - 1] - g[:, k])
+    return gap <= rel * np.maximum(np.abs(g[:, k - 1]), np.abs(g[:, k]))

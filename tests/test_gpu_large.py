@@ -64,3 +64,36 @@ def test_c4_slice_prefill_and_decode_match_oracle(gpu: None) -> None:
     for got, exp in zip(outs, want):
         helpers.assert_bf16_logits(np.asarray(got, np.float32), exp)
         assert int(np.argmax(got)) == int(np.argmax(exp))
+
+
+def test_flash_prefill_chunks_cache_and_window_match_oracle(gpu: None) -> None:
+    """Long prefill chunks through the flash kernel: several 128-row query blocks, own key tiles below the diagonal
+    (mask-free), a second chunk that reads live ring-cache tiles, a windowed layer (layer 0, window 160), decode
+    steps in between and the ring wrapping. Steps whose oracle routing has a near-tie at the top-k boundary in some
+    layer for the row whose logits are returned (helpers.near_tie) are held to the greedy token only."""
+    cfg = dataclasses.replace(models.gpt_oss_20b, num_hidden_layers=2, hidden_size=1024, intermediate_size=1024,
+                              num_attention_heads=16, num_key_value_heads=2, num_experts=8, experts_per_token=2,
+                              vocab_size=8192, sliding_window=160)
+    model = models.random_transformer(cfg, seed=21, std=0.02, dtype=torch.bfloat16)
+    tokens = np.random.default_rng(22).integers(0, cfg.vocab_size, 780)
+    chunks = [700, 1, 1, 1, 1, 76]
+    prefill = chroma_b200.compile_model(model, _TMP / "flpre", steps=384, context=640)
+    decode = chroma_b200.compile_model(model, _TMP / "fldec", steps=1, context=640)
+    assert prefill.stats["tensor_core_path"]
+    ref = og.Decoder(og.Config.from_model_config(cfg), og.Params.from_module(model), context=640, prefill_steps=384,
+                     sliding_window=160)
+    strict = 0
+    with chroma_b200.Decoder(prefill, decode, sliding_window=160) as dec:
+        offset = 0
+        for size in chunks:
+            part = tokens[offset : offset + size]
+            offset += size
+            got = np.asarray(dec.append(part), np.float32)
+            trace = og.Trace()
+            want = ref.append(part, trace)
+            assert int(np.argmax(got)) == int(np.argmax(want))
+            last = size - 1 - 384 * ((size - 1) // 384) if size > 1 else 0  # last real row of the final chunk
+            if not any(helpers.near_tie(g[last], cfg.experts_per_token).any() for g in trace.gates[-2:]):
+                helpers.assert_bf16_logits(got, want)
+                strict += 1
+    assert strict >= 4
