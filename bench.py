@@ -41,6 +41,8 @@ A100_DECODE_STEP_MS = 3.27  # reference, docs/benchmarks.md:37
 A100_FWD8_MS = 4.25  # reference, docs/benchmarks.md:23
 CONTEXT = 256
 PREFILL = 8
+# DRAM bytes of one k_vocab launch of this workload, from an ncu capture (102.98 MB read + 3.87 MB written).
+VOCAB_NCU_TRAFFIC = 106_851_584
 
 
 def parse() -> argparse.Namespace:
@@ -478,7 +480,9 @@ def main() -> None:
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {
             "kernel": "k_vocab (unembedding GEMV, 201088 x 128 fp32, 1 row)", "bound": "hbm", "achieved": achieved,
-            "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
+            "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": VOCAB_NCU_TRAFFIC,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_vocab<float, 1> launch of "
+                              "this workload (profiles/k_vocab_dev_decode_step.md)",
             "algorithmic_bytes": vocab_bytes, "launch_us": vocab_t * 1e6,
             "peak_source": f"{pk['source']} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
             "timing": f"launched alone after an L2 flush, CUDA events, mean of {reps}",
