@@ -177,9 +177,14 @@ def prefill_flops(cfg, batch: int, n: int) -> float:  # type: ignore[no-untyped-
     return cfg.num_hidden_layers * (gemm + attention) + 2 * batch * cfg.vocab_size * d
 
 
-def bench_c4(args: argparse.Namespace, rng: np.random.Generator, max_over_ranks) -> dict:  # type: ignore[no-untyped-def]
-    """GPT-OSS-20B-shaped prefill of 4 x 2048 tokens (config C4) on this GPU: bf16 weights N(0, 0.02) generated in
-    device memory, the batched prefill program through BatchDecoder (tokens in from the host, greedy ids out)."""
+def bench_c4(args: argparse.Namespace, rng: np.random.Generator, max_over_ranks, barrier, rank: int = 0,
+             world: int = 1) -> dict:  # type: ignore[no-untyped-def]
+    """GPT-OSS-20B-shaped prefill of 4 x 2048 tokens per GPU (config C4): bf16 weights N(0, 0.02) generated in
+    device memory, the batched prefill program through BatchDecoder (tokens in from the host, greedy ids out).
+
+    With several ranks (torchrun) the 32 experts are split over the GPUs (expert parallel, csrc/ep.cuh): each rank
+    holds E / world experts plus the replicated attention, router and embeddings, prefills its own 4 x 2048 tokens
+    (weak scaling), and exchanges routed rows with the other ranks every layer over NVLink peer memory."""
     import torch
 
     import chroma_b200
@@ -191,45 +196,60 @@ def bench_c4(args: argparse.Namespace, rng: np.random.Generator, max_over_ranks)
     if args.c4_layers:
         cfg = dataclasses.replace(cfg, num_hidden_layers=args.c4_layers)
     batch, n = 4, 2048
-    plan_p, regions = synthetic_gptoss(cfg, steps=n, context=n)
-    plan_d, _ = synthetic_gptoss(cfg, steps=1, context=n)
+    plan_p, regions = synthetic_gptoss(cfg, steps=n, context=n, ep_world=world)
+    plan_d, _ = synthetic_gptoss(cfg, steps=1, context=n, ep_world=world)
     wbuf = torch.empty(plan_p["desc"]["weight_bytes"], dtype=torch.uint8, device="cuda")
-    gen = torch.Generator(device="cuda").manual_seed(20)
-    for _, off, numel, is_norm in regions:
+    shared_gen = torch.Generator(device="cuda").manual_seed(20)  # replicated weights: the same on every rank
+    expert_gen = torch.Generator(device="cuda").manual_seed(1000 + rank)  # this rank's experts
+    for name, off, numel, is_norm in regions:
         if is_norm:
             wbuf[off : off + numel * 4].view(torch.float32).fill_(1.0)
         else:
+            gen = expert_gen if ".mlp.mlp" in name else shared_gen
             wbuf[off : off + numel * 2].view(torch.bfloat16).normal_(0.0, 0.02, generator=gen)
     torch.cuda.synchronize()
-    pre = chroma_b200.Program.from_native(Native(plan_p, device_weights=wbuf.data_ptr()))
-    dec = chroma_b200.Program.from_native(Native(plan_d, device_weights=wbuf.data_ptr()))
+    group = None
+    if world > 1:
+        group = chroma_b200.ExpertGroup(rank, world, max_pairs=batch * n * cfg.experts_per_token,
+                                        hidden=cfg.hidden_size, experts=cfg.num_experts)
+    pre = chroma_b200.Program.from_native(Native(plan_p, device_weights=wbuf.data_ptr(), ep=group))
+    dec = chroma_b200.Program.from_native(Native(plan_d, device_weights=wbuf.data_ptr(), ep=group))
     bd = chroma_b200.BatchDecoder(pre, dec, batch)
     tokens = rng.integers(0, cfg.vocab_size, (batch, n))
     reps = max(2, min(5, args.steps // 40))
     for _ in range(max(1, min(3, args.warmup))):
         bd.reset()
+        barrier()
         bd.append(tokens, argmax=True)
     times = []
     for _ in range(reps):
         bd.reset()
-        torch.cuda.synchronize()
+        barrier()
         t0 = time.perf_counter()
         ids = bd.append(tokens, argmax=True)
         times.append(time.perf_counter() - t0)
     t = max_over_ranks(statistics.median(times))
-    flops = prefill_flops(cfg, batch, n)
+    flops = prefill_flops(cfg, batch, n) * world
     peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops_sustained"] if (ROOT / "MEASURED_PEAKS.json").exists() else 1400.0
+    barrier()
     bd.close()
-    del pre, dec, wbuf
+    del pre, dec
+    if group is not None:
+        group.close()
+    del wbuf
     torch.cuda.empty_cache()
     return {
-        "workload": "C4: GPT-OSS-20B-shaped prefill (24 layers, d=2880, 64/8 heads, 32 experts top-4, bf16 N(0,0.02)), "
-                    "4 x 2048 tokens, 1 GPU, all experts local",
-        "tokens_per_s": batch * n / t, "ms": t * 1e3, "reps": reps,
-        "e2e": {"api": "BatchDecoder.append(tokens[4, 2048], argmax=True)", "h2d_bytes": batch * n * 8 + batch * 16,
-                "d2h_bytes": batch * 8 + 4},
+        "workload": f"C4: GPT-OSS-20B-shaped prefill ({cfg.num_hidden_layers} layers, d=2880, 64/8 heads, 32 experts "
+                    f"top-4, bf16 N(0,0.02)), 4 x 2048 tokens per GPU, {world} GPU(s), "
+                    + ("all experts local" if world == 1 else f"expert parallel ({cfg.num_experts // world} experts "
+                                                               "per GPU, NVLink peer-memory dispatch/return)"),
+        "tokens_per_s": world * batch * n / t, "ms": t * 1e3, "reps": reps, "n_gpus": world,
+        "scaling": "weak",
+        "e2e": {"api": "BatchDecoder.append(tokens[4, 2048], argmax=True) on every rank",
+                "h2d_bytes": batch * n * 8 + batch * 16, "d2h_bytes": batch * 8 + 4},
         "algorithmic_tflop": flops / 1e12, "achieved_tflops": flops / t / 1e12,
-        "frac_of_bf16_sustained": flops / t / 1e12 / peak, "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained",
+        "frac_of_bf16_sustained": flops / t / 1e12 / (peak * world),
+        "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (x GPUs)",
         "argmax_head": [int(v) for v in ids[:2]],
     }
 
@@ -273,7 +293,7 @@ def main() -> None:
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     if args.c4_only:
-        c4 = bench_c4(args, np.random.default_rng(0), max_over_ranks)
+        c4 = bench_c4(args, np.random.default_rng(rank), max_over_ranks, barrier, rank, world)
         if rank == 0:
             print(json.dumps({"c4_prefill": c4}), flush=True)
         if dist is not None:
@@ -444,7 +464,7 @@ def main() -> None:
     micro.close()
     del mout
 
-    c4 = bench_c4(args, rng, max_over_ranks) if not args.skip_c4 else None
+    c4 = bench_c4(args, rng, max_over_ranks, barrier, rank, world) if not args.skip_c4 else None
 
     cpu = None
     if rank == 0 and world == 1:

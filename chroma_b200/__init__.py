@@ -11,6 +11,7 @@ from pathlib import Path
 from typing import Any
 
 from chroma_b200._src.decoder import BatchDecoder, Decoder
+from chroma_b200._src.experts import ExpertGroup
 from chroma_b200._src.program import Program
 
 
@@ -21,12 +22,14 @@ def compile(input: Any, output: str | Path, *, blas: bool = True, backend: str =
     return compile_for_backend(input, output, blas=blas, backend=backend)
 
 
-def compile_model(model: Any, output: str | Path, *, steps: int, context: int | None = None, last: bool = False) -> Program:
+def compile_model(model: Any, output: str | Path, *, steps: int, context: int | None = None, last: bool = False,
+                  experts: ExpertGroup | None = None) -> Program:
     """Compile a ``chroma_b200.models.Transformer`` straight from its parameters (no ``torch.export``): a forward
-    over ``steps`` tokens, or with ``context`` a KV-cached step of ``steps`` rows (the prefill/decode programs)."""
+    over ``steps`` tokens, or with ``context`` a KV-cached step of ``steps`` rows (the prefill/decode programs).
+    With ``experts`` (an ``ExpertGroup``), this rank's share of the experts only, bound to the group."""
     from chroma_b200._src.compiler import compile_model as _compile_model
 
-    return _compile_model(model, output, steps=steps, context=context, last=last)
+    return _compile_model(model, output, steps=steps, context=context, last=last, experts=experts)
 
 
-__all__ = ["BatchDecoder", "Decoder", "Program", "compile", "compile_model"]
+__all__ = ["BatchDecoder", "Decoder", "ExpertGroup", "Program", "compile", "compile_model"]

@@ -366,11 +366,13 @@ def _lower_micro(g: _Graph) -> Lowered:
                                                                "unreused_workspace_bytes": 0})
 
 
-def gptoss_layout(config: Any) -> list[tuple[str, tuple[int, ...], bool]]:
-    """(name, shape, is_fp32_norm) of every weight tensor in packing order (include/chroma_b200.h layout)."""
+def gptoss_layout(config: Any, ep_world: int = 1) -> list[tuple[str, tuple[int, ...], bool]]:
+    """(name, shape, is_fp32_norm) of every weight tensor in packing order (include/chroma_b200.h layout). With
+    ``ep_world`` > 1 the expert tensors hold one rank's share (E / ep_world experts); the router keeps all E."""
     d, V, L = config.hidden_size, config.vocab_size, config.num_hidden_layers
     H, KV, hd = config.num_attention_heads, config.num_key_value_heads, config.head_dim
     E, I = config.num_experts, config.intermediate_size
+    El = E // ep_world
     out = [("embedding.weight", (V, d), False), ("norm.scale", (d,), True), ("unembedding.weight", (V, d), False)]
     for layer in range(L):
         b = f"block.{layer}."
@@ -379,8 +381,8 @@ def gptoss_layout(config: Any) -> list[tuple[str, tuple[int, ...], bool]]:
             (b + "attn.qkv.weight", ((H + 2 * KV) * hd, d), False), (b + "attn.qkv.bias", ((H + 2 * KV) * hd,), False),
             (b + "attn.out.weight", (d, H * hd), False), (b + "attn.out.bias", (d,), False),
             (b + "mlp.norm.scale", (d,), True), (b + "mlp.gate.weight", (E, d), False), (b + "mlp.gate.bias", (E,), False),
-            (b + "mlp.mlp1_weight", (E, 2 * I, d), False), (b + "mlp.mlp1_bias", (E, 2 * I), False),
-            (b + "mlp.mlp2_weight", (E, d, I), False), (b + "mlp.mlp2_bias", (E, d), False),
+            (b + "mlp.mlp1_weight", (El, 2 * I, d), False), (b + "mlp.mlp1_bias", (El, 2 * I), False),
+            (b + "mlp.mlp2_weight", (El, d, I), False), (b + "mlp.mlp2_bias", (El, d), False),
         ]
     return out
 
@@ -425,7 +427,7 @@ def _gptoss_desc(config: Any, dtype: str, steps: int, context: int | None, last:
 
 
 def synthetic_gptoss(config: Any, *, steps: int, context: int | None = None, dtype: str = "bfloat16",
-                     last: bool = False) -> tuple[dict[str, Any], list[tuple[str, int, int, bool]]]:
+                     last: bool = False, ep_world: int = 1) -> tuple[dict[str, Any], list[tuple[str, int, int, bool]]]:
     """The plan of a GPT-OSS program whose weights will be written straight into device memory (no host copy): returns
     (plan, regions) with regions = (name, byte offset, element count, is_fp32_norm) in packing order. Use with
     ``Native(plan, device_weights=ptr)`` over a buffer of ``plan["desc"]["weight_bytes"]`` bytes."""
@@ -433,7 +435,7 @@ def synthetic_gptoss(config: Any, *, steps: int, context: int | None = None, dty
 
     es = 2 if dtype == "bfloat16" else 4
     regions, total = [], 0
-    for name, shape, is_norm in gptoss_layout(config):
+    for name, shape, is_norm in gptoss_layout(config, ep_world):
         total = (total + ALIGN - 1) // ALIGN * ALIGN
         numel = math.prod(shape)
         regions.append((name, total, numel, is_norm))
@@ -450,12 +452,14 @@ def synthetic_gptoss(config: Any, *, steps: int, context: int | None = None, dty
     return plan, regions
 
 
-def lower_model(model: Any, *, steps: int, context: int | None = None, last: bool = False) -> Lowered:
+def lower_model(model: Any, *, steps: int, context: int | None = None, last: bool = False,
+                experts: range | None = None) -> Lowered:
     """A GPT-OSS program straight from a ``chroma_b200.models.Transformer`` (no export).
 
     ``context=None``: ``Transformer.forward`` over ``steps`` tokens (``last=True``: the UncachedTransformer variant
     returning one row); otherwise a CachedTransformer step of ``steps`` rows against a ``context``-row cache. The
-    plan is the one ``lower`` recognises from the corresponding export.
+    plan is the one ``lower`` recognises from the corresponding export. ``experts``: the global expert indices
+    this rank of an expert-parallel group owns (``ExpertGroup.local``); the expert tensors are sliced to them.
     """
     import math as _math
 
@@ -463,6 +467,10 @@ def lower_model(model: Any, *, steps: int, context: int | None = None, last: boo
 
     config = model.config
     state = {k: v.detach() for k, v in model.state_dict().items()}
+    if experts is not None:
+        for k in list(state):
+            if k.endswith(("mlp.mlp1_weight", "mlp.mlp1_bias", "mlp.mlp2_weight", "mlp.mlp2_bias")):
+                state[k] = state[k][experts.start : experts.stop].contiguous()
     dtype = _DTYPE_NAMES[str(state["embedding.weight"].dtype)]
     conc, inv_freq = rope_tables(config)
 
@@ -620,9 +628,20 @@ def lower_micro(weight: np.ndarray, rows: int, cols: int, eps: float = 1e-5) -> 
 
 
 def compile_model(model: Any, output: str | os.PathLike[str], *, steps: int, context: int | None = None,
-                  last: bool = False) -> Program:
-    """Write and load the artefact of a GPT-OSS model without exporting it (see ``lower_model``)."""
-    return Program(write_artifact(lower_model(model, steps=steps, context=context, last=last), output))
+                  last: bool = False, experts: Any = None) -> Program:
+    """Write and load the artefact of a GPT-OSS model without exporting it (see ``lower_model``).
+
+    ``experts``: an ``ExpertGroup``; the artefact then holds this rank's experts only, its manifest records the
+    group's rank and size, and the returned program is bound to the group (``Program(dir)`` refuses such an
+    artefact: it cannot run without its group)."""
+    if experts is None:
+        return Program(write_artifact(lower_model(model, steps=steps, context=context, last=last), output))
+    lowered = lower_model(model, steps=steps, context=context, last=last, experts=experts.local)
+    lowered.plan["expert_parallel"] = {"rank": experts.rank, "world": experts.world}
+    directory = write_artifact(lowered, output)
+    manifest = json.loads((directory / "model.json").read_text())
+    native = nat.Native(manifest["b200"], str(directory / manifest["weights"]), ep=experts)
+    return Program.from_native(native, manifest["stats"])
 
 
 def compile_for_backend(program: Any, output: str | os.PathLike[str], *, blas: bool = True, backend: str = "cuda") -> Program:

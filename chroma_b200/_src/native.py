@@ -89,7 +89,14 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "chroma_b200_decoder_advance": (ctypes.c_int, [_VP, _I64P, _I64P, _I32, _VP, _I64P, _CP, _SZ]),
     "chroma_b200_decoder_step_launches": (ctypes.c_int32, [_VP]),
     "chroma_b200_decoder_launch_vocab": (ctypes.c_int, [_VP, _VP, _CP, _SZ]),
+    "chroma_b200_ep_create": (ctypes.c_int, [_I32, _I32, ctypes.c_int64, _I32, _I32, ctypes.POINTER(_VP), _CP, _SZ]),
+    "chroma_b200_ep_handle": (ctypes.c_int, [_VP, _VP, _CP, _SZ]),
+    "chroma_b200_ep_open": (ctypes.c_int, [_VP, _VP, _CP, _SZ]),
+    "chroma_b200_ep_destroy": (None, [_VP]),
+    "chroma_b200_create_ep": (ctypes.c_int, [ctypes.POINTER(Desc), _CP, _VP, _VP, ctypes.POINTER(_VP), _CP, _SZ]),
 }
+
+EP_HANDLE_BYTES = 64  # CHROMA_B200_EP_HANDLE_BYTES
 
 _lib: ctypes.CDLL | None = None
 _lib_lock = threading.Lock()
@@ -154,12 +161,19 @@ def dtype_of(name: str) -> np.dtype:
 class Native:
     """Owns one ``chroma_b200_program``."""
 
-    def __init__(self, plan: dict[str, Any], weights_path: str | None = None, *, device_weights: int | None = None) -> None:
+    def __init__(self, plan: dict[str, Any], weights_path: str | None = None, *, device_weights: int | None = None,
+                 ep: Any = None) -> None:
         self.plan = plan
         self._keep: list[Any] = []
         desc = self._desc(plan)
         handle = _VP()
-        if device_weights is not None:
+        if ep is not None:
+            # An expert-parallel program: weights hold this rank's experts only; the group outlives the program.
+            self._keep.append(ep)
+            path = str(weights_path).encode() if device_weights is None else None
+            call("chroma_b200_create_ep", ctypes.byref(desc), path, _VP(device_weights) if device_weights is not None
+                 else None, ep.handle, ctypes.byref(handle))
+        elif device_weights is not None:
             call("chroma_b200_create_device", ctypes.byref(desc), _VP(device_weights), ctypes.byref(handle))
         else:
             call("chroma_b200_create", ctypes.byref(desc), str(weights_path).encode(), ctypes.byref(handle))
@@ -257,6 +271,9 @@ def model_class(plan: dict[str, Any]) -> type:
 
     class Model:
         def __init__(self, weights_path: str) -> None:
+            if plan.get("expert_parallel"):
+                raise ValueError("This artefact holds one rank's experts of an expert-parallel group; load it with "
+                                 "chroma_b200.compile_model(..., experts=group) on every rank")
             self._native = Native(plan, weights_path)
 
         @property

@@ -1,0 +1,233 @@
+// Expert parallelism over NVLink peer memory: the MoE block of the GPT-OSS-20B/120B-shaped programs with the experts
+// split across the GPUs of one node (rank r owns experts [r*El, (r+1)*El), El = E / world).
+//
+// Every rank runs the same program on its own tokens (data parallel for attention, norms and the router). Per
+// layer, the exchange that the reference's single-device einsums (chroma/models/gpt_oss.py:243-265,
+// chroma/_src/codegen/gpu.py:390-424) never needed is done with stores into the peers' memory, so no host round
+// trip or library collective sits between the routing and the expert GEMMs:
+//
+//   k_ep_push_counts  routed (token, slot) counts per global expert -> every peer's count table [src][E]; flag
+//   k_ep_plan         wait for all count tables; per owner and expert the row where this rank's rows start in the
+//                     owner's grouped layout (expert-major, source-rank minor), and the local groups' row offsets
+//   k_ep_dispatch     each (token, slot) claims a row and stores the token's normalised activations plus its origin
+//                     (src rank, pair index) into the owning rank's receive buffer; the last CTA flags every peer
+//   k_ep_wait         wait until every peer's flag for this phase reaches the layer's epoch
+//   (local grouped SwiGLU GEMM + expert GEMM over the received rows)
+//   k_ep_return       each received row's expert output goes back to its source rank's return buffer at the pair
+//                     index; the last CTA flags every peer
+//   (k_ep_wait, then k_moe_combine over the returned rows in slot order)
+//
+// Synchronisation: each phase has a flag per source rank in the receiver's memory. Flags only grow: the sender
+// writes the layer's epoch (a device counter every rank advances once per MoE layer, so all ranks agree) with a
+// release store after a system-scope fence; the receiver polls with acquire loads. Every wait is bounded
+// (EpArgs::timeout_ns of wall time): a rank that never arrives makes the waiter raise kErrTimeout and return, and
+// the host reports it; the group's epochs then disagree, so it must be recreated.
+// Buffer reuse across layers is safe without extra barriers: a rank can only start layer l+1's dispatch after it
+// received every peer's layer-l returns, which peers send only after their layer-l GEMMs finished reading.
+//
+// Only plain loads and stores touch peer memory. TMA reads only this GPU's own memory (the received rows).
+#pragma once
+
+#include "tma.cuh"
+
+namespace cb200 {
+
+constexpr int kEpMaxWorld = 8;
+constexpr int kEpMaxExperts = 256;
+
+// Header of each rank's shared (IPC-exported) buffer.
+struct EpHeader {
+    unsigned cnt_flag[kEpMaxWorld];
+    unsigned disp_flag[kEpMaxWorld];
+    unsigned comb_flag[kEpMaxWorld];
+    unsigned pad[64 - 3 * kEpMaxWorld];
+    int counts[kEpMaxWorld][kEpMaxExperts];  // [src rank][global expert]
+};
+
+enum EpPhase : int { kEpCounts = 0, kEpDispatch = 1, kEpCombine = 2 };
+
+struct EpArgs {
+    int rank, world, E, El, d;
+    long long pmax;               // rows of the return buffer (pairs per rank)
+    long long cap;                // rows of the receive buffer (world * pmax)
+    char* peer[kEpMaxWorld];      // base of each rank's shared buffer (peer[rank] is this rank's own)
+    size_t off_meta, off_x, off_y;  // offsets of the receive metadata, receive rows and return rows
+    unsigned* epoch;              // this rank's epoch counter (local memory)
+    unsigned* done;               // last-CTA counter (local memory)
+    unsigned long long timeout_ns;  // bound of every wait for another rank
+};
+
+__device__ __forceinline__ EpHeader* ep_header(const EpArgs& a, int r) { return reinterpret_cast<EpHeader*>(a.peer[r]); }
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait of one thread until *flag >= epoch (flags never decrease; wrap-safe comparison). Gives up after
+// `timeout_ns` of wall time (the global timer), raising kErrTimeout.
+__device__ __forceinline__ bool ep_wait_flag(const unsigned* flag, unsigned epoch, unsigned long long timeout_ns,
+                                             unsigned* err) {
+    const unsigned long long start = global_ns();
+    for (unsigned i = 0;; ++i) {
+        if (int(ld_acquire_sys(flag) - epoch) >= 0) return true;
+        if ((i & 63) == 63) {
+            if (global_ns() - start > timeout_ns) break;
+            __nanosleep(256);
+        }
+    }
+    atomicOr(err, kErrTimeout);
+    return false;
+}
+
+__device__ __forceinline__ unsigned* ep_flag(const EpArgs& a, int owner, int phase, int src) {
+    EpHeader* h = ep_header(a, owner);
+    return phase == kEpCounts ? &h->cnt_flag[src] : (phase == kEpDispatch ? &h->disp_flag[src] : &h->comb_flag[src]);
+}
+
+// Called by every thread of a CTA after its peer stores: the last CTA of the grid raises this rank's flag for
+// `phase` on every peer. Classic last-block pattern at system scope: each CTA fences its stores before counting
+// itself done; the last one fences again before the release stores of the flags.
+__device__ __forceinline__ void ep_signal_when_last(const EpArgs& a, int phase) {
+    __shared__ bool last;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(a.done, 1u);
+        last = prev == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last) {
+        __threadfence_system();
+        if (threadIdx.x == 0) *a.done = 0u;
+        const unsigned epoch = *reinterpret_cast<volatile unsigned*>(a.epoch);
+        if (threadIdx.x < unsigned(a.world)) st_release_sys(ep_flag(a, int(threadIdx.x), phase, a.rank), epoch);
+    }
+}
+
+// 1 CTA. Advances the epoch, copies this rank's per-expert counts into every peer's table, flags them, and clears
+// the counts for the next layer.
+__global__ void k_ep_push_counts(EpArgs a, int* __restrict__ counts) {
+    __shared__ unsigned epoch;
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x == 0) {
+        epoch = *a.epoch + 1u;
+        *a.epoch = epoch;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < a.world * a.E; i += blockDim.x) {
+        const int q = i / a.E, e = i % a.E;
+        ep_header(a, q)->counts[a.rank][e] = counts[e];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < unsigned(a.world)) st_release_sys(ep_flag(a, int(threadIdx.x), kEpCounts, a.rank), epoch);
+    for (int e = threadIdx.x; e < a.E; e += blockDim.x) counts[e] = 0;
+}
+
+// 1 CTA. Waits for every rank's counts, then: cursor[e] = first row of this rank's rows for global expert e in the
+// owner's receive buffer; offsets[0..El] = row offsets of the local experts' groups; *recv_total = offsets[El].
+__global__ void k_ep_plan(EpArgs a, int* __restrict__ cursor, int* __restrict__ offsets, int* __restrict__ recv_total,
+                          unsigned* err) {
+    __shared__ int ok;
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x == 0) ok = 1;
+    __syncthreads();
+    const unsigned epoch = *reinterpret_cast<volatile unsigned*>(a.epoch);
+    if (threadIdx.x < unsigned(a.world) && !ep_wait_flag(&ep_header(a, a.rank)->cnt_flag[threadIdx.x], epoch, a.timeout_ns, err))
+        ok = 0;
+    __syncthreads();
+    if (!ok) return;
+    // The tables were written by other GPUs: volatile loads, never a stale L1 line.
+    const volatile EpHeader* h = ep_header(a, a.rank);
+    if (threadIdx.x < unsigned(a.world)) {  // thread q walks owner q's layout
+        const int q = threadIdx.x;
+        int row = 0;
+        for (int el = 0; el < a.El; ++el) {
+            const int e = q * a.El + el;
+            if (q == a.rank) offsets[el] = row;
+            for (int src = 0; src < a.world; ++src) {
+                if (src == a.rank) cursor[e] = row;
+                row += h->counts[src][e];
+            }
+        }
+        if (q == a.rank) {
+            offsets[a.El] = row;
+            *recv_total = row;
+            if (row > a.cap) atomicOr(err, kErrIndex);
+        }
+    }
+}
+
+// One warp per (token, slot) pair, grid-stride. Stores the token's row and its origin into the owner's buffers.
+__global__ void __launch_bounds__(256) k_ep_dispatch(EpArgs a, const int* __restrict__ ridx, int pairs, int k,
+                                                     const __nv_bfloat16* __restrict__ xn, int* __restrict__ cursor,
+                                                     unsigned* err) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    pdl_wait();
+    pdl_trigger();
+    for (int i = blockIdx.x * warps + warp; i < pairs; i += gridDim.x * warps) {
+        int row = 0, q = 0;
+        if (lane == 0) {
+            const int e = ridx[i];
+            q = e / a.El;
+            row = atomicAdd(cursor + e, 1);
+            if (row < a.cap)
+                reinterpret_cast<int*>(a.peer[q] + a.off_meta)[row] = int(a.rank * a.pmax + i);
+            else
+                atomicOr(err, kErrIndex);
+        }
+        row = __shfl_sync(0xffffffffu, row, 0);
+        q = __shfl_sync(0xffffffffu, q, 0);
+        if (row >= a.cap) continue;
+        const uint4* src = reinterpret_cast<const uint4*>(xn + size_t(i / k) * a.d);
+        uint4* dst = reinterpret_cast<uint4*>(a.peer[q] + a.off_x) + size_t(row) * (a.d / 8);
+        for (int c = lane; c < a.d / 8; c += 32) dst[c] = src[c];
+    }
+    ep_signal_when_last(a, kEpDispatch);
+}
+
+// 1 CTA: wait until every rank raised its flag for `phase` on this rank.
+__global__ void k_ep_wait(EpArgs a, int phase, unsigned* err) {
+    pdl_wait();
+    pdl_trigger();
+    const unsigned epoch = *reinterpret_cast<volatile unsigned*>(a.epoch);
+    if (threadIdx.x < unsigned(a.world)) ep_wait_flag(ep_flag(a, a.rank, phase, int(threadIdx.x)), epoch, a.timeout_ns, err);
+}
+
+// One warp per received row, grid-stride: the expert output row goes back to its source rank's return buffer.
+__global__ void __launch_bounds__(256) k_ep_return(EpArgs a, const __nv_bfloat16* __restrict__ y, const int* __restrict__ recv_total,
+                                                   unsigned* err) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    pdl_wait();
+    pdl_trigger();
+    const int total = *recv_total;
+    const int* meta = reinterpret_cast<const int*>(a.peer[a.rank] + a.off_meta);
+    for (int j = blockIdx.x * warps + warp; j < total && j < a.cap; j += gridDim.x * warps) {
+        const long long m = __ldcg(meta + j);
+        const int src = int(m / a.pmax);
+        const long long i = m % a.pmax;
+        if (src < 0 || src >= a.world) {
+            if (lane == 0) atomicOr(err, kErrIndex);
+            continue;
+        }
+        const uint4* from = reinterpret_cast<const uint4*>(y + size_t(j) * a.d);
+        uint4* to = reinterpret_cast<uint4*>(a.peer[src] + a.off_y) + size_t(i) * (a.d / 8);
+        for (int c = lane; c < a.d / 8; c += 32) to[c] = from[c];
+    }
+    ep_signal_when_last(a, kEpCombine);
+}
+
+}  // namespace cb200

@@ -151,7 +151,8 @@ __global__ void k_route_scatter(const int* __restrict__ ridx, int pairs, int k, 
     for (int c = lane; c < d / 8; c += 32) dst[c] = src[c];
 }
 
-// grid = tokens; x[t] = bf16(x[t] + bf16(sum_s w[t,s] * y[perm[t,s]])) summed in slot order.
+// grid = tokens; x[t] = bf16(x[t] + bf16(sum_s w[t,s] * y[perm[t,s]])) summed in slot order (perm == nullptr:
+// y row t*k + s, the layout of the expert-parallel return buffer).
 __global__ void __launch_bounds__(256) k_moe_combine(const bf16* __restrict__ y, const int* __restrict__ perm,
                                                      const float* __restrict__ rw, int k, int d, bf16* __restrict__ x) {
     const int t = blockIdx.x;
@@ -160,7 +161,7 @@ __global__ void __launch_bounds__(256) k_moe_combine(const bf16* __restrict__ y,
     int rows[8];
     float w[8];
     for (int s = 0; s < k; ++s) {
-        rows[s] = perm[size_t(t) * k + s];
+        rows[s] = perm ? perm[size_t(t) * k + s] : t * k + s;
         w[s] = rw[size_t(t) * k + s];
     }
     for (int c = threadIdx.x * 2; c < d; c += blockDim.x * 2) {

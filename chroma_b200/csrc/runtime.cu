@@ -12,6 +12,7 @@
 
 #include "../../include/chroma_b200.h"
 #include "flash.cuh"
+#include "ep.cuh"
 #include "gemm.cuh"
 #include "gptoss.cuh"
 #include "large.cuh"
@@ -21,6 +22,8 @@
 #include <cstdlib>
 #include <cstring>
 #include <algorithm>
+#include <array>
+#include <vector>
 #include <fstream>
 #include <map>
 #include <memory>
@@ -304,8 +307,54 @@ static void launch_vocab(cudaStream_t s, const Dims& dm, int sms, const float* x
 }
 
 // ---------------------------------------------------------------------------------------------------------
+// ---------------------------------------------------------------------------------------------------------
+// Expert-parallel group: this rank's IPC-exported buffer (header, receive metadata, receive rows, return rows),
+// the peers' buffers opened from their handles, and the rank-local epoch / last-CTA counters.
+struct EpGroup {
+    int rank = 0, world = 1, E = 0, d = 0, device = 0;
+    long long pmax = 0, cap = 0;
+    size_t off_meta = 0, off_x = 0, off_y = 0;
+    DevBuf shared, local;
+    std::array<char*, kEpMaxWorld> peer{};
+    std::vector<void*> opened;
+    bool open = false;
+    unsigned long long timeout_ns = 10'000'000'000ull;  // CHROMA_B200_EP_TIMEOUT_MS overrides (read at creation)
+
+    ~EpGroup() {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(device);
+        cudaDeviceSynchronize();
+        for (void* q : opened) cudaIpcCloseMemHandle(q);
+        cudaSetDevice(prev);
+    }
+
+    EpArgs args(int El) const {
+        EpArgs a{};
+        a.rank = rank;
+        a.world = world;
+        a.E = E;
+        a.El = El;
+        a.d = d;
+        a.pmax = pmax;
+        a.cap = cap;
+        for (int q = 0; q < kEpMaxWorld; ++q) a.peer[q] = peer[size_t(q)];
+        a.off_meta = off_meta;
+        a.off_x = off_x;
+        a.off_y = off_y;
+        a.epoch = local.as<unsigned>();
+        a.done = local.as<unsigned>() + 1;
+        a.timeout_ns = timeout_ns;
+        return a;
+    }
+    __nv_bfloat16* recv_rows() const { return reinterpret_cast<__nv_bfloat16*>(shared.as<char>() + off_x); }
+    __nv_bfloat16* return_rows() const { return reinterpret_cast<__nv_bfloat16*>(shared.as<char>() + off_y); }
+};
+
 struct Model {
     chroma_b200_desc desc{};
+    std::shared_ptr<EpGroup> ep;  // expert-parallel group, or null (all experts local)
+    int El = 0;                   // experts held by this program (E / world)
     Dims dm{};
     std::vector<int32_t> layer_window;
     std::vector<int64_t> offsets;
@@ -442,7 +491,8 @@ struct LargeExec {
     bf16 *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *glog = nullptr, *grouped = nullptr,
          *act = nullptr, *y = nullptr, *tf16 = nullptr, *scratch_k = nullptr, *scratch_v = nullptr;
     float *rw = nullptr, *tf32 = nullptr, *partial = nullptr;
-    int *ridx = nullptr, *perm = nullptr, *counts = nullptr, *cursor = nullptr, *offsets = nullptr, *tiles = nullptr;
+    int *ridx = nullptr, *perm = nullptr, *counts = nullptr, *cursor = nullptr, *offsets = nullptr, *tiles = nullptr,
+        *recv_total = nullptr;
     size_t arena_bytes = 0;
     int launches = 0;
 
@@ -462,11 +512,17 @@ struct LargeExec {
         key_chunk = 256;
         chunks = (ctx + n + key_chunk - 1) / key_chunk;
         const size_t heads = size_t(d.H + 2 * d.KV) * d.hd;
+        // Expert parallel: the grouped expert inputs arrive in the group's receive buffer (up to cap rows from all
+        // ranks); the expert activations and outputs cover those rows.
+        const bool ep = model.ep != nullptr;
+        if (ep && (long long)P > model.ep->pmax)
+            throw ValueError("expert-parallel group sized for fewer (token, expert) pairs than this program routes");
+        const size_t R = ep ? size_t(model.ep->cap) : P;
         std::vector<size_t> sizes = {
             N * d.d * 2, N * d.d * 2, N * heads * 2, N * d.H * d.hd * 2, N * d.H * d.hd * 2, N * d.E * 2,
-            P * d.d * 2, P * d.I * 2, P * d.d * 2, size_t(rows) * d.d * 2, N * d.KV * d.hd * 2, N * d.KV * d.hd * 2,
-            P * 4, size_t(rows) * d.d * 4, N * d.KV * d.G * size_t(chunks) * (d.hd + 2) * 4,
-            P * 4, P * 4, size_t(d.E) * 4, size_t(d.E) * 4, size_t(d.E + 1) * 4, size_t(d.E + 1) * 4,
+            ep ? 0 : P * d.d * 2, R * d.I * 2, R * d.d * 2, size_t(rows) * d.d * 2, N * d.KV * d.hd * 2,
+            N * d.KV * d.hd * 2, P * 4, size_t(rows) * d.d * 4, N * d.KV * d.G * size_t(chunks) * (d.hd + 2) * 4,
+            P * 4, P * 4, size_t(d.E) * 4, size_t(d.E) * 4, size_t(d.E + 1) * 4, size_t(d.E + 1) * 4, 4,
         };
         std::vector<size_t> off(sizes.size());
         arena_bytes = 0;
@@ -499,6 +555,7 @@ struct LargeExec {
         cursor = static_cast<int*>(at(18));
         offsets = static_cast<int*>(at(19));
         tiles = static_cast<int*>(at(20));
+        recv_total = static_cast<int*>(at(21));
         counters = DevBuf(N * d.KV * sizeof(unsigned));
         check(cudaMemset(counters.p, 0, counters.bytes), "attention counters");
     }
@@ -598,17 +655,46 @@ struct LargeExec {
             launch(s, dim3((N + 7) / 8), dim3(256), 0, k_router, glog, N, dm.E, dm.k, ridx, rw,
                    io.routes ? io.routes + size_t(l) * N * dm.k : nullptr);
             launch(s, dim3((P + 255) / 256), dim3(256), 0, k_route_count, ridx, P, counts);
-            launch(s, dim3(1), dim3(32), 0, k_route_offsets, counts, dm.E, offsets, cursor);
-            launch(s, dim3((P + 7) / 8), dim3(256), 0, k_route_scatter, ridx, P, dm.k, dm.d, xn, cursor, perm, grouped);
-            gemm(s, grouped, P, w.w1, 2 * dm.I, dm.d, kEpiSwiglu, w.b1, act, dm.I, nullptr, dm.E, offsets, err);
-            gemm(s, act, P, w.w2, dm.d, dm.I, kEpiExpert, w.b2, y, dm.d, nullptr, dm.E, offsets, err);
-            launch(s, dim3(N), dim3(256), 0, k_moe_combine, y, perm, rw, dm.k, dm.d, x);
-            launches += 11;
+            if (m->ep) {
+                enqueue_ep_experts(s, w, err);
+            } else {
+                launch(s, dim3(1), dim3(32), 0, k_route_offsets, counts, dm.E, offsets, cursor);
+                launch(s, dim3((P + 7) / 8), dim3(256), 0, k_route_scatter, ridx, P, dm.k, dm.d, xn, cursor, perm,
+                       grouped);
+                gemm(s, grouped, P, w.w1, 2 * dm.I, dm.d, kEpiSwiglu, w.b1, act, dm.I, nullptr, dm.E, offsets, err);
+                gemm(s, act, P, w.w2, dm.d, dm.I, kEpiExpert, w.b2, y, dm.d, nullptr, dm.E, offsets, err);
+                launch(s, dim3(N), dim3(256), 0, k_moe_combine, y, perm, rw, dm.k, dm.d, x);
+                launches += 3;
+            }
+            launches += 8;
         }
         launch(s, dim3(rows), dim3(256), 0, k_norm_rows, x, rows, io.rows, n, reinterpret_cast<const float*>(m->at(1)),
                dm.d, dm.eps, tf32, tf16, io.keys, err);
         ++launches;
         enqueue_vocab(s, io, err);
+    }
+
+    // The experts of one layer across the expert-parallel group (ep.cuh): counts to every rank, row plan, dispatch
+    // of the (token, slot) rows to their owners, grouped GEMMs over the rows this rank received, return of the
+    // outputs to their sources, weighted combine in slot order.
+    void enqueue_ep_experts(cudaStream_t s, const LayerW<bf16>& w, unsigned* err) {
+        const Dims& dm = m->dm;
+        const EpGroup& g = *m->ep;
+        const EpArgs a = g.args(m->El);
+        const int N = B * n, P = N * dm.k, cap = int(g.cap);
+        launch(s, dim3(1), dim3(256), 0, k_ep_push_counts, a, counts);
+        launch(s, dim3(1), dim3(32), 0, k_ep_plan, a, cursor, offsets, recv_total, err);
+        launch(s, dim3(unsigned(std::max(1, std::min((P + 7) / 8, sms * 4)))), dim3(256), 0, k_ep_dispatch, a,
+               static_cast<const int*>(ridx), P, dm.k, static_cast<const bf16*>(xn), cursor, err);
+        launch(s, dim3(1), dim3(32), 0, k_ep_wait, a, int(kEpDispatch), err);
+        gemm(s, g.recv_rows(), cap, w.w1, 2 * dm.I, dm.d, kEpiSwiglu, w.b1, act, dm.I, nullptr, m->El, offsets, err);
+        gemm(s, act, cap, w.w2, dm.d, dm.I, kEpiExpert, w.b2, y, dm.d, nullptr, m->El, offsets, err);
+        launch(s, dim3(unsigned(sms * 4)), dim3(256), 0, k_ep_return, a, static_cast<const bf16*>(y),
+               static_cast<const int*>(recv_total), err);
+        launch(s, dim3(1), dim3(32), 0, k_ep_wait, a, int(kEpCombine), err);
+        launch(s, dim3(N), dim3(256), 0, k_moe_combine, static_cast<const bf16*>(g.return_rows()),
+               static_cast<const int*>(nullptr), static_cast<const float*>(rw), dm.k, dm.d, x);
+        launches += 7;
     }
 
     void enqueue_vocab(cudaStream_t s, const GptIO& io, unsigned* err) {
@@ -934,10 +1020,20 @@ template <typename F> int guarded(char* err, size_t n, F&& f) {
     }
 }
 
+// The device error word after a call: an out-of-range index (IndexError, as runtime.h:160-162), or a bounded
+// wait that gave up (a TMA/tensor-core pipeline stage, or another rank of an expert-parallel group that did not
+// arrive).
+void raise_device_errors(unsigned word) {
+    if (word & kErrIndex) throw IndexError("Tensor index out of range");
+    if (word & kErrTimeout)
+        throw std::runtime_error("a bounded device wait timed out (an expert-parallel rank did not arrive, or a "
+                                 "pipeline stage stalled); expert-parallel groups must be recreated after this");
+}
+
 void read_error_word(cudaStream_t s, DevBuf& err, unsigned* host) {
     check(cudaMemcpyAsync(host, err.p, sizeof(unsigned), cudaMemcpyDeviceToHost, s), "Read index error");
     check(cudaStreamSynchronize(s), "CUDA execution");
-    if (*host & kErrIndex) throw IndexError("Tensor index out of range");
+    raise_device_errors(*host);
 }
 
 }  // namespace
@@ -945,7 +1041,7 @@ void read_error_word(cudaStream_t s, DevBuf& err, unsigned* host) {
 extern "C" {
 
 static void create_program(const chroma_b200_desc* desc, const char* weights_path, const void* device_weights,
-                           chroma_b200_program** out);
+                           chroma_b200_program** out, std::shared_ptr<EpGroup> ep = nullptr);
 
 int chroma_b200_create(const chroma_b200_desc* desc, const char* weights_path, chroma_b200_program** out, char* err,
                        size_t err_len) {
@@ -963,12 +1059,101 @@ int chroma_b200_create_device(const chroma_b200_desc* desc, const void* device_w
     });
 }
 
+struct chroma_b200_ep {
+    std::shared_ptr<EpGroup> group;
+};
+
+int chroma_b200_ep_create(int32_t rank, int32_t world, int64_t max_pairs, int32_t hidden, int32_t experts,
+                          chroma_b200_ep** out, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!out) throw ValueError("null argument");
+        if (world < 1 || world > kEpMaxWorld || rank < 0 || rank >= world)
+            throw ValueError("expert-parallel rank/world out of range (world <= 8)");
+        if (experts < 1 || experts > kEpMaxExperts || experts % world)
+            throw ValueError("experts must divide evenly over the group (at most 256)");
+        if (hidden < 8 || hidden % 8 || max_pairs < 1 || max_pairs > (int64_t(1) << 31) / world)
+            throw ValueError("expert-parallel buffer shape out of range");
+        auto g = std::make_shared<EpGroup>();
+        check(cudaGetDevice(&g->device), "cudaGetDevice");
+        g->rank = rank;
+        g->world = world;
+        g->E = experts;
+        g->d = hidden;
+        g->pmax = max_pairs;
+        g->cap = max_pairs * world;
+        auto align = [](size_t b) { return (b + 1023) / 1024 * 1024; };
+        g->off_meta = align(sizeof(EpHeader));
+        g->off_x = g->off_meta + align(size_t(g->cap) * 4);
+        g->off_y = g->off_x + align(size_t(g->cap) * hidden * 2);
+        g->shared = DevBuf(g->off_y + align(size_t(max_pairs) * hidden * 2));
+        check(cudaMemset(g->shared.p, 0, g->off_x), "expert-parallel header");
+        g->local = DevBuf(256);
+        check(cudaMemset(g->local.p, 0, 256), "expert-parallel counters");
+        check(cudaDeviceSynchronize(), "expert-parallel init");
+        g->peer[size_t(rank)] = g->shared.as<char>();
+        if (const char* ms = std::getenv("CHROMA_B200_EP_TIMEOUT_MS")) {
+            const long long v = std::atoll(ms);
+            if (v > 0) g->timeout_ns = (unsigned long long)v * 1000000ull;
+        }
+        *out = new chroma_b200_ep{std::move(g)};
+    });
+}
+
+int chroma_b200_ep_handle(const chroma_b200_ep* ep, void* handle, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!ep || !handle) throw ValueError("null argument");
+        cudaIpcMemHandle_t h;
+        check(cudaIpcGetMemHandle(&h, ep->group->shared.p), "cudaIpcGetMemHandle");
+        std::memcpy(handle, &h, sizeof(h));
+    });
+}
+
+int chroma_b200_ep_open(chroma_b200_ep* ep, const void* handles, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!ep || !handles) throw ValueError("null argument");
+        EpGroup& g = *ep->group;
+        if (g.open) throw ValueError("expert-parallel group already open");
+        const char* h = static_cast<const char*>(handles);
+        for (int q = 0; q < g.world; ++q) {
+            if (q == g.rank) continue;
+            cudaIpcMemHandle_t mh;
+            std::memcpy(&mh, h + size_t(q) * sizeof(mh), sizeof(mh));
+            void* ptr = nullptr;
+            check(cudaIpcOpenMemHandle(&ptr, mh, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+            g.opened.push_back(ptr);
+            g.peer[size_t(q)] = static_cast<char*>(ptr);
+        }
+        g.open = true;
+    });
+}
+
+void chroma_b200_ep_destroy(chroma_b200_ep* ep) { delete ep; }
+
+int chroma_b200_create_ep(const chroma_b200_desc* desc, const char* weights_path, const void* device_weights,
+                          chroma_b200_ep* ep, chroma_b200_program** out, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!desc || !ep || !out || (weights_path == nullptr) == (device_weights == nullptr))
+            throw ValueError("null argument (exactly one of weights_path / device_weights)");
+        create_program(desc, weights_path, device_weights, out, ep->group);
+    });
+}
+
 }  // extern "C"
 
 static void create_program(const chroma_b200_desc* desc, const char* weights_path, const void* device_weights,
-                           chroma_b200_program** out) {
+                           chroma_b200_program** out, std::shared_ptr<EpGroup> ep) {
     {
         validate_desc(*desc);
+        if (ep) {
+            if (!ep->open) throw ValueError("expert-parallel group not opened (exchange the handles first)");
+            if (!is_large(*desc) || desc->kind == CHROMA_B200_MICRO)
+                throw ValueError("expert parallelism needs a large-width bf16 GPT-OSS program (hidden >= 1024, head_dim 64)");
+            if (desc->experts != ep->E || desc->hidden != ep->d)
+                throw ValueError("program and expert-parallel group disagree on experts / hidden size");
+            int dev = 0;
+            check(cudaGetDevice(&dev), "cudaGetDevice");
+            if (dev != ep->device) throw ValueError("expert-parallel group lives on another device");
+        }
         auto p = std::make_unique<chroma_b200_program>();
         check(cudaGetDevice(&p->device), "cudaGetDevice");
         cudaDeviceProp prop{};
@@ -979,6 +1164,8 @@ static void create_program(const chroma_b200_desc* desc, const char* weights_pat
         Model& m = p->model;
         m.desc = *desc;
         m.device = p->device;
+        m.ep = ep;
+        m.El = ep ? desc->experts / ep->world : desc->experts;
         m.offsets.assign(desc->offsets, desc->offsets + desc->num_offsets);
         for (int64_t off : m.offsets)
             if (off < 0 || off >= desc->weight_bytes || off % 16) throw ValueError("weight offset out of range or unaligned");
@@ -1138,7 +1325,7 @@ int chroma_b200_check(chroma_b200_program* p, void* stream, char* err, size_t er
         check(cudaMemcpyAsync(eh, p->err.p, sizeof(unsigned), cudaMemcpyDeviceToHost, s), "Read index error");
         check(cudaMemsetAsync(p->err.p, 0, sizeof(unsigned), s), "Reset index error");
         check(cudaStreamSynchronize(s), "CUDA execution");
-        if (*eh & kErrIndex) throw IndexError("Tensor index out of range");
+        raise_device_errors(*eh);
     });
 }
 
@@ -1365,7 +1552,7 @@ int chroma_b200_decoder_step(chroma_b200_decoder* d, int32_t use_decode, const i
                 check(cudaMemcpyAsync(logits, d->logits.p, size_t(d->B) * d->V * d->es, cudaMemcpyDeviceToHost, s),
                       "Download logits");
             check(cudaStreamSynchronize(s), "CUDA execution");
-            if (*eh & kErrIndex) throw IndexError("Tensor index out of range");
+            raise_device_errors(*eh);
             if (argmax)
                 for (int b = 0; b < d->B; ++b) argmax[b] = argmax_index(static_cast<unsigned long long>(am[b]));
         } catch (...) {
@@ -1426,6 +1613,7 @@ int chroma_b200_decoder_advance(chroma_b200_decoder* d, const int64_t* tokens, c
             d->advance_graph = Graph();
         }
         check(cudaMemsetAsync(d->counter.p, 0, sizeof(int), s), "advance counter");
+        check(cudaMemsetAsync(d->err.p, 0, sizeof(unsigned), s), "Reset index error");
         GptExec& e = d->ex[1];
         for (int i = 0; i < steps; ++i) {
             d->advance_graph.run(s, [&](cudaStream_t st) {
@@ -1455,7 +1643,7 @@ int chroma_b200_decoder_advance(chroma_b200_decoder* d, const int64_t* tokens, c
             check(cudaMemcpyAsync(ids, d->record.p, size_t(steps) * d->B * 8, cudaMemcpyDeviceToHost, s), "advance ids");
             check(cudaMemcpyAsync(eh, d->err.p, sizeof(unsigned), cudaMemcpyDeviceToHost, s), "Read index error");
             check(cudaStreamSynchronize(s), "advance");
-            if (*eh & kErrIndex) throw IndexError("Tensor index out of range");
+            raise_device_errors(*eh);
         }
     });
 }

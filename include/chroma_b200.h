@@ -167,6 +167,33 @@ int chroma_b200_decoder_read(chroma_b200_decoder* decoder, void* keys, void* val
                              size_t err_len);
 void chroma_b200_decoder_destroy(chroma_b200_decoder* decoder);
 
+/* ---- Expert parallelism across the GPUs of one node ---------------------------------------------------------------
+ * No reference counterpart: the reference runs every expert on one device (the MoE einsums of
+ * chroma/models/gpt_oss.py:243-265 lowered by chroma/_src/codegen/gpu.py:390-424). Here rank r of a group of `world`
+ * processes (one GPU each) owns experts [r*E/world, (r+1)*E/world) and exchanges the routed rows with the other ranks
+ * through their device memory (NVLink peer stores, no host round trip, capturable in CUDA graphs).
+ *
+ * Setup, once per process: create the group on the current device, export this rank's handle, gather every rank's
+ * handle in rank order through any host channel (e.g. torch.distributed), open them. Then create programs with
+ * chroma_b200_create_ep: their weights hold the local experts only (tensors 9-12 of each layer with E/world experts;
+ * the router weights stay [E, d]). All ranks must run the same programs in the same order: every MoE layer waits
+ * (bounded, ~1 s) for all ranks; a rank that does not arrive turns into a RUNTIME error on the others. */
+#define CHROMA_B200_EP_HANDLE_BYTES 64
+typedef struct chroma_b200_ep chroma_b200_ep;
+/* `max_pairs`: the most (token, expert) pairs one call of any program on this rank routes (rows x top_k). */
+int chroma_b200_ep_create(int32_t rank, int32_t world, int64_t max_pairs, int32_t hidden, int32_t experts,
+                          chroma_b200_ep** out, char* err, size_t err_len);
+/* Writes CHROMA_B200_EP_HANDLE_BYTES bytes identifying this rank's shared buffer to other processes. */
+int chroma_b200_ep_handle(const chroma_b200_ep* ep, void* handle, char* err, size_t err_len);
+/* `handles`: world x CHROMA_B200_EP_HANDLE_BYTES bytes, every rank's handle in rank order. */
+int chroma_b200_ep_open(chroma_b200_ep* ep, const void* handles, char* err, size_t err_len);
+/* The group stays alive while programs created on it do. */
+void chroma_b200_ep_destroy(chroma_b200_ep* ep);
+/* chroma_b200_create (weights_path) or chroma_b200_create_device (device_weights) for an expert-parallel program:
+ * exactly one of the two is non-NULL. */
+int chroma_b200_create_ep(const chroma_b200_desc* desc, const char* weights_path, const void* device_weights,
+                          chroma_b200_ep* ep, chroma_b200_program** out, char* err, size_t err_len);
+
 #ifdef __cplusplus
 }
 #endif
