@@ -55,6 +55,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--skip-c4", action="store_true", help="skip the GPT-OSS-20B-shaped prefill measurement")
     ap.add_argument("--c4-only", action="store_true", help="run only the GPT-OSS-20B-shaped prefill measurement")
     ap.add_argument("--c4-layers", type=int, default=0, help="layers of the C4 model (0: all 24; fewer for profiling)")
+    ap.add_argument("--skip-c5", action="store_true", help="skip the GPT-OSS-120B-shaped decode (multi-GPU runs)")
+    ap.add_argument("--c5-only", action="store_true", help="run only the GPT-OSS-120B-shaped decode (needs >= 2 GPUs)")
+    ap.add_argument("--c5-layers", type=int, default=0, help="layers of the C5 model (0: all 36)")
     return ap.parse_args()
 
 
@@ -254,6 +257,91 @@ def bench_c4(args: argparse.Namespace, rng: np.random.Generator, max_over_ranks,
     }
 
 
+def bench_c5(args: argparse.Namespace, max_over_ranks, barrier, rank: int, world: int) -> dict:  # type: ignore[no-untyped-def]
+    """GPT-OSS-120B-shaped greedy decode (config C5): 256 sequences over all ranks (256 / world each, data parallel
+    attention), a 4,096-token bf16 cache per sequence filled with N(0, 1) values, current tokens at position 4,096;
+    the 128 experts split over the ranks (expert parallel over NVLink peer memory). One step = one token for every
+    sequence: 36 layers, vocab projection, argmax fed back, all on the device (``BatchDecoder.advance_device``)."""
+    import torch
+
+    import chroma_b200
+    from chroma_b200 import models
+    from chroma_b200._src.compiler import synthetic_gptoss
+    from chroma_b200._src.native import Native
+
+    cfg = models.gpt_oss_120b
+    if args.c5_layers:
+        cfg = dataclasses.replace(cfg, num_hidden_layers=args.c5_layers)
+    total, ctx = 256, 4096
+    if total % world or (world < 2 and not args.c5_layers):
+        return {"unavailable": "C5 needs 2 or more GPUs dividing 256 sequences (233 GB of expert weights); "
+                               "one GPU runs it only with fewer layers (--c5-layers)"}
+    B, L, KV, hd = total // world, cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim
+    plan, regions = synthetic_gptoss(cfg, steps=1, context=ctx, ep_world=world)
+    wbuf = torch.empty(plan["desc"]["weight_bytes"], dtype=torch.uint8, device="cuda")
+    shared_gen = torch.Generator(device="cuda").manual_seed(50)
+    expert_gen = torch.Generator(device="cuda").manual_seed(5000 + rank)
+    for name, off, numel, is_norm in regions:
+        if is_norm:
+            wbuf[off : off + numel * 4].view(torch.float32).fill_(1.0)
+        else:
+            gen = expert_gen if ".mlp.mlp" in name else shared_gen
+            wbuf[off : off + numel * 2].view(torch.bfloat16).normal_(0.0, 0.02, generator=gen)
+    group = chroma_b200.ExpertGroup(rank, world, max_pairs=B * cfg.experts_per_token, hidden=cfg.hidden_size,
+                                    experts=cfg.num_experts, exchange=None if world > 1 else (lambda h: [h]))
+    pre = chroma_b200.Program.from_native(Native(plan, device_weights=wbuf.data_ptr(), ep=group))
+    dec = chroma_b200.Program.from_native(Native(plan, device_weights=wbuf.data_ptr(), ep=group))
+    bd = chroma_b200.BatchDecoder(pre, dec, B)
+    cache_gen = torch.Generator(device="cuda").manual_seed(700 + rank)
+    for b in range(B):  # one sequence at a time keeps the staging small
+        k = torch.randn((1, L, ctx, KV, hd), generator=cache_gen, device="cuda").to(torch.bfloat16)
+        v = torch.randn((1, L, ctx, KV, hd), generator=cache_gen, device="cuda").to(torch.bfloat16)
+        bd.load_cache(b, k, v, np.array([ctx]))
+    del k, v
+    torch.cuda.synchronize()
+    tokens = np.random.default_rng(900 + rank).integers(0, cfg.vocab_size, B)
+    barrier()
+    bd.generate(tokens, 1)  # consumes the current tokens (position 4096) and leaves the argmax on the device
+    stream = torch.cuda.current_stream()
+    warm = max(3, args.warmup)
+    barrier()
+    bd.advance_device(warm, stream.cuda_stream)
+    steps = max(10, min(50, args.steps))
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    bd.advance_device(steps, stream.cuda_stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    ids = bd.generate(np.asarray(tokens), 1)[:, 0]
+    barrier()
+    d, I, E, k_ = cfg.hidden_size, cfg.intermediate_size, cfg.num_experts, cfg.experts_per_token
+    expert_bytes = (2 * I * d + d * I + 2 * I + d) * 2
+    attn_bytes = ((cfg.num_attention_heads + 2 * KV) * hd * d + d * cfg.num_attention_heads * hd) * 2
+    per_rank = L * ((E // world) * expert_bytes + attn_bytes + E * d * 2 + B * ctx * KV * hd * 2 * 2)
+    per_rank += cfg.vocab_size * d * 2
+    bd.close()
+    del pre, dec
+    group.close()
+    del wbuf
+    torch.cuda.empty_cache()
+    pk = peaks()["hbm_gbs"]
+    return {
+        "workload": f"C5: GPT-OSS-120B-shaped greedy decode ({L} layers, d=2880, 64/8 heads, 128 experts top-4, bf16 "
+                    f"N(0,0.02)), {total} sequences ({B} per GPU) with a 4,096-token bf16 cache, {world} GPUs, "
+                    f"{E // world} experts per GPU (NVLink peer-memory dispatch/return), vocab replicated",
+        "tokens_per_s": total * steps / t, "ms_per_step": t * 1e3 / steps, "steps": steps, "n_gpus": world,
+        "scaling": "strong (256 sequences in total)",
+        "hbm_bytes_per_step_per_gpu": per_rank,
+        "roofline_frac": per_rank / (t / steps) / 1e9 / pk,
+        "roofline_note": "all experts of the rank assumed touched (B x top-4 routes over E / world experts); "
+                         "measured copy peak of one GPU",
+        "e2e": None,
+        "argmax_head": [int(v) for v in ids[:2]],
+    }
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
@@ -292,6 +380,13 @@ def main() -> None:
     # streams) and the CUDA events below bracket exactly the queued work.
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
+    if args.c5_only:
+        c5 = bench_c5(args, max_over_ranks, barrier, rank, world)
+        if rank == 0:
+            print(json.dumps({"c5_decode": c5}), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
     if args.c4_only:
         c4 = bench_c4(args, np.random.default_rng(rank), max_over_ranks, barrier, rank, world)
         if rank == 0:
@@ -465,6 +560,8 @@ def main() -> None:
     del mout
 
     c4 = bench_c4(args, rng, max_over_ranks, barrier, rank, world) if not args.skip_c4 else None
+    # C5 needs the experts of the 120B-shaped model spread over 2 or more GPUs.
+    c5 = bench_c5(args, max_over_ranks, barrier, rank, world) if world > 1 and not args.skip_c5 else None
 
     cpu = None
     if rank == 0 and world == 1:
@@ -516,6 +613,7 @@ def main() -> None:
                   "device_us": micro_t * 1e6, "algorithmic_bytes": micro_bytes,
                   "achieved_gbs": micro_bytes / micro_t / 1e9, "frac": micro_bytes / micro_t / 1e9 / pk["hbm_gbs"]},
         "c4_prefill": c4,
+        "c5_decode": c5,
         "fwd8": {"device_ms": fwd_dev_ms, "e2e_ms": fwd_e2e_ms, "vs_a100_e2e": A100_FWD8_MS / fwd_e2e_ms,
                  "h2d_bytes": 64, "d2h_bytes": 8 * V * 4, "api": "Program(tokens[8], out=logits)"},
     }

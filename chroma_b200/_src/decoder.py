@@ -21,6 +21,8 @@ return greedy argmax ids instead of logits (the ids are computed on the device).
 
 from __future__ import annotations
 
+import ctypes
+
 import threading
 from collections.abc import Sequence
 from dataclasses import dataclass, replace
@@ -407,6 +409,30 @@ class BatchDecoder:
             self._native.advance(tokens, self._position, steps, 0, ids)
             self._position = self._position + steps
             return ids.T.copy()
+
+    def load_cache(self, first: int, keys: Any, values: Any, positions: np.ndarray) -> None:
+        """Install committed caches for sequences [first, first + len(positions)): ``keys``/``values`` shaped
+        [count, layers, context, kv_heads, head_dim] in the cache dtype, as NumPy arrays or CUDA tensors (anything
+        with ``data_ptr()``); ``positions`` [count] = tokens already in each sequence. The ring then holds each
+        sequence's last ``context`` positions (slot = position % context), and its next token is at ``positions``."""
+        pos = np.asarray(positions, np.int64).reshape(-1)
+        count = len(pos)
+        slots = np.full((count, self.context), -1, np.int64)
+        for i, p in enumerate(pos):
+            held = np.arange(max(0, int(p) - self.context), int(p), dtype=np.int64)
+            slots[i, held % self.context] = held
+
+        def ptr(a: Any) -> int:
+            if hasattr(a, "data_ptr"):
+                return int(a.data_ptr())
+            a = np.ascontiguousarray(a)
+            return int(a.ctypes.data)
+
+        with self._lock:
+            self._flush()
+            nat.call("chroma_b200_decoder_write", self._native.handle, int(first), count, nat._VP(ptr(keys)),
+                     nat._VP(ptr(values)), slots.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)))
+            self._position[first : first + count] = pos
 
     def advance_device(self, steps: int, stream: int) -> None:
         """Continue greedy decoding from the device state left by ``generate`` without any host transfer; queued on

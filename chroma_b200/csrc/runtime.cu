@@ -487,6 +487,8 @@ static bool is_large(const chroma_b200_desc& d) {
 struct LargeExec {
     const Model* m = nullptr;
     int B = 1, n = 1, ctx = 0, mask_mode = kMaskBuffer, window = 0, sms = 148, chunks = 1, key_chunk = 256, rows = 1;
+    int fd_splits = 1, fd_split_keys = 64;  // flash decoding: key splits per (sequence, KV head)
+    float* fd_part = nullptr;
     DevBuf arena, counters;
     bf16 *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *glog = nullptr, *grouped = nullptr,
          *act = nullptr, *y = nullptr, *tf16 = nullptr, *scratch_k = nullptr, *scratch_v = nullptr;
@@ -518,11 +520,20 @@ struct LargeExec {
         if (ep && (long long)P > model.ep->pmax)
             throw ValueError("expert-parallel group sized for fewer (token, expert) pairs than this program routes");
         const size_t R = ep ? size_t(model.ep->cap) : P;
+        // Flash decoding splits: enough CTAs to fill the GPU a few times over, whole 64-key tiles per split.
+        if (ctx > 0) {
+            const int tiles = (ctx + kFdKeys - 1) / kFdKeys;
+            const int want = std::max(1, (sms * 6 + B * d.KV - 1) / (B * d.KV));
+            fd_splits = std::min(tiles, want);
+            fd_split_keys = (tiles + fd_splits - 1) / fd_splits * kFdKeys;
+            fd_splits = (ctx + fd_split_keys - 1) / fd_split_keys;
+        }
         std::vector<size_t> sizes = {
             N * d.d * 2, N * d.d * 2, N * heads * 2, N * d.H * d.hd * 2, N * d.H * d.hd * 2, N * d.E * 2,
             ep ? 0 : P * d.d * 2, R * d.I * 2, R * d.d * 2, size_t(rows) * d.d * 2, N * d.KV * d.hd * 2,
             N * d.KV * d.hd * 2, P * 4, size_t(rows) * d.d * 4, N * d.KV * d.G * size_t(chunks) * (d.hd + 2) * 4,
             P * 4, P * 4, size_t(d.E) * 4, size_t(d.E) * 4, size_t(d.E + 1) * 4, size_t(d.E + 1) * 4, 4,
+            size_t(B) * d.KV * fd_splits * kFdRows * (2 + kFaDim) * 4,
         };
         std::vector<size_t> off(sizes.size());
         arena_bytes = 0;
@@ -556,6 +567,7 @@ struct LargeExec {
         offsets = static_cast<int*>(at(19));
         tiles = static_cast<int*>(at(20));
         recv_total = static_cast<int*>(at(21));
+        fd_part = static_cast<float*>(at(22));
         counters = DevBuf(N * d.KV * sizeof(unsigned));
         check(cudaMemset(counters.p, 0, counters.bytes), "attention counters");
     }
@@ -629,6 +641,25 @@ struct LargeExec {
                 fa.pos0 = mask_mode == kMaskSlots ? io.pos0 : nullptr;
                 if (mask_mode != kMaskSlots) fa.ctx = 0;
                 launch(s, dim3((n + kFaRows - 1) / kFaRows, dm.H, B), dim3(kFaThreads), kFaSmemBytes, k_flash_prefill, q, fa, ck, cv,
+                       static_cast<const bf16*>(nk), static_cast<const bf16*>(nv), w.sinks, attn);
+            } else if (mask_mode == kMaskSlots && n * dm.G <= kFdRows) {
+                DecodeArgs a;
+                a.n = n;
+                a.ctx = ctx;
+                a.B = B;
+                a.H = dm.H;
+                a.KV = dm.KV;
+                a.G = dm.G;
+                a.splits = fd_splits;
+                a.split_keys = fd_split_keys;
+                a.cache_seq_stride = size_t(L) * ctx * dm.KV * dm.hd;
+                a.window = win;
+                a.scale_log2 = dm.sm_scale * 1.4426950408889634f;
+                a.slots = io.slots;
+                a.pos0 = io.pos0;
+                a.part = fd_part;
+                a.counters = counters.as<unsigned>();
+                launch(s, dim3(B, dm.KV, fd_splits), dim3(kFdThreads), kFdSmemBytes, k_flash_decode, q, a, ck, cv,
                        static_cast<const bf16*>(nk), static_cast<const bf16*>(nv), w.sinks, attn);
             } else {
                 AttnArgs a;
@@ -1681,6 +1712,25 @@ int chroma_b200_decoder_read(chroma_b200_decoder* d, void* keys, void* values, i
         if (values) check(cudaMemcpyAsync(values, d->cache_v.p, d->cache_v.bytes, cudaMemcpyDeviceToHost, d->stream), "read");
         if (slots) check(cudaMemcpyAsync(slots, d->slots.p, d->slots.bytes, cudaMemcpyDeviceToHost, d->stream), "read");
         check(cudaStreamSynchronize(d->stream), "read");
+    });
+}
+
+int chroma_b200_decoder_write(chroma_b200_decoder* d, int32_t first, int32_t count, const void* keys,
+                              const void* values, const int64_t* slots, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!d || !keys || !values || !slots) throw ValueError("null argument");
+        if (first < 0 || count < 1 || first + count > d->B) throw ValueError("sequence range outside the batch");
+        DeviceGuard guard(d->device);
+        const size_t per_seq = d->cache_k.bytes / size_t(d->B);
+        const size_t slot_bytes = size_t(d->ctx) * 8;
+        char* ck = d->cache_k.as<char>() + size_t(first) * per_seq;
+        char* cv = d->cache_v.as<char>() + size_t(first) * per_seq;
+        check(cudaMemcpyAsync(ck, keys, size_t(count) * per_seq, cudaMemcpyDefault, d->stream), "write keys");
+        check(cudaMemcpyAsync(cv, values, size_t(count) * per_seq, cudaMemcpyDefault, d->stream), "write values");
+        check(cudaMemcpyAsync(d->slots.as<char>() + size_t(first) * slot_bytes, slots, size_t(count) * slot_bytes,
+                              cudaMemcpyDefault, d->stream),
+              "write slots");
+        check(cudaStreamSynchronize(d->stream), "write");
     });
 }
 

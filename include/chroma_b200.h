@@ -165,6 +165,13 @@ int chroma_b200_decoder_reset(chroma_b200_decoder* decoder, char* err, size_t er
 /* Copies the committed cache and slot positions to host buffers ([batch, L, ctx, KV, hd] twice, [batch, ctx]). */
 int chroma_b200_decoder_read(chroma_b200_decoder* decoder, void* keys, void* values, int64_t* slots, char* err,
                              size_t err_len);
+/* Inverse of decoder_read for sequences [first, first + count): writes their committed cache ([count, L, ctx, KV,
+ * hd] keys and values in the cache's storage type) and slot positions ([count, ctx], -1 = empty). Host or device
+ * pointers (unified addressing). Rows staged by a step and not yet committed must be committed first. For caches
+ * restored from elsewhere and for synthetic benchmark caches. No reference counterpart (the reference passes the
+ * whole cache in with every call, decoder.py:115-130). */
+int chroma_b200_decoder_write(chroma_b200_decoder* decoder, int32_t first, int32_t count, const void* keys,
+                              const void* values, const int64_t* slots, char* err, size_t err_len);
 void chroma_b200_decoder_destroy(chroma_b200_decoder* decoder);
 
 /* ---- Expert parallelism across the GPUs of one node ---------------------------------------------------------------
