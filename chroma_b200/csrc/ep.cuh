@@ -6,16 +6,15 @@
 // chroma/_src/codegen/gpu.py:390-424) never needed is done with stores into the peers' memory, so no host round
 // trip or library collective sits between the routing and the expert GEMMs:
 //
-//   k_ep_push_counts  routed (token, slot) counts per global expert -> every peer's count table [src][E]; flag
-//   k_ep_plan         wait for all count tables; per owner and expert the row where this rank's rows start in the
-//                     owner's grouped layout (expert-major, source-rank minor), and the local groups' row offsets
+//   k_ep_counts       routed (token, slot) counts per global expert -> every peer's count table [src][E]; flag;
+//                     wait for all tables; per owner and expert the row where this rank's rows start in the owner's
+//                     grouped layout (expert-major, source-rank minor), and the local groups' row offsets
 //   k_ep_dispatch     each (token, slot) claims a row and stores the token's normalised activations plus its origin
 //                     (src rank, pair index) into the owning rank's receive buffer; the last CTA flags every peer
-//   k_ep_wait         wait until every peer's flag for this phase reaches the layer's epoch
-//   (local grouped SwiGLU GEMM + expert GEMM over the received rows)
+//   (local grouped SwiGLU GEMM, whose prologue waits for every rank's dispatch flag, + expert GEMM)
 //   k_ep_return       each received row's expert output goes back to its source rank's return buffer at the pair
 //                     index; the last CTA flags every peer
-//   (k_ep_wait, then k_moe_combine over the returned rows in slot order)
+//   (k_moe_combine waits for every rank's return flag, then sums the returned rows in slot order)
 //
 // Synchronisation: each phase has a flag per source rank in the receiver's memory. Flags only grow: the sender
 // writes the layer's epoch (a device counter every rank advances once per MoE layer, so all ranks agree) with a
@@ -59,37 +58,6 @@ struct EpArgs {
 
 __device__ __forceinline__ EpHeader* ep_header(const EpArgs& a, int r) { return reinterpret_cast<EpHeader*>(a.peer[r]); }
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Bounded wait of one thread until *flag >= epoch (flags never decrease; wrap-safe comparison). Gives up after
-// `timeout_ns` of wall time (the global timer), raising kErrTimeout.
-__device__ __forceinline__ bool ep_wait_flag(const unsigned* flag, unsigned epoch, unsigned long long timeout_ns,
-                                             unsigned* err) {
-    const unsigned long long start = global_ns();
-    for (unsigned i = 0;; ++i) {
-        if (int(ld_acquire_sys(flag) - epoch) >= 0) return true;
-        if ((i & 63) == 63) {
-            if (global_ns() - start > timeout_ns) break;
-            __nanosleep(256);
-        }
-    }
-    atomicOr(err, kErrTimeout);
-    return false;
-}
-
 __device__ __forceinline__ unsigned* ep_flag(const EpArgs& a, int owner, int phase, int src) {
     EpHeader* h = ep_header(a, owner);
     return phase == kEpCounts ? &h->cnt_flag[src] : (phase == kEpDispatch ? &h->disp_flag[src] : &h->comb_flag[src]);
@@ -115,15 +83,20 @@ __device__ __forceinline__ void ep_signal_when_last(const EpArgs& a, int phase) 
     }
 }
 
-// 1 CTA. Advances the epoch, copies this rank's per-expert counts into every peer's table, flags them, and clears
-// the counts for the next layer.
-__global__ void k_ep_push_counts(EpArgs a, int* __restrict__ counts) {
+// 1 CTA. Advances the epoch, copies this rank's per-expert counts into every peer's table and flags them, clears
+// the counts for the next layer, waits for every rank's counts, then plans the rows: cursor[e] = first row of this
+// rank's rows for global expert e in the owner's receive buffer; offsets[0..El] = row offsets of the local experts'
+// groups; *recv_total = offsets[El].
+__global__ void k_ep_counts(EpArgs a, int* __restrict__ counts, int* __restrict__ cursor, int* __restrict__ offsets,
+                            int* __restrict__ recv_total, unsigned* err) {
     __shared__ unsigned epoch;
+    __shared__ int ok;
     pdl_wait();
     pdl_trigger();
     if (threadIdx.x == 0) {
         epoch = *a.epoch + 1u;
         *a.epoch = epoch;
+        ok = 1;
     }
     __syncthreads();
     for (int i = threadIdx.x; i < a.world * a.E; i += blockDim.x) {
@@ -134,19 +107,8 @@ __global__ void k_ep_push_counts(EpArgs a, int* __restrict__ counts) {
     __syncthreads();
     if (threadIdx.x < unsigned(a.world)) st_release_sys(ep_flag(a, int(threadIdx.x), kEpCounts, a.rank), epoch);
     for (int e = threadIdx.x; e < a.E; e += blockDim.x) counts[e] = 0;
-}
-
-// 1 CTA. Waits for every rank's counts, then: cursor[e] = first row of this rank's rows for global expert e in the
-// owner's receive buffer; offsets[0..El] = row offsets of the local experts' groups; *recv_total = offsets[El].
-__global__ void k_ep_plan(EpArgs a, int* __restrict__ cursor, int* __restrict__ offsets, int* __restrict__ recv_total,
-                          unsigned* err) {
-    __shared__ int ok;
-    pdl_wait();
-    pdl_trigger();
-    if (threadIdx.x == 0) ok = 1;
-    __syncthreads();
-    const unsigned epoch = *reinterpret_cast<volatile unsigned*>(a.epoch);
-    if (threadIdx.x < unsigned(a.world) && !ep_wait_flag(&ep_header(a, a.rank)->cnt_flag[threadIdx.x], epoch, a.timeout_ns, err))
+    if (threadIdx.x < unsigned(a.world) &&
+        !wait_flag_geq(&ep_header(a, a.rank)->cnt_flag[threadIdx.x], epoch, a.timeout_ns, err))
         ok = 0;
     __syncthreads();
     if (!ok) return;
@@ -169,6 +131,14 @@ __global__ void k_ep_plan(EpArgs a, int* __restrict__ cursor, int* __restrict__ 
             if (row > a.cap) atomicOr(err, kErrIndex);
         }
     }
+}
+
+// Wait of the first `world` threads of a CTA for every rank's flag of `phase` to reach the current epoch; returns
+// false (error raised) if a wait gave up. The caller synchronises the CTA afterwards.
+__device__ __forceinline__ bool ep_wait_all(const EpArgs& a, int phase, unsigned* err) {
+    if (threadIdx.x >= unsigned(a.world)) return true;
+    const unsigned epoch = *reinterpret_cast<volatile unsigned*>(a.epoch);
+    return wait_flag_geq(ep_flag(a, a.rank, phase, int(threadIdx.x)), epoch, a.timeout_ns, err);
 }
 
 // One warp per (token, slot) pair, grid-stride. Stores the token's row and its origin into the owner's buffers.
@@ -197,14 +167,6 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(EpArgs a, const int* __rest
         for (int c = lane; c < a.d / 8; c += 32) dst[c] = src[c];
     }
     ep_signal_when_last(a, kEpDispatch);
-}
-
-// 1 CTA: wait until every rank raised its flag for `phase` on this rank.
-__global__ void k_ep_wait(EpArgs a, int phase, unsigned* err) {
-    pdl_wait();
-    pdl_trigger();
-    const unsigned epoch = *reinterpret_cast<volatile unsigned*>(a.epoch);
-    if (threadIdx.x < unsigned(a.world)) ep_wait_flag(ep_flag(a, a.rank, phase, int(threadIdx.x)), epoch, a.timeout_ns, err);
 }
 
 // One warp per received row, grid-stride: the expert output row goes back to its source rank's return buffer.

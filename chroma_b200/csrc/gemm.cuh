@@ -45,7 +45,12 @@ struct GemmArgs {
     float alpha, limit;             // SwiGLU slope and clamp
     int groups;                     // 1 for a dense GEMM
     const int* offsets;             // [groups + 1] row offsets of each group in A (device), or nullptr (dense)
-    const int* tile_starts;         // [groups + 1] prefix sums of 128-row tiles per group (device), or nullptr
+    // Optional: A (and the offsets) are written by other GPUs; wait until each of wait_count flags reaches *wait_epoch
+    // (expert-parallel dispatch) before reading them.
+    const unsigned* wait_flags;
+    int wait_count;
+    const unsigned* wait_epoch;
+    unsigned long long wait_timeout_ns;
 };
 
 __device__ __forceinline__ float round_bf16(float x) { return bf16_round(x); }
@@ -225,9 +230,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
     // Weights and activations of this GEMM are produced by earlier kernels: wait before reading the offsets.
     pdl_wait();
     pdl_trigger();
-    for (int i = threadIdx.x; i <= g.groups; i += blockDim.x) {
-        s_offsets[i] = g.offsets ? g.offsets[i] : (i == 0 ? 0 : g.M);
-        s_tiles[i] = g.tile_starts ? g.tile_starts[i] : (i == 0 ? 0 : (g.M + kGemmBM - 1) / kGemmBM);
+    __syncthreads();  // barrier and abort_flag initialisation visible to every thread
+    if (g.wait_flags && int(threadIdx.x) < g.wait_count &&
+        !wait_flag_geq(g.wait_flags + threadIdx.x, *reinterpret_cast<const volatile unsigned*>(g.wait_epoch),
+                       g.wait_timeout_ns, err))
+        abort_flag = 1;  // published by the __syncthreads below, before any role starts
+    for (int i = threadIdx.x; i <= g.groups; i += blockDim.x) s_offsets[i] = g.offsets ? g.offsets[i] : (i == 0 ? 0 : g.M);
+    __syncthreads();
+    if (warp == 0) {
+        // s_tiles[grp] = sum over earlier groups of ceil(rows / 128): lane l scans groups [8l, 8l + 8), then the lanes'
+        // totals are scanned across the warp (groups <= 256).
+        int local[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int grp = lane * 8 + j;
+            local[j] = sum;
+            if (grp < g.groups) sum += (s_offsets[grp + 1] - s_offsets[grp] + kGemmBM - 1) / kGemmBM;
+        }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (lane * 8 + j < g.groups) s_tiles[lane * 8 + j] = incl - sum + local[j];
+        if (lane == 31) s_tiles[g.groups] = incl;
     }
     tc_fence_before();
     __syncthreads();
@@ -326,20 +355,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);
-    }
-}
-
-// Prefix sums of 128-row tiles per group from row offsets: tile_starts[g] = sum_{h<g} ceil(count_h / 128).
-__global__ void k_gemm_tile_starts(const int* offsets, int groups, int* tile_starts) {
-    pdl_wait();
-    pdl_trigger();
-    if (threadIdx.x == 0 && blockIdx.x == 0) {
-        int acc = 0;
-        for (int i = 0; i < groups; ++i) {
-            tile_starts[i] = acc;
-            acc += (offsets[i + 1] - offsets[i] + kGemmBM - 1) / kGemmBM;
-        }
-        tile_starts[groups] = acc;
     }
 }
 

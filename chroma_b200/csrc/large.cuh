@@ -5,10 +5,11 @@
 //   k_embed_bf16    embedding rows -> residual stream x                       (gpt_oss.py:304-306)
 //   k_rms_bf16      x -> bf16(x * rsqrt(mean(x^2) + eps) * w)                 (gpt_oss.py:30-41)
 //   k_rope_split    fused QKV output -> q (RoPE), new K rows (RoPE), new V rows (gpt_oss.py:44-54, 189-202)
-//   k_router        gate logits -> top-k experts (sorted, lowest index on ties) + softmax weights (gpt_oss.py:246-247)
-//   k_route_count / k_route_offsets / k_route_scatter
-//                   group the (token, slot) pairs by expert: counts, row offsets, and the gathered expert inputs
-//   k_moe_combine   x += bf16(sum_s w[t,s] * y[row(t,s)])                     (gpt_oss.py:263-265)
+//   k_route_fused   norm -> gate logits -> top-k experts (sorted, lowest index on ties) + softmax weights, and the
+//                   per-expert counts (gpt_oss.py:243-247)
+//   k_route_offsets / k_route_scatter
+//                   group the (token, slot) pairs by expert: row offsets and the gathered expert inputs
+//   k_moe_combine   x += bf16(sum_s w[t,s] * y[row(t,s)]) (gpt_oss.py:263-265), optionally the next layer's norm
 //   k_norm_rows     final RMSNorm of the rows whose logits are wanted (fp32 and bf16 copies)
 //   k_argmax_rows   greedy argmax keys over bf16 logits rows
 #pragma once
@@ -93,29 +94,6 @@ __global__ void __launch_bounds__(256) k_rope_split(const bf16* __restrict__ qkv
     }
 }
 
-// One warp per token: gate logits [N][E] (bf16) -> sorted top-k indices and softmax weights.
-__global__ void k_router(const bf16* __restrict__ logits, int ntok, int E, int k, int* __restrict__ ridx,
-                         float* __restrict__ rw, int* __restrict__ routes) {
-    __shared__ float g[8][256];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * 8 + warp;
-    pdl_wait();
-    pdl_trigger();
-    if (t >= ntok) return;
-    for (int e = lane; e < E; e += 32) g[warp][e] = __bfloat162float(logits[size_t(t) * E + e]);
-    __syncwarp();
-    warp_topk_softmax<bf16>(g[warp], E, k, ridx + size_t(t) * k, rw + size_t(t) * k);
-    __syncwarp();
-    if (routes && lane < k) routes[size_t(t) * k + lane] = ridx[size_t(t) * k + lane];
-}
-
-__global__ void k_route_count(const int* __restrict__ ridx, int pairs, int* __restrict__ counts) {
-    pdl_wait();
-    pdl_trigger();
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < pairs) atomicAdd(counts + ridx[i], 1);
-}
-
 // Single CTA: offsets[e] = exclusive prefix sum of counts; cursor[e] = offsets[e]; counts cleared for the next layer.
 __global__ void k_route_offsets(int* __restrict__ counts, int E, int* __restrict__ offsets, int* __restrict__ cursor) {
     pdl_wait();
@@ -151,19 +129,48 @@ __global__ void k_route_scatter(const int* __restrict__ ridx, int pairs, int k, 
     for (int c = lane; c < d / 8; c += 32) dst[c] = src[c];
 }
 
+// Optional duties of k_moe_combine: wait for the expert outputs other GPUs return (expert parallel), and the next
+// layer's attention RMSNorm of the updated row (saves a launch and a re-read of x).
+struct CombineExtra {
+    const unsigned* wait_flags;  // [wait_count] flags, each must reach *wait_epoch; nullptr: no wait
+    int wait_count;
+    const unsigned* wait_epoch;
+    unsigned long long wait_timeout_ns;
+    unsigned* err;
+    const float* norm_w;  // next layer's attention norm scale, or nullptr
+    float eps;
+    bf16* xn;             // [tokens][d] normalised rows
+};
+
 // grid = tokens; x[t] = bf16(x[t] + bf16(sum_s w[t,s] * y[perm[t,s]])) summed in slot order (perm == nullptr:
-// y row t*k + s, the layout of the expert-parallel return buffer).
+// y row t*k + s, the layout of the expert-parallel return buffer). With ex.norm_w, also xn[t] = bf16(x[t] * inv * w)
+// with inv = 1/sqrt(mean(x[t]^2) + eps), the arithmetic of k_rms_bf16.
 __global__ void __launch_bounds__(256) k_moe_combine(const bf16* __restrict__ y, const int* __restrict__ perm,
-                                                     const float* __restrict__ rw, int k, int d, bf16* __restrict__ x) {
+                                                     const float* __restrict__ rw, int k, int d, bf16* __restrict__ x,
+                                                     CombineExtra ex) {
+    __shared__ float red[32];
+    __shared__ int ok;
     const int t = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
     pdl_wait();
     pdl_trigger();
+    if (ex.wait_flags) {
+        if (threadIdx.x == 0) ok = 1;
+        __syncthreads();
+        if (int(threadIdx.x) < ex.wait_count &&
+            !wait_flag_geq(ex.wait_flags + threadIdx.x, *reinterpret_cast<const volatile unsigned*>(ex.wait_epoch),
+                           ex.wait_timeout_ns, ex.err))
+            ok = 0;
+        __syncthreads();
+        if (!ok) return;
+    }
     int rows[8];
     float w[8];
     for (int s = 0; s < k; ++s) {
         rows[s] = perm ? perm[size_t(t) * k + s] : t * k + s;
         w[s] = rw[size_t(t) * k + s];
     }
+    float sq = 0.f;
     for (int c = threadIdx.x * 2; c < d; c += blockDim.x * 2) {
         float a0 = 0.f, a1 = 0.f;
         for (int s = 0; s < k; ++s) {
@@ -173,7 +180,26 @@ __global__ void __launch_bounds__(256) k_moe_combine(const bf16* __restrict__ y,
         }
         __nv_bfloat162* xp = reinterpret_cast<__nv_bfloat162*>(x + size_t(t) * d + c);
         const float2 xv = __bfloat1622float2(*xp);
-        *xp = __floats2bfloat162_rn(bf16_round(xv.x + bf16_round(a0)), bf16_round(xv.y + bf16_round(a1)));
+        const float n0 = bf16_round(xv.x + bf16_round(a0)), n1 = bf16_round(xv.y + bf16_round(a1));
+        *xp = __floats2bfloat162_rn(n0, n1);
+        sq = fmaf(n0, n0, sq);
+        sq = fmaf(n1, n1, sq);
+    }
+    if (!ex.norm_w) return;
+    sq = warp_sum(sq);
+    if (lane == 0) red[warp] = sq;
+    __syncthreads();
+    if (warp == 0) {
+        float tot = lane < warps ? red[lane] : 0.f;
+        tot = warp_sum(tot);
+        if (lane == 0) red[0] = 1.0f / sqrtf(tot / float(d) + ex.eps);
+    }
+    __syncthreads();
+    const float inv = red[0];
+    for (int c = threadIdx.x * 2; c < d; c += blockDim.x * 2) {  // each thread re-reads the columns it wrote
+        const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(x + size_t(t) * d + c));
+        *reinterpret_cast<__nv_bfloat162*>(ex.xn + size_t(t) * d + c) = __floats2bfloat162_rn(
+            __fmul_rn(__fmul_rn(v.x, inv), ex.norm_w[c]), __fmul_rn(__fmul_rn(v.y, inv), ex.norm_w[c + 1]));
     }
 }
 
@@ -230,6 +256,102 @@ __global__ void __launch_bounds__(1024) k_argmax_rows(const bf16* __restrict__ l
     if (threadIdx.x == 0) {
         for (int w = 1; w < warps; ++w) best = max(best, red[w]);
         keys[r] = max(best, red[0]);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// MoE routing in one launch: RMSNorm of the residual rows (-> xn, the experts' input), gate logits (bf16, + bias),
+// top-k with softmax weights, and the per-expert counts the grouping needs (gpt_oss.py:243-247).
+// grid = (ceil(ntok / 8), ceil(E / 32)); block = kThreads. CTA (tile, eb) normalises its 8 rows and computes gate
+// logits for experts [32 eb, 32 eb + 32) with register-resident weight fragments; the last CTA of the token tile to
+// finish (atomic counter, reset by it) runs top-k over all E logits of its rows.
+constexpr int kRouteExperts = 32;
+
+__global__ void __launch_bounds__(kThreads) k_route_fused(const bf16* __restrict__ x, int ntok, int d, float eps,
+                                                          const float* __restrict__ norm_w, const bf16* __restrict__ gate_w,
+                                                          const bf16* __restrict__ gate_b, int E, int k,
+                                                          bf16* __restrict__ xn, bf16* __restrict__ glog,
+                                                          int* __restrict__ ridx, float* __restrict__ rw,
+                                                          int* __restrict__ routes, int* __restrict__ counts,
+                                                          unsigned* __restrict__ tile_counters) {
+    extern __shared__ float rsm[];
+    constexpr int TT = kTileTokens, MR = 2;
+    float* xs = rsm;               // [TT][d]
+    float* gl = xs + TT * d;       // [TT][E]
+    float* inv = gl + TT * E;      // [TT]
+    __shared__ bool s_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t0 = blockIdx.x * TT, tt = min(TT, ntok - t0);
+    const int e_begin = blockIdx.y * kRouteExperts, e_end = min(E, e_begin + kRouteExperts);
+    // This warp's first two expert rows: loaded before waiting on the producer of x (weights only).
+    int e0 = e_begin + warp * MR;
+    const bf16* rows[MR] = {gate_w + size_t(min(e0, E - 1)) * d, gate_w + size_t(min(e0 + 1, E - 1)) * d};
+    Frag<MR> f;
+    frag_load<bf16, MR>(f, rows, max(0, min(MR, e_end - e0)), d, 0);
+    pdl_wait();
+    pdl_trigger();
+    for (int i = threadIdx.x * 8; i < tt * d; i += blockDim.x * 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(x + size_t(t0) * d + i);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f2 = __bfloat1622float2(h[j]);
+            xs[i + 2 * j] = f2.x;
+            xs[i + 2 * j + 1] = f2.y;
+        }
+    }
+    __syncthreads();
+    // RMSNorm: same arithmetic as k_rms_bf16 (fp32 sum of squares, bf16(x * inv * w)).
+    rows_rmsnorm<bf16>(xs, tt, d, eps, norm_w, inv);
+    if (blockIdx.y == 0)
+        for (int i = threadIdx.x * 2; i < tt * d; i += blockDim.x * 2)
+            *reinterpret_cast<__nv_bfloat162*>(xn + size_t(t0) * d + i) = __floats2bfloat162_rn(xs[i], xs[i + 1]);
+    for (; e0 < e_end; e0 += kWarps * MR) {
+        const int nr = min(MR, e_end - e0);
+        if (e0 != e_begin + warp * MR) {
+            rows[0] = gate_w + size_t(e0) * d;
+            rows[1] = gate_w + size_t(min(e0 + 1, E - 1)) * d;
+            frag_load<bf16, MR>(f, rows, nr, d, 0);
+        }
+        float acc[MR][TT];
+        warp_gemv<bf16, MR, TT>(f, rows, nr, xs, d, tt, acc);
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < MR; ++r) {
+                if (r >= nr) break;
+                const float b = __bfloat162float(gate_b[e0 + r]);
+#pragma unroll
+                for (int t = 0; t < TT; ++t)
+                    if (t < tt) glog[size_t(t0 + t) * E + e0 + r] = __float2bfloat16_rn(__fadd_rn(acc[r][t], b));
+            }
+        }
+    }
+    // Last expert block of this token tile: top-k over all E gate logits of each row.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        bool last = true;
+        if (gridDim.y > 1) {
+            const unsigned prev = atomicAdd(tile_counters + blockIdx.x, 1u);
+            last = prev == gridDim.y - 1;
+            if (last) tile_counters[blockIdx.x] = 0u;
+        }
+        s_last = last;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < tt * E; i += blockDim.x) gl[i] = __bfloat162float(__ldcg(glog + size_t(t0) * E + i));
+    __syncthreads();
+    for (int t = warp; t < tt; t += kWarps) {
+        int* ri = ridx + size_t(t0 + t) * k;
+        warp_topk_softmax<bf16>(gl + t * E, E, k, ri, rw + size_t(t0 + t) * k);
+        __syncwarp();
+        if (lane < k) {
+            const int e = ri[lane];
+            atomicAdd(counts + e, 1);
+            if (routes) routes[size_t(t0 + t) * k + lane] = e;
+        }
     }
 }
 

@@ -185,7 +185,7 @@ static CUtensorMap bf16_tile_map(const void* base, uint64_t rows, uint64_t cols,
 }
 
 // C = A . B^T on the tensor cores. Dense when groups == 1 and offsets == nullptr; grouped otherwise (offsets and
-// tile_scratch are device arrays of groups + 1 ints; tile_scratch receives the per-group tile prefix sums).
+// offsets is a device array of groups + 1 ints; tile_scratch is unused).
 static void gemm_bf16(cudaStream_t s, const void* A, const void* B, GemmArgs g, int rows_a, int rows_b, void* tile_scratch,
                       int sms, unsigned* err) {
     if (g.groups < 1 || g.groups > kGemmMaxGroups) throw ValueError("GEMM group count out of range");
@@ -194,11 +194,7 @@ static void gemm_bf16(cudaStream_t s, const void* A, const void* B, GemmArgs g, 
     const bool narrow = g.N <= 32;
     const CUtensorMap ma = bf16_tile_map(A, uint64_t(rows_a), uint64_t(g.K), kGemmBM);
     const CUtensorMap mb = bf16_tile_map(B, uint64_t(rows_b), uint64_t(g.K), narrow ? 32 : 256);
-    if (g.offsets) {
-        if (!tile_scratch) throw ValueError("grouped GEMM needs tile scratch");
-        launch(s, dim3(1), dim3(32), 0, k_gemm_tile_starts, g.offsets, g.groups, static_cast<int*>(tile_scratch));
-        g.tile_starts = static_cast<const int*>(tile_scratch);
-    }
+    (void)tile_scratch;  // tile prefix sums are computed in the kernel's prologue
     const int bn = narrow ? 32 : 256;
     const int tiles = g.offsets ? sms : ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + bn - 1) / bn);
     const dim3 grid(unsigned(std::max(1, std::min(tiles, sms))));
@@ -489,7 +485,7 @@ struct LargeExec {
     int B = 1, n = 1, ctx = 0, mask_mode = kMaskBuffer, window = 0, sms = 148, chunks = 1, key_chunk = 256, rows = 1;
     int fd_splits = 1, fd_split_keys = 64;  // flash decoding: key splits per (sequence, KV head)
     float* fd_part = nullptr;
-    DevBuf arena, counters;
+    DevBuf arena, counters, route_counters;
     bf16 *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *glog = nullptr, *grouped = nullptr,
          *act = nullptr, *y = nullptr, *tf16 = nullptr, *scratch_k = nullptr, *scratch_v = nullptr;
     float *rw = nullptr, *tf32 = nullptr, *partial = nullptr;
@@ -570,11 +566,19 @@ struct LargeExec {
         fd_part = static_cast<float*>(at(22));
         counters = DevBuf(N * d.KV * sizeof(unsigned));
         check(cudaMemset(counters.p, 0, counters.bytes), "attention counters");
+        route_counters = DevBuf((N + kTileTokens - 1) / kTileTokens * sizeof(unsigned));
+        check(cudaMemset(route_counters.p, 0, route_counters.bytes), "routing counters");
     }
 
     void gemm(cudaStream_t s, const bf16* A, int M, const bf16* W, int N, int K, int epi, const bf16* bias, bf16* C,
-              int ldc, const bf16* residual, int groups, const int* offs, unsigned* err) {
+              int ldc, const bf16* residual, int groups, const int* offs, unsigned* err, const EpArgs* wait = nullptr) {
         GemmArgs g{};
+        if (wait) {  // A arrives from the other ranks: wait for their dispatch flags in the prologue
+            g.wait_flags = &reinterpret_cast<const EpHeader*>(wait->peer[wait->rank])->disp_flag[0];
+            g.wait_count = wait->world;
+            g.wait_epoch = wait->epoch;
+            g.wait_timeout_ns = wait->timeout_ns;
+        }
         g.M = M;
         g.N = N;
         g.K = K;
@@ -589,7 +593,7 @@ struct LargeExec {
         g.groups = groups;
         g.offsets = offs;
         gemm_bf16(s, A, W, g, M, groups * N, tiles, sms, err);
-        launches += offs ? 2 : 1;
+        ++launches;
     }
 
     void enqueue(cudaStream_t s, const GptIO& io, unsigned* err) {
@@ -620,7 +624,10 @@ struct LargeExec {
                 ck = nk;
                 cv = nv;
             }
-            launch(s, dim3(N), dim3(256), 0, k_rms_bf16, x, dm.d, dm.eps, w.attn_norm, xn);
+            if (l == 0) {  // later layers: the previous layer's combine already wrote this norm
+                launch(s, dim3(N), dim3(256), 0, k_rms_bf16, x, dm.d, dm.eps, w.attn_norm, xn);
+                ++launches;
+            }
             gemm(s, xn, N, w.qkv_w, heads, dm.d, kEpiStore, w.qkv_b, qkv, heads, nullptr, 1, nullptr, err);
             launch(s, dim3(N), dim3(256), 0, k_rope_split, qkv, dm.H, dm.KV, dm.hd, io.positions,
                    m->inv_freq.as<const float>(), dm.conc, q, nk, nv);
@@ -681,23 +688,33 @@ struct LargeExec {
                        static_cast<const bf16*>(nk), static_cast<const bf16*>(nv), bias, w.sinks, attn);
             }
             gemm(s, attn, N, w.out_w, dm.d, dm.H * dm.hd, kEpiResidual, w.out_b, x, dm.d, x, 1, nullptr, err);
-            launch(s, dim3(N), dim3(256), 0, k_rms_bf16, x, dm.d, dm.eps, w.mlp_norm, xn);
-            gemm(s, xn, N, w.gate_w, dm.E, dm.d, kEpiStore, w.gate_b, glog, dm.E, nullptr, 1, nullptr, err);
-            launch(s, dim3((N + 7) / 8), dim3(256), 0, k_router, glog, N, dm.E, dm.k, ridx, rw,
-                   io.routes ? io.routes + size_t(l) * N * dm.k : nullptr);
-            launch(s, dim3((P + 255) / 256), dim3(256), 0, k_route_count, ridx, P, counts);
+            {
+                const unsigned eb = unsigned((dm.E + kRouteExperts - 1) / kRouteExperts);
+                const size_t smem = (size_t(kTileTokens) * (dm.d + dm.E) + kTileTokens) * 4;
+                launch(s, dim3(unsigned((N + kTileTokens - 1) / kTileTokens), eb), dim3(kThreads), smem, k_route_fused,
+                       static_cast<const bf16*>(x), N, dm.d, dm.eps, w.mlp_norm, w.gate_w, w.gate_b, dm.E, dm.k, xn,
+                       glog, ridx, rw, io.routes ? io.routes + size_t(l) * N * dm.k : static_cast<int*>(nullptr), counts,
+                       route_counters.as<unsigned>());
+            }
+            CombineExtra ex{};
+            if (l + 1 < L) {  // fuse the next layer's attention norm into the combine
+                ex.norm_w = m->layer<bf16>(l + 1).attn_norm;
+                ex.eps = dm.eps;
+                ex.xn = xn;
+            }
             if (m->ep) {
-                enqueue_ep_experts(s, w, err);
+                enqueue_ep_experts(s, w, ex, err);
             } else {
                 launch(s, dim3(1), dim3(32), 0, k_route_offsets, counts, dm.E, offsets, cursor);
                 launch(s, dim3((P + 7) / 8), dim3(256), 0, k_route_scatter, ridx, P, dm.k, dm.d, xn, cursor, perm,
                        grouped);
                 gemm(s, grouped, P, w.w1, 2 * dm.I, dm.d, kEpiSwiglu, w.b1, act, dm.I, nullptr, dm.E, offsets, err);
                 gemm(s, act, P, w.w2, dm.d, dm.I, kEpiExpert, w.b2, y, dm.d, nullptr, dm.E, offsets, err);
-                launch(s, dim3(N), dim3(256), 0, k_moe_combine, y, perm, rw, dm.k, dm.d, x);
+                launch(s, dim3(N), dim3(256), 0, k_moe_combine, static_cast<const bf16*>(y), static_cast<const int*>(perm),
+                       static_cast<const float*>(rw), dm.k, dm.d, x, ex);
                 launches += 3;
             }
-            launches += 8;
+            launches += 3;
         }
         launch(s, dim3(rows), dim3(256), 0, k_norm_rows, x, rows, io.rows, n, reinterpret_cast<const float*>(m->at(1)),
                dm.d, dm.eps, tf32, tf16, io.keys, err);
@@ -708,24 +725,26 @@ struct LargeExec {
     // The experts of one layer across the expert-parallel group (ep.cuh): counts to every rank, row plan, dispatch
     // of the (token, slot) rows to their owners, grouped GEMMs over the rows this rank received, return of the
     // outputs to their sources, weighted combine in slot order.
-    void enqueue_ep_experts(cudaStream_t s, const LayerW<bf16>& w, unsigned* err) {
+    void enqueue_ep_experts(cudaStream_t s, const LayerW<bf16>& w, CombineExtra ex, unsigned* err) {
         const Dims& dm = m->dm;
         const EpGroup& g = *m->ep;
         const EpArgs a = g.args(m->El);
         const int N = B * n, P = N * dm.k, cap = int(g.cap);
-        launch(s, dim3(1), dim3(256), 0, k_ep_push_counts, a, counts);
-        launch(s, dim3(1), dim3(32), 0, k_ep_plan, a, cursor, offsets, recv_total, err);
+        launch(s, dim3(1), dim3(256), 0, k_ep_counts, a, counts, cursor, offsets, recv_total, err);
         launch(s, dim3(unsigned(std::max(1, std::min((P + 7) / 8, sms * 4)))), dim3(256), 0, k_ep_dispatch, a,
                static_cast<const int*>(ridx), P, dm.k, static_cast<const bf16*>(xn), cursor, err);
-        launch(s, dim3(1), dim3(32), 0, k_ep_wait, a, int(kEpDispatch), err);
-        gemm(s, g.recv_rows(), cap, w.w1, 2 * dm.I, dm.d, kEpiSwiglu, w.b1, act, dm.I, nullptr, m->El, offsets, err);
+        gemm(s, g.recv_rows(), cap, w.w1, 2 * dm.I, dm.d, kEpiSwiglu, w.b1, act, dm.I, nullptr, m->El, offsets, err, &a);
         gemm(s, act, cap, w.w2, dm.d, dm.I, kEpiExpert, w.b2, y, dm.d, nullptr, m->El, offsets, err);
         launch(s, dim3(unsigned(sms * 4)), dim3(256), 0, k_ep_return, a, static_cast<const bf16*>(y),
                static_cast<const int*>(recv_total), err);
-        launch(s, dim3(1), dim3(32), 0, k_ep_wait, a, int(kEpCombine), err);
+        ex.wait_flags = &reinterpret_cast<const EpHeader*>(a.peer[a.rank])->comb_flag[0];
+        ex.wait_count = a.world;
+        ex.wait_epoch = a.epoch;
+        ex.wait_timeout_ns = a.timeout_ns;
+        ex.err = err;
         launch(s, dim3(N), dim3(256), 0, k_moe_combine, static_cast<const bf16*>(g.return_rows()),
-               static_cast<const int*>(nullptr), static_cast<const float*>(rw), dm.k, dm.d, x);
-        launches += 7;
+               static_cast<const int*>(nullptr), static_cast<const float*>(rw), dm.k, dm.d, x, ex);
+        launches += 4;
     }
 
     void enqueue_vocab(cudaStream_t s, const GptIO& io, unsigned* err) {

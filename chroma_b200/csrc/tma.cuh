@@ -60,4 +60,36 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned b
         : "memory");
 }
 
+// ---- Cross-GPU flags (system scope) ---------------------------------------------------------------------
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait of one thread until *flag >= epoch (flags never decrease; wrap-safe comparison), for flags another
+// GPU raises. Gives up after `timeout_ns` of wall time (the global timer), raising kErrTimeout.
+__device__ __forceinline__ bool wait_flag_geq(const unsigned* flag, unsigned epoch, unsigned long long timeout_ns,
+                                             unsigned* err) {
+    const unsigned long long start = global_ns();
+    for (unsigned i = 0;; ++i) {
+        if (int(ld_acquire_sys(flag) - epoch) >= 0) return true;
+        if ((i & 63) == 63) {
+            if (global_ns() - start > timeout_ns) break;
+            __nanosleep(256);
+        }
+    }
+    atomicOr(err, kErrTimeout);
+    return false;
+}
+
 }  // namespace cb200

@@ -121,7 +121,7 @@ int chroma_b200_vocab_argmax_static(const chroma_b200_program* program, const fl
 /* bf16 tensor-core GEMM on device buffers, C = A[m, k] . B^T with B stored [groups * n, k] row-major (nn.Linear
  * layout), fp32 accumulation, fused epilogue. Dense when `offsets` is NULL (groups = 1). Grouped (MoE experts) when
  * `offsets` [groups + 1] (device, int32) gives each group's row range in A: rows of group g use B rows
- * [g*n, (g+1)*n) and bias row g; `tile_scratch` then needs groups + 1 int32 of device memory. C has n columns
+ * [g*n, (g+1)*n) and bias row g. `tile_scratch` is unused (kept for binary compatibility; may be NULL). C has n columns
  * (n / 2 for the SwiGLU epilogue). Replaces the cuBLAS SGEMM of Runner::linear (runtime.h:175-181) and the generated
  * per-expert einsum loops (gpu.py:390-424). Queued on `stream`; a stuck pipeline sets bit 2 of `error_word`. */
 int chroma_b200_gemm_bf16(const void* a, const void* b, const void* bias, const void* residual, void* c, int32_t m,
