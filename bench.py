@@ -58,6 +58,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--skip-c5", action="store_true", help="skip the GPT-OSS-120B-shaped decode (multi-GPU runs)")
     ap.add_argument("--c5-only", action="store_true", help="run only the GPT-OSS-120B-shaped decode (needs >= 2 GPUs)")
     ap.add_argument("--c5-layers", type=int, default=0, help="layers of the C5 model (0: all 36)")
+    ap.add_argument("--c5-sequences", type=int, default=256, help="sequences of the C5 decode over all GPUs")
     return ap.parse_args()
 
 
@@ -272,12 +273,15 @@ def bench_c5(args: argparse.Namespace, max_over_ranks, barrier, rank: int, world
     cfg = models.gpt_oss_120b
     if args.c5_layers:
         cfg = dataclasses.replace(cfg, num_hidden_layers=args.c5_layers)
-    total, ctx = 256, 4096
+    total, ctx = args.c5_sequences, 4096
     if total % world or (world < 2 and not args.c5_layers):
         return {"unavailable": "C5 needs 2 or more GPUs dividing 256 sequences (233 GB of expert weights); "
                                "one GPU runs it only with fewer layers (--c5-layers)"}
     B, L, KV, hd = total // world, cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim
-    plan, regions = synthetic_gptoss(cfg, steps=1, context=ctx, ep_world=world)
+    from chroma_b200._src.experts import vocab_shard
+
+    shard = vocab_shard(rank, world, cfg.vocab_size)  # vocab column shard: this rank's unembedding rows
+    plan, regions = synthetic_gptoss(cfg, steps=1, context=ctx, ep_world=world, vocab_rows=len(shard))
     wbuf = torch.empty(plan["desc"]["weight_bytes"], dtype=torch.uint8, device="cuda")
     shared_gen = torch.Generator(device="cuda").manual_seed(50)
     expert_gen = torch.Generator(device="cuda").manual_seed(5000 + rank)
@@ -285,10 +289,11 @@ def bench_c5(args: argparse.Namespace, max_over_ranks, barrier, rank: int, world
         if is_norm:
             wbuf[off : off + numel * 4].view(torch.float32).fill_(1.0)
         else:
-            gen = expert_gen if ".mlp.mlp" in name else shared_gen
+            gen = expert_gen if (".mlp.mlp" in name or name == "unembedding.weight") else shared_gen
             wbuf[off : off + numel * 2].view(torch.bfloat16).normal_(0.0, 0.02, generator=gen)
     group = chroma_b200.ExpertGroup(rank, world, max_pairs=B * cfg.experts_per_token, hidden=cfg.hidden_size,
-                                    experts=cfg.num_experts, exchange=None if world > 1 else (lambda h: [h]))
+                                    experts=cfg.num_experts, vocab_rows=B, vocab=cfg.vocab_size,
+                                    exchange=None if world > 1 else (lambda h: [h]))
     pre = chroma_b200.Program.from_native(Native(plan, device_weights=wbuf.data_ptr(), ep=group))
     dec = chroma_b200.Program.from_native(Native(plan, device_weights=wbuf.data_ptr(), ep=group))
     bd = chroma_b200.BatchDecoder(pre, dec, B)
@@ -320,7 +325,7 @@ def bench_c5(args: argparse.Namespace, max_over_ranks, barrier, rank: int, world
     expert_bytes = (2 * I * d + d * I + 2 * I + d) * 2
     attn_bytes = ((cfg.num_attention_heads + 2 * KV) * hd * d + d * cfg.num_attention_heads * hd) * 2
     per_rank = L * ((E // world) * expert_bytes + attn_bytes + E * d * 2 + B * ctx * KV * hd * 2 * 2)
-    per_rank += cfg.vocab_size * d * 2
+    per_rank += len(shard) * d * 2
     bd.close()
     del pre, dec
     group.close()
@@ -330,7 +335,8 @@ def bench_c5(args: argparse.Namespace, max_over_ranks, barrier, rank: int, world
     return {
         "workload": f"C5: GPT-OSS-120B-shaped greedy decode ({L} layers, d=2880, 64/8 heads, 128 experts top-4, bf16 "
                     f"N(0,0.02)), {total} sequences ({B} per GPU) with a 4,096-token bf16 cache, {world} GPUs, "
-                    f"{E // world} experts per GPU (NVLink peer-memory dispatch/return), vocab replicated",
+                    f"{E // world} experts per GPU (NVLink peer-memory dispatch/return), vocab column shard of "
+                    f"{len(shard)} rows per GPU",
         "tokens_per_s": total * steps / t, "ms_per_step": t * 1e3 / steps, "steps": steps, "n_gpus": world,
         "scaling": "strong (256 sequences in total)",
         "hbm_bytes_per_step_per_gpu": per_rank,

@@ -366,14 +366,16 @@ def _lower_micro(g: _Graph) -> Lowered:
                                                                "unreused_workspace_bytes": 0})
 
 
-def gptoss_layout(config: Any, ep_world: int = 1) -> list[tuple[str, tuple[int, ...], bool]]:
+def gptoss_layout(config: Any, ep_world: int = 1, vocab_rows: int | None = None) -> list[tuple[str, tuple[int, ...], bool]]:
     """(name, shape, is_fp32_norm) of every weight tensor in packing order (include/chroma_b200.h layout). With
-    ``ep_world`` > 1 the expert tensors hold one rank's share (E / ep_world experts); the router keeps all E."""
+    ``ep_world`` > 1 the expert tensors hold one rank's share (E / ep_world experts); the router keeps all E.
+    ``vocab_rows``: the unembedding rows of a vocab shard (default: all V)."""
     d, V, L = config.hidden_size, config.vocab_size, config.num_hidden_layers
     H, KV, hd = config.num_attention_heads, config.num_key_value_heads, config.head_dim
     E, I = config.num_experts, config.intermediate_size
     El = E // ep_world
-    out = [("embedding.weight", (V, d), False), ("norm.scale", (d,), True), ("unembedding.weight", (V, d), False)]
+    Vu = V if vocab_rows is None else vocab_rows
+    out = [("embedding.weight", (V, d), False), ("norm.scale", (d,), True), ("unembedding.weight", (Vu, d), False)]
     for layer in range(L):
         b = f"block.{layer}."
         out += [
@@ -427,7 +429,8 @@ def _gptoss_desc(config: Any, dtype: str, steps: int, context: int | None, last:
 
 
 def synthetic_gptoss(config: Any, *, steps: int, context: int | None = None, dtype: str = "bfloat16",
-                     last: bool = False, ep_world: int = 1) -> tuple[dict[str, Any], list[tuple[str, int, int, bool]]]:
+                     last: bool = False, ep_world: int = 1,
+                     vocab_rows: int | None = None) -> tuple[dict[str, Any], list[tuple[str, int, int, bool]]]:
     """The plan of a GPT-OSS program whose weights will be written straight into device memory (no host copy): returns
     (plan, regions) with regions = (name, byte offset, element count, is_fp32_norm) in packing order. Use with
     ``Native(plan, device_weights=ptr)`` over a buffer of ``plan["desc"]["weight_bytes"]`` bytes."""
@@ -435,7 +438,7 @@ def synthetic_gptoss(config: Any, *, steps: int, context: int | None = None, dty
 
     es = 2 if dtype == "bfloat16" else 4
     regions, total = [], 0
-    for name, shape, is_norm in gptoss_layout(config, ep_world):
+    for name, shape, is_norm in gptoss_layout(config, ep_world, vocab_rows):
         total = (total + ALIGN - 1) // ALIGN * ALIGN
         numel = math.prod(shape)
         regions.append((name, total, numel, is_norm))
@@ -453,7 +456,7 @@ def synthetic_gptoss(config: Any, *, steps: int, context: int | None = None, dty
 
 
 def lower_model(model: Any, *, steps: int, context: int | None = None, last: bool = False,
-                experts: range | None = None) -> Lowered:
+                experts: range | None = None, vocab_rows: range | None = None) -> Lowered:
     """A GPT-OSS program straight from a ``chroma_b200.models.Transformer`` (no export).
 
     ``context=None``: ``Transformer.forward`` over ``steps`` tokens (``last=True``: the UncachedTransformer variant
@@ -471,6 +474,8 @@ def lower_model(model: Any, *, steps: int, context: int | None = None, last: boo
         for k in list(state):
             if k.endswith(("mlp.mlp1_weight", "mlp.mlp1_bias", "mlp.mlp2_weight", "mlp.mlp2_bias")):
                 state[k] = state[k][experts.start : experts.stop].contiguous()
+    if vocab_rows is not None:  # a vocab shard: this rank's unembedding rows only
+        state["unembedding.weight"] = state["unembedding.weight"][vocab_rows.start : vocab_rows.stop].contiguous()
     dtype = _DTYPE_NAMES[str(state["embedding.weight"].dtype)]
     conc, inv_freq = rope_tables(config)
 
@@ -636,7 +641,8 @@ def compile_model(model: Any, output: str | os.PathLike[str], *, steps: int, con
     artefact: it cannot run without its group)."""
     if experts is None:
         return Program(write_artifact(lower_model(model, steps=steps, context=context, last=last), output))
-    lowered = lower_model(model, steps=steps, context=context, last=last, experts=experts.local)
+    lowered = lower_model(model, steps=steps, context=context, last=last, experts=experts.local,
+                          vocab_rows=experts.vocab_slice)
     lowered.plan["expert_parallel"] = {"rank": experts.rank, "world": experts.world}
     directory = write_artifact(lowered, output)
     manifest = json.loads((directory / "model.json").read_text())

@@ -7,8 +7,9 @@ The host side only sets the group up: each rank exports a handle to its shared b
 rank order through a host channel (``torch.distributed`` by default), and every rank opens the others'.
 
 Programs bound to a group (``Native(plan, ..., ep=group)``, ``compile_model(..., experts=group)``) hold the local
-experts only. Every rank must call the same programs in the same order; a rank that does not arrive within about a
-second at a MoE layer turns into a ``RuntimeError`` on the others.
+experts only. Every rank must call the same programs in the same order; a rank that does not arrive within the bounded
+wait (10 s, or ``CHROMA_B200_EP_TIMEOUT_MS`` when the group is created) turns into a ``RuntimeError`` on the others,
+after which the group must be recreated.
 """
 
 from __future__ import annotations
@@ -39,20 +40,33 @@ def local_experts(rank: int, world: int, experts: int) -> range:
     return range(rank * per, (rank + 1) * per)
 
 
+def vocab_shard(rank: int, world: int, vocab: int) -> range:
+    """The unembedding rows rank ``rank`` holds when the vocab projection is sharded: ceil(V / world) per rank."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a group of {world}")
+    per = -(-vocab // world)
+    return range(min(vocab, rank * per), min(vocab, (rank + 1) * per))
+
+
 class ExpertGroup:
     """One rank's membership in an expert-parallel group on the current CUDA device.
 
     ``max_pairs``: the most (token, expert) pairs one call of any program on this rank routes (rows x top_k); it
     sizes the receive buffer (``world * max_pairs`` rows of ``hidden`` bf16) and the return buffer.
+    ``vocab_rows`` > 0 (with ``vocab`` = V) also shards the vocab projection by vocab rows: this rank's programs hold
+    unembedding rows ``vocab_slice`` only, and each call's final rows are projected on every rank's shard (at most
+    ``vocab_rows`` final rows per call on a rank).
     ``exchange``: gathers one ``bytes`` handle per rank, in rank order (default ``torch_exchange``).
     """
 
-    def __init__(self, rank: int, world: int, *, max_pairs: int, hidden: int, experts: int,
-                 exchange: Callable[[bytes], Sequence[bytes]] | None = None) -> None:
+    def __init__(self, rank: int, world: int, *, max_pairs: int, hidden: int, experts: int, vocab_rows: int = 0,
+                 vocab: int = 0, exchange: Callable[[bytes], Sequence[bytes]] | None = None) -> None:
         self.rank, self.world, self.experts, self.hidden, self.max_pairs = rank, world, experts, hidden, max_pairs
         self.local = local_experts(rank, world, experts)
+        self.vocab_slice = vocab_shard(rank, world, vocab) if vocab_rows > 0 else None
         handle = ctypes.c_void_p()
-        nat.call("chroma_b200_ep_create", rank, world, max_pairs, hidden, experts, ctypes.byref(handle))
+        nat.call("chroma_b200_ep_create", rank, world, max_pairs, hidden, experts, vocab_rows, vocab,
+                 ctypes.byref(handle))
         self.handle = handle
         try:
             mine = ctypes.create_string_buffer(nat.EP_HANDLE_BYTES)

@@ -101,4 +101,16 @@ __device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes, int lan
         asm volatile("prefetch.global.L2 [%0];" ::"l"(c + off));
 }
 
+// Orderable 64-bit argmax key: larger value wins, then the lower index (numpy.argmax: first occurrence).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    unsigned u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    if (isnan(v)) u = 0xffffffffu;
+    return (static_cast<unsigned long long>(u) << 32) | (0xffffffffu - static_cast<unsigned>(idx));
+}
+
+__host__ __device__ inline int64_t argmax_index(unsigned long long key) {
+    return int64_t(0xffffffffu - static_cast<unsigned>(key & 0xffffffffull));
+}
+
 }  // namespace cb200

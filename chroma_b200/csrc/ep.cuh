@@ -39,11 +39,13 @@ struct EpHeader {
     unsigned cnt_flag[kEpMaxWorld];
     unsigned disp_flag[kEpMaxWorld];
     unsigned comb_flag[kEpMaxWorld];
-    unsigned pad[64 - 3 * kEpMaxWorld];
+    unsigned vrow_flag[kEpMaxWorld];  // vocab shard: final rows gathered
+    unsigned vkey_flag[kEpMaxWorld];  // vocab shard: argmax keys (and logits) returned
+    unsigned pad[64 - 5 * kEpMaxWorld];
     int counts[kEpMaxWorld][kEpMaxExperts];  // [src rank][global expert]
 };
 
-enum EpPhase : int { kEpCounts = 0, kEpDispatch = 1, kEpCombine = 2 };
+enum EpPhase : int { kEpCounts = 0, kEpDispatch = 1, kEpCombine = 2, kEpVocabRows = 3, kEpVocabKeys = 4 };
 
 struct EpArgs {
     int rank, world, E, El, d;
@@ -54,13 +56,24 @@ struct EpArgs {
     unsigned* epoch;              // this rank's epoch counter (local memory)
     unsigned* done;               // last-CTA counter (local memory)
     unsigned long long timeout_ns;  // bound of every wait for another rank
+    // Vocab column shard (vrows_max == 0: off): rank r holds unembedding rows [r*Vl, r*Vl + Vr).
+    int vrows_max, V, Vl;
+    size_t off_vrows;             // [world * vrows_max][d] bf16: every rank's final rows
+    size_t off_vkeys;             // [world][vrows_max] u64: each rank's argmax keys for this rank's rows
+    size_t off_vlogits;           // [vrows_max][V] bf16: this rank's logits rows, gathered from the shards
 };
 
 __device__ __forceinline__ EpHeader* ep_header(const EpArgs& a, int r) { return reinterpret_cast<EpHeader*>(a.peer[r]); }
 
 __device__ __forceinline__ unsigned* ep_flag(const EpArgs& a, int owner, int phase, int src) {
     EpHeader* h = ep_header(a, owner);
-    return phase == kEpCounts ? &h->cnt_flag[src] : (phase == kEpDispatch ? &h->disp_flag[src] : &h->comb_flag[src]);
+    switch (phase) {
+        case kEpCounts: return &h->cnt_flag[src];
+        case kEpDispatch: return &h->disp_flag[src];
+        case kEpCombine: return &h->comb_flag[src];
+        case kEpVocabRows: return &h->vrow_flag[src];
+        default: return &h->vkey_flag[src];
+    }
 }
 
 // Called by every thread of a CTA after its peer stores: the last CTA of the grid raises this rank's flag for
@@ -112,8 +125,11 @@ __global__ void k_ep_counts(EpArgs a, int* __restrict__ counts, int* __restrict_
         ok = 0;
     __syncthreads();
     if (!ok) return;
-    // The tables were written by other GPUs: volatile loads, never a stale L1 line.
+    // Stage the table (written by other GPUs: volatile loads, never a stale L1 line) in shared memory, in parallel.
+    __shared__ int table[kEpMaxWorld][kEpMaxExperts];
     const volatile EpHeader* h = ep_header(a, a.rank);
+    for (int i = threadIdx.x; i < a.world * a.E; i += blockDim.x) table[i / a.E][i % a.E] = h->counts[i / a.E][i % a.E];
+    __syncthreads();
     if (threadIdx.x < unsigned(a.world)) {  // thread q walks owner q's layout
         const int q = threadIdx.x;
         int row = 0;
@@ -122,7 +138,7 @@ __global__ void k_ep_counts(EpArgs a, int* __restrict__ counts, int* __restrict_
             if (q == a.rank) offsets[el] = row;
             for (int src = 0; src < a.world; ++src) {
                 if (src == a.rank) cursor[e] = row;
-                row += h->counts[src][e];
+                row += table[src][e];
             }
         }
         if (q == a.rank) {
@@ -190,6 +206,83 @@ __global__ void __launch_bounds__(256) k_ep_return(EpArgs a, const __nv_bfloat16
         for (int c = lane; c < a.d / 8; c += 32) to[c] = from[c];
     }
     ep_signal_when_last(a, kEpCombine);
+}
+
+// ---- Vocab column shard ---------------------------------------------------------------------------------------------
+// The unembedding is split by vocab rows: every rank projects ALL ranks' final rows onto its shard, then each row's
+// owner gets the shard's argmax key (and, when full logits are wanted, the shard's logits).
+//
+//   k_vocab_share_rows   this rank's `rows` final rows -> every rank's gather buffer at [rank * rows + r]; clears the
+//                        local key array; the last CTA flags every rank (kEpVocabRows)
+//   (GEMM over the world * rows gathered rows and the local shard; its prologue waits for kEpVocabRows; argmax keys
+//    with the shard's column offset)
+//   k_vocab_return       keys (and logits rows) of rank q's rows -> rank q; the last CTA flags every rank (kEpVocabKeys)
+//   k_vocab_finish       waits for kEpVocabKeys; keys_out[r] = max over the shards' keys; logits rows copied out
+
+// One warp per (destination rank, row), grid-stride.
+__global__ void __launch_bounds__(256) k_vocab_share_rows(EpArgs a, const __nv_bfloat16* __restrict__ rows_in, int rows,
+                                                          unsigned long long* __restrict__ keys_local) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    pdl_wait();
+    pdl_trigger();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.world * rows; i += gridDim.x * blockDim.x) keys_local[i] = 0ull;
+    for (int i = blockIdx.x * warps + warp; i < a.world * rows; i += gridDim.x * warps) {
+        const int q = i / rows, r = i % rows;
+        const uint4* src = reinterpret_cast<const uint4*>(rows_in + size_t(r) * a.d);
+        uint4* dst = reinterpret_cast<uint4*>(a.peer[q] + a.off_vrows) + (size_t(a.rank) * rows + r) * (a.d / 8);
+        for (int c = lane; c < a.d / 8; c += 32) dst[c] = src[c];
+    }
+    ep_signal_when_last(a, kEpVocabRows);
+}
+
+// One warp per (destination rank q, row r of q), grid-stride. keys_local / logits_shard rows are [q * rows + r].
+__global__ void __launch_bounds__(256) k_vocab_return(EpArgs a, const unsigned long long* __restrict__ keys_local,
+                                                      const __nv_bfloat16* __restrict__ logits_shard, int Vr, int rows,
+                                                      int want_logits) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    pdl_wait();
+    pdl_trigger();
+    for (int i = blockIdx.x * warps + warp; i < a.world * rows; i += gridDim.x * warps) {
+        const int q = i / rows, r = i % rows;
+        if (lane == 0)
+            reinterpret_cast<unsigned long long*>(a.peer[q] + a.off_vkeys)[size_t(a.rank) * a.vrows_max + r] = keys_local[i];
+        if (want_logits) {
+            const __nv_bfloat16* src = logits_shard + size_t(i) * Vr;
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.peer[q] + a.off_vlogits) + size_t(r) * a.V +
+                                 size_t(a.rank) * a.Vl;
+            for (int c = lane; c < Vr; c += 32) dst[c] = src[c];
+        }
+    }
+    ep_signal_when_last(a, kEpVocabKeys);
+}
+
+// grid-stride over rows (keys) and logits elements; every CTA first waits for all ranks' returns.
+__global__ void __launch_bounds__(256) k_vocab_finish(EpArgs a, int rows, unsigned long long* __restrict__ keys_out,
+                                                      __nv_bfloat16* __restrict__ logits_out, int want_logits,
+                                                      unsigned* err) {
+    __shared__ int ok;
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x == 0) ok = 1;
+    __syncthreads();
+    if (threadIdx.x < unsigned(a.world)) {
+        const unsigned epoch = *reinterpret_cast<volatile unsigned*>(a.epoch);
+        if (!wait_flag_geq(ep_flag(a, a.rank, kEpVocabKeys, int(threadIdx.x)), epoch, a.timeout_ns, err)) ok = 0;
+    }
+    __syncthreads();
+    if (!ok) return;
+    const unsigned long long* table = reinterpret_cast<const unsigned long long*>(a.peer[a.rank] + a.off_vkeys);
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+        unsigned long long best = 0ull;
+        for (int q = 0; q < a.world; ++q) best = max(best, __ldcg(table + size_t(q) * a.vrows_max + r));
+        if (keys_out) keys_out[r] = best;
+    }
+    if (!want_logits) return;
+    const uint4* src = reinterpret_cast<const uint4*>(a.peer[a.rank] + a.off_vlogits);
+    uint4* dst = reinterpret_cast<uint4*>(logits_out);
+    const size_t n16 = size_t(rows) * a.V / 8;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n16; i += size_t(gridDim.x) * blockDim.x)
+        dst[i] = __ldcg(src + i);
 }
 
 }  // namespace cb200

@@ -51,6 +51,14 @@ struct GemmArgs {
     int wait_count;
     const unsigned* wait_epoch;
     unsigned long long wait_timeout_ns;
+    // Optional: greedy argmax keys per row (kEpiStore): the largest bf16 output, lowest column on ties (atomicMax of
+    // argmax_key over each thread's columns of a tile; the caller zeroes the keys).
+    unsigned long long* argmax_keys;
+    int argmax_col_offset;  // added to the column index in the keys (a vocab shard's first global row)
+    // Split-K (dense only): ksplit > 1 splits the K blocks over ksplit tiles whose raw fp32 sums go to
+    // partial[ks][M][N]; k_gemm_splitk_epilogue then adds them in order and applies the epilogue.
+    int ksplit;
+    float* partial;
 };
 
 __device__ __forceinline__ float round_bf16(float x) { return bf16_round(x); }
@@ -101,7 +109,8 @@ __device__ __forceinline__ void stage_store(const GemmArgs& g, const uint32_t (&
 // One 32-row x 32-column accumulator chunk of an epilogue warp: `v` holds row (row_base + lane), columns
 // [col0, col0 + 32). Fast path (vec): 16-byte residual loads and output stores, coalesced through `stage`.
 __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& g, const float (&v)[32], const __nv_bfloat16* bias,
-                                                    int row_base, int row_end, int col0, bool vec, uint8_t* stage) {
+                                                    int row_base, int row_end, int col0, bool vec, uint8_t* stage,
+                                                    unsigned long long& best) {
     const int lane = threadIdx.x & 31;
     const int row = row_base + lane;
     if (vec && col0 + 32 <= g.N) {
@@ -159,6 +168,10 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& g, const flo
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(y[2 * j], y[2 * j + 1]);
+            if (g.argmax_keys) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) best = max(best, argmax_key(y[j], g.argmax_col_offset + col0 + j));
+            }
             stage_store<4>(g, w, row_base, row_end, col0, stage);
         }
         return;
@@ -186,6 +199,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& g, const flo
         float y = g.epi == kEpiExpert ? round_bf16(round_bf16(v[j]) + b) : round_bf16(v[j] + b);
         if (res) y = round_bf16(__bfloat162float(res[j]) + y);
         out[j] = __float2bfloat16_rn(y);
+        if (g.argmax_keys) best = max(best, argmax_key(y, g.argmax_col_offset + col0 + j));
     }
 }
 
@@ -262,11 +276,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
     __syncthreads();
     tc_fence_after();
     const int total_m = s_tiles[g.groups];
-    const int total = total_m * ntiles_n;
+    const int ksplit = g.ksplit > 1 ? g.ksplit : 1;
+    const int mn_tiles = total_m * ntiles_n;
+    const int total = mn_tiles * ksplit;
+    const int kb_per = (kblocks + ksplit - 1) / ksplit;
     const uint32_t tmem = tmem_base;
+    // Split-K part of tile t: K blocks [kb_lo, kb_hi).
+    auto k_range = [&](int t, int& kb_lo, int& kb_hi) {
+        const int ks = t / mn_tiles;
+        kb_lo = ks * kb_per;
+        kb_hi = min(kblocks, kb_lo + kb_per);
+    };
 
     // Tile t -> (group, first row, row end, n0). Consecutive tiles share an m-tile (A reuse) and sweep the group's B.
     auto tile_of = [&](int t, int& grp, int& row0, int& row_end, int& n0) {
+        t %= mn_tiles;
         const int mt = t / ntiles_n;
         n0 = (t % ntiles_n) * BN;
         int lo = 0, hi = g.groups - 1;
@@ -284,9 +308,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
         if (lane == 0) {
             int it = 0;
             for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x) {
-                int grp, row0, row_end, n0;
+                int grp, row0, row_end, n0, kb_lo, kb_hi;
                 tile_of(t, grp, row0, row_end, n0);
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                k_range(t, kb_lo, kb_hi);
+                for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
                     const int s = it % kGemmStages;
                     if (!mbar_wait(&empty[s], unsigned(((it / kGemmStages) & 1) ^ 1), err)) { abort_flag = 1; break; }
                     uint8_t* sa = gsm + size_t(s) * STAGE;
@@ -305,7 +330,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
                 if (!mbar_wait(&tmem_empty[acc], unsigned(((tile_it >> 1) & 1) ^ 1), err)) { abort_flag = 1; break; }
                 tc_fence_after();
                 const uint32_t d = tmem + uint32_t(acc * BN);
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                int kb_lo, kb_hi;
+                k_range(t, kb_lo, kb_hi);
+                for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
                     const int s = it % kGemmStages;
                     if (!mbar_wait(&full[s], unsigned((it / kGemmStages) & 1), err)) { abort_flag = 1; break; }
                     tc_fence_after();
@@ -314,7 +341,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
                     const uint64_t db = umma_desc_sw128(sa + A_BYTES);
 #pragma unroll
                     for (int k = 0; k < kGemmBK / 16; ++k)  // advance 16 elements = 32 bytes = 2 in the >>4 field
-                        umma_bf16(d, da + 2 * k, db + 2 * k, idesc, kb > 0 || k > 0);
+                        umma_bf16(d, da + 2 * k, db + 2 * k, idesc, kb > kb_lo || k > 0);
                     umma_commit(&empty[s]);
                 }
                 if (abort_flag) break;
@@ -337,14 +364,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
             tile_of(t, grp, row0, row_end, n0);
             const __nv_bfloat16* bias = g.bias ? g.bias + size_t(grp) * g.N : nullptr;
             const uint32_t taddr = tmem + uint32_t(acc * BN) + (uint32_t(q * 32) << 16);
+            unsigned long long best = 0ull;
+            const int row = row0 + q * 32 + lane;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 float v[32];
                 tmem_load32(taddr + uint32_t(c * 32), v);
                 const int col0 = n0 + c * 32;
                 if (col0 >= g.N) continue;
-                gemm_epilogue_chunk(g, v, bias, row0 + q * 32, row_end, col0, vec, stage);
+                if (ksplit > 1) {  // raw partial sums; the split-K epilogue kernel finishes them
+                    if (row < row_end) {
+                        float* dst = g.partial + (size_t(t / mn_tiles) * g.M + row) * g.N + col0;
+                        const int ncols = min(32, g.N - col0);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < ncols) dst[j] = v[j];
+                    }
+                    continue;
+                }
+                gemm_epilogue_chunk(g, v, bias, row0 + q * 32, row_end, col0, vec, stage, best);
             }
+            if (g.argmax_keys && ksplit == 1 && row < row_end && best) atomicMax(g.argmax_keys + row, best);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tmem_empty[acc]);
@@ -355,6 +395,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// Split-K epilogue: C[r][c] from the ksplit partial sums (added in split order), with the kEpiStore or kEpiResidual
+// epilogue of the GEMM and its argmax keys. grid = (ceil(N / 512), M); block = 256 (2 columns per thread).
+__global__ void __launch_bounds__(256) k_gemm_splitk_epilogue(GemmArgs g) {
+    __shared__ unsigned long long red[8];
+    const int r = blockIdx.y;
+    const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+    pdl_wait();
+    pdl_trigger();
+    unsigned long long best = 0ull;
+    if (c < g.N) {
+        float a0 = 0.f, a1 = 0.f;
+        for (int ks = 0; ks < g.ksplit; ++ks) {
+            const float* p = g.partial + (size_t(ks) * g.M + r) * g.N + c;
+            a0 += p[0];
+            if (c + 1 < g.N) a1 += p[1];
+        }
+        const float b0 = g.bias ? __bfloat162float(g.bias[c]) : 0.f;
+        const float b1 = g.bias && c + 1 < g.N ? __bfloat162float(g.bias[c + 1]) : 0.f;
+        float y0 = round_bf16(a0 + b0), y1 = round_bf16(a1 + b1);
+        if (g.epi == kEpiResidual) {
+            y0 = round_bf16(__bfloat162float(g.residual[size_t(r) * g.ldr + c]) + y0);
+            if (c + 1 < g.N) y1 = round_bf16(__bfloat162float(g.residual[size_t(r) * g.ldr + c + 1]) + y1);
+        }
+        __nv_bfloat16* out = g.C + size_t(r) * g.ldc + c;
+        out[0] = __float2bfloat16_rn(y0);
+        if (c + 1 < g.N) out[1] = __float2bfloat16_rn(y1);
+        best = argmax_key(y0, g.argmax_col_offset + c);
+        if (c + 1 < g.N) best = max(best, argmax_key(y1, g.argmax_col_offset + c + 1));
+    }
+    if (!g.argmax_keys) return;
+    for (int o = 16; o; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; ++w) best = max(best, red[w]);
+        atomicMax(g.argmax_keys + r, max(best, red[0]));
     }
 }
 

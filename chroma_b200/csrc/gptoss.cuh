@@ -688,18 +688,6 @@ __global__ void k_final_norm(const float* __restrict__ x, int nrows, const int64
         out[size_t(r) * dm.d + c] = Store<T>::round(__fmul_rn(__fmul_rn(xr[c], inv), norm_w[c]));
 }
 
-// Orderable 64-bit argmax key: larger value wins, then the lower index (numpy.argmax: first occurrence).
-__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
-    unsigned u = __float_as_uint(v);
-    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    if (isnan(v)) u = 0xffffffffu;
-    return (static_cast<unsigned long long>(u) << 32) | (0xffffffffu - static_cast<unsigned>(idx));
-}
-
-__host__ __device__ inline int64_t argmax_index(unsigned long long key) {
-    return int64_t(0xffffffffu - static_cast<unsigned>(key & 0xffffffffull));
-}
-
 // Vocab projection: logits[r][v] = sum_c xs[r][c] * W[v][c] for up to R rows per pass. 8 lanes per vocab row, 4 rows
 // per warp step, U steps unrolled (4 for a single activation row, 2 otherwise): every lane issues its 16-byte
 // streaming loads for 4*U vocab rows before any FMA. With `keys`, each row's greedy argmax is reduced in-block and merged with one 64-bit atomicMax per block.

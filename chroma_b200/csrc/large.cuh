@@ -11,7 +11,6 @@
 //                   group the (token, slot) pairs by expert: row offsets and the gathered expert inputs
 //   k_moe_combine   x += bf16(sum_s w[t,s] * y[row(t,s)]) (gpt_oss.py:263-265), optionally the next layer's norm
 //   k_norm_rows     final RMSNorm of the rows whose logits are wanted (fp32 and bf16 copies)
-//   k_argmax_rows   greedy argmax keys over bf16 logits rows
 #pragma once
 
 #include "gptoss.cuh"
@@ -19,6 +18,7 @@
 namespace cb200 {
 
 using bf16 = __nv_bfloat16;
+constexpr int kEpMaxGate = 256;  // most experts a router ranks
 
 __global__ void k_embed_bf16(const int64_t* __restrict__ tokens, int ntok, const bf16* __restrict__ emb, int V, int d,
                              bf16* __restrict__ x, unsigned* err) {
@@ -64,33 +64,69 @@ __global__ void __launch_bounds__(256) k_rms_bf16(const bf16* __restrict__ x, in
     }
 }
 
-// grid = tokens; block = 256. qkv [N][(H+2KV)*hd] -> q [N][H][hd] (RoPE), k_out/v_out rows [N][KV][hd].
+// grid = tokens; block = 256. qkv [N][(H+2KV)*hd] -> q [N][H][hd] (RoPE), k_out/v_out rows [N][KV][hd]. The hd/2
+// (cos, sin) pairs of the token's position are computed once into shared memory (rounded like the reference's
+// cos/sin tensors, gpt_oss.py:44-54); each thread then rotates two adjacent (lo, hi) pairs with 4-byte accesses.
 __global__ void __launch_bounds__(256) k_rope_split(const bf16* __restrict__ qkv, int H, int KV, int hd,
                                                     const float* __restrict__ positions, const float* __restrict__ inv_freq,
                                                     float conc, bf16* __restrict__ q, bf16* __restrict__ k_out,
                                                     bf16* __restrict__ v_out) {
+    __shared__ float cs[64][2];
     const int t = blockIdx.x;
     const int half = hd / 2, heads = H + 2 * KV;
     pdl_wait();
     pdl_trigger();
     const float pos = positions[t];
+    for (int j = threadIdx.x; j < half; j += blockDim.x) {
+        float sn, c;
+        sincosf(__fmul_rn(pos, inv_freq[j]), &sn, &c);
+        cs[j][0] = bf16_round(__fmul_rn(c, conc));
+        cs[j][1] = bf16_round(__fmul_rn(sn, conc));
+    }
+    __syncthreads();
     const bf16* row = qkv + size_t(t) * heads * hd;
-    for (int i = threadIdx.x; i < heads * half; i += blockDim.x) {
-        const int hh = i / half, j = i % half;
-        const float lo = __bfloat162float(row[hh * hd + j]), hi = __bfloat162float(row[hh * hd + j + half]);
-        float o1 = lo, o2 = hi;
+    const int pairs2 = half / 2;  // 2 rotation pairs per thread step
+    for (int i = threadIdx.x; i < heads * pairs2; i += blockDim.x) {
+        const int hh = i / pairs2, j = (i % pairs2) * 2;
+        const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(row + hh * hd + j));
+        const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(row + hh * hd + j + half));
+        float o1[2] = {lo.x, lo.y}, o2[2] = {hi.x, hi.y};
         if (hh < H + KV) {
-            float s, c;
-            sincosf(__fmul_rn(pos, inv_freq[j]), &s, &c);
-            c = bf16_round(__fmul_rn(c, conc));
-            s = bf16_round(__fmul_rn(s, conc));
-            o1 = bf16_round(__fsub_rn(bf16_round(__fmul_rn(lo, c)), bf16_round(__fmul_rn(hi, s))));
-            o2 = bf16_round(__fadd_rn(bf16_round(__fmul_rn(hi, c)), bf16_round(__fmul_rn(lo, s))));
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const float c = cs[j + u][0], sn = cs[j + u][1];
+                const float l = u ? lo.y : lo.x, h = u ? hi.y : hi.x;
+                o1[u] = bf16_round(__fsub_rn(bf16_round(__fmul_rn(l, c)), bf16_round(__fmul_rn(h, sn))));
+                o2[u] = bf16_round(__fadd_rn(bf16_round(__fmul_rn(h, c)), bf16_round(__fmul_rn(l, sn))));
+            }
         }
         bf16* dst = hh < H ? q + (size_t(t) * H + hh) * hd
                            : (hh < H + KV ? k_out + (size_t(t) * KV + hh - H) * hd : v_out + (size_t(t) * KV + hh - H - KV) * hd);
-        dst[j] = __float2bfloat16_rn(o1);
-        dst[j + half] = __float2bfloat16_rn(o2);
+        *reinterpret_cast<__nv_bfloat162*>(dst + j) = __floats2bfloat162_rn(o1[0], o1[1]);
+        *reinterpret_cast<__nv_bfloat162*>(dst + j + half) = __floats2bfloat162_rn(o2[0], o2[1]);
+    }
+}
+
+// One warp per token: gate logits [N][E] (bf16, from the tensor-core gate GEMM) -> sorted top-k experts, softmax
+// weights, per-expert counts and the optional routing record (the many-token counterpart of k_route_fused).
+__global__ void __launch_bounds__(256) k_route_topk(const bf16* __restrict__ logits, int ntok, int E, int k,
+                                                    int* __restrict__ ridx, float* __restrict__ rw,
+                                                    int* __restrict__ routes, int* __restrict__ counts) {
+    __shared__ float g[8][kEpMaxGate];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + warp;
+    pdl_wait();
+    pdl_trigger();
+    if (t >= ntok) return;
+    for (int e = lane; e < E; e += 32) g[warp][e] = __bfloat162float(logits[size_t(t) * E + e]);
+    __syncwarp();
+    int* ri = ridx + size_t(t) * k;
+    warp_topk_softmax<bf16>(g[warp], E, k, ri, rw + size_t(t) * k);
+    __syncwarp();
+    if (lane < k) {
+        const int e = ri[lane];
+        atomicAdd(counts + e, 1);
+        if (routes) routes[size_t(t) * k + lane] = e;
     }
 }
 
@@ -126,6 +162,7 @@ __global__ void k_route_scatter(const int* __restrict__ ridx, int pairs, int k, 
     row = __shfl_sync(0xffffffffu, row, 0);
     const uint4* src = reinterpret_cast<const uint4*>(xn + size_t(i / k) * d);
     uint4* dst = reinterpret_cast<uint4*>(grouped + size_t(row) * d);
+#pragma unroll 4
     for (int c = lane; c < d / 8; c += 32) dst[c] = src[c];
 }
 
@@ -144,7 +181,7 @@ struct CombineExtra {
 
 // grid = tokens; x[t] = bf16(x[t] + bf16(sum_s w[t,s] * y[perm[t,s]])) summed in slot order (perm == nullptr:
 // y row t*k + s, the layout of the expert-parallel return buffer). With ex.norm_w, also xn[t] = bf16(x[t] * inv * w)
-// with inv = 1/sqrt(mean(x[t]^2) + eps), the arithmetic of k_rms_bf16.
+// with inv = 1/sqrt(mean(x[t]^2) + eps) (the sum of squares in another order than k_rms_bf16's).
 __global__ void __launch_bounds__(256) k_moe_combine(const bf16* __restrict__ y, const int* __restrict__ perm,
                                                      const float* __restrict__ rw, int k, int d, bf16* __restrict__ x,
                                                      CombineExtra ex) {
@@ -170,20 +207,32 @@ __global__ void __launch_bounds__(256) k_moe_combine(const bf16* __restrict__ y,
         rows[s] = perm ? perm[size_t(t) * k + s] : t * k + s;
         w[s] = rw[size_t(t) * k + s];
     }
+    // 8 columns per thread per step (16-byte loads of the k expert rows and of x); d is a multiple of 8.
     float sq = 0.f;
-    for (int c = threadIdx.x * 2; c < d; c += blockDim.x * 2) {
-        float a0 = 0.f, a1 = 0.f;
+    for (int c = threadIdx.x * 8; c < d; c += blockDim.x * 8) {
+        float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         for (int s = 0; s < k; ++s) {
-            const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(y + size_t(rows[s]) * d + c));
-            a0 = __fadd_rn(a0, __fmul_rn(v.x, w[s]));
-            a1 = __fadd_rn(a1, __fmul_rn(v.y, w[s]));
+            const uint4 u = *reinterpret_cast<const uint4*>(y + size_t(rows[s]) * d + c);
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 v = __bfloat1622float2(h[j]);
+                a[2 * j] = __fadd_rn(a[2 * j], __fmul_rn(v.x, w[s]));
+                a[2 * j + 1] = __fadd_rn(a[2 * j + 1], __fmul_rn(v.y, w[s]));
+            }
         }
-        __nv_bfloat162* xp = reinterpret_cast<__nv_bfloat162*>(x + size_t(t) * d + c);
-        const float2 xv = __bfloat1622float2(*xp);
-        const float n0 = bf16_round(xv.x + bf16_round(a0)), n1 = bf16_round(xv.y + bf16_round(a1));
-        *xp = __floats2bfloat162_rn(n0, n1);
-        sq = fmaf(n0, n0, sq);
-        sq = fmaf(n1, n1, sq);
+        uint4* xp = reinterpret_cast<uint4*>(x + size_t(t) * d + c);
+        uint4 xu = *xp;
+        __nv_bfloat162* xh = reinterpret_cast<__nv_bfloat162*>(&xu);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 xv = __bfloat1622float2(xh[j]);
+            const float n0 = bf16_round(xv.x + bf16_round(a[2 * j])), n1 = bf16_round(xv.y + bf16_round(a[2 * j + 1]));
+            xh[j] = __floats2bfloat162_rn(n0, n1);
+            sq = fmaf(n0, n0, sq);
+            sq = fmaf(n1, n1, sq);
+        }
+        *xp = xu;
     }
     if (!ex.norm_w) return;
     sq = warp_sum(sq);
@@ -196,10 +245,16 @@ __global__ void __launch_bounds__(256) k_moe_combine(const bf16* __restrict__ y,
     }
     __syncthreads();
     const float inv = red[0];
-    for (int c = threadIdx.x * 2; c < d; c += blockDim.x * 2) {  // each thread re-reads the columns it wrote
-        const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(x + size_t(t) * d + c));
-        *reinterpret_cast<__nv_bfloat162*>(ex.xn + size_t(t) * d + c) = __floats2bfloat162_rn(
-            __fmul_rn(__fmul_rn(v.x, inv), ex.norm_w[c]), __fmul_rn(__fmul_rn(v.y, inv), ex.norm_w[c + 1]));
+    for (int c = threadIdx.x * 8; c < d; c += blockDim.x * 8) {  // each thread re-reads the columns it wrote
+        uint4 u = *reinterpret_cast<const uint4*>(x + size_t(t) * d + c);
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 v = __bfloat1622float2(h[j]);
+            h[j] = __floats2bfloat162_rn(__fmul_rn(__fmul_rn(v.x, inv), ex.norm_w[c + 2 * j]),
+                                         __fmul_rn(__fmul_rn(v.y, inv), ex.norm_w[c + 2 * j + 1]));
+        }
+        *reinterpret_cast<uint4*>(ex.xn + size_t(t) * d + c) = u;
     }
 }
 
@@ -240,52 +295,33 @@ __global__ void __launch_bounds__(256) k_norm_rows(const bf16* __restrict__ x, i
     }
 }
 
-// One CTA per row of bf16 logits: argmax key (larger value, then lower index).
-__global__ void __launch_bounds__(1024) k_argmax_rows(const bf16* __restrict__ logits, int V, unsigned long long* __restrict__ keys) {
-    __shared__ unsigned long long red[32];
-    const int r = blockIdx.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
-    pdl_wait();
-    pdl_trigger();
-    unsigned long long best = 0ull;
-    const bf16* row = logits + size_t(r) * V;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) best = max(best, argmax_key(__bfloat162float(row[v]), v));
-    for (int o = 16; o; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
-    if (lane == 0) red[warp] = best;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < warps; ++w) best = max(best, red[w]);
-        keys[r] = max(best, red[0]);
-    }
-}
-
 // ---------------------------------------------------------------------------------------------------------------
 // MoE routing in one launch: RMSNorm of the residual rows (-> xn, the experts' input), gate logits (bf16, + bias),
 // top-k with softmax weights, and the per-expert counts the grouping needs (gpt_oss.py:243-247).
-// grid = (ceil(ntok / 8), ceil(E / 32)); block = kThreads. CTA (tile, eb) normalises its 8 rows and computes gate
-// logits for experts [32 eb, 32 eb + 32) with register-resident weight fragments; the last CTA of the token tile to
-// finish (atomic counter, reset by it) runs top-k over all E logits of its rows.
-constexpr int kRouteExperts = 32;
+// grid = (ceil(ntok / 8), ceil(E / epc)); block = kThreads. CTA (tile, eb) normalises its 8 rows and computes gate
+// logits for experts [epc eb, epc eb + epc) (one weight row per warp at a time, register-resident fragments); the
+// last CTA of the token tile to finish (atomic counter, reset by it) runs top-k over all E logits of its rows. Many
+// token tiles: epc = E (no redundant norms); few (decode): small epc spreads the gate weights over more SMs.
 
 __global__ void __launch_bounds__(kThreads) k_route_fused(const bf16* __restrict__ x, int ntok, int d, float eps,
                                                           const float* __restrict__ norm_w, const bf16* __restrict__ gate_w,
-                                                          const bf16* __restrict__ gate_b, int E, int k,
+                                                          const bf16* __restrict__ gate_b, int E, int epc, int k,
                                                           bf16* __restrict__ xn, bf16* __restrict__ glog,
                                                           int* __restrict__ ridx, float* __restrict__ rw,
                                                           int* __restrict__ routes, int* __restrict__ counts,
                                                           unsigned* __restrict__ tile_counters) {
     extern __shared__ float rsm[];
-    constexpr int TT = kTileTokens, MR = 2;
+    constexpr int TT = kTileTokens, MR = 1;
     float* xs = rsm;               // [TT][d]
     float* gl = xs + TT * d;       // [TT][E]
     float* inv = gl + TT * E;      // [TT]
     __shared__ bool s_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = blockIdx.x * TT, tt = min(TT, ntok - t0);
-    const int e_begin = blockIdx.y * kRouteExperts, e_end = min(E, e_begin + kRouteExperts);
+    const int e_begin = blockIdx.y * epc, e_end = min(E, e_begin + epc);
     // This warp's first two expert rows: loaded before waiting on the producer of x (weights only).
     int e0 = e_begin + warp * MR;
-    const bf16* rows[MR] = {gate_w + size_t(min(e0, E - 1)) * d, gate_w + size_t(min(e0 + 1, E - 1)) * d};
+    const bf16* rows[MR] = {gate_w + size_t(min(e0, E - 1)) * d};
     Frag<MR> f;
     frag_load<bf16, MR>(f, rows, max(0, min(MR, e_end - e0)), d, 0);
     pdl_wait();
@@ -310,7 +346,6 @@ __global__ void __launch_bounds__(kThreads) k_route_fused(const bf16* __restrict
         const int nr = min(MR, e_end - e0);
         if (e0 != e_begin + warp * MR) {
             rows[0] = gate_w + size_t(e0) * d;
-            rows[1] = gate_w + size_t(min(e0 + 1, E - 1)) * d;
             frag_load<bf16, MR>(f, rows, nr, d, 0);
         }
         float acc[MR][TT];

@@ -186,8 +186,18 @@ static CUtensorMap bf16_tile_map(const void* base, uint64_t rows, uint64_t cols,
 
 // C = A . B^T on the tensor cores. Dense when groups == 1 and offsets == nullptr; grouped otherwise (offsets and
 // offsets is a device array of groups + 1 ints; tile_scratch is unused).
+// Split-K factor for a dense GEMM that would leave most SMs idle (decode-sized M): enough splits to give every SM a
+// tile, at least 4 K blocks per split, at most 8 splits.
+static int splitk_choice(int M, int N, int K, int bn, int sms) {
+    const int tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + bn - 1) / bn);
+    const int kblocks = (K + kGemmBK - 1) / kGemmBK;
+    if (tiles * 2 > sms) return 1;
+    const int k = std::min({8, sms / std::max(1, tiles), kblocks / 4});
+    return k >= 2 ? k : 1;
+}
+
 static void gemm_bf16(cudaStream_t s, const void* A, const void* B, GemmArgs g, int rows_a, int rows_b, void* tile_scratch,
-                      int sms, unsigned* err) {
+                      int sms, unsigned* err, float* splitk_ws = nullptr, size_t splitk_ws_bytes = 0) {
     if (g.groups < 1 || g.groups > kGemmMaxGroups) throw ValueError("GEMM group count out of range");
     if (g.K % 8) throw ValueError("GEMM K must be a multiple of 8");
     if (g.epi == kEpiSwiglu && g.N % 32) throw ValueError("SwiGLU epilogue needs N a multiple of 32");
@@ -196,11 +206,22 @@ static void gemm_bf16(cudaStream_t s, const void* A, const void* B, GemmArgs g, 
     const CUtensorMap mb = bf16_tile_map(B, uint64_t(rows_b), uint64_t(g.K), narrow ? 32 : 256);
     (void)tile_scratch;  // tile prefix sums are computed in the kernel's prologue
     const int bn = narrow ? 32 : 256;
-    const int tiles = g.offsets ? sms : ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + bn - 1) / bn);
+    int tiles = g.offsets ? sms : ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + bn - 1) / bn);
+    g.ksplit = 1;
+    if (!g.offsets && splitk_ws && (g.epi == kEpiStore || g.epi == kEpiResidual)) {
+        const int k = splitk_choice(g.M, g.N, g.K, bn, sms);
+        if (k > 1 && size_t(k) * g.M * g.N * 4 <= splitk_ws_bytes) {
+            g.ksplit = k;
+            g.partial = splitk_ws;
+            tiles *= k;
+        }
+    }
     const dim3 grid(unsigned(std::max(1, std::min(tiles, sms))));
     const size_t smem = size_t(kGemmStages) * (kGemmBM + bn) * kGemmBK * 2 + 4 * kGemmStageBytes + 1024;
     if (narrow) launch(s, grid, dim3(kGemmThreads), smem, k_gemm_bf16<32>, ma, mb, g, err);
     else launch(s, grid, dim3(kGemmThreads), smem, k_gemm_bf16<256>, ma, mb, g, err);
+    if (g.ksplit > 1)
+        launch(s, dim3(unsigned((g.N + 511) / 512), unsigned(g.M)), dim3(256), 0, k_gemm_splitk_epilogue, g);
 }
 
 // ---------------------------------------------------------------------------------------------------------
@@ -310,6 +331,9 @@ struct EpGroup {
     int rank = 0, world = 1, E = 0, d = 0, device = 0;
     long long pmax = 0, cap = 0;
     size_t off_meta = 0, off_x = 0, off_y = 0;
+    int vrows_max = 0, V = 0, Vl = 0;  // vocab column shard (vrows_max == 0: off)
+    size_t off_vrows = 0, off_vkeys = 0, off_vlogits = 0;
+    int vocab_rows_here() const { return std::max(0, std::min(Vl, V - rank * Vl)); }
     DevBuf shared, local;
     std::array<char*, kEpMaxWorld> peer{};
     std::vector<void*> opened;
@@ -341,6 +365,12 @@ struct EpGroup {
         a.epoch = local.as<unsigned>();
         a.done = local.as<unsigned>() + 1;
         a.timeout_ns = timeout_ns;
+        a.vrows_max = vrows_max;
+        a.V = V;
+        a.Vl = Vl;
+        a.off_vrows = off_vrows;
+        a.off_vkeys = off_vkeys;
+        a.off_vlogits = off_vlogits;
         return a;
     }
     __nv_bfloat16* recv_rows() const { return reinterpret_cast<__nv_bfloat16*>(shared.as<char>() + off_x); }
@@ -485,7 +515,9 @@ struct LargeExec {
     int B = 1, n = 1, ctx = 0, mask_mode = kMaskBuffer, window = 0, sms = 148, chunks = 1, key_chunk = 256, rows = 1;
     int fd_splits = 1, fd_split_keys = 64;  // flash decoding: key splits per (sequence, KV head)
     float* fd_part = nullptr;
-    DevBuf arena, counters, route_counters;
+    DevBuf arena, counters, route_counters, splitk, vlogits, vkeys;
+    float* splitk_ws = nullptr;
+    size_t splitk_bytes = 0;
     bf16 *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *glog = nullptr, *grouped = nullptr,
          *act = nullptr, *y = nullptr, *tf16 = nullptr, *scratch_k = nullptr, *scratch_v = nullptr;
     float *rw = nullptr, *tf32 = nullptr, *partial = nullptr;
@@ -568,14 +600,43 @@ struct LargeExec {
         check(cudaMemset(counters.p, 0, counters.bytes), "attention counters");
         route_counters = DevBuf((N + kTileTokens - 1) / kTileTokens * sizeof(unsigned));
         check(cudaMemset(route_counters.p, 0, route_counters.bytes), "routing counters");
+        // Split-K workspace for the dense projections of decode-sized row counts (QKV and out; the vocab GEMM has
+        // enough tiles).
+        for (const int cols : {int(heads), d.d}) {
+            const int k = splitk_choice(int(N), cols, cols == d.d ? d.H * d.hd : d.d, 256, sms);
+            if (k > 1) splitk_bytes = std::max(splitk_bytes, size_t(k) * N * size_t(cols) * 4);
+        }
+        if (splitk_bytes) {
+            splitk = DevBuf(splitk_bytes);
+            splitk_ws = splitk.as<float>();
+        }
+        if (model.ep && model.ep->vrows_max > 0) {  // vocab column shard
+            if (rows > model.ep->vrows_max)
+                throw ValueError("expert-parallel group's vocab shard sized for fewer final rows than this program selects");
+            const size_t all = size_t(model.ep->world) * rows;
+            vlogits = DevBuf(all * size_t(std::max(1, model.ep->vocab_rows_here())) * 2);
+            vkeys = DevBuf(all * 8);
+        }
     }
 
+    // A (rows of another rank) is complete once each of `count` flags reaches *epoch.
+    struct FlagWait {
+        const unsigned* flags;
+        int count;
+        const unsigned* epoch;
+        unsigned long long timeout_ns;
+    };
+    static FlagWait ep_wait(const EpArgs& a, const unsigned* flags) { return {flags, a.world, a.epoch, a.timeout_ns}; }
+
     void gemm(cudaStream_t s, const bf16* A, int M, const bf16* W, int N, int K, int epi, const bf16* bias, bf16* C,
-              int ldc, const bf16* residual, int groups, const int* offs, unsigned* err, const EpArgs* wait = nullptr) {
+              int ldc, const bf16* residual, int groups, const int* offs, unsigned* err, const FlagWait* wait = nullptr,
+              unsigned long long* argmax_keys = nullptr, int argmax_col_offset = 0) {
         GemmArgs g{};
-        if (wait) {  // A arrives from the other ranks: wait for their dispatch flags in the prologue
-            g.wait_flags = &reinterpret_cast<const EpHeader*>(wait->peer[wait->rank])->disp_flag[0];
-            g.wait_count = wait->world;
+        g.argmax_keys = argmax_keys;
+        g.argmax_col_offset = argmax_col_offset;
+        if (wait) {  // A arrives from the other ranks: wait for their flags in the prologue
+            g.wait_flags = wait->flags;
+            g.wait_count = wait->count;
             g.wait_epoch = wait->epoch;
             g.wait_timeout_ns = wait->timeout_ns;
         }
@@ -592,8 +653,8 @@ struct LargeExec {
         g.limit = m->dm.limit;
         g.groups = groups;
         g.offsets = offs;
-        gemm_bf16(s, A, W, g, M, groups * N, tiles, sms, err);
-        ++launches;
+        gemm_bf16(s, A, W, g, M, groups * N, tiles, sms, err, splitk_ws, splitk_bytes);
+        launches += offs == nullptr && splitk_choice(M, N, K, N <= 32 ? 32 : 256, sms) > 1 ? 2 : 1;
     }
 
     void enqueue(cudaStream_t s, const GptIO& io, unsigned* err) {
@@ -689,12 +750,24 @@ struct LargeExec {
             }
             gemm(s, attn, N, w.out_w, dm.d, dm.H * dm.hd, kEpiResidual, w.out_b, x, dm.d, x, 1, nullptr, err);
             {
-                const unsigned eb = unsigned((dm.E + kRouteExperts - 1) / kRouteExperts);
-                const size_t smem = (size_t(kTileTokens) * (dm.d + dm.E) + kTileTokens) * 4;
-                launch(s, dim3(unsigned((N + kTileTokens - 1) / kTileTokens), eb), dim3(kThreads), smem, k_route_fused,
-                       static_cast<const bf16*>(x), N, dm.d, dm.eps, w.mlp_norm, w.gate_w, w.gate_b, dm.E, dm.k, xn,
-                       glog, ridx, rw, io.routes ? io.routes + size_t(l) * N * dm.k : static_cast<int*>(nullptr), counts,
-                       route_counters.as<unsigned>());
+                int* rec = io.routes ? io.routes + size_t(l) * N * dm.k : static_cast<int*>(nullptr);
+                const int tiles_t = (N + kTileTokens - 1) / kTileTokens;
+                if (tiles_t >= sms) {
+                    // Many tokens: norm, gate logits on the tensor cores, then top-k + counts.
+                    launch(s, dim3(N), dim3(256), 0, k_rms_bf16, x, dm.d, dm.eps, w.mlp_norm, xn);
+                    gemm(s, xn, N, w.gate_w, dm.E, dm.d, kEpiStore, w.gate_b, glog, dm.E, nullptr, 1, nullptr, err);
+                    launch(s, dim3(unsigned((N + 7) / 8)), dim3(256), 0, k_route_topk, static_cast<const bf16*>(glog), N,
+                           dm.E, dm.k, ridx, rw, rec, counts);
+                    ++launches;
+                } else {
+                    // Decode-sized: one fused kernel; experts split over CTAs so the gate weights stream from ~1 wave.
+                    const int epc = std::max(8, (dm.E * tiles_t + sms - 1) / sms);
+                    const unsigned eb = unsigned((dm.E + epc - 1) / epc);
+                    const size_t smem = (size_t(kTileTokens) * (dm.d + dm.E) + kTileTokens) * 4;
+                    launch(s, dim3(unsigned(tiles_t), eb), dim3(kThreads), smem, k_route_fused,
+                           static_cast<const bf16*>(x), N, dm.d, dm.eps, w.mlp_norm, w.gate_w, w.gate_b, dm.E, epc, dm.k,
+                           xn, glog, ridx, rw, rec, counts, route_counters.as<unsigned>());
+                }
             }
             CombineExtra ex{};
             if (l + 1 < L) {  // fuse the next layer's attention norm into the combine
@@ -733,9 +806,12 @@ struct LargeExec {
         launch(s, dim3(1), dim3(256), 0, k_ep_counts, a, counts, cursor, offsets, recv_total, err);
         launch(s, dim3(unsigned(std::max(1, std::min((P + 7) / 8, sms * 4)))), dim3(256), 0, k_ep_dispatch, a,
                static_cast<const int*>(ridx), P, dm.k, static_cast<const bf16*>(xn), cursor, err);
-        gemm(s, g.recv_rows(), cap, w.w1, 2 * dm.I, dm.d, kEpiSwiglu, w.b1, act, dm.I, nullptr, m->El, offsets, err, &a);
+        const FlagWait dispatched = ep_wait(a, &reinterpret_cast<const EpHeader*>(a.peer[a.rank])->disp_flag[0]);
+        gemm(s, g.recv_rows(), cap, w.w1, 2 * dm.I, dm.d, kEpiSwiglu, w.b1, act, dm.I, nullptr, m->El, offsets, err,
+             &dispatched);
         gemm(s, act, cap, w.w2, dm.d, dm.I, kEpiExpert, w.b2, y, dm.d, nullptr, m->El, offsets, err);
-        launch(s, dim3(unsigned(sms * 4)), dim3(256), 0, k_ep_return, a, static_cast<const bf16*>(y),
+        launch(s, dim3(unsigned(std::max(1, std::min(sms * 4, (cap + 7) / 8)))), dim3(256), 0, k_ep_return, a,
+               static_cast<const bf16*>(y),
                static_cast<const int*>(recv_total), err);
         ex.wait_flags = &reinterpret_cast<const EpHeader*>(a.peer[a.rank])->comb_flag[0];
         ex.wait_count = a.world;
@@ -750,16 +826,32 @@ struct LargeExec {
     void enqueue_vocab(cudaStream_t s, const GptIO& io, unsigned* err) {
         const Dims& dm = m->dm;
         const bf16* W = reinterpret_cast<const bf16*>(m->at(2));
+        if (m->ep && m->ep->vrows_max > 0) {
+            // Vocab column shard (ep.cuh): all ranks' final rows x this rank's vocab rows; keys/logits to the owners.
+            const EpGroup& g = *m->ep;
+            const EpArgs a = g.args(m->El);
+            const int Vr = g.vocab_rows_here(), all = g.world * rows;
+            const bool want_logits = io.keys == nullptr;
+            launch(s, dim3(unsigned(std::max(1, std::min(sms, (all + 7) / 8)))), dim3(256), 0, k_vocab_share_rows, a,
+                   static_cast<const bf16*>(tf16), rows, vkeys.as<unsigned long long>());
+            const FlagWait gathered = ep_wait(a, &reinterpret_cast<const EpHeader*>(a.peer[a.rank])->vrow_flag[0]);
+            gemm(s, reinterpret_cast<const bf16*>(a.peer[a.rank] + a.off_vrows), all, W, Vr, dm.d, kEpiStore, nullptr,
+                 vlogits.as<bf16>(), Vr, nullptr, 1, nullptr, err, &gathered, vkeys.as<unsigned long long>(),
+                 g.rank * g.Vl);
+            launch(s, dim3(unsigned(std::max(1, std::min(sms, (all + 7) / 8)))), dim3(256), 0, k_vocab_return, a,
+                   static_cast<const unsigned long long*>(vkeys.as<unsigned long long>()),
+                   static_cast<const bf16*>(vlogits.as<bf16>()), Vr, rows, int(want_logits));
+            launch(s, dim3(unsigned(want_logits ? sms : 1)), dim3(256), 0, k_vocab_finish, a, rows, io.keys,
+                   static_cast<bf16*>(io.logits), int(want_logits), err);
+            launches += 3;
+            return;
+        }
         if (rows < 16) {
             launch_vocab<bf16>(s, dm, sms, tf32, rows, W, static_cast<bf16*>(io.logits), io.keys, err);
             ++launches;
-        } else {
+        } else {  // greedy argmax fused into the GEMM epilogue (keys zeroed by k_norm_rows)
             gemm(s, tf16, rows, W, dm.V, dm.d, kEpiStore, nullptr, static_cast<bf16*>(io.logits), dm.V, nullptr, 1, nullptr,
-                 err);
-            if (io.keys) {
-                launch(s, dim3(rows), dim3(1024), 0, k_argmax_rows, static_cast<const bf16*>(io.logits), dm.V, io.keys);
-                ++launches;
-            }
+                 err, nullptr, io.keys);
         }
     }
 };
@@ -1114,7 +1206,7 @@ struct chroma_b200_ep {
 };
 
 int chroma_b200_ep_create(int32_t rank, int32_t world, int64_t max_pairs, int32_t hidden, int32_t experts,
-                          chroma_b200_ep** out, char* err, size_t err_len) {
+                          int32_t vocab_rows, int32_t vocab, chroma_b200_ep** out, char* err, size_t err_len) {
     return guarded(err, err_len, [&] {
         if (!out) throw ValueError("null argument");
         if (world < 1 || world > kEpMaxWorld || rank < 0 || rank >= world)
@@ -1135,7 +1227,18 @@ int chroma_b200_ep_create(int32_t rank, int32_t world, int64_t max_pairs, int32_
         g->off_meta = align(sizeof(EpHeader));
         g->off_x = g->off_meta + align(size_t(g->cap) * 4);
         g->off_y = g->off_x + align(size_t(g->cap) * hidden * 2);
-        g->shared = DevBuf(g->off_y + align(size_t(max_pairs) * hidden * 2));
+        size_t bytes = g->off_y + align(size_t(max_pairs) * hidden * 2);
+        if (vocab_rows > 0) {
+            if (vocab < world || vocab % 8) throw ValueError("vocab shard needs a vocab that is a multiple of 8");
+            g->vrows_max = vocab_rows;
+            g->V = vocab;
+            g->Vl = (vocab + world - 1) / world;
+            g->off_vrows = bytes;
+            g->off_vkeys = g->off_vrows + align(size_t(world) * vocab_rows * hidden * 2);
+            g->off_vlogits = g->off_vkeys + align(size_t(world) * vocab_rows * 8);
+            bytes = g->off_vlogits + align(size_t(vocab_rows) * vocab * 2);
+        }
+        g->shared = DevBuf(bytes);
         check(cudaMemset(g->shared.p, 0, g->off_x), "expert-parallel header");
         g->local = DevBuf(256);
         check(cudaMemset(g->local.p, 0, 256), "expert-parallel counters");

@@ -187,9 +187,14 @@ void chroma_b200_decoder_destroy(chroma_b200_decoder* decoder);
  * (bounded, ~1 s) for all ranks; a rank that does not arrive turns into a RUNTIME error on the others. */
 #define CHROMA_B200_EP_HANDLE_BYTES 64
 typedef struct chroma_b200_ep chroma_b200_ep;
-/* `max_pairs`: the most (token, expert) pairs one call of any program on this rank routes (rows x top_k). */
+/* `max_pairs`: the most (token, expert) pairs one call of any program on this rank routes (rows x top_k).
+ * `vocab_rows` > 0 also splits the vocab projection by vocab rows (column shard of the logits): rank r holds
+ * unembedding rows [r*ceil(V/world), ...) (tensor [2] of its programs has only those rows), every rank projects all
+ * ranks' final rows onto its shard, and each row's owner receives the shards' argmax keys (and logits when a call
+ * returns logits). `vocab_rows` is the most final rows one call selects on a rank; `vocab` = V (a multiple of 8).
+ * 0 keeps the vocab projection replicated. */
 int chroma_b200_ep_create(int32_t rank, int32_t world, int64_t max_pairs, int32_t hidden, int32_t experts,
-                          chroma_b200_ep** out, char* err, size_t err_len);
+                          int32_t vocab_rows, int32_t vocab, chroma_b200_ep** out, char* err, size_t err_len);
 /* Writes CHROMA_B200_EP_HANDLE_BYTES bytes identifying this rank's shared buffer to other processes. */
 int chroma_b200_ep_handle(const chroma_b200_ep* ep, void* handle, char* err, size_t err_len);
 /* `handles`: world x CHROMA_B200_EP_HANDLE_BYTES bytes, every rank's handle in rank order. */

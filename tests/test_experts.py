@@ -38,6 +38,16 @@ def test_local_experts_partition() -> None:
         local_experts(2, 2, 8)
 
 
+def test_vocab_shard_partition() -> None:
+    from chroma_b200._src.experts import vocab_shard
+
+    parts = [vocab_shard(r, 8, 201088) for r in range(8)]
+    assert all(len(p) == 25136 for p in parts) and parts[7].stop == 201088
+    assert [p.start for p in parts] == [25136 * r for r in range(8)]
+    odd = [vocab_shard(r, 3, 10) for r in range(3)]
+    assert [list(p) for p in odd] == [[0, 1, 2, 3], [4, 5, 6, 7], [8, 9]]
+
+
 def test_sharded_layout_keeps_router_and_splits_experts() -> None:
     cfg = tiny_config(8)
     full = dict((n, s) for n, s, _ in compiler.gptoss_layout(cfg))
@@ -48,6 +58,9 @@ def test_sharded_layout_keeps_router_and_splits_experts() -> None:
             assert half[name] == (full[name][0] // 2, *full[name][1:])
         else:
             assert half[name] == full[name]
+    vocab_half = dict((n, s) for n, s, _ in compiler.gptoss_layout(cfg, 2, 128))
+    assert vocab_half["unembedding.weight"] == (128, cfg.hidden_size)
+    assert vocab_half["embedding.weight"] == full["embedding.weight"]
     plan, _ = compiler.synthetic_gptoss(cfg, steps=4, ep_world=2)
     full_plan, _ = compiler.synthetic_gptoss(cfg, steps=4)
     assert plan["desc"]["experts"] == 8 and plan["desc"]["weight_bytes"] < full_plan["desc"]["weight_bytes"]
@@ -59,12 +72,17 @@ def test_lowered_shard_is_the_slice_of_the_full_model() -> None:
     full = compiler.lower_model(model, steps=4)
     names = [n for n, _, _ in compiler.gptoss_layout(cfg)]
     for rank in range(2):
-        shard = compiler.lower_model(model, steps=4, experts=local_experts(rank, 2, 4))
+        from chroma_b200._src.experts import vocab_shard
+
+        vocab = vocab_shard(rank, 2, cfg.vocab_size)
+        shard = compiler.lower_model(model, steps=4, experts=local_experts(rank, 2, 4), vocab_rows=vocab)
         assert len(shard.tensors) == len(full.tensors)
         for name, a, b in zip(names, shard.tensors, full.tensors):
             if name.endswith(("mlp1_weight", "mlp1_bias", "mlp2_weight", "mlp2_bias")):
                 per = b.shape[0] // 2
                 np.testing.assert_array_equal(a.view(np.uint8), b[rank * per : (rank + 1) * per].view(np.uint8))
+            elif name == "unembedding.weight":
+                np.testing.assert_array_equal(a.view(np.uint8), b[vocab.start : vocab.stop].view(np.uint8))
             else:
                 np.testing.assert_array_equal(a.view(np.uint8), b.view(np.uint8))
 
@@ -89,8 +107,8 @@ def _exchange_rank(rank: int, world: int, port: int, out_dir: str) -> None:
 
     def fake_call(name: str, *args):  # type: ignore[no-untyped-def]
         if name == "chroma_b200_ep_create":
-            r, w, pairs, hidden, e, out = args
-            assert (r, w, pairs, hidden, e) == (rank, world, 64, 2880, 32)
+            r, w, pairs, hidden, e, vrows, vocab, out = args
+            assert (r, w, pairs, hidden, e, vrows, vocab) == (rank, world, 64, 2880, 32, 0, 0)
             out._obj.value = 1000 + rank
         elif name == "chroma_b200_ep_handle":
             ctypes.memmove(args[1], bytes([rank + 1]) * native.EP_HANDLE_BYTES, native.EP_HANDLE_BYTES)

@@ -3,6 +3,7 @@
 * One rank (world 1): the whole exchange path runs against this GPU's own buffers; logits, routes and a decode
   sequence must be bit-identical to the program with all experts local (each expert row's GEMM output does not
   depend on which rows share its tile, and the combine sums slots in the same order).
+* Vocab column shard (1 and 2 ranks): greedy ids identical to the replicated vocab, logits within bf16 rounding.
 * Two ranks (needs 2 GPUs, one process each): every rank's logits equal those of a single-GPU program with all
   experts on the same tokens, bit for bit; then one rank stays away (alive, between calls, nothing in flight) and
   the other rank's call ends in a RuntimeError after the bounded wait, with its GPU still usable.
@@ -23,6 +24,7 @@ import torch
 
 import chroma_b200
 from chroma_b200 import models
+from tests import helpers
 
 pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
@@ -61,6 +63,29 @@ def test_single_rank_group_matches_all_local_experts(gpu: None, tmp_path: Path) 
     group.close()
 
 
+def test_single_rank_vocab_shard_matches_replicated_vocab(gpu: None, tmp_path: Path) -> None:
+    model = ep_model()
+    tokens = np.random.default_rng(33).integers(0, 8192, 40)
+    group = chroma_b200.ExpertGroup(0, 1, max_pairs=64 * 2, hidden=1024, experts=8, vocab_rows=8, vocab=8192,
+                                    exchange=lambda h: [h])
+    assert group.vocab_slice == range(0, 8192)
+    outs = []
+    for experts in (None, group):
+        pre = chroma_b200.compile_model(model, tmp_path / f"vpre{experts is None}", steps=32, context=96, experts=experts)
+        dec = chroma_b200.compile_model(model, tmp_path / f"vdec{experts is None}", steps=1, context=96, experts=experts)
+        with chroma_b200.BatchDecoder(pre, dec, 2) as bd:
+            seqs = np.stack([tokens[:32], tokens[8:40]])
+            logits = np.asarray(bd.append(seqs))
+            ids = bd.append(seqs[:, -1:], argmax=True)
+            outs.append((logits, ids, bd.generate(ids, 4)))
+    # Two rows take the SIMT vocab kernel when replicated and the tensor-core GEMM when sharded: the same sums in
+    # another order, so logits agree to the bf16 rounding of the last bit; the greedy ids are identical.
+    helpers.assert_bf16_logits(outs[1][0].astype(np.float32), outs[0][0].astype(np.float32), rel=1e-2)
+    np.testing.assert_array_equal(outs[0][1], outs[1][1])
+    np.testing.assert_array_equal(outs[0][2], outs[1][2])
+    group.close()
+
+
 def test_group_rejects_mismatched_programs(gpu: None, tmp_path: Path) -> None:
     group = chroma_b200.ExpertGroup(0, 1, max_pairs=8, hidden=1024, experts=8, exchange=lambda h: [h])
     with pytest.raises(ValueError, match="pairs"):
@@ -95,6 +120,24 @@ def _two_rank_child(rank: int, world: int, port: int, out_dir: str) -> None:
     for got in results:
         np.testing.assert_array_equal(got.view(np.uint16), want.view(np.uint16))
     np.testing.assert_array_equal(ep.native.routes(), full.native.routes())
+    # Vocab column shard as well: decode through a batched decoder, logits gathered from both ranks' shards.
+    vgroup = chroma_b200.ExpertGroup(rank, world, max_pairs=64 * 2, hidden=1024, experts=8, vocab_rows=4, vocab=8192)
+    assert len(vgroup.vocab_slice) == 4096
+    outs = []
+    for experts in (None, vgroup):
+        pre = chroma_b200.compile_model(model, tmp / f"vpre{experts is None}", steps=32, context=96, experts=experts)
+        dec = chroma_b200.compile_model(model, tmp / f"vdec{experts is None}", steps=1, context=96, experts=experts)
+        with chroma_b200.BatchDecoder(pre, dec, 2) as bd:
+            seqs = np.stack([tokens[:32], tokens[16:48]])
+            if experts is not None:
+                dist.barrier()
+            logits = np.asarray(bd.append(seqs))
+            ids = bd.append(seqs[:, -1:], argmax=True)
+            outs.append((logits, ids, bd.generate(ids, 4)))
+    helpers.assert_bf16_logits(outs[1][0].astype(np.float32), outs[0][0].astype(np.float32), rel=1e-2)
+    np.testing.assert_array_equal(outs[0][1], outs[1][1])
+    np.testing.assert_array_equal(outs[0][2], outs[1][2])
+    vgroup.close()
     # Failure: rank 1 stays out of the next call (alive, idle at a host barrier); rank 0 must time out cleanly.
     dist.barrier()
     status = "ok"
