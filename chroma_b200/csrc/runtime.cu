@@ -895,6 +895,9 @@ struct GptExec {
         const size_t N = size_t(B) * n;
         const int last = 5 * (L - 1);
         key_chunk = d.hd <= 32 ? 512 : 256;
+        // Few (row, kv head) pairs (small-batch fp32 decode): split the keys finer so more CTAs share the latency.
+        // bf16 programs keep whole chunks: a single chunk rounds the probabilities where the reference does.
+        if (model.desc.storage == CHROMA_B200_FP32 && N * size_t(d.KV) <= 8) key_chunk = 64;
         chunks = (ctx + n + key_chunk - 1) / key_chunk;
         auto round = [](size_t b) { return (b + 255) / 256 * 256; };
         std::vector<Alloc> a = {
