@@ -55,6 +55,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--skip-c4", action="store_true", help="skip the GPT-OSS-20B-shaped prefill measurement")
     ap.add_argument("--c4-only", action="store_true", help="run only the GPT-OSS-20B-shaped prefill measurement")
     ap.add_argument("--c4-layers", type=int, default=0, help="layers of the C4 model (0: all 24; fewer for profiling)")
+    ap.add_argument("--decode-only", action="store_true", help="only the headline decode measurement (profiling)")
     ap.add_argument("--skip-c5", action="store_true", help="skip the GPT-OSS-120B-shaped decode (multi-GPU runs)")
     ap.add_argument("--c5-only", action="store_true", help="run only the GPT-OSS-120B-shaped decode (needs >= 2 GPUs)")
     ap.add_argument("--c5-layers", type=int, default=0, help="layers of the C5 model (0: all 36)")
@@ -443,6 +444,13 @@ def main() -> None:
     t_rank = sum(step_ms) / 1e3
     t_max = max_over_ranks(t_rank)
     value = world * args.steps / t_max
+    if args.decode_only:
+        if rank == 0:
+            print(json.dumps({"decode_only": {"value": value, "ms_per_step": 1e3 * t_max / args.steps}}), flush=True)
+        bd1.close()
+        if dist is not None:
+            dist.destroy_process_group()
+        return
 
     # ---- roofline: vocab kernel alone (L2 flushed before each launch)
     vocab_ms = []

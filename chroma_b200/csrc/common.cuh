@@ -101,6 +101,13 @@ __device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes, int lan
         asm volatile("prefetch.global.L2 [%0];" ::"l"(c + off));
 }
 
+// Grid-stride L2 prefetch of a byte range (one 128-byte line per thread step).
+__global__ void k_prefetch_l2(const char* base, size_t bytes) {
+    const size_t lines = (bytes + 127) / 128;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < lines; i += size_t(gridDim.x) * blockDim.x)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(base + i * 128));
+}
+
 // Orderable 64-bit argmax key: larger value wins, then the lower index (numpy.argmax: first occurrence).
 __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
     unsigned u = __float_as_uint(v);

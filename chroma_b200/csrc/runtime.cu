@@ -874,6 +874,23 @@ struct GptExec {
     bool large_path = false;
     LargeExec large;
 
+    // Layer-weight prefetch (dev-sized models): every layer's weights (a contiguous range of the weights buffer,
+    // ~30 MB for the dev model) are pulled into L2 by a kernel on a side stream at the start of each step, so the
+    // latency-bound layer kernels, the MoE ones whose weights depend on the routing included, hit L2.
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
+    const char* prefetch_base = nullptr;
+    size_t prefetch_bytes = 0;
+
+    GptExec() = default;
+    GptExec(const GptExec&) = delete;
+    GptExec& operator=(const GptExec&) = delete;
+    ~GptExec() {
+        if (side) cudaStreamDestroy(side);
+        if (fork_ev) cudaEventDestroy(fork_ev);
+        if (join_ev) cudaEventDestroy(join_ev);
+    }
+
     void init(const Model& model, int batch, int rows_per_seq, int context, int mode, int win, bool selected_rows) {
         m = &model;
         B = batch;
@@ -894,6 +911,17 @@ struct GptExec {
         const int L = model.desc.layers;
         const size_t N = size_t(B) * n;
         const int last = 5 * (L - 1);
+        {
+            const size_t first = size_t(model.offsets.at(3));
+            const size_t bytes = size_t(model.desc.weight_bytes) - first;
+            if (bytes <= (size_t(48) << 20)) {
+                prefetch_base = model.weights->ptr + first;
+                prefetch_bytes = bytes;
+                check(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking), "prefetch stream");
+                check(cudaEventCreateWithFlags(&fork_ev, cudaEventDisableTiming), "prefetch event");
+                check(cudaEventCreateWithFlags(&join_ev, cudaEventDisableTiming), "prefetch event");
+            }
+        }
         key_chunk = d.hd <= 32 ? 512 : 256;
         // Few (row, kv head) pairs (small-batch fp32 decode): split the keys finer so more CTAs share the latency.
         // bf16 programs keep whole chunks: a single chunk rounds the probabilities where the reference does.
@@ -944,6 +972,14 @@ struct GptExec {
         const int N = B * n;
         const int L = m->desc.layers;
         launches = 0;
+        if (side) {  // fork: the prefetch runs beside the whole step and joins at its end
+            check(cudaEventRecord(fork_ev, s), "prefetch fork");
+            check(cudaStreamWaitEvent(side, fork_ev, 0), "prefetch fork");
+            k_prefetch_l2<<<64, 256, 0, side>>>(prefetch_base, prefetch_bytes);
+            check(cudaGetLastError(), "prefetch launch");
+            check(cudaEventRecord(join_ev, side), "prefetch join");
+            ++launches;
+        }
         launch(s, dim3(N), dim3(128), 0, k_embed<T>, io.tokens, N, reinterpret_cast<const T*>(m->at(0)), dm.V, dm.d, x,
                err);
         ++launches;
@@ -1002,6 +1038,7 @@ struct GptExec {
                reinterpret_cast<const float*>(m->at(1)), dm, tf, io.keys, err);
         enqueue_vocab_t<T>(s);
         launches += 2;
+        if (side) check(cudaStreamWaitEvent(s, join_ev, 0), "prefetch join");
     }
 
     // The vocab projection alone (reads the final-norm rows left by the last run).
