@@ -398,6 +398,189 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
     }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// The same GEMM on CTA pairs (cta_group::2): a 2-CTA cluster computes 256 x 256 output tiles, each CTA streaming
+// only its 128 rows of A and its 128 rows of B (32 KB per 64-wide K stage instead of 48 KB for the same MMA work
+// per SM), so 6 stages fit in shared memory. The leader CTA issues the 256-row MMAs; each CTA drains its own 128 x
+// 256 accumulator (two per CTA in TMEM, double-buffered) with the epilogue above. Dense and grouped; no split-K.
+constexpr int kPairStages = 6;
+constexpr int kPairBM = 256;  // rows per pair tile (128 per CTA)
+constexpr int kPairBN = 256;  // columns per pair tile (each CTA loads 128 rows of B)
+constexpr size_t kPairSmemBytes = size_t(kPairStages) * 2 * 128 * kGemmBK * 2 + 4 * kGemmStageBytes + 1024;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    k_gemm_bf16_pair(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, GemmArgs g,
+                     unsigned* err) {
+    constexpr int HALF = 128 * kGemmBK * 2;  // one CTA's A (or B) rows of a stage
+    constexpr int STAGE = 2 * HALF;
+    constexpr uint32_t TMEM_COLS = 2 * kPairBN;
+    extern __shared__ uint8_t psm_raw[];
+    uint8_t* gsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(psm_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t full[kPairStages], empty[kPairStages], tmem_full[2], tmem_empty[2];
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int abort_flag;
+    __shared__ int s_tiles[kGemmMaxGroups + 1];
+    __shared__ int s_offsets[kGemmMaxGroups + 1];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+    const int ntiles_n = (g.N + kPairBN - 1) / kPairBN;
+    const int kblocks = (g.K + kGemmBK - 1) / kGemmBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPairStages; ++s) {
+            mbar_init(&full[s], 1);   // the leader's expect_tx; both CTAs' bytes
+            mbar_init(&empty[s], 1);  // one MMA commit per round
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tmem_full[a], 1);
+            mbar_init(&tmem_empty[a], 8);  // leader only: 4 epilogue warps of each CTA
+        }
+        abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&map_a);
+        prefetch_tensormap(&map_b);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(&tmem_base, TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA signal
+    tc_fence_after();
+    pdl_wait();
+    pdl_trigger();
+    if (g.wait_flags && int(threadIdx.x) < g.wait_count &&
+        !wait_flag_geq(g.wait_flags + threadIdx.x, *reinterpret_cast<const volatile unsigned*>(g.wait_epoch),
+                       g.wait_timeout_ns, err))
+        abort_flag = 1;
+    for (int i = threadIdx.x; i <= g.groups; i += blockDim.x) s_offsets[i] = g.offsets ? g.offsets[i] : (i == 0 ? 0 : g.M);
+    __syncthreads();
+    if (warp == 0) {  // 256-row tiles per group, prefix-summed (as in k_gemm_bf16)
+        int local[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int grp = lane * 8 + j;
+            local[j] = sum;
+            if (grp < g.groups) sum += (s_offsets[grp + 1] - s_offsets[grp] + kPairBM - 1) / kPairBM;
+        }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (lane * 8 + j < g.groups) s_tiles[lane * 8 + j] = incl - sum + local[j];
+        if (lane == 31) s_tiles[g.groups] = incl;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const int total = s_tiles[g.groups] * ntiles_n;
+    const uint32_t tmem = tmem_base;
+
+    auto tile_of = [&](int t, int& grp, int& row0, int& row_end, int& n0) {
+        const int mt = t / ntiles_n;
+        n0 = (t % ntiles_n) * kPairBN;
+        int lo = 0, hi = g.groups - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (s_tiles[mid] <= mt) lo = mid;
+            else hi = mid - 1;
+        }
+        grp = lo;
+        row0 = s_offsets[grp] + (mt - s_tiles[grp]) * kPairBM;
+        row_end = min(row0 + kPairBM, s_offsets[grp + 1]);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {  // producer, both CTAs: own halves of A and B, counted on the leader's full barrier
+            int it = 0;
+            for (int t = cluster; t < total && !abort_flag; t += nclusters) {
+                int grp, row0, row_end, n0;
+                tile_of(t, grp, row0, row_end, n0);
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kPairStages;
+                    if (!mbar_wait(&empty[s], unsigned(((it / kPairStages) & 1) ^ 1), err)) { abort_flag = 1; break; }
+                    uint8_t* sa = gsm + size_t(s) * STAGE;
+                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * STAGE);
+                    const uint32_t fb = cluster_addr(&full[s], 0);
+                    tma_load_2d_pair(sa, &map_a, kb * kGemmBK, row0 + int(rank) * 128, fb);
+                    tma_load_2d_pair(sa + HALF, &map_b, kb * kGemmBK, grp * g.N + n0 + int(rank) * 128, fb);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {  // MMA issue (leader only); commits go to both CTAs' barriers
+            constexpr uint32_t idesc = umma_idesc_bf16(kPairBM, kPairBN);
+            int it = 0, tile_it = 0;
+            for (int t = cluster; t < total && !abort_flag; t += nclusters, ++tile_it) {
+                const int acc = tile_it & 1;
+                if (!mbar_wait(&tmem_empty[acc], unsigned(((tile_it >> 1) & 1) ^ 1), err)) { abort_flag = 1; break; }
+                tc_fence_after();
+                const uint32_t d = tmem + uint32_t(acc * kPairBN);
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kPairStages;
+                    if (!mbar_wait(&full[s], unsigned((it / kPairStages) & 1), err)) { abort_flag = 1; break; }
+                    tc_fence_after();
+                    const uint8_t* sa = gsm + size_t(s) * STAGE;
+                    const uint64_t da = umma_desc_sw128(sa);
+                    const uint64_t db = umma_desc_sw128(sa + HALF);
+#pragma unroll
+                    for (int k = 0; k < kGemmBK / 16; ++k) umma_bf16_pair(d, da + 2 * k, db + 2 * k, idesc, kb > 0 || k > 0);
+                    umma_commit_pair(cluster_addr(&empty[s], 0));
+                    umma_commit_pair(cluster_addr(&empty[s], 1));
+                }
+                if (abort_flag) break;
+                umma_commit_pair(cluster_addr(&tmem_full[acc], 0));
+                umma_commit_pair(cluster_addr(&tmem_full[acc], 1));
+            }
+        }
+    } else {
+        // Epilogue warps 2..5 of each CTA: TMEM quadrant q = warp % 4 holds this CTA's tile rows [32q, 32q + 32).
+        const int q = warp & 3;
+        uint8_t* stage = gsm + size_t(kPairStages) * STAGE + size_t(q) * kGemmStageBytes;
+        const bool vec = ((reinterpret_cast<uintptr_t>(g.C) | reinterpret_cast<uintptr_t>(g.residual) |
+                           reinterpret_cast<uintptr_t>(g.bias)) & 15) == 0 &&
+                         g.ldc % 8 == 0 && g.N % 8 == 0 && (g.epi != kEpiResidual || g.ldr % 8 == 0);
+        int tile_it = 0;
+        for (int t = cluster; t < total && !abort_flag; t += nclusters, ++tile_it) {
+            const int acc = tile_it & 1;
+            if (!mbar_wait(&tmem_full[acc], unsigned((tile_it >> 1) & 1), err)) { abort_flag = 1; break; }
+            tc_fence_after();
+            int grp, row0, row_end, n0;
+            tile_of(t, grp, row0, row_end, n0);
+            const int rbase = row0 + int(rank) * 128 + q * 32;
+            const __nv_bfloat16* bias = g.bias ? g.bias + size_t(grp) * g.N : nullptr;
+            const uint32_t taddr = tmem + uint32_t(acc * kPairBN) + (uint32_t(q * 32) << 16);
+            unsigned long long best = 0ull;
+#pragma unroll 1
+            for (int c = 0; c < kPairBN / 32; ++c) {
+                float v[32];
+                tmem_load32(taddr + uint32_t(c * 32), v);
+                const int col0 = n0 + c * 32;
+                if (col0 >= g.N) continue;
+                gemm_epilogue_chunk(g, v, bias, rbase, row_end, col0, vec, stage, best);
+            }
+            if (g.argmax_keys && rbase + lane < row_end && best) atomicMax(g.argmax_keys + rbase + lane, best);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(cluster_addr(&tmem_empty[acc], 0));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, TMEM_COLS);
+    }
+}
+
 // Split-K epilogue: C[r][c] from the ksplit partial sums (added in split order), with the kEpiStore or kEpiResidual
 // epilogue of the GEMM and its argmax keys. grid = (ceil(N / 512), M); block = 256 (2 columns per thread).
 __global__ void __launch_bounds__(256) k_gemm_splitk_epilogue(GemmArgs g) {

@@ -203,6 +203,22 @@ static void gemm_bf16(cudaStream_t s, const void* A, const void* B, GemmArgs g, 
     if (g.epi == kEpiSwiglu && g.N % 32) throw ValueError("SwiGLU epilogue needs N a multiple of 32");
     const bool narrow = g.N <= 32;
     const CUtensorMap ma = bf16_tile_map(A, uint64_t(rows_a), uint64_t(g.K), kGemmBM);
+    // The CTA-pair kernel (256 x 256 tiles over two SMs, two thirds of the operand bytes per SM) measured faster only
+    // for the grouped SwiGLU GEMM of the prefill MoE (0.93 vs 0.99 ms at 32,768 x 5,760 x 2,880); the single-CTA
+    // kernel wins the dense and expert-down shapes. CHROMA_B200_PAIR_GEMM=0/1 forces it off/on where it applies.
+    static const char* pair_env = std::getenv("CHROMA_B200_PAIR_GEMM");
+    const bool pair_auto = g.offsets && g.epi == kEpiSwiglu && rows_a >= 8192;
+    const bool pair_on = pair_env ? pair_env[0] == '1' : pair_auto;
+    if (pair_on && !narrow && sms >= 2) {
+        const int pair_tiles = g.offsets ? sms : ((g.M + kPairBM - 1) / kPairBM) * ((g.N + kPairBN - 1) / kPairBN);
+        if (g.offsets ? rows_a >= 8192 : (g.M >= 1024 && pair_tiles * 2 >= sms)) {
+            const CUtensorMap mb2 = bf16_tile_map(B, uint64_t(rows_b), uint64_t(g.K), 128);
+            g.ksplit = 1;
+            const dim3 grid(unsigned(2 * std::max(1, std::min(pair_tiles, sms / 2))));
+            launch(s, grid, dim3(kGemmThreads), kPairSmemBytes, k_gemm_bf16_pair, ma, mb2, g, err);
+            return;
+        }
+    }
     const CUtensorMap mb = bf16_tile_map(B, uint64_t(rows_b), uint64_t(g.K), narrow ? 32 : 256);
     (void)tile_scratch;  // tile prefix sums are computed in the kernel's prologue
     const int bn = narrow ? 32 : 256;

@@ -7,6 +7,10 @@ results agree to 1 bf16 ulp: rtol 1e-2, atol 1e-2 x the output scale.
 
 from __future__ import annotations
 
+import os
+import sys
+from pathlib import Path
+
 import ctypes
 
 import numpy as np
@@ -84,6 +88,56 @@ def test_grouped_swiglu_and_expert(gpu: None) -> None:
     g = torch.Generator(device="cuda").manual_seed(2)
     E, k, i2 = 8, 2880, 5760
     counts = [0, 130, 1, 257, 0, 64, 500, 7]
+    offsets = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    m = int(offsets[-1])
+    a = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    w1 = (torch.randn(E * i2, k, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    b1 = torch.randn(E, i2, generator=g, device="cuda").to(torch.bfloat16)
+    off = torch.from_numpy(offsets).cuda()
+    got = gemm(a, w1, b1, epi=SWIGLU, groups=E, offsets=off, n=i2)
+    want = torch.empty(m, i2 // 2, device="cuda")
+    for e in range(E):
+        lo, hi = int(offsets[e]), int(offsets[e + 1])
+        if hi > lo:
+            want[lo:hi] = reference(a[lo:hi], w1[e * i2 : (e + 1) * i2], b1[e], None, SWIGLU)
+    check(got, want)
+    w2 = (torch.randn(E * k, i2 // 2, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    b2 = torch.randn(E, k, generator=g, device="cuda").to(torch.bfloat16)
+    got2 = gemm(got, w2, b2, epi=EXPERT, groups=E, offsets=off, n=k)
+    want2 = torch.empty(m, k, device="cuda")
+    for e in range(E):
+        lo, hi = int(offsets[e]), int(offsets[e + 1])
+        if hi > lo:
+            want2[lo:hi] = reference(got[lo:hi], w2[e * k : (e + 1) * k], b2[e], None, EXPERT)
+    check(got2, want2)
+
+
+def test_pair_kernel_dense_residual_ragged(gpu: None, monkeypatch: pytest.MonkeyPatch) -> None:
+    """The CTA-pair kernel on dense problems (forced; by default it serves only the grouped SwiGLU GEMM): 256-row
+    tiles that end mid-tile, N not a multiple of 256. Runs in a subprocess so the environment switch is read fresh."""
+    import subprocess
+
+    code = "import tests.test_gpu_gemm as t; t._pair_dense_body()"
+    env = dict(os.environ, CHROMA_B200_PAIR_GEMM="1")
+    subprocess.run([sys.executable, "-c", code], check=True, env=env, cwd=str(Path(__file__).resolve().parents[1]))
+
+
+def _pair_dense_body() -> None:
+    g = torch.Generator(device="cuda").manual_seed(5)
+    m, n, k = 3000, 2880, 4096
+    a = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    b = (torch.randn(n, k, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    bias = torch.randn(n, generator=g, device="cuda").to(torch.bfloat16)
+    res = torch.randn(m, n, generator=g, device="cuda").to(torch.bfloat16)
+    check(gemm(a, b, bias, res, RESIDUAL), reference(a, b, bias, res, RESIDUAL))
+    check(gemm(a, b, bias), reference(a, b, bias, None, STORE))
+
+
+def test_pair_kernel_grouped_ragged(gpu: None) -> None:
+    """Grouped problems of >= 8192 rows take the CTA-pair kernel; groups end inside 256-row tiles, some are empty."""
+    g = torch.Generator(device="cuda").manual_seed(6)
+    E, k, i2 = 8, 2880, 5760
+    counts = [0, 2050, 1, 3000, 0, 777, 2500, 7]
     offsets = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
     m = int(offsets[-1])
     a = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
