@@ -38,6 +38,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 A100_DECODE_STEP_MS = 3.27  # reference, docs/benchmarks.md:37
+# The reference's compiled CPU program (blas=False, 1 thread) for one C4-width layer over 16 tokens plus the vocab
+# projection of those 16 rows (oracle/_ref/c4_slice_fwd16): 22.5 GFLOP in 10.59 s = 2.12 GFLOP/s, timed in the
+# build container (the 3.9 GB program does not travel to the GPU hosts). C4/C5 CPU baselines extrapolate by FLOPs.
+REF_CPU_GFLOPS = 22.5 / 10.59
 A100_FWD8_MS = 4.25  # reference, docs/benchmarks.md:23
 CONTEXT = 256
 PREFILL = 8
@@ -182,6 +186,14 @@ def prefill_flops(cfg, batch: int, n: int) -> float:  # type: ignore[no-untyped-
     return cfg.num_hidden_layers * (gemm + attention) + 2 * batch * cfg.vocab_size * d
 
 
+def decode_flops_per_token(cfg, ctx: int) -> float:  # type: ignore[no-untyped-def]
+    """Algorithmic FLOPs of one cached decode token (projections, router, top-k experts, attention over ctx, vocab)."""
+    d, H, KV, hd, E, k, I = (cfg.hidden_size, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim,
+                             cfg.num_experts, cfg.experts_per_token, cfg.intermediate_size)
+    per_layer = 2 * ((H + 2 * KV) * hd * d + d * H * hd + E * d + k * (2 * I * d + d * I)) + 4 * H * ctx * hd
+    return cfg.num_hidden_layers * per_layer + 2 * cfg.vocab_size * d
+
+
 def bench_c4(args: argparse.Namespace, rng: np.random.Generator, max_over_ranks, barrier, rank: int = 0,
              world: int = 1) -> dict:  # type: ignore[no-untyped-def]
     """GPT-OSS-20B-shaped prefill of 4 x 2048 tokens per GPU (config C4): bf16 weights N(0, 0.02) generated in
@@ -256,6 +268,10 @@ def bench_c4(args: argparse.Namespace, rng: np.random.Generator, max_over_ranks,
         "frac_of_bf16_sustained": flops / t / 1e12 / (peak * world),
         "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (x GPUs)",
         "argmax_head": [int(v) for v in ids[:2]],
+        "cpu_baseline": {"value": batch * n / (prefill_flops(cfg, batch, n) / 1e9 / REF_CPU_GFLOPS), "unit": "tokens/s",
+                         "cores": 1, "kind": "reference (extrapolated)",
+                         "sample": "reference compiled CPU program for one C4-width layer, 16 tokens (10.59 s in the "
+                                   "build container, 2.12 GFLOP/s), extrapolated by FLOPs to this prefill"},
     }
 
 
@@ -346,6 +362,10 @@ def bench_c5(args: argparse.Namespace, max_over_ranks, barrier, rank: int, world
                          "measured copy peak of one GPU",
         "e2e": None,
         "argmax_head": [int(v) for v in ids[:2]],
+        "cpu_baseline": {"value": 1.0 / (decode_flops_per_token(cfg, ctx) / 1e9 / REF_CPU_GFLOPS), "unit": "tokens/s",
+                         "cores": 1, "kind": "reference (extrapolated)",
+                         "sample": "the C4-layer CPU rate (2.12 GFLOP/s, reference compiled program, 1 thread) "
+                                   "applied to one C5 decode token's FLOPs"},
     }
 
 
