@@ -80,6 +80,21 @@ def routes_match(ours: np.ndarray, ref: np.ndarray, gates: np.ndarray, k: int) -
     return ok
 
 
+def routes_match_near(ours: np.ndarray, ref: np.ndarray, gates: np.ndarray, k: int, rel: float = 1 / 64) -> np.ndarray:
+    """Per (layer, token): True when the routing equals the reference's, or differs only among experts whose gate
+    logits lie within ``rel`` (relative) of the k-th largest: near-ties that the accumulation order of earlier GEMMs
+    decides (see ``near_tie``). Experts clearly above the boundary must be selected by both."""
+    ok = np.all(ours == ref, axis=-1)
+    for idx in zip(*np.nonzero(~ok)):
+        g = np.asarray(gates[idx], np.float64)
+        kth = np.sort(g)[::-1][k - 1]
+        tol = rel * max(abs(kth), 1e-6)
+        a, b = set(ours[idx].tolist()), set(ref[idx].tolist())
+        clear = set(np.nonzero(g > kth + tol)[0].tolist())
+        ok[idx] = clear <= a and clear <= b and all(abs(g[e] - kth) <= tol for e in a ^ b)
+    return ok
+
+
 def assert_bf16_logits(got: np.ndarray, want: np.ndarray, rel: float = 2e-2, elementwise_share: float = 0.99) -> None:
     """bf16 logits bar: every |got - want| <= rel * (largest |want| of its row), and at least `elementwise_share` of
     the elements also within rel relative / rel absolute. Elementwise relative error alone is ill-conditioned for

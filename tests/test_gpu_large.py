@@ -99,25 +99,26 @@ def test_flash_prefill_chunks_cache_and_window_match_oracle(gpu: None) -> None:
     assert strict >= 4
 
 
-def test_128_expert_routing_prefill_and_decode_match_oracle(gpu: None) -> None:
-    """C5's routing shape (128 experts, top-4) at reduced widths: a 16-token prefill and decode steps against the
-    oracle; rows whose returned token has a near-tie at the top-4 boundary are held to the greedy token only."""
+def test_128_expert_routing_matches_oracle(gpu: None) -> None:
+    """C5's routing shape (128 experts, top-4) at reduced widths, a 16-token forward against the oracle: with 128
+    bf16 gate logits per token, near-ties at the top-4 boundary are common, so routes must match except among
+    experts within 1/64 of the boundary (helpers.routes_match_near); tokens routed identically in every layer are
+    held to the bf16 logits bar and the greedy token."""
     cfg = dataclasses.replace(models.gpt_oss_120b, num_hidden_layers=2, hidden_size=1024, intermediate_size=1024,
                               num_attention_heads=16, num_key_value_heads=2, vocab_size=8192)
     assert cfg.num_experts == 128 and cfg.experts_per_token == 4
     model = models.random_transformer(cfg, seed=41, std=0.02, dtype=torch.bfloat16)
-    tokens = np.random.default_rng(42).integers(0, cfg.vocab_size, 22)
-    prefill = chroma_b200.compile_model(model, _TMP / "e128pre", steps=16, context=64)
-    decode = chroma_b200.compile_model(model, _TMP / "e128dec", steps=1, context=64)
-    ref = og.Decoder(og.Config.from_model_config(cfg), og.Params.from_module(model), context=64, prefill_steps=16)
-    strict = 0
-    with chroma_b200.Decoder(prefill, decode) as dec:
-        for part in [tokens[:16]] + [tokens[i : i + 1] for i in range(16, 22)]:
-            got = np.asarray(dec.append(part), np.float32)
-            trace = og.Trace()
-            want = ref.append(part, trace)
-            assert int(np.argmax(got)) == int(np.argmax(want))
-            if not any(helpers.near_tie(g[len(part) - 1], 4).any() for g in trace.gates[-2:]):
-                helpers.assert_bf16_logits(got, want)
-                strict += 1
-    assert strict >= 4
+    tokens = np.random.default_rng(42).integers(0, cfg.vocab_size, 16)
+    with chroma_b200.compile_model(model, _TMP / "e128fwd", steps=16) as program:
+        assert program.stats["tensor_core_path"]
+        logits = np.asarray(program(tokens), np.float32)
+        routes = program.native.routes()
+    trace = og.Trace()
+    want = og.forward(og.Config.from_model_config(cfg), og.Params.from_module(model), tokens, trace)
+    ref_routes, gates = np.stack(trace.routes), np.stack(trace.gates)
+    ok = helpers.routes_match_near(routes, ref_routes, gates, 4)
+    assert ok.all(), np.argwhere(~ok)
+    exact = np.all(routes == ref_routes, axis=-1).all(axis=0)
+    assert exact.sum() >= 6, exact
+    helpers.assert_bf16_logits(logits[exact], want[exact])
+    np.testing.assert_array_equal(np.argmax(logits[exact], -1), np.argmax(want[exact], -1))
