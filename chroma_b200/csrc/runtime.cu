@@ -12,6 +12,7 @@
 
 #include "../../include/chroma_b200.h"
 #include "flash.cuh"
+#include "flash_tc.cuh"
 #include "ep.cuh"
 #include "gemm.cuh"
 #include "gptoss.cuh"
@@ -181,6 +182,30 @@ static CUtensorMap bf16_tile_map(const void* base, uint64_t rows, uint64_t cols,
                                       elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+    return map;
+}
+
+// bf16 tensor of rank 3 or 4 (dims innermost first, byte strides of dims 1..rank-1) read in boxes with the 128-byte
+// swizzle; the innermost box is 64 elements (one 128-byte row).
+static CUtensorMap bf16_map_nd(const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                               const uint32_t* box) {
+    if (reinterpret_cast<uintptr_t>(base) % 16) throw ValueError("TMA operands need 16-byte aligned bases");
+    for (int i = 0; i < rank - 1; ++i)
+        if (strides[i] % 16) throw ValueError("TMA strides must be multiples of 16 bytes");
+    CUtensorMap map;
+    cuuint64_t d[5];
+    cuuint64_t st[4];
+    cuuint32_t bx[5], el[5];
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        bx[i] = box[i];
+        el[i] = 1;
+    }
+    for (int i = 0; i < rank - 1; ++i) st[i] = strides[i];
+    const CUresult res = encode_tiled()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cuuint32_t(rank), const_cast<void*>(base), d,
+                                        st, bx, el, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (res != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(res)));
     return map;
 }
 
@@ -724,6 +749,42 @@ struct LargeExec {
                 fa.slots = mask_mode == kMaskSlots ? io.slots : nullptr;
                 fa.pos0 = mask_mode == kMaskSlots ? io.pos0 : nullptr;
                 if (mask_mode != kMaskSlots) fa.ctx = 0;
+                // CHROMA_B200_FLASH_TC=1 selects the tcgen05 flash kernel (correct, but slower than the mma.sync one
+                // until its softmax overlaps the tensor core: 1.05 vs 0.71 ms per C4 layer).
+                static const bool tc_flash = [] {
+                    const char* e = std::getenv("CHROMA_B200_FLASH_TC");
+                    return e && e[0] == '1';
+                }();
+                if (tc_flash) {
+                    // tcgen05 flash attention: Q, K, V tiles through TMA tensor maps.
+                    FlashMaps fm;
+                    const uint64_t KVb = uint64_t(dm.KV) * 128;
+                    {
+                        const uint64_t dims[3] = {64, uint64_t(dm.H), uint64_t(N)};
+                        const uint64_t st[2] = {128, uint64_t(dm.H) * 128};
+                        const uint32_t box[3] = {64, 1, kFtRows};
+                        fm.q = bf16_map_nd(q, 3, dims, st, box);
+                    }
+                    {
+                        const uint64_t dims[3] = {64, uint64_t(dm.KV), uint64_t(N)};
+                        const uint64_t st[2] = {128, KVb};
+                        const uint32_t box[3] = {64, 1, kFtKeys};
+                        fm.kn = bf16_map_nd(nk, 3, dims, st, box);
+                        fm.vn = bf16_map_nd(nv, 3, dims, st, box);
+                    }
+                    if (fa.ctx > 0) {
+                        const uint64_t dims[4] = {64, uint64_t(dm.KV), uint64_t(ctx), uint64_t(B)};
+                        const uint64_t st[3] = {128, KVb, uint64_t(L) * ctx * KVb};
+                        const uint32_t box[4] = {64, 1, kFtKeys, 1};
+                        fm.kc = bf16_map_nd(ck, 4, dims, st, box);
+                        fm.vc = bf16_map_nd(cv, 4, dims, st, box);
+                    } else {
+                        fm.kc = fm.kn;
+                        fm.vc = fm.vn;
+                    }
+                    launch(s, dim3((n + kFtRows - 1) / kFtRows, dm.H, B), dim3(kFtThreads), kFtSmemBytes,
+                           k_flash_prefill_tc, fm, fa, w.sinks, attn, err);
+                } else
                 launch(s, dim3((n + kFaRows - 1) / kFaRows, dm.H, B), dim3(kFaThreads), kFaSmemBytes, k_flash_prefill, q, fa, ck, cv,
                        static_cast<const bf16*>(nk), static_cast<const bf16*>(nv), w.sinks, attn);
             } else if (mask_mode == kMaskSlots && n * dm.G <= kFdRows) {

@@ -119,3 +119,14 @@ def near_tie(gates: np.ndarray, k: int, rel: float = 1 / 64) -> np.ndarray:
         return np.zeros(g.shape[0], bool)
     gap = np.abs(g[:, k - 1] - g[:, k])
     return gap <= rel * np.maximum(np.abs(g[:, k - 1]), np.abs(g[:, k]))
+
+
+def assert_greedy_token(got: np.ndarray, want: np.ndarray, rel: float = 1e-2) -> None:
+    """The greedy token of each row equals the reference's, unless the reference's own top logits are within
+    ``rel`` x the row's largest |logit| of each other (a bf16 near-tie that summation order decides); then the
+    chosen token must be one of those near-top logits."""
+    got, want = np.atleast_2d(np.asarray(got, np.float64)), np.atleast_2d(np.asarray(want, np.float64))
+    for g, w in zip(got, want):
+        a, b = int(np.argmax(g)), int(np.argmax(w))
+        if a != b:
+            assert w[a] >= w[b] - rel * np.max(np.abs(w)), f"greedy token {a} (ref {w[a]:.5g}) vs {b} (ref {w[b]:.5g})"

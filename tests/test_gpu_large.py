@@ -91,7 +91,7 @@ def test_flash_prefill_chunks_cache_and_window_match_oracle(gpu: None) -> None:
             got = np.asarray(dec.append(part), np.float32)
             trace = og.Trace()
             want = ref.append(part, trace)
-            assert int(np.argmax(got)) == int(np.argmax(want))
+            helpers.assert_greedy_token(got, want)
             last = size - 1 - 384 * ((size - 1) // 384) if size > 1 else 0  # last real row of the final chunk
             if not any(helpers.near_tie(g[last], cfg.experts_per_token).any() for g in trace.gates[-2:]):
                 helpers.assert_bf16_logits(got, want)
@@ -122,3 +122,15 @@ def test_128_expert_routing_matches_oracle(gpu: None) -> None:
     assert exact.sum() >= 6, exact
     helpers.assert_bf16_logits(logits[exact], want[exact])
     np.testing.assert_array_equal(np.argmax(logits[exact], -1), np.argmax(want[exact], -1))
+
+
+def test_tcgen05_flash_kernel_matches_oracle(gpu: None) -> None:
+    """The tcgen05 flash-attention kernel (opt-in, CHROMA_B200_FLASH_TC=1) through the same long-chunk case, in a
+    subprocess so the switch is read fresh."""
+    import os
+    import subprocess
+    import sys
+
+    code = "import tests.test_gpu_large as t; t.test_flash_prefill_chunks_cache_and_window_match_oracle(None)"
+    env = dict(os.environ, CHROMA_B200_FLASH_TC="1")
+    subprocess.run([sys.executable, "-c", code], check=True, env=env, cwd=str(Path(__file__).resolve().parents[1]))
