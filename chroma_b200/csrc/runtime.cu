@@ -13,6 +13,7 @@
 #include "../../include/chroma_b200.h"
 #include "flash.cuh"
 #include "flash_tc.cuh"
+#include "decode_cluster.cuh"
 #include "ep.cuh"
 #include "gemm.cuh"
 #include "gptoss.cuh"
@@ -24,6 +25,7 @@
 #include <cstring>
 #include <algorithm>
 #include <array>
+#include <type_traits>
 #include <vector>
 #include <fstream>
 #include <map>
@@ -151,6 +153,31 @@ static void launch(cudaStream_t s, dim3 grid, dim3 block, size_t smem, void (*ke
     cfg.numAttrs = 1;
     check(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), "kernel launch");
 }
+
+// Launch configuration of a kernel run as thread-block clusters of `cluster` CTAs (sizes above 8 are opted in),
+// with programmatic dependent launch like launch().
+struct ClusterLaunch {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[2];
+    template <typename... Params>
+    ClusterLaunch(cudaStream_t s, dim3 grid, dim3 block, size_t smem, int cluster, void (*kernel)(Params...)) {
+        check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)), "smem attribute");
+        if (cluster > 8) check(cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                               "cluster size attribute");
+        cfg.gridDim = grid;
+        cfg.blockDim = block;
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s;
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = unsigned(cluster);
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+    }
+};
 
 // ---------------------------------------------------------------------------------------------------------
 // TMA tensor maps. cuTensorMapEncodeTiled is a driver entry point, fetched at run time (no link against libcuda).
@@ -959,6 +986,12 @@ struct GptExec {
     const char* prefetch_base = nullptr;
     size_t prefetch_bytes = 0;
 
+    // One-token decode of dev-sized fp32 models: every layer in one cluster launch (decode_cluster.cuh).
+    bool cluster_decode = false;
+    int dc_kpc = 0;
+    size_t dc_smem = 0;
+    DevBuf dc_layers, dc_windows;
+
     GptExec() = default;
     GptExec(const GptExec&) = delete;
     GptExec& operator=(const GptExec&) = delete;
@@ -1042,6 +1075,82 @@ struct GptExec {
         }
         counters = DevBuf(N * d.KV * sizeof(unsigned));
         check(cudaMemset(counters.p, 0, counters.bytes), "attention counters");
+        init_cluster_decode();
+    }
+
+    // The cluster path takes a single new token of a cached fp32 program whose widths fit its fixed work split
+    // (d = H*hd = I = 128: one row of 128 per warp and lane-float4; QKV rows <= 2 per warp; k*I pairs <= 4 per
+    // warp; E <= 16 gate rows; head_dim dividing 32 with room for the (max, sum) pair; ctx + 1 keys over 16 CTAs of
+    // at most 32 keys) and whose shared memory fits. CHROMA_B200_DECODE_CLUSTER=0 keeps the per-layer kernels.
+    void init_cluster_decode() {
+        const Dims& d = m->dm;
+        const int L = m->desc.layers;
+        const char* env = std::getenv("CHROMA_B200_DECODE_CLUSTER");
+        if (env && env[0] == '0') return;
+        if (m->desc.storage != CHROMA_B200_FP32 || m->desc.kind != CHROMA_B200_GPTOSS_CACHED) return;
+        if (mask_mode != kMaskSlots || B * n != 1) return;
+        if (d.d != 128 || d.H * d.hd != 128 || d.I != 128) return;
+        if ((d.H + 2 * d.KV) * d.hd > kDcRows1 * kDcWarps || d.k > kDcMaxK || d.k * d.I > kDcPairs * kDcWarps) return;
+        if (d.E > kDcMaxE || d.E < d.k || d.hd % 4 != 0 || 32 % d.hd != 0 || d.hd + 2 > 32) return;
+        const int kpc = (ctx + 1 + kDcC - 1) / kDcC;
+        if (kpc > 32) return;
+        const DcLayout lay(d, L, kpc);
+        const size_t smem = size_t(lay.total) * 4;
+        if (smem > 200 * 1024) return;
+        ClusterLaunch cl(nullptr, dim3(kDcC), dim3(kThreads), smem, kDcC, k_decode_cluster<1>);
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, k_decode_cluster<1>, &cl.cfg) != cudaSuccess || clusters < 1) {
+            cudaGetLastError();
+            return;
+        }
+        std::vector<LayerW<float>> lw(static_cast<size_t>(L));
+        std::vector<int> win(static_cast<size_t>(L));
+        for (int l = 0; l < L; ++l) {
+            lw[size_t(l)] = m->layer<float>(l);
+            win[size_t(l)] = m->layer_window[size_t(l)] != 0 ? window : ctx;
+        }
+        dc_layers = DevBuf(lw.size() * sizeof(LayerW<float>));
+        dc_windows = DevBuf(win.size() * sizeof(int));
+        check(cudaMemcpy(dc_layers.p, lw.data(), dc_layers.bytes, cudaMemcpyHostToDevice), "cluster layer table");
+        check(cudaMemcpy(dc_windows.p, win.data(), dc_windows.bytes, cudaMemcpyHostToDevice), "cluster window table");
+        dc_kpc = kpc;
+        dc_smem = smem;
+        cluster_decode = true;
+    }
+
+    // Kernels of this repository one enqueue() launches (the side-stream prefetch included).
+    int planned_launches() const {
+        if (large_path) return large.launches;
+        const int pre = side ? 1 : 0;
+        return cluster_decode ? pre + 2 : pre + 1 + 5 * m->desc.layers + 2;
+    }
+
+    void enqueue_cluster_decode(cudaStream_t s) {
+        DecodeClusterArgs a;
+        a.dm = m->dm;
+        a.L = m->desc.layers;
+        a.ctx = ctx;
+        a.kpc = dc_kpc;
+        a.layers = dc_layers.as<const LayerW<float>>();
+        a.windows = dc_windows.as<const int>();
+        a.emb = reinterpret_cast<const float*>(m->at(0));
+        a.final_norm = reinterpret_cast<const float*>(m->at(1));
+        a.inv_freq = m->inv_freq.as<const float>();
+        a.tokens = io.tokens;
+        a.positions = io.positions;
+        a.pos0 = io.pos0;
+        a.slots = io.slots;
+        a.cache_k = static_cast<const float*>(io.cache_k);
+        a.cache_v = static_cast<const float*>(io.cache_v);
+        a.new_k = static_cast<float*>(io.new_k);
+        a.new_v = static_cast<float*>(io.new_v);
+        a.routes = io.routes;
+        a.rows = io.rows;
+        a.tf = tf;
+        a.keys = io.keys;
+        a.err = err;
+        ClusterLaunch cl(s, dim3(kDcC), dim3(kThreads), dc_smem, kDcC, k_decode_cluster<1>);
+        check(cudaLaunchKernelEx(&cl.cfg, k_decode_cluster<1>, a), "cluster decode launch");
     }
 
     template <typename T> void enqueue_t(cudaStream_t s) {
@@ -1056,6 +1165,15 @@ struct GptExec {
             check(cudaGetLastError(), "prefetch launch");
             check(cudaEventRecord(join_ev, side), "prefetch join");
             ++launches;
+        }
+        if constexpr (std::is_same_v<T, float>) {
+            if (cluster_decode) {
+                enqueue_cluster_decode(s);
+                enqueue_vocab_t<T>(s);
+                launches += 2;
+                if (side) check(cudaStreamWaitEvent(s, join_ev, 0), "prefetch join");
+                return;
+            }
         }
         launch(s, dim3(N), dim3(128), 0, k_embed<T>, io.tokens, N, reinterpret_cast<const T*>(m->at(0)), dm.V, dm.d, x,
                err);
@@ -1919,8 +2037,8 @@ int chroma_b200_decoder_advance(chroma_b200_decoder* d, const int64_t* tokens, c
 }
 
 int32_t chroma_b200_decoder_step_launches(const chroma_b200_decoder* d) {
-    // positions + decode program (embed, 5 per layer, final norm, vocab with fused argmax) + commit + advance
-    return d ? 1 + (1 + 5 * d->L + 2) + 2 : 0;
+    // positions + decode program (with its L2 prefetch) + commit + advance
+    return d ? 1 + d->ex[1].planned_launches() + 2 : 0;
 }
 
 int chroma_b200_decoder_launch_vocab(chroma_b200_decoder* d, void* stream, char* err, size_t err_len) {

@@ -129,6 +129,35 @@ def test_c2_decoder_ring_wrap(gpu: None) -> None:
         np.testing.assert_allclose(out[:, g["sample_cols"]], want, **FP32)
 
 
+def _decode_sequence(prefill: str, decode: str, tokens: np.ndarray) -> tuple[np.ndarray, int]:
+    with chroma_b200.Decoder(chroma_b200.Program(prefill), chroma_b200.Program(decode)) as dec:
+        outs = [dec.append(tokens[:8])] + [dec.append([int(t)]) for t in tokens[8:]]
+        return np.concatenate(outs), dec._native.step_launches
+
+
+def test_c2_cluster_decode_matches_per_layer_kernels(gpu: None) -> None:
+    """The one-launch cluster decode of the batch-1 fp32 program against the per-layer kernel chain
+    (CHROMA_B200_DECODE_CLUSTER=0, in a subprocess) through 292 decode steps and a ring wrap: greedy ids identical,
+    logits within fp32 rounding (the two paths split the keys of the softmax differently)."""
+    tokens = golden("c2_decode")["long_tokens"]
+    prefill, decode = dev_pair()
+    out = _TMP / "per_layer.npz"
+    code = (
+        "import sys, numpy as np\n"
+        "import tests.test_gpu_gptoss as t\n"
+        "logits, launches = t._decode_sequence(sys.argv[1], sys.argv[2], np.load(sys.argv[3])['long_tokens'])\n"
+        "np.savez(sys.argv[4], logits=logits, launches=launches)\n"
+    )
+    env = dict(os.environ, CHROMA_B200_DECODE_CLUSTER="0", PYTHONPATH=str(ROOT))
+    subprocess.run([sys.executable, "-c", code, str(prefill), str(decode), str(ROOT / "tests/golden/c2_decode.npz"),
+                    str(out)], check=True, env=env, cwd=str(ROOT))
+    ref = np.load(out)
+    got, launches = _decode_sequence(str(prefill), str(decode), tokens)
+    assert launches < 8 < int(ref["launches"]), (launches, int(ref["launches"]))
+    np.testing.assert_array_equal(np.argmax(got, -1), np.argmax(ref["logits"], -1))
+    np.testing.assert_allclose(got, ref["logits"], rtol=1e-5, atol=1e-6)
+
+
 def test_c2_batch_decoder_matches_reference(gpu: None) -> None:
     g = golden("c2_decode")
     prefill, decode = dev_pair()
