@@ -1,33 +1,40 @@
 // One-token decode step of a dev-sized GPT-OSS model (fp32 storage) through EVERY layer in one launch: a cluster
-// of kDcC CTAs on kDcC SMs, the phases of each layer separated by hardware cluster barriers, activations exchanged
-// through distributed shared memory. It replaces the per-layer chain k_attn_in -> k_attention -> k_out ->
-// k_moe_up -> k_moe_down (5 dependent launches per layer, each a few microseconds of launch and drain latency
-// around well under a microsecond of work) for the batch-1 decode program (chroma/_src/decoding/cached.py:22-60
-// per step; the block of gpt_oss.py:189-265).
+// of kDcC CTAs on kDcC SMs exchanging activations through distributed shared memory. It replaces the per-layer
+// chain k_attn_in -> k_attention -> k_out -> k_moe_up -> k_moe_down (5 dependent launches per layer, each a few
+// microseconds of launch and drain latency around well under a microsecond of work) for the batch-1 decode program
+// (chroma/_src/decoding/cached.py:22-60 per step; the block of gpt_oss.py:189-265).
 //
-// Every CTA keeps its own copy of the small activations (residual x, x2, the QKV row, the attention output, the
-// expert activations) in shared memory; a phase's outputs are split over the cluster's kDcC*kWarps warps and each
-// result is stored into all kDcC copies (st.shared::cluster) before the barrier that ends the phase:
+// Every CTA keeps its own copy of the small activations (residual x, x2, the QKV row, the attention partials, the
+// expert activations) in shared memory. A phase's outputs are split over the cluster's kDcC*kWarps warps and each
+// result is pushed into all kDcC copies with st.async, whose bytes complete a transaction count on the receiving
+// CTA's mbarrier for that buffer; a CTA starts the next phase when its mbarrier has seen every byte. No fence or
+// cluster barrier sits between phases, so weight loads issued ahead stay in flight across them.
 //
-//   P1  RMSNorm (per CTA) -> QKV rows (2 per warp) -> +bias                 -> raw[]       barrier
-//       RoPE on the gathered row (per CTA); CTA 0 stages the new K/V rows for the commit kernel
+//   P1  RMSNorm (per warp) -> QKV rows (2 per warp) -> +bias                     -> raw[]
+//       RoPE on the gathered row (per CTA, cos/sin of the step's position computed once); CTA 0 stages the new
+//       K/V rows for the commit kernel
 //   P2  attention over this CTA's ceil((ctx+1)/kDcC) keys (the K/V slices of every layer are copied into shared
-//       memory by cp.async at the start), one warp per query head: (max, sum, P.V) partials -> parts[]    barrier
+//       memory by cp.async at the start), one warp per query head: (max, sum, P.V) partials -> parts[]
 //       every CTA merges the kDcC partials of every head with the sink logit (split-KV softmax, cached.py:36-47)
-//   P3  out-projection row (1 per warp) + bias + residual                   -> x2[]        barrier
-//   P4  RMSNorm + gate + top-k + softmax (per CTA), then 4 (glu, linear) row pairs of the selected experts per
-//       warp -> clamped SwiGLU                                                -> act[]       barrier
-//   P5  mlp2 column (1 per warp) of each selected expert + bias, weighted combine in slot order + residual
-//                                                                            -> x[]         barrier
+//   P3  out-projection row (1 per warp) + bias + residual                       -> x2[]
+//   P4  RMSNorm + gate rows (per CTA), top-k + softmax (per warp), then one (glu, linear) row pair of each selected
+//       expert per warp -> clamped SwiGLU                                        -> act[]
+//   P5  mlp2 column (1 per warp) of each selected expert + bias, weighted combine in slot order + residual -> x[]
 //
-// Weight rows a warp will use next are loaded into registers one phase ahead (the static QKV / out / gate rows of
-// layer l+1 during P5 of layer l; the routed expert rows of P4 and P5 together, right after the routing), so the
-// latency of the L2 reads overlaps the previous phase. The rounding points and summation orders of each dot
-// product are those of the per-layer kernels (gptoss.cuh); only the attention's split over keys differs (kDcC
-// chunks instead of 64-key chunks), as in any split-KV decode.
+// The routed expert rows are not known before P4, so at the start of every layer each CTA bulk-copies (TMA) the
+// rows its warps would use of EVERY expert (mlp1 rows 2*gw, 2*gw+1 and mlp2 row gw of each expert, with their
+// biases: 145 KB for the dev model) into shared memory behind P1-P3; P4 and P5 then read them at shared-memory
+// latency instead of waiting on L2 after the routing.
 //
-// Every CTA executes the same barrier sequence (no early exits), so the cluster barriers cannot wait on a CTA that
-// left; the kernel has no spin-waits.
+// Buffer reuse is safe without barriers: a CTA reads each exchanged buffer only before it pushes its next phase's
+// outputs, and a sender can only reach the same phase of the next layer after receiving those outputs.
+//
+// The static QKV / out / gate / norm rows of layer l+1 are loaded into registers during P5 of layer l.
+// The rounding points and summation orders of the projections are those of the per-layer kernels (gptoss.cuh);
+// the attention's split over keys and its merge order differ, as in any split-KV decode.
+//
+// Every wait is bounded (tma.cuh's poll limit): a stuck exchange raises kErrTimeout, later waits are skipped and
+// the kernel runs to its end, where one cluster barrier keeps every CTA resident until no store can target it.
 #pragma once
 
 #include "flash.cuh"
@@ -39,9 +46,10 @@ namespace cb200 {
 constexpr int kDcC = 16;                 // CTAs per cluster (non-portable size: opted in at launch)
 constexpr int kDcWarps = kDcC * kWarps;  // warps sharing each phase
 constexpr int kDcRows1 = 2;              // QKV rows per warp
-constexpr int kDcPairs = 4;              // (glu, linear) row pairs per warp
 constexpr int kDcMaxK = 4;               // experts per token
-constexpr int kDcMaxE = 2 * kWarps;      // gate rows (2 per warp)
+constexpr int kDcMaxE = 2 * kWarps;      // gate rows (2 per warp), also <= 32 for the one-slot warp top-k
+
+enum DcBar : int { kDcRaw = 0, kDcParts, kDcX2, kDcAct, kDcXs, kDcExperts, kDcBars };
 
 struct DecodeClusterArgs {
     Dims dm;
@@ -66,56 +74,96 @@ struct DecodeClusterArgs {
     unsigned* err;
 };
 
-// Shared-memory carve-up (in floats), identical on host and device.
+__host__ __device__ inline int dc_up4(int v) { return (v + 3) & ~3; }
+
+// Shared-memory carve-up (in floats), identical on host and device. The host admits d = H*hd = I = kDcWarps, so
+// warp gw owns pair gw of every expert's mlp1 (rows 2gw, 2gw+1) and row gw of every expert's mlp2.
 struct DcLayout {
-    int xs, xn, raw, qkv, parts, att, x2, gl, sidx, sw, inv, act, prow, kst, ks, vs, total;
+    int ps, kvs;  // floats per (CTA, head) partial; per cached key row (padded: conflict-free 16-byte reads)
+    int r1c, r2c; // mlp1 / mlp2 rows per CTA and expert
+    int lw, xs, raw, qkv, cs, parts, att, x2, gl, act, prow, kst, w1s, w2s, b1s, b2s, ks, vs, total;
     __host__ __device__ DcLayout(const Dims& dm, int L, int kpc) {
-        auto up4 = [](int v) { return (v + 3) & ~3; };
         const int r1 = (dm.H + 2 * dm.KV) * dm.hd;
+        ps = dc_up4(dm.hd + 2);
+        kvs = dm.KV * dm.hd + 4;
+        r1c = 2 * kWarps;
+        r2c = kWarps;
         int o = 0;
-        xs = o; o += up4(dm.d);
-        xn = o; o += up4(dm.d);
-        raw = o; o += up4(r1);
-        qkv = o; o += up4(r1);
-        parts = o; o += up4(kDcC * dm.H * (dm.hd + 2));
-        att = o; o += up4(dm.H * dm.hd);
-        x2 = o; o += up4(dm.d);
-        gl = o; o += up4(dm.E);
-        sidx = o; o += 8;
-        sw = o; o += 8;
-        inv = o; o += 4;
-        act = o; o += up4(dm.k * dm.I);
+        lw = o; o += dc_up4(L * int(sizeof(LayerW<float>) / 4));
+        xs = o; o += dc_up4(dm.d);
+        raw = o; o += dc_up4(r1);
+        qkv = o; o += dc_up4(r1);
+        cs = o; o += dc_up4(dm.hd);  // (cos, sin) * concentration per rotary frequency
+        parts = o; o += kDcC * dm.H * ps;
+        att = o; o += dc_up4(dm.H * dm.hd);
+        x2 = o; o += dc_up4(dm.d);
+        gl = o; o += dc_up4(dm.E);
+        act = o; o += dc_up4(dm.k * dm.I);
         prow = o; o += kWarps * 32;
-        kst = o; o += up4(2 * kpc);  // int64 times of this CTA's cache rows
-        ks = o; o += up4(L * kpc * dm.KV * dm.hd);
-        vs = o; o += up4(L * kpc * dm.KV * dm.hd);
+        kst = o; o += dc_up4(2 * kpc);  // int64 times of this CTA's cache rows
+        w1s = o; o += dm.E * r1c * dm.d;
+        w2s = o; o += dm.E * r2c * dm.I;
+        b1s = o; o += dm.E * r1c;
+        b2s = o; o += dm.E * r2c;
+        ks = o; o += L * kpc * kvs;
+        vs = o; o += L * kpc * kvs;
         total = o;
+    }
+    __host__ __device__ unsigned bytes(int bar, const Dims& dm) const {
+        switch (bar) {
+            case kDcRaw: return unsigned((dm.H + 2 * dm.KV) * dm.hd) * 4u;
+            case kDcParts: return unsigned(kDcC * dm.H * ps) * 4u;
+            case kDcX2: return unsigned(dm.d) * 4u;
+            case kDcAct: return unsigned(dm.k * dm.I) * 4u;
+            case kDcXs: return unsigned(dm.d) * 4u;
+            default: return unsigned(dm.E * (r1c * dm.d + r2c * dm.I + r1c + r2c)) * 4u;
+        }
     }
 };
 
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+// Remote store of 4 / 16 bytes into the shared memory of another CTA of the cluster, completing that many bytes of
+// transaction on the mbarrier `bar` (a shared::cluster address in the same CTA as `addr`).
+__device__ __forceinline__ void st_async_b32(uint32_t addr, float v, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr),
+                 "r"(__float_as_uint(v)), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void st_async_v4(uint32_t addr, float4 v, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+                 "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
+                 "r"(__float_as_uint(v.w)), "r"(bar)
+                 : "memory");
 }
 
-// Lanes 0..kDcC-1 store `v` (uniform over the warp) at `p`'s offset in CTA `lane` of the cluster.
-__device__ __forceinline__ void cluster_broadcast(float* p, float v) {
-    const int lane = threadIdx.x & 31;
-    if (lane < kDcC) st_cluster_f32(cluster_addr(p, uint32_t(lane)), v);
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, unsigned parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
 }
 
-// Warp dot product of one weight row held as NJ float4 per lane (elements lane*4 + 128*j) with a shared-memory row:
-// per-lane FMA chain then the butterfly sum, the order of warp_gemv in gptoss.cuh.
+// Lanes 0..kDcC-1 push `v` (uniform over the warp) to byte offset `off` of CTA `lane`'s shared memory, completing
+// on that CTA's mbarrier at `bar`; `rsm` / `rbar` are the lane's shared::cluster bases of that CTA's dynamic shared
+// memory and mbarrier array.
+__device__ __forceinline__ void dc_push(uint32_t rsm, uint32_t rbar, uint32_t off, int bar, float v) {
+    if ((threadIdx.x & 31) < kDcC) st_async_b32(rsm + off, v, rbar + 8u * unsigned(bar));
+}
+
+// Warp dot product of one weight row held as NJ float4 per lane (elements lane*4 + 128*j) with an activation row
+// held the same way: per-lane FMA chain then the butterfly sum, the order of warp_gemv in gptoss.cuh.
 template <int NJ>
-__device__ __forceinline__ float dc_dot(const float (&w)[NJ][4], const float* x) {
-    const int lane = threadIdx.x & 31;
+__device__ __forceinline__ float dc_dot(const float (&w)[NJ][4], const float (&x)[NJ][4]) {
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < NJ; ++j) {
-        const float4 v = *reinterpret_cast<const float4*>(x + lane * 4 + 128 * j);
-        s = fmaf(w[j][0], v.x, s);
-        s = fmaf(w[j][1], v.y, s);
-        s = fmaf(w[j][2], v.z, s);
-        s = fmaf(w[j][3], v.w, s);
+        s = fmaf(w[j][0], x[j][0], s);
+        s = fmaf(w[j][1], x[j][1], s);
+        s = fmaf(w[j][2], x[j][2], s);
+        s = fmaf(w[j][3], x[j][3], s);
     }
     return warp_sum(s);
 }
@@ -127,20 +175,30 @@ __device__ __forceinline__ void dc_load(float (&w)[NJ][4], const float* row) {
     for (int j = 0; j < NJ; ++j) load4(row + lane * 4 + 128 * j, w[j]);
 }
 
-// out = x * (1/sqrt(mean(x^2) + eps)) * w over one row (the reduction order of rows_rmsnorm). Ends synchronised.
-__device__ __forceinline__ void dc_norm(const float* x, float* out, int d, float eps, const float* __restrict__ w,
-                                        float* inv) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp == 0) {
-        float s = 0.f;
-        for (int c = lane; c < d; c += 32) s = fmaf(x[c], x[c], s);
-        s = warp_sum(s);
-        if (lane == 0) *inv = 1.0f / sqrtf(s / float(d) + eps);
+template <int NJ>
+__device__ __forceinline__ void dc_read(float (&x)[NJ][4], const float* row) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+        const float4 v = *reinterpret_cast<const float4*>(row + lane * 4 + 128 * j);
+        x[j][0] = v.x; x[j][1] = v.y; x[j][2] = v.z; x[j][3] = v.w;
     }
-    __syncthreads();
-    const float iv = *inv;
-    for (int c = threadIdx.x; c < d; c += blockDim.x) out[c] = __fmul_rn(__fmul_rn(x[c], iv), w[c]);
-    __syncthreads();
+}
+
+// This lane's elements of RMSNorm(x) * w, computed by every warp on its own (the reduction order of
+// rows_rmsnorm: lane-strided FMA chain, butterfly sum), so no block barrier is needed.
+template <int NJ>
+__device__ __forceinline__ void dc_norm(float (&out)[NJ][4], const float* x, int d, float eps, const float (&w)[NJ][4]) {
+    const int lane = threadIdx.x & 31;
+    float s = 0.f;
+    for (int c = lane; c < d; c += 32) s = fmaf(x[c], x[c], s);
+    s = warp_sum(s);
+    const float iv = 1.0f / sqrtf(s / float(d) + eps);
+    dc_read<NJ>(out, x);
+#pragma unroll
+    for (int j = 0; j < NJ; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) out[j][i] = __fmul_rn(__fmul_rn(out[j][i], iv), w[j][i]);
 }
 
 // Per-warp weight rows of one layer that do not depend on the routing.
@@ -150,6 +208,9 @@ template <int NJ> struct DcStatic {
     float out[NJ][4];
     float out_b;
     float gate[2][NJ][4];
+    float gate_b[2];
+    float attn_norm[NJ][4];
+    float mlp_norm[NJ][4];
 };
 
 template <int NJ>
@@ -171,29 +232,91 @@ __device__ __forceinline__ void dc_load_static(DcStatic<NJ>& s, const LayerW<flo
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
         const int e = warp + kWarps * u;
-        if (e < dm.E) dc_load<NJ>(s.gate[u], w.gate_w + size_t(e) * dm.d);
+        if (e < dm.E) {
+            dc_load<NJ>(s.gate[u], w.gate_w + size_t(e) * dm.d);
+            s.gate_b[u] = w.gate_b[e];
+        }
+    }
+    dc_load<NJ>(s.attn_norm, w.attn_norm);
+    dc_load<NJ>(s.mlp_norm, w.mlp_norm);
+}
+
+// Top-k of n <= 32 gate logits in shared memory with the ranking of warp_topk_softmax (NaN highest, ties to the
+// lowest index, sorted), then the softmax of the k values in slot order. Lane e counts the logits that outrank its
+// own (independent comparisons, no shuffle chain); the lane of rank r fills slot r. Every lane ends with all k
+// (index, weight) pairs.
+__device__ __forceinline__ bool dc_outranks(float a, int ia, float b, int ib) {
+    if (isnan(a) != isnan(b)) return isnan(a);
+    if (a != b && !(isnan(a) && isnan(b))) return a > b;
+    return ia < ib;
+}
+
+__device__ __forceinline__ void dc_topk(const float* gl, int n, int k, int (&idx)[kDcMaxK], float (&wt)[kDcMaxK]) {
+    const int lane = threadIdx.x & 31;
+    const float g = lane < n ? gl[lane] : 0.f;
+    int rank = 0;
+    for (int j = 0; j < n; ++j) rank += dc_outranks(gl[j], j, g, lane) ? 1 : 0;
+    float vals[kDcMaxK];
+#pragma unroll
+    for (int r = 0; r < kDcMaxK; ++r) {
+        const unsigned m = __ballot_sync(0xffffffffu, lane < n && rank == r);
+        idx[r] = m ? __ffs(int(m)) - 1 : 0;
+        vals[r] = __shfl_sync(0xffffffffu, g, idx[r]);
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kDcMaxK; ++r)
+        if (r < k) mx = fmaxf(mx, vals[r]);
+    float e[kDcMaxK], s = 0.f;
+#pragma unroll
+    for (int r = 0; r < kDcMaxK; ++r) {
+        e[r] = 0.f;
+        if (r < k) { e[r] = expf(vals[r] - mx); s += e[r]; }
+    }
+#pragma unroll
+    for (int r = 0; r < kDcMaxK; ++r) wt[r] = r < k ? e[r] / s : 0.f;
+}
+
+// Bulk-copies layer `w`'s expert rows of this CTA (every expert's mlp1 rows [2*kWarps*rank, +2*kWarps), mlp2 rows
+// [kWarps*rank, +kWarps) and their biases) into shared memory, completing on `bar`. Issued by one warp, one expert
+// per lane; all global addresses are 16-byte aligned (256-byte aligned tensors, 16-byte multiples of rows).
+__device__ __forceinline__ void dc_stage_experts(const LayerW<float>& w, const Dims& dm, const DcLayout& lay, float* dsm,
+                                                 int rank, uint64_t* bar) {
+    const int lane = threadIdx.x & 31;
+    if (lane == 0) mbar_arrive_expect_tx(bar, lay.bytes(kDcExperts, dm));
+    __syncwarp();
+    for (int e = lane; e < dm.E; e += 32) {
+        bulk_load(dsm + lay.w1s + size_t(e) * lay.r1c * dm.d, w.w1 + (size_t(e) * 2 * dm.I + size_t(lay.r1c) * rank) * dm.d,
+                  unsigned(lay.r1c * dm.d * 4), bar);
+        bulk_load(dsm + lay.w2s + size_t(e) * lay.r2c * dm.I, w.w2 + (size_t(e) * dm.d + size_t(lay.r2c) * rank) * dm.I,
+                  unsigned(lay.r2c * dm.I * 4), bar);
+        bulk_load(dsm + lay.b1s + e * lay.r1c, w.b1 + size_t(e) * 2 * dm.I + lay.r1c * rank, unsigned(lay.r1c * 4), bar);
+        bulk_load(dsm + lay.b2s + e * lay.r2c, w.b2 + size_t(e) * dm.d + lay.r2c * rank, unsigned(lay.r2c * 4), bar);
     }
 }
 
-// NJ = d / 128 = H*hd / 128 = I / 128 (the host admits only such models).
+// NJ = d / 128 = H*hd / 128 = I / 128 (the host admits only d = H*hd = I = 128).
 template <int NJ>
 __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArgs a) {
-    extern __shared__ __align__(16) float dsm[];
+    extern __shared__ __align__(128) float dsm[];
+    __shared__ uint64_t bars[kDcBars];
     const Dims dm = a.dm;
     const DcLayout lay(dm, a.L, a.kpc);
+    const LayerW<float>* lws = reinterpret_cast<const LayerW<float>*>(dsm + lay.lw);
     float* xs = dsm + lay.xs;
-    float* xn = dsm + lay.xn;
     float* raw = dsm + lay.raw;
     float* qkv = dsm + lay.qkv;
+    float* cs = dsm + lay.cs;
     float* parts = dsm + lay.parts;
     float* att = dsm + lay.att;
     float* x2 = dsm + lay.x2;
     float* gl = dsm + lay.gl;
-    int* sidx = reinterpret_cast<int*>(dsm + lay.sidx);
-    float* sw = dsm + lay.sw;
-    float* inv = dsm + lay.inv;
     float* act = dsm + lay.act;
     int64_t* kst = reinterpret_cast<int64_t*>(dsm + lay.kst);
+    const float* w1s = dsm + lay.w1s;
+    const float* w2s = dsm + lay.w2s;
+    const float* b1s = dsm + lay.b1s;
+    const float* b2s = dsm + lay.b2s;
     float* Ks = dsm + lay.ks;
     float* Vs = dsm + lay.vs;
 
@@ -202,13 +325,46 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
     const int gw = rank * kWarps + warp;
     const int d = dm.d, hd = dm.hd, H = dm.H, KV = dm.KV, I = dm.I;
     const int r1 = (H + 2 * KV) * hd;
-    const int row_kv = KV * hd;
+    const int row_kv = KV * hd, kvs = lay.kvs, ps = lay.ps;
     const int j0 = rank * a.kpc;                         // this CTA's first key
     const int nk = max(0, min(a.kpc, a.ctx + 1 - j0));   // its keys, the new token's included
     const int nkc = max(0, min(a.kpc, a.ctx - j0));      // of which cache rows
+    // shared::cluster bases of CTA `lane`'s dynamic shared memory and mbarriers (lanes < kDcC push to CTA lane).
+    const uint32_t rsm = cluster_addr(dsm, uint32_t(lane % kDcC));
+    const uint32_t rbar = cluster_addr(bars, uint32_t(lane % kDcC));
+    auto off = [&](const float* p) { return uint32_t(p - dsm) * 4u; };
+    bool live = true;  // false after a timed-out wait (thread 0)
 
+    // Thread 0 waits for the buffer's phase of layer l and re-arms it for layer l + 1; then the block proceeds.
+    auto sync = [&](int bar, int l) {
+        if (threadIdx.x == 0) {
+            if (live) {
+                unsigned i = 0;
+                while (i < kMaxPolls && !mbar_try_wait_cluster(&bars[bar], unsigned(l & 1))) ++i;
+                if (i == kMaxPolls) {
+                    atomicOr(a.err, kErrTimeout);
+                    live = false;
+                }
+            }
+            if (l + 1 < a.L) mbar_arrive_expect_tx(&bars[bar], lay.bytes(bar, dm));
+        }
+        __syncthreads();
+    };
+
+    {  // layer table -> shared memory
+        const unsigned long long* src = reinterpret_cast<const unsigned long long*>(a.layers);
+        unsigned long long* dst = reinterpret_cast<unsigned long long*>(dsm + lay.lw);
+        for (int i = threadIdx.x; i < a.L * int(sizeof(LayerW<float>) / 8); i += blockDim.x) dst[i] = src[i];
+    }
     DcStatic<NJ> st;
     dc_load_static<NJ>(st, a.layers[0], dm, gw);
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < kDcBars; ++b) mbar_init(&bars[b], 1);
+        fence_barrier_init();
+        for (int b = 0; b < kDcExperts; ++b) mbar_arrive_expect_tx(&bars[b], lay.bytes(b, dm));
+    }
+    __syncthreads();
+    if (warp == kWarps - 1) dc_stage_experts(a.layers[0], dm, lay, dsm, rank, &bars[kDcExperts]);
     pdl_wait();
     pdl_trigger();
 
@@ -218,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
         for (int i = threadIdx.x; i < a.L * per_layer; i += blockDim.x) {
             const int l = i / per_layer, rem = i % per_layer, jj = rem / row4, c = (rem % row4) * 4;
             const size_t src = (size_t(l) * a.ctx + j0 + jj) * row_kv + c;
-            const int dst = (l * a.kpc + jj) * row_kv + c;
+            const int dst = (l * a.kpc + jj) * kvs + c;
             cp_async16(Ks + dst, a.cache_k + src);
             cp_async16(Vs + dst, a.cache_v + src);
         }
@@ -231,23 +387,33 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
     }
     const float pos = a.positions[0];
     const int64_t t_i = a.pos0[0];
+    for (int j = threadIdx.x; j < hd / 2; j += blockDim.x) {
+        float s, c;
+        sincosf(__fmul_rn(pos, a.inv_freq[j]), &s, &c);
+        cs[2 * j] = __fmul_rn(c, dm.conc);
+        cs[2 * j + 1] = __fmul_rn(s, dm.conc);
+    }
     cp_async_wait<0>();
     __syncthreads();
-    cluster_sync_all();  // every CTA of the cluster is running before the first remote store
+    cluster_sync_all();  // every CTA runs and has armed its mbarriers before the first remote store
 
     for (int l = 0; l < a.L; ++l) {
-        const LayerW<float> w = a.layers[l];
+        const LayerW<float>& w = lws[l];
+        if (l > 0) {
+            sync(kDcXs, l - 1);  // also: every warp finished reading the previous layer's staged expert rows
+            if (warp == kWarps - 1) dc_stage_experts(w, dm, lay, dsm, rank, &bars[kDcExperts]);
+        }
         // ---- P1: norm, QKV rows, bias -> raw[] of every CTA
-        dc_norm(xs, xn, d, dm.eps, w.attn_norm, inv);
+        {
+            float xn[NJ][4];
+            dc_norm<NJ>(xn, xs, d, dm.eps, st.attn_norm);
 #pragma unroll
-        for (int u = 0; u < kDcRows1; ++u) {
-            const int r = gw + kDcWarps * u;
-            if (r < r1) {
-                const float acc = dc_dot<NJ>(st.qkv[u], xn);
-                cluster_broadcast(raw + r, __fadd_rn(acc, st.qkv_b[u]));
+            for (int u = 0; u < kDcRows1; ++u) {
+                const int r = gw + kDcWarps * u;
+                if (r < r1) dc_push(rsm, rbar, off(raw + r), kDcRaw, __fadd_rn(dc_dot<NJ>(st.qkv[u], xn), st.qkv_b[u]));
             }
         }
-        cluster_sync_all();
+        sync(kDcRaw, l);
         // RoPE of the q and k heads (gpt_oss.py:44-54), v heads copied; CTA 0 stages the new K/V rows.
         {
             const int half = hd / 2;
@@ -256,11 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
                 const float lo = raw[h * hd + j], hi = raw[h * hd + j + half];
                 float o1 = lo, o2 = hi;
                 if (h < H + KV) {
-                    const float angle = __fmul_rn(pos, a.inv_freq[j]);
-                    float s, c;
-                    sincosf(angle, &s, &c);
-                    c = __fmul_rn(c, dm.conc);
-                    s = __fmul_rn(s, dm.conc);
+                    const float c = cs[2 * j], s = cs[2 * j + 1];
                     o1 = __fsub_rn(__fmul_rn(lo, c), __fmul_rn(hi, s));
                     o2 = __fadd_rn(__fmul_rn(hi, c), __fmul_rn(lo, s));
                 }
@@ -277,20 +439,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
         __syncthreads();
         // ---- P2: attention partials over this CTA's keys, one warp per query head
         {
-            const float* Kl = Ks + size_t(l) * a.kpc * row_kv;
-            const float* Vl = Vs + size_t(l) * a.kpc * row_kv;
+            const float* Kl = Ks + size_t(l) * a.kpc * kvs;
+            const float* Vl = Vs + size_t(l) * a.kpc * kvs;
             const int window = a.windows[l];
             float* prow = dsm + lay.prow + warp * 32;
             const int groups = 32 / hd, g = lane / hd, dd = lane % hd;
+            const int chunks = ps / 4;
             for (int hq = warp; hq < H; hq += kWarps) {
                 const int kvh = hq / dm.G;
                 const float* qv = qkv + hq * hd;
                 float s = -INFINITY;
                 if (lane < nk) {
                     const int j = j0 + lane;
-                    const float* kr = j < a.ctx ? Kl + lane * row_kv + kvh * hd : qkv + (H + kvh) * hd;
+                    const float* kr = j < a.ctx ? Kl + lane * kvs + kvh * hd : qkv + (H + kvh) * hd;
                     float dot = 0.f;
-                    for (int e = 0; e < hd; ++e) dot = fmaf(qv[e], kr[e], dot);
+                    for (int e = 0; e < hd; e += 4) {
+                        const float4 k4 = *reinterpret_cast<const float4*>(kr + e);
+                        const float4 q4 = *reinterpret_cast<const float4*>(qv + e);
+                        dot = fmaf(q4.x, k4.x, dot);
+                        dot = fmaf(q4.y, k4.y, dot);
+                        dot = fmaf(q4.z, k4.z, dot);
+                        dot = fmaf(q4.w, k4.w, dot);
+                    }
                     s = __fmul_rn(dot, dm.sm_scale);
                     const int64_t t_j = j < a.ctx ? kst[lane] : t_i;
                     const bool valid = j >= a.ctx || t_j >= 0;
@@ -303,95 +473,100 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
                 prow[lane] = p;
                 __syncwarp();
                 float acc = 0.f;
-                for (int jj = g; jj < nk; jj += groups) {
-                    const int j = j0 + jj;
-                    const float* vr = j < a.ctx ? Vl + jj * row_kv + kvh * hd : qkv + (H + KV + kvh) * hd;
-                    acc = fmaf(prow[jj], vr[dd], acc);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {  // keys g, g + groups, ... (at most 32 / groups of them)
+                    const int jj = g + groups * i;
+                    if (i * groups < 32 && jj < nk) {
+                        const int j = j0 + jj;
+                        const float* vr = j < a.ctx ? Vl + jj * kvs + kvh * hd : qkv + (H + KV + kvh) * hd;
+                        acc = fmaf(prow[jj], vr[dd], acc);
+                    }
                 }
                 for (int o = hd; o < 32; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                // Partial = (max, sum, o[0..hd)) padded to ps floats; value i lives on lane i; pushed as float4s.
                 const float ov = __shfl_sync(0xffffffffu, acc, (lane + 30) & 31);  // lane i <- o[i - 2]
-                const float val = lane == 0 ? mx : (lane == 1 ? lsum : ov);
-                if (lane < hd + 2) {
-                    float* dst = parts + (rank * H + hq) * (hd + 2) + lane;
-#pragma unroll 4
-                    for (int r = 0; r < kDcC; ++r) st_cluster_f32(cluster_addr(dst, uint32_t(r)), val);
+                const float val = lane == 0 ? mx : (lane == 1 ? lsum : (lane < hd + 2 ? ov : 0.f));
+                const uint32_t base = off(parts + (rank * H + hq) * ps);
+                for (int t0 = 0; t0 < chunks * kDcC; t0 += 32) {
+                    const int t = t0 + lane;
+                    const int q = t % chunks, r = t / chunks;
+                    float4 v4;
+                    v4.x = __shfl_sync(0xffffffffu, val, (4 * q) & 31);
+                    v4.y = __shfl_sync(0xffffffffu, val, (4 * q + 1) & 31);
+                    v4.z = __shfl_sync(0xffffffffu, val, (4 * q + 2) & 31);
+                    v4.w = __shfl_sync(0xffffffffu, val, (4 * q + 3) & 31);
+                    const uint32_t rs = __shfl_sync(0xffffffffu, rsm, r & 31);
+                    const uint32_t rb = __shfl_sync(0xffffffffu, rbar, r & 31);
+                    if (t < chunks * kDcC) st_async_v4(rs + base + 16u * unsigned(q), v4, rb + 8u * kDcParts);
                 }
                 __syncwarp();
             }
         }
-        cluster_sync_all();
-        // Merge the kDcC partials of every head with its sink (the split-KV merge of k_attention).
+        sync(kDcParts, l);
+        // Merge the kDcC partials of every head with its sink (the split-KV merge of k_attention), lane c holding
+        // partial c's rescale factor.
         for (int hq = warp; hq < H; hq += kWarps) {
             const float sink = w.sinks[hq];
-            float M = sink;
-            for (int c = 0; c < kDcC; ++c) M = fmaxf(M, parts[(c * H + hq) * (hd + 2)]);
-            float Lsum = expf(sink - M);
+            const float* ph = parts + hq * ps;
+            const float mc = lane < kDcC ? ph[lane * H * ps] : -INFINITY;
+            const float M = fmaxf(sink, warp_max(mc));
+            const float ec = mc != -INFINITY ? expf(mc - M) : 0.f;
+            const float lc = lane < kDcC ? ph[lane * H * ps + 1] : 0.f;
+            const float Lsum = __fadd_rn(expf(sink - M), warp_sum(lc * ec));
+            float o = 0.f;
+#pragma unroll
             for (int c = 0; c < kDcC; ++c) {
-                const float mc = parts[(c * H + hq) * (hd + 2)];
-                if (mc != -INFINITY) Lsum += parts[(c * H + hq) * (hd + 2) + 1] * expf(mc - M);
+                const float e = __shfl_sync(0xffffffffu, ec, c);
+                if (lane < hd) o = fmaf(ph[c * H * ps + 2 + lane], e, o);
             }
-            if (lane < hd) {
-                float o = 0.f;
-                for (int c = 0; c < kDcC; ++c) {
-                    const float mc = parts[(c * H + hq) * (hd + 2)];
-                    if (mc != -INFINITY) o += parts[(c * H + hq) * (hd + 2) + 2 + lane] * expf(mc - M);
-                }
-                att[hq * hd + lane] = o / Lsum;
-            }
+            if (lane < hd) att[hq * hd + lane] = o / Lsum;
         }
         __syncthreads();
         // ---- P3: out-projection + bias + residual -> x2[]
         if (gw < d) {
-            const float acc = dc_dot<NJ>(st.out, att);
-            cluster_broadcast(x2 + gw, __fadd_rn(xs[gw], __fadd_rn(acc, st.out_b)));
+            float av[NJ][4];
+            dc_read<NJ>(av, att);
+            dc_push(rsm, rbar, off(x2 + gw), kDcX2, __fadd_rn(xs[gw], __fadd_rn(dc_dot<NJ>(st.out, av), st.out_b)));
         }
-        cluster_sync_all();
-        // ---- P4: norm, gate, top-k, softmax (every CTA), then the selected experts' mlp1 pairs -> act[]
-        dc_norm(x2, xn, d, dm.eps, w.mlp_norm, inv);
+        sync(kDcX2, l);
+        // ---- P4: norm and gate rows (per CTA), top-k and softmax (per warp), one mlp1 pair of each selected expert
+        float xn[NJ][4];
+        dc_norm<NJ>(xn, x2, d, dm.eps, st.mlp_norm);
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             const int e = warp + kWarps * u;
             if (e < dm.E) {
                 const float acc = dc_dot<NJ>(st.gate[u], xn);
-                if (lane == 0) gl[e] = __fadd_rn(acc, w.gate_b[e]);
+                if (lane == 0) gl[e] = __fadd_rn(acc, st.gate_b[u]);
+            }
+        }
+        if (threadIdx.x == 0 && live) {  // this layer's staged expert rows
+            unsigned i = 0;
+            while (i < kMaxPolls && !mbar_try_wait(&bars[kDcExperts], unsigned(l & 1))) ++i;
+            if (i == kMaxPolls) {
+                atomicOr(a.err, kErrTimeout);
+                live = false;
             }
         }
         __syncthreads();
-        if (warp == 0) warp_topk_softmax<float>(gl, dm.E, dm.k, sidx, sw);
-        __syncthreads();
-        if (rank == 0 && a.routes && threadIdx.x < dm.k) a.routes[size_t(l) * dm.k + threadIdx.x] = sidx[threadIdx.x];
-        float w1[kDcPairs][2][NJ][4], b1[kDcPairs][2];
-        float w2[kDcMaxK][NJ][4], b2[kDcMaxK];
+        int sidx[kDcMaxK];
+        float sw[kDcMaxK];
+        dc_topk(gl, dm.E, dm.k, sidx, sw);
+        if (rank == 0 && warp == 0 && a.routes) {
 #pragma unroll
-        for (int u = 0; u < kDcPairs; ++u) {
-            const int P = gw + kDcWarps * u;
-            if (P < dm.k * I) {
-                const int s = P / I, p = P % I;
-                const int e = int(checked_row(sidx[s], dm.E, true, a.err));
-                const float* W1 = w.w1 + (size_t(e) * 2 * I + 2 * p) * d;
-                dc_load<NJ>(w1[u][0], W1);
-                dc_load<NJ>(w1[u][1], W1 + d);
-                b1[u][0] = w.b1[size_t(e) * 2 * I + 2 * p];
-                b1[u][1] = w.b1[size_t(e) * 2 * I + 2 * p + 1];
-            }
-        }
-        if (gw < d) {
-#pragma unroll
-            for (int u = 0; u < kDcMaxK; ++u) {
-                if (u < dm.k) {
-                    const int e = int(checked_row(sidx[u], dm.E, true, a.err));
-                    dc_load<NJ>(w2[u], w.w2 + (size_t(e) * d + gw) * I);
-                    b2[u] = w.b2[size_t(e) * d + gw];
-                }
-            }
+            for (int r = 0; r < kDcMaxK; ++r)
+                if (r == lane && r < dm.k) a.routes[size_t(l) * dm.k + r] = sidx[r];
         }
 #pragma unroll
-        for (int u = 0; u < kDcPairs; ++u) {
-            const int P = gw + kDcWarps * u;
-            if (P < dm.k * I) {
-                const int s = P / I, p = P % I;
-                const float hg = __fadd_rn(dc_dot<NJ>(w1[u][0], xn), b1[u][0]);
-                const float hlin = __fadd_rn(dc_dot<NJ>(w1[u][1], xn), b1[u][1]);
+        for (int u = 0; u < kDcMaxK; ++u) {
+            if (u < dm.k) {
+                const int e = int(checked_row(sidx[u], dm.E, true, a.err));
+                float wg[NJ][4], wl[NJ][4];
+                const float* W1 = w1s + (size_t(e) * lay.r1c + 2 * warp) * d;
+                dc_read<NJ>(wg, W1);
+                dc_read<NJ>(wl, W1 + d);
+                const float hg = __fadd_rn(dc_dot<NJ>(wg, xn), b1s[e * lay.r1c + 2 * warp]);
+                const float hlin = __fadd_rn(dc_dot<NJ>(wl, xn), b1s[e * lay.r1c + 2 * warp + 1]);
                 // Clamped SwiGLU (gpt_oss.py:212-219), the arithmetic of k_moe_up.
                 const float glu = fminf(hg, dm.limit);
                 const float lin = fminf(fmaxf(hlin, -dm.limit), dm.limit);
@@ -399,34 +574,41 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
                 const float sg = 1.0f / (1.0f + expf(-z));
                 const float og = __fmul_rn(glu, sg);
                 const float l1 = __fadd_rn(lin, 1.0f);
-                cluster_broadcast(act + s * I + p, __fmul_rn(og, l1));
+                dc_push(rsm, rbar, off(act + u * I + gw), kDcAct, __fmul_rn(og, l1));
             }
         }
-        cluster_sync_all();
+        sync(kDcAct, l);
         // ---- P5: mlp2 columns, weighted combine in slot order, residual -> x[]; next layer's static rows
-        float xnew = 0.f;
-        if (gw < d) {
+        {
             float comb = 0.f;
 #pragma unroll
             for (int u = 0; u < kDcMaxK; ++u) {
                 if (u < dm.k) {
-                    const float part = dc_dot<NJ>(w2[u], act + u * I);
-                    comb = __fadd_rn(comb, __fmul_rn(__fadd_rn(part, b2[u]), sw[u]));
+                    const int e = int(checked_row(sidx[u], dm.E, true, a.err));
+                    float w2r[NJ][4], av[NJ][4];
+                    dc_read<NJ>(w2r, w2s + (size_t(e) * lay.r2c + warp) * I);
+                    dc_read<NJ>(av, act + u * I);
+                    comb = __fadd_rn(comb, __fmul_rn(__fadd_rn(dc_dot<NJ>(w2r, av), b2s[e * lay.r2c + warp]), sw[u]));
                 }
             }
-            xnew = __fadd_rn(x2[gw], comb);
+            dc_push(rsm, rbar, off(xs + gw), kDcXs, __fadd_rn(x2[gw], comb));
         }
-        if (l + 1 < a.L) dc_load_static<NJ>(st, a.layers[l + 1], dm, gw);
-        if (gw < d) cluster_broadcast(xs + gw, xnew);
-        cluster_sync_all();
+        if (l + 1 < a.L) dc_load_static<NJ>(st, lws[l + 1], dm, gw);
     }
+    sync(kDcXs, a.L - 1);
 
     // Final RMSNorm of the token's row (gpt_oss.py:309) for the vocab kernel; clears the argmax key.
-    if (rank == 0) {
-        if (a.rows) checked_row(a.rows[0], 1, true, a.err);
-        dc_norm(xs, a.tf, d, dm.eps, a.final_norm, inv);
-        if (threadIdx.x == 0 && a.keys) a.keys[0] = 0ull;
+    if (rank == 0 && warp == 0) {
+        if (a.rows && lane == 0) checked_row(a.rows[0], 1, true, a.err);
+        float fw[NJ][4], out[NJ][4];
+        dc_load<NJ>(fw, a.final_norm);
+        dc_norm<NJ>(out, xs, d, dm.eps, fw);
+#pragma unroll
+        for (int j = 0; j < NJ; ++j)
+            *reinterpret_cast<float4*>(a.tf + lane * 4 + 128 * j) = make_float4(out[j][0], out[j][1], out[j][2], out[j][3]);
+        if (lane == 0 && a.keys) a.keys[0] = 0ull;
     }
+    cluster_sync_all();  // no CTA leaves while another may still store into it
 }
 
 }  // namespace cb200

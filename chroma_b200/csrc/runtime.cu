@@ -1079,9 +1079,10 @@ struct GptExec {
     }
 
     // The cluster path takes a single new token of a cached fp32 program whose widths fit its fixed work split
-    // (d = H*hd = I = 128: one row of 128 per warp and lane-float4; QKV rows <= 2 per warp; k*I pairs <= 4 per
-    // warp; E <= 16 gate rows; head_dim dividing 32 with room for the (max, sum) pair; ctx + 1 keys over 16 CTAs of
-    // at most 32 keys) and whose shared memory fits. CHROMA_B200_DECODE_CLUSTER=0 keeps the per-layer kernels.
+    // (d = H*hd = I = 128: one row of 128 per warp and lane-float4, one mlp1 pair and one mlp2 row of each expert
+    // per warp; QKV rows <= 2 per warp; k <= 4; E <= 16 gate rows; head_dim dividing 32 with room for the
+    // (max, sum) pair; ctx + 1 keys over 16 CTAs of at most 32 keys) and whose shared memory (every expert's rows
+    // of the CTA included) fits. CHROMA_B200_DECODE_CLUSTER=0 keeps the per-layer kernels.
     void init_cluster_decode() {
         const Dims& d = m->dm;
         const int L = m->desc.layers;
@@ -1090,13 +1091,14 @@ struct GptExec {
         if (m->desc.storage != CHROMA_B200_FP32 || m->desc.kind != CHROMA_B200_GPTOSS_CACHED) return;
         if (mask_mode != kMaskSlots || B * n != 1) return;
         if (d.d != 128 || d.H * d.hd != 128 || d.I != 128) return;
-        if ((d.H + 2 * d.KV) * d.hd > kDcRows1 * kDcWarps || d.k > kDcMaxK || d.k * d.I > kDcPairs * kDcWarps) return;
+        if ((d.H + 2 * d.KV) * d.hd > kDcRows1 * kDcWarps || d.k > kDcMaxK) return;
+        if (reinterpret_cast<uintptr_t>(m->weights->ptr) % 16 != 0) return;  // bulk copies of the expert rows
         if (d.E > kDcMaxE || d.E < d.k || d.hd % 4 != 0 || 32 % d.hd != 0 || d.hd + 2 > 32) return;
         const int kpc = (ctx + 1 + kDcC - 1) / kDcC;
         if (kpc > 32) return;
         const DcLayout lay(d, L, kpc);
         const size_t smem = size_t(lay.total) * 4;
-        if (smem > 200 * 1024) return;
+        if (smem + 1024 > 227 * 1024) return;
         ClusterLaunch cl(nullptr, dim3(kDcC), dim3(kThreads), smem, kDcC, k_decode_cluster<1>);
         int clusters = 0;
         if (cudaOccupancyMaxActiveClusters(&clusters, k_decode_cluster<1>, &cl.cfg) != cudaSuccess || clusters < 1) {
