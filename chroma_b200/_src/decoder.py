@@ -103,6 +103,7 @@ class NativeDecoder:
         self.steps = (prefill.inputs[0]["shape"][0], 1)
         self.logit_dtype = nat.dtype_of(decode.outputs[0]["dtype"])
         self.vocab = decode.outputs[0]["shape"][1]
+        self.pinned = nat.PinnedPool()  # returned logits live in page-locked memory
 
     def step(self, which: int, tokens: np.ndarray, count: int, positions: np.ndarray,
              logits: np.ndarray | None, argmax: np.ndarray | None) -> None:
@@ -151,6 +152,9 @@ class NativeDecoder:
         handle, self.handle = getattr(self, "handle", None), None
         if handle:
             nat.lib().chroma_b200_decoder_destroy(handle)
+        pinned = getattr(self, "pinned", None)
+        if pinned is not None:
+            pinned.close()
 
     def __del__(self) -> None:
         try:
@@ -273,7 +277,7 @@ class Decoder:
             state = self._flush()
             chunk = np.zeros(steps, dtype=np.int64)
             chunk[:count] = ids[offset : offset + count]
-            logits = np.empty((1, self.vocab_size), dtype=self._logit_dtype)
+            logits = self._native.pinned.array((1, self.vocab_size), self._logit_dtype)
             self._native.step(index, chunk, count, np.array([state.position], np.int64), logits, None)
             rows = (state.position + np.arange(count)) % self.context
             slots = state.slots.copy()
@@ -392,7 +396,7 @@ class BatchDecoder:
                     out = np.empty(self.batch, np.int64)
                     self._native.step(index, chunk, count, first, None, out)
                 else:
-                    out = np.empty((self.batch, self.vocab_size), self._native.logit_dtype)
+                    out = self._native.pinned.array((self.batch, self.vocab_size), self._native.logit_dtype)
                     self._native.step(index, chunk, count, first, out, None)
                 self._staged = (index, count, first)
                 self._position = first + count

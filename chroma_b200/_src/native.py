@@ -96,6 +96,8 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "chroma_b200_ep_open": (ctypes.c_int, [_VP, _VP, _CP, _SZ]),
     "chroma_b200_ep_destroy": (None, [_VP]),
     "chroma_b200_create_ep": (ctypes.c_int, [ctypes.POINTER(Desc), _CP, _VP, _VP, ctypes.POINTER(_VP), _CP, _SZ]),
+    "chroma_b200_host_alloc": (ctypes.c_int, [_SZ, ctypes.POINTER(_VP), _CP, _SZ]),
+    "chroma_b200_host_free": (None, [_VP]),
 }
 
 EP_HANDLE_BYTES = 64  # CHROMA_B200_EP_HANDLE_BYTES
@@ -136,6 +138,68 @@ def call(name: str, *args: Any) -> None:
     status = getattr(lib(), name)(*args, err, len(err))
     if status != OK:
         raise _ERRORS.get(status, RuntimeError)(err.value.decode(errors="replace") or name)
+
+
+# ---------------------------------------------------------------------------------------------------------
+# Page-locked result arrays.
+
+
+class _PinnedBlock:
+    """One page-locked host block exported as a buffer (PEP 688): numpy arrays made from it keep it alive, and it
+    returns to its pool when the last of them is gone."""
+
+    def __init__(self, pool: "PinnedPool", ptr: int, nbytes: int) -> None:
+        self._pool, self._ptr, self._nbytes = pool, ptr, nbytes
+        self._mem = (ctypes.c_char * nbytes).from_address(ptr)
+
+    def __buffer__(self, flags: int) -> memoryview:
+        return memoryview(self._mem)
+
+    def __del__(self) -> None:
+        try:
+            self._pool.give_back(self._ptr, self._nbytes)
+        except Exception:  # interpreter shutdown
+            pass
+
+
+class PinnedPool:
+    """Recycles page-locked host blocks for the arrays a decoder returns every step, so the device-to-host copy of
+    a step's logits is one DMA at link speed instead of a copy through the driver's staging buffer."""
+
+    def __init__(self, keep: int = 4) -> None:
+        self._free: dict[int, list[int]] = {}
+        self._keep = keep
+        self._lock = threading.Lock()
+
+    def array(self, shape: tuple[int, ...], dtype: Any) -> np.ndarray:
+        dtype = np.dtype(dtype)
+        count = int(np.prod(shape))
+        nbytes = max(1, count * dtype.itemsize)
+        with self._lock:
+            free = self._free.get(nbytes)
+            ptr = free.pop() if free else None
+        if ptr is None:
+            out = _VP()
+            call("chroma_b200_host_alloc", _SZ(nbytes), ctypes.byref(out))
+            ptr = int(out.value)
+        return np.frombuffer(_PinnedBlock(self, ptr, nbytes), dtype, count=count).reshape(shape)
+
+    def give_back(self, ptr: int, nbytes: int) -> None:
+        with self._lock:
+            free = self._free.setdefault(nbytes, [])
+            if len(free) < self._keep:
+                free.append(ptr)
+                return
+        lib().chroma_b200_host_free(_VP(ptr))
+
+    def close(self) -> None:
+        """Frees the idle blocks; blocks still behind live arrays are freed when those arrays go."""
+        with self._lock:
+            idle = [p for ptrs in self._free.values() for p in ptrs]
+            self._free.clear()
+            self._keep = 0
+        for p in idle:
+            lib().chroma_b200_host_free(_VP(p))
 
 
 # ---------------------------------------------------------------------------------------------------------

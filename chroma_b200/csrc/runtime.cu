@@ -294,10 +294,12 @@ static void gemm_bf16(cudaStream_t s, const void* A, const void* B, GemmArgs g, 
 
 // ---------------------------------------------------------------------------------------------------------
 // Small utility kernels.
-__global__ void k_positions(const int64_t* pos0, int B, int n, float* positions, int64_t* last, int count) {
+__global__ void k_positions(const int64_t* pos0, int B, int n, float* positions, int64_t* last, int count,
+                            unsigned* err) {
     pdl_wait();
     pdl_trigger();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i == 0 && err) *err = 0u;  // the step's error word starts clear
     if (i < B * n) positions[i] = float(pos0[i / n] + i % n);
     if (i < B) last[i] = count - 1;
 }
@@ -1354,8 +1356,11 @@ struct chroma_b200_decoder {
     int device = 0, B = 1, ctx = 0, window = 0, L = 0, row = 0, V = 0, steps = 1;
     size_t es = 4;
     cudaStream_t stream = nullptr;
-    DevBuf cache_k, cache_v, slots, pos0, commit_pos, tokens, positions, last, logits, keys, err;
-    std::unique_ptr<PinnedBuf> host_in, host_out;
+    DevBuf cache_k, cache_v, slots, io_in, commit_pos, positions, last, logits, keys, err;
+    int64_t* pos0 = nullptr;    // [B] in io_in, followed by
+    int64_t* tokens = nullptr;  // [B][steps]: one host-to-device copy per step uploads both
+    std::unique_ptr<PinnedBuf> host_in, host_out, host_commit;
+    cudaEvent_t commit_ev = nullptr;  // the last commit's upload of host_commit
     GptExec ex[2];
     DevBuf new_k[2], new_v[2];
     Graph graph[2][2];
@@ -1370,6 +1375,7 @@ struct chroma_b200_decoder {
             cudaSetDevice(device);
             cudaStreamSynchronize(stream);
             cudaStreamDestroy(stream);
+            if (commit_ev) cudaEventDestroy(commit_ev);
             cudaSetDevice(prev);
         }
     }
@@ -1874,9 +1880,10 @@ int chroma_b200_decoder_create(chroma_b200_program* prefill, chroma_b200_program
         check(cudaMemset(d->cache_v.p, 0, cache), "cache");
         d->slots = DevBuf(size_t(batch) * d->ctx * 8);
         check(cudaMemset(d->slots.p, 0xff, size_t(batch) * d->ctx * 8), "slots");
-        d->pos0 = DevBuf(size_t(batch) * 8);
+        d->io_in = DevBuf(size_t(batch) * (d->steps + 1) * 8);
+        d->pos0 = d->io_in.as<int64_t>();
+        d->tokens = d->pos0 + batch;
         d->commit_pos = DevBuf(size_t(batch) * 8);
-        d->tokens = DevBuf(size_t(batch) * d->steps * 8);
         d->positions = DevBuf(size_t(batch) * d->steps * 4);
         d->last = DevBuf(size_t(batch) * 8);
         d->logits = DevBuf(size_t(batch) * d->V * d->es);
@@ -1885,6 +1892,8 @@ int chroma_b200_decoder_create(chroma_b200_program* prefill, chroma_b200_program
         check(cudaMemset(d->err.p, 0, sizeof(unsigned)), "cudaMemset");
         d->host_in = std::make_unique<PinnedBuf>(size_t(batch) * (d->steps + 1) * 8);
         d->host_out = std::make_unique<PinnedBuf>(size_t(batch) * 8 + 16);
+        d->host_commit = std::make_unique<PinnedBuf>(size_t(batch) * 8);
+        check(cudaEventCreateWithFlags(&d->commit_ev, cudaEventDisableTiming), "commit event");
         for (int i = 0; i < 2; ++i) {
             const int n = d->models[i]->desc.tokens;
             const size_t staged = size_t(d->L) * batch * n * d->row * d->es;
@@ -1893,14 +1902,14 @@ int chroma_b200_decoder_create(chroma_b200_program* prefill, chroma_b200_program
             GptExec& e = d->ex[i];
             e.init(*d->models[i], batch, n, d->ctx, kMaskSlots, d->window, true);
             e.err = d->err.as<unsigned>();
-            e.io.tokens = d->tokens.as<const int64_t>();
+            e.io.tokens = d->tokens;
             e.io.positions = d->positions.as<const float>();
             e.io.cache_k = d->cache_k.p;
             e.io.cache_v = d->cache_v.p;
             e.io.new_k = d->new_k[i].p;
             e.io.new_v = d->new_v[i].p;
             e.io.slots = d->slots.as<const int64_t>();
-            e.io.pos0 = d->pos0.as<const int64_t>();
+            e.io.pos0 = d->pos0;
             e.io.rows = d->last.as<const int64_t>();
             e.io.logits = d->logits.p;
             e.io.keys = nullptr;
@@ -1921,15 +1930,13 @@ int chroma_b200_decoder_step(chroma_b200_decoder* d, int32_t use_decode, const i
         DeviceGuard guard(d->device);
         cudaStream_t s = d->stream;
         int64_t* hin = static_cast<int64_t*>(d->host_in->p);
-        std::memcpy(hin, tokens, size_t(d->B) * n * 8);
-        std::memcpy(hin + size_t(d->B) * n, positions, size_t(d->B) * 8);
+        std::memcpy(hin, positions, size_t(d->B) * 8);
+        std::memcpy(hin + d->B, tokens, size_t(d->B) * n * 8);
         try {
-            check(cudaMemsetAsync(d->err.p, 0, sizeof(unsigned), s), "Reset index error");
-            check(cudaMemcpyAsync(d->tokens.p, hin, size_t(d->B) * n * 8, cudaMemcpyHostToDevice, s), "Upload tokens");
-            check(cudaMemcpyAsync(d->pos0.p, hin + size_t(d->B) * n, size_t(d->B) * 8, cudaMemcpyHostToDevice, s),
-                  "Upload positions");
-            launch(s, dim3((d->B * n + 255) / 256), dim3(256), 0, k_positions, d->pos0.as<const int64_t>(), d->B, n,
-                   d->positions.as<float>(), d->last.as<int64_t>(), count);
+            check(cudaMemcpyAsync(d->pos0, hin, size_t(d->B) * (n + 1) * 8, cudaMemcpyHostToDevice, s),
+                  "Upload positions and tokens");
+            launch(s, dim3((d->B * n + 255) / 256), dim3(256), 0, k_positions, static_cast<const int64_t*>(d->pos0), d->B,
+                   n, d->positions.as<float>(), d->last.as<int64_t>(), count, d->err.as<unsigned>());
             // The argmax flag changes the kernel arguments, so each (program, argmax) pair has its own captured graph.
             e.io.keys = argmax ? d->keys.as<unsigned long long>() : nullptr;
             d->graph[which][argmax ? 1 : 0].run(s, [&](cudaStream_t st) { e.enqueue(st); });
@@ -1960,10 +1967,14 @@ int chroma_b200_decoder_commit(chroma_b200_decoder* d, int32_t use_decode, int32
         const GptExec& e = d->ex[which];
         if (count < 1 || count > e.n) throw ValueError("count out of range for this program");
         DeviceGuard guard(d->device);
-        // Re-upload the chunk's positions: committing is idempotent and independent of later steps' pos0.
-        int64_t* hin = static_cast<int64_t*>(d->host_in->p);
+        // Re-upload the chunk's positions: committing is idempotent and independent of later steps' pos0. The commit
+        // is only enqueued (everything that reads the caches runs on the same stream); its pinned upload buffer is
+        // reused once the previous commit's copy has completed.
+        check(cudaEventSynchronize(d->commit_ev), "commit buffer");
+        int64_t* hin = static_cast<int64_t*>(d->host_commit->p);
         std::memcpy(hin, positions, size_t(d->B) * 8);
         check(cudaMemcpyAsync(d->commit_pos.p, hin, size_t(d->B) * 8, cudaMemcpyHostToDevice, d->stream), "commit positions");
+        check(cudaEventRecord(d->commit_ev, d->stream), "commit event");
         const dim3 grid(unsigned(d->L * d->B * count));
         const int threads = std::min(256, ((d->row + 31) / 32) * 32);
         if (d->es == 2)
@@ -1975,7 +1986,6 @@ int chroma_b200_decoder_commit(chroma_b200_decoder* d, int32_t use_decode, int32
             launch(d->stream, grid, dim3(threads), 0, k_commit<float>, d->new_k[which].as<const float>(),
                    d->new_v[which].as<const float>(), d->L, d->B, e.n, count, d->ctx, d->row, 1,
                    d->commit_pos.as<const int64_t>(), d->cache_k.as<float>(), d->cache_v.as<float>(), d->slots.as<int64_t>());
-        check(cudaStreamSynchronize(d->stream), "commit");
     });
 }
 
@@ -1990,10 +2000,9 @@ int chroma_b200_decoder_advance(chroma_b200_decoder* d, const int64_t* tokens, c
         if (tokens) {
             int64_t* hin = static_cast<int64_t*>(d->host_in->p);
             check(cudaStreamSynchronize(s), "advance");
-            std::memcpy(hin, tokens, size_t(d->B) * 8);
-            std::memcpy(hin + d->B, positions, size_t(d->B) * 8);
-            check(cudaMemcpyAsync(d->tokens.p, hin, size_t(d->B) * 8, cudaMemcpyHostToDevice, s), "advance tokens");
-            check(cudaMemcpyAsync(d->pos0.p, hin + d->B, size_t(d->B) * 8, cudaMemcpyHostToDevice, s), "advance positions");
+            std::memcpy(hin, positions, size_t(d->B) * 8);
+            std::memcpy(hin + d->B, tokens, size_t(d->B) * 8);
+            check(cudaMemcpyAsync(d->pos0, hin, size_t(d->B) * 16, cudaMemcpyHostToDevice, s), "advance positions and tokens");
         }
         if (!d->record.p || d->capacity < steps) {
             check(cudaStreamSynchronize(s), "advance");
@@ -2007,8 +2016,8 @@ int chroma_b200_decoder_advance(chroma_b200_decoder* d, const int64_t* tokens, c
         GptExec& e = d->ex[1];
         for (int i = 0; i < steps; ++i) {
             d->advance_graph.run(s, [&](cudaStream_t st) {
-                launch(st, dim3((d->B + 255) / 256), dim3(256), 0, k_positions, d->pos0.as<const int64_t>(), d->B, 1,
-                       d->positions.as<float>(), d->last.as<int64_t>(), 1);
+                launch(st, dim3((d->B + 255) / 256), dim3(256), 0, k_positions, static_cast<const int64_t*>(d->pos0), d->B,
+                       1, d->positions.as<float>(), d->last.as<int64_t>(), 1, static_cast<unsigned*>(nullptr));
                 e.io.keys = d->keys.as<unsigned long long>();
                 e.enqueue(st);
                 const dim3 grid(unsigned(d->L * d->B));
@@ -2016,15 +2025,15 @@ int chroma_b200_decoder_advance(chroma_b200_decoder* d, const int64_t* tokens, c
                 if (d->es == 2)
                     launch(st, grid, dim3(threads), 0, k_commit<__nv_bfloat16>, d->new_k[1].as<const __nv_bfloat16>(),
                            d->new_v[1].as<const __nv_bfloat16>(), d->L, d->B, 1, 1, d->ctx, d->row, 1,
-                           d->pos0.as<const int64_t>(), d->cache_k.as<__nv_bfloat16>(), d->cache_v.as<__nv_bfloat16>(),
+                           static_cast<const int64_t*>(d->pos0), d->cache_k.as<__nv_bfloat16>(), d->cache_v.as<__nv_bfloat16>(),
                            d->slots.as<int64_t>());
                 else
                     launch(st, grid, dim3(threads), 0, k_commit<float>, d->new_k[1].as<const float>(),
                            d->new_v[1].as<const float>(), d->L, d->B, 1, 1, d->ctx, d->row, 1,
-                           d->pos0.as<const int64_t>(), d->cache_k.as<float>(), d->cache_v.as<float>(),
+                           static_cast<const int64_t*>(d->pos0), d->cache_k.as<float>(), d->cache_v.as<float>(),
                            d->slots.as<int64_t>());
                 launch(st, dim3(1), dim3(std::min(1024, ((d->B + 31) / 32) * 32)), 0, k_advance,
-                       d->keys.as<const unsigned long long>(), d->B, d->tokens.as<int64_t>(), d->pos0.as<int64_t>(),
+                       d->keys.as<const unsigned long long>(), d->B, d->tokens, d->pos0,
                        d->record.as<int64_t>(), d->counter.as<int>(), d->capacity);
             });
         }
@@ -2094,5 +2103,17 @@ int chroma_b200_decoder_write(chroma_b200_decoder* d, int32_t first, int32_t cou
 }
 
 void chroma_b200_decoder_destroy(chroma_b200_decoder* d) { delete d; }
+
+int chroma_b200_host_alloc(size_t bytes, void** out, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!out) throw ValueError("null argument");
+        *out = nullptr;
+        check(cudaMallocHost(out, bytes ? bytes : 1), "cudaMallocHost");
+    });
+}
+
+void chroma_b200_host_free(void* p) {
+    if (p) cudaFreeHost(p);
+}
 
 }  // extern "C"

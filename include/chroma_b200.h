@@ -174,6 +174,12 @@ int chroma_b200_decoder_write(chroma_b200_decoder* decoder, int32_t first, int32
                               const void* values, const int64_t* slots, char* err, size_t err_len);
 void chroma_b200_decoder_destroy(chroma_b200_decoder* decoder);
 
+/* Page-locked host memory for results the caller keeps (the decoders' returned logits): device-to-host copies
+ * into it run at full link speed without a driver staging copy. The reference returns fresh numpy arrays
+ * (chroma/_src/decoding/decoder.py:115-130); the Python layer returns numpy arrays over these blocks. */
+int chroma_b200_host_alloc(size_t bytes, void** out, char* err, size_t err_len);
+void chroma_b200_host_free(void* p);
+
 /* ---- Expert parallelism across the GPUs of one node ---------------------------------------------------------------
  * No reference counterpart: the reference runs every expert on one device (the MoE einsums of
  * chroma/models/gpt_oss.py:243-265 lowered by chroma/_src/codegen/gpu.py:390-424). Here rank r of a group of `world`

@@ -158,6 +158,25 @@ def test_c2_cluster_decode_matches_per_layer_kernels(gpu: None) -> None:
     np.testing.assert_allclose(got, ref["logits"], rtol=1e-5, atol=1e-6)
 
 
+def test_decoder_logits_are_independent_page_locked_arrays(gpu: None) -> None:
+    """Returned logits live in recycled page-locked blocks: a result the caller keeps is never overwritten by later
+    steps, results are writable, and a block comes back to the pool only when its last view is gone."""
+    with dev_decoder() as dec:
+        a = dec.append([1, 2, 3])
+        kept = a.copy()
+        view = a[:, :16]
+        b = dec.append([4])
+        del a
+        c = dec.append([5])
+        np.testing.assert_array_equal(view, kept[:, :16])
+        assert b.flags.writeable and c.flags.writeable and c.flags.c_contiguous
+        assert not np.shares_memory(b, c)
+        b[0, 0] = 0.0
+        with dev_decoder() as ref:
+            want = ref.append([1, 2, 3, 4, 5])
+        np.testing.assert_allclose(c, want, **FP32)
+
+
 def test_c2_batch_decoder_matches_reference(gpu: None) -> None:
     g = golden("c2_decode")
     prefill, decode = dev_pair()
