@@ -108,6 +108,23 @@ __global__ void k_prefetch_l2(const char* base, size_t bytes) {
         asm volatile("prefetch.global.L2 [%0];" ::"l"(base + i * 128));
 }
 
+// L2 prefetch of `bytes` (a multiple of 16) at 16-byte aligned `p` by the TMA engine: one instruction, no data
+// returned to the SM.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Grid-stride bulk L2 prefetch of a 16-byte aligned range in 64 KiB pieces (one thread per piece).
+__global__ void k_prefetch_l2_bulk(const char* base, size_t bytes) {
+    constexpr size_t kPiece = 64 * 1024;
+    const size_t pieces = (bytes + kPiece - 1) / kPiece;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < pieces; i += size_t(gridDim.x) * blockDim.x) {
+        const size_t off = i * kPiece;
+        const size_t n = bytes - off < kPiece ? bytes - off : kPiece;
+        bulk_prefetch_l2(base + off, unsigned(n & ~size_t(15)));
+    }
+}
+
 // Orderable 64-bit argmax key: larger value wins, then the lower index (numpy.argmax: first occurrence).
 __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
     unsigned u = __float_as_uint(v);

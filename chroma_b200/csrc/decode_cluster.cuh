@@ -14,7 +14,8 @@
 //       RoPE on the gathered row (per CTA, cos/sin of the step's position computed once); CTA 0 stages the new
 //       K/V rows for the commit kernel
 //   P2  attention over this CTA's ceil((ctx+1)/kDcC) keys (the K/V slices of every layer are copied into shared
-//       memory by cp.async at the start), one warp per query head: (max, sum, P.V) partials -> parts[]
+//       memory by cp.async at the start; the CTA holding the new token's key appends its row after RoPE), one warp
+//       per query head: (max, sum, P.V) partials -> parts[]
 //       every CTA merges the kDcC partials of every head with the sink logit (split-KV softmax, cached.py:36-47)
 //   P3  out-projection row (1 per warp) + bias + residual                       -> x2[]
 //   P4  RMSNorm + gate rows (per CTA), top-k + softmax (per warp), then one (glu, linear) row pair of each selected
@@ -29,7 +30,9 @@
 // Buffer reuse is safe without barriers: a CTA reads each exchanged buffer only before it pushes its next phase's
 // outputs, and a sender can only reach the same phase of the next layer after receiving those outputs.
 //
-// The static QKV / out / gate / norm rows of layer l+1 are loaded into registers during P5 of layer l.
+// The static QKV / out / norm rows of layer l+1 are loaded into registers after P3 of layer l, its gate rows after
+// P4. Each layer's weights are pulled into L2 (bulk prefetch, 1/kDcC per CTA) one layer ahead, so the L2 holds only
+// the layers in flight and the vocab matrix (prefetched beside the kernel for the vocab GEMV) stays resident.
 // The rounding points and summation orders of the projections are those of the per-layer kernels (gptoss.cuh);
 // the attention's split over keys and its merge order differ, as in any split-KV decode.
 //
@@ -81,8 +84,8 @@ __host__ __device__ inline int dc_up4(int v) { return (v + 3) & ~3; }
 struct DcLayout {
     int ps, kvs;  // floats per (CTA, head) partial; per cached key row (padded: conflict-free 16-byte reads)
     int r1c, r2c; // mlp1 / mlp2 rows per CTA and expert
-    int lw, xs, raw, qkv, cs, parts, att, x2, gl, act, prow, kst, w1s, w2s, b1s, b2s, ks, vs, total;
-    __host__ __device__ DcLayout(const Dims& dm, int L, int kpc) {
+    int lw, xs, raw, qkv, cs, parts, att, x2, gl, act, prow, w1s, w2s, b1s, b2s, ks, vs, total;
+    __host__ __device__ DcLayout(const Dims& dm, int L, int kpc, bool stage) {
         const int r1 = (dm.H + 2 * dm.KV) * dm.hd;
         ps = dc_up4(dm.hd + 2);
         kvs = dm.KV * dm.hd + 4;
@@ -100,11 +103,11 @@ struct DcLayout {
         gl = o; o += dc_up4(dm.E);
         act = o; o += dc_up4(dm.k * dm.I);
         prow = o; o += kWarps * 32;
-        kst = o; o += dc_up4(2 * kpc);  // int64 times of this CTA's cache rows
-        w1s = o; o += dm.E * r1c * dm.d;
-        w2s = o; o += dm.E * r2c * dm.I;
-        b1s = o; o += dm.E * r1c;
-        b2s = o; o += dm.E * r2c;
+        const int se = stage ? dm.E : 0;  // staged experts
+        w1s = o; o += se * r1c * dm.d;
+        w2s = o; o += se * r2c * dm.I;
+        b1s = o; o += se * r1c;
+        b2s = o; o += se * r2c;
         ks = o; o += L * kpc * kvs;
         vs = o; o += L * kpc * kvs;
         total = o;
@@ -188,9 +191,11 @@ __device__ __forceinline__ void dc_read(float (&x)[NJ][4], const float* row) {
 // This lane's elements of RMSNorm(x) * w, computed by every warp on its own (the reduction order of
 // rows_rmsnorm: lane-strided FMA chain, butterfly sum), so no block barrier is needed.
 template <int NJ>
-__device__ __forceinline__ void dc_norm(float (&out)[NJ][4], const float* x, int d, float eps, const float (&w)[NJ][4]) {
+__device__ __forceinline__ void dc_norm(float (&out)[NJ][4], const float* x, float eps, const float (&w)[NJ][4]) {
+    constexpr int d = 128 * NJ;
     const int lane = threadIdx.x & 31;
     float s = 0.f;
+#pragma unroll
     for (int c = lane; c < d; c += 32) s = fmaf(x[c], x[c], s);
     s = warp_sum(s);
     const float iv = 1.0f / sqrtf(s / float(d) + eps);
@@ -213,9 +218,9 @@ template <int NJ> struct DcStatic {
     float mlp_norm[NJ][4];
 };
 
+// The rows P1-P3 use (loaded for layer l+1 once P3 of layer l has used them) ...
 template <int NJ>
-__device__ __forceinline__ void dc_load_static(DcStatic<NJ>& s, const LayerW<float>& w, const Dims& dm, int gw) {
-    const int warp = threadIdx.x >> 5;
+__device__ __forceinline__ void dc_load_static_attn(DcStatic<NJ>& s, const LayerW<float>& w, const Dims& dm, int gw) {
     const int r1 = (dm.H + 2 * dm.KV) * dm.hd;
 #pragma unroll
     for (int u = 0; u < kDcRows1; ++u) {
@@ -225,10 +230,15 @@ __device__ __forceinline__ void dc_load_static(DcStatic<NJ>& s, const LayerW<flo
             s.qkv_b[u] = w.qkv_b[r];
         }
     }
-    if (gw < dm.d) {
-        dc_load<NJ>(s.out, w.out_w + size_t(gw) * dm.H * dm.hd);
-        s.out_b = w.out_b[gw];
-    }
+    dc_load<NJ>(s.out, w.out_w + size_t(gw) * dm.H * dm.hd);
+    s.out_b = w.out_b[gw];
+    dc_load<NJ>(s.attn_norm, w.attn_norm);
+}
+
+// ... and the rows of P4's router (loaded for layer l+1 once P4 of layer l has computed its gate logits).
+template <int NJ>
+__device__ __forceinline__ void dc_load_static_mlp(DcStatic<NJ>& s, const LayerW<float>& w, const Dims& dm) {
+    const int warp = threadIdx.x >> 5;
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
         const int e = warp + kWarps * u;
@@ -237,44 +247,47 @@ __device__ __forceinline__ void dc_load_static(DcStatic<NJ>& s, const LayerW<flo
             s.gate_b[u] = w.gate_b[e];
         }
     }
-    dc_load<NJ>(s.attn_norm, w.attn_norm);
     dc_load<NJ>(s.mlp_norm, w.mlp_norm);
 }
 
-// Top-k of n <= 32 gate logits in shared memory with the ranking of warp_topk_softmax (NaN highest, ties to the
-// lowest index, sorted), then the softmax of the k values in slot order. Lane e counts the logits that outrank its
-// own (independent comparisons, no shuffle chain); the lane of rank r fills slot r. Every lane ends with all k
-// (index, weight) pairs.
-__device__ __forceinline__ bool dc_outranks(float a, int ia, float b, int ib) {
-    if (isnan(a) != isnan(b)) return isnan(a);
-    if (a != b && !(isnan(a) && isnan(b))) return a > b;
-    return ia < ib;
-}
-
+// Top-k of n <= kDcMaxE gate logits in shared memory with the ranking of warp_topk_softmax (NaN highest, ties to
+// the lowest index, sorted), then the softmax of the k values in slot order. Lane e holds expert e's logit as an
+// orderable 64-bit key (argmax_key of the logit with -0 taken as +0) and counts the keys above its own; the lane
+// of rank r owns slot r and computes its exponent and weight. Every lane ends with all k (index, weight) pairs.
 __device__ __forceinline__ void dc_topk(const float* gl, int n, int k, int (&idx)[kDcMaxK], float (&wt)[kDcMaxK]) {
     const int lane = threadIdx.x & 31;
     const float g = lane < n ? gl[lane] : 0.f;
+    const unsigned long long key = lane < n ? argmax_key(g + 0.0f, lane) : 0ull;
     int rank = 0;
-    for (int j = 0; j < n; ++j) rank += dc_outranks(gl[j], j, g, lane) ? 1 : 0;
-    float vals[kDcMaxK];
+#pragma unroll
+    for (int j = 0; j < kDcMaxE; ++j) rank += __shfl_sync(0xffffffffu, key, j) > key ? 1 : 0;
+    const bool sel = lane < n && rank < k;
+    const float mx = warp_max(sel ? g : -INFINITY);
+    const float e = sel ? expf(g - mx) : 0.f;
+    float s = 0.f;
 #pragma unroll
     for (int r = 0; r < kDcMaxK; ++r) {
-        const unsigned m = __ballot_sync(0xffffffffu, lane < n && rank == r);
+        const unsigned m = __ballot_sync(0xffffffffu, sel && rank == r);
         idx[r] = m ? __ffs(int(m)) - 1 : 0;
-        vals[r] = __shfl_sync(0xffffffffu, g, idx[r]);
+        const float er = __shfl_sync(0xffffffffu, e, idx[r]);
+        if (r < k) s += er;  // slot order, as the sequential softmax
     }
-    float mx = -INFINITY;
+    const float own = sel ? e / s : 0.f;
 #pragma unroll
-    for (int r = 0; r < kDcMaxK; ++r)
-        if (r < k) mx = fmaxf(mx, vals[r]);
-    float e[kDcMaxK], s = 0.f;
-#pragma unroll
-    for (int r = 0; r < kDcMaxK; ++r) {
-        e[r] = 0.f;
-        if (r < k) { e[r] = expf(vals[r] - mx); s += e[r]; }
-    }
-#pragma unroll
-    for (int r = 0; r < kDcMaxK; ++r) wt[r] = r < k ? e[r] / s : 0.f;
+    for (int r = 0; r < kDcMaxK; ++r) wt[r] = r < k ? __shfl_sync(0xffffffffu, own, idx[r]) : 0.f;
+}
+
+// L2 prefetch of this CTA's 1/kDcC share of layer l's weights (its tensors are packed contiguously from attn_norm;
+// the last one, b2, ends E*d floats after its start).
+__device__ __forceinline__ void dc_prefetch_layer(const LayerW<float>* lws, int l, int L, const Dims& dm, int rank) {
+    const char* beg = reinterpret_cast<const char*>(lws[l].attn_norm);
+    const char* end = l + 1 < L ? reinterpret_cast<const char*>(lws[l + 1].attn_norm)
+                                : reinterpret_cast<const char*>(lws[l].b2 + size_t(dm.E) * dm.d);
+    const size_t share = ((size_t(end - beg) + kDcC - 1) / kDcC + 15) & ~size_t(15);
+    const size_t off = share * size_t(rank);
+    if (off >= size_t(end - beg)) return;
+    const size_t n = (size_t(end - beg) - off < share ? size_t(end - beg) - off : share) & ~size_t(15);
+    for (size_t o = 0; o < n; o += 32768) bulk_prefetch_l2(beg + off + o, unsigned(n - o < 32768 ? n - o : 32768));
 }
 
 // Bulk-copies layer `w`'s expert rows of this CTA (every expert's mlp1 rows [2*kWarps*rank, +2*kWarps), mlp2 rows
@@ -295,13 +308,15 @@ __device__ __forceinline__ void dc_stage_experts(const LayerW<float>& w, const D
     }
 }
 
-// NJ = d / 128 = H*hd / 128 = I / 128 (the host admits only d = H*hd = I = 128).
-template <int NJ>
+// NJ = d / 128 = H*hd / 128 = I / 128 (the host admits only d = H*hd = I = 128); HD = head_dim. STAGE: the expert
+// rows of every expert are bulk-copied into shared memory at the start of each layer (false: the routed rows are
+// loaded into registers right after the routing).
+template <int NJ, int HD, bool STAGE>
 __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArgs a) {
     extern __shared__ __align__(128) float dsm[];
     __shared__ uint64_t bars[kDcBars];
     const Dims dm = a.dm;
-    const DcLayout lay(dm, a.L, a.kpc);
+    const DcLayout lay(dm, a.L, a.kpc, STAGE);
     const LayerW<float>* lws = reinterpret_cast<const LayerW<float>*>(dsm + lay.lw);
     float* xs = dsm + lay.xs;
     float* raw = dsm + lay.raw;
@@ -312,7 +327,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
     float* x2 = dsm + lay.x2;
     float* gl = dsm + lay.gl;
     float* act = dsm + lay.act;
-    int64_t* kst = reinterpret_cast<int64_t*>(dsm + lay.kst);
     const float* w1s = dsm + lay.w1s;
     const float* w2s = dsm + lay.w2s;
     const float* b1s = dsm + lay.b1s;
@@ -320,12 +334,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
     float* Ks = dsm + lay.ks;
     float* Vs = dsm + lay.vs;
 
+    constexpr int d = 128 * NJ, I = 128 * NJ;
     const int rank = int(cluster_ctarank());
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gw = rank * kWarps + warp;
-    const int d = dm.d, hd = dm.hd, H = dm.H, KV = dm.KV, I = dm.I;
-    const int r1 = (H + 2 * KV) * hd;
-    const int row_kv = KV * hd, kvs = lay.kvs, ps = lay.ps;
+    const int H = dm.H, KV = dm.KV;
+    const int r1 = (H + 2 * KV) * HD;
+    const int row_kv = KV * HD, kvs = lay.kvs;
+    constexpr int ps = (HD + 2 + 3) & ~3;
     const int j0 = rank * a.kpc;                         // this CTA's first key
     const int nk = max(0, min(a.kpc, a.ctx + 1 - j0));   // its keys, the new token's included
     const int nkc = max(0, min(a.kpc, a.ctx - j0));      // of which cache rows
@@ -335,17 +351,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
     auto off = [&](const float* p) { return uint32_t(p - dsm) * 4u; };
     bool live = true;  // false after a timed-out wait (thread 0)
 
+    auto wait_bar = [&](int bar, unsigned parity, bool cluster_scope) {
+        if (!live) return;
+        unsigned i = 0;
+        while (i < kMaxPolls && !(cluster_scope ? mbar_try_wait_cluster(&bars[bar], parity)
+                                                : mbar_try_wait(&bars[bar], parity)))
+            ++i;
+        if (i == kMaxPolls) {
+            atomicOr(a.err, kErrTimeout);
+            live = false;
+        }
+    };
     // Thread 0 waits for the buffer's phase of layer l and re-arms it for layer l + 1; then the block proceeds.
     auto sync = [&](int bar, int l) {
         if (threadIdx.x == 0) {
-            if (live) {
-                unsigned i = 0;
-                while (i < kMaxPolls && !mbar_try_wait_cluster(&bars[bar], unsigned(l & 1))) ++i;
-                if (i == kMaxPolls) {
-                    atomicOr(a.err, kErrTimeout);
-                    live = false;
-                }
-            }
+            wait_bar(bar, unsigned(l & 1), true);
             if (l + 1 < a.L) mbar_arrive_expect_tx(&bars[bar], lay.bytes(bar, dm));
         }
         __syncthreads();
@@ -357,14 +377,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
         for (int i = threadIdx.x; i < a.L * int(sizeof(LayerW<float>) / 8); i += blockDim.x) dst[i] = src[i];
     }
     DcStatic<NJ> st;
-    dc_load_static<NJ>(st, a.layers[0], dm, gw);
+    dc_load_static_attn<NJ>(st, a.layers[0], dm, gw);
+    dc_load_static_mlp<NJ>(st, a.layers[0], dm);
     if (threadIdx.x == 0) {
         for (int b = 0; b < kDcBars; ++b) mbar_init(&bars[b], 1);
         fence_barrier_init();
         for (int b = 0; b < kDcExperts; ++b) mbar_arrive_expect_tx(&bars[b], lay.bytes(b, dm));
     }
     __syncthreads();
-    if (warp == kWarps - 1) dc_stage_experts(a.layers[0], dm, lay, dsm, rank, &bars[kDcExperts]);
+    if (threadIdx.x == 32) {  // layers 0 and 1 into L2 (later layers: one ahead, at the start of each layer)
+        dc_prefetch_layer(lws, 0, a.L, dm, rank);
+        if (a.L > 1) dc_prefetch_layer(lws, 1, a.L, dm, rank);
+    }
+    if (STAGE && warp == kWarps - 1) dc_stage_experts(a.layers[0], dm, lay, dsm, rank, &bars[kDcExperts]);
     pdl_wait();
     pdl_trigger();
 
@@ -379,7 +404,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
             cp_async16(Vs + dst, a.cache_v + src);
         }
         cp_async_commit();
-        for (int jj = threadIdx.x; jj < nkc; jj += blockDim.x) kst[jj] = a.slots[j0 + jj];
     }
     {
         const int64_t row = checked_row(a.tokens[0], dm.V, false, a.err);
@@ -387,7 +411,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
     }
     const float pos = a.positions[0];
     const int64_t t_i = a.pos0[0];
-    for (int j = threadIdx.x; j < hd / 2; j += blockDim.x) {
+    // Lane jj's key of this CTA: how far before the new token it lies (the new token itself: 0) and whether its cache
+    // row holds a position at all (slots -1 = empty).
+    int key_age = 0;
+    bool key_valid = false;
+    if (lane < nk) {
+        const int j = j0 + lane;
+        const int64_t t_j = j < a.ctx ? a.slots[j] : t_i;
+        key_valid = (j >= a.ctx || t_j >= 0) && t_j <= t_i;
+        key_age = key_valid ? int(t_i - t_j < (int64_t(1) << 30) ? t_i - t_j : (int64_t(1) << 30)) : 0;
+    }
+    for (int j = threadIdx.x; j < HD / 2; j += blockDim.x) {
         float s, c;
         sincosf(__fmul_rn(pos, a.inv_freq[j]), &s, &c);
         cs[2 * j] = __fmul_rn(c, dm.conc);
@@ -401,12 +435,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
         const LayerW<float>& w = lws[l];
         if (l > 0) {
             sync(kDcXs, l - 1);  // also: every warp finished reading the previous layer's staged expert rows
-            if (warp == kWarps - 1) dc_stage_experts(w, dm, lay, dsm, rank, &bars[kDcExperts]);
+            if (STAGE && warp == kWarps - 1) dc_stage_experts(w, dm, lay, dsm, rank, &bars[kDcExperts]);
+            if (threadIdx.x == 32 && l + 1 < a.L) dc_prefetch_layer(lws, l + 1, a.L, dm, rank);
         }
         // ---- P1: norm, QKV rows, bias -> raw[] of every CTA
         {
             float xn[NJ][4];
-            dc_norm<NJ>(xn, xs, d, dm.eps, st.attn_norm);
+            dc_norm<NJ>(xn, xs, dm.eps, st.attn_norm);
 #pragma unroll
             for (int u = 0; u < kDcRows1; ++u) {
                 const int r = gw + kDcWarps * u;
@@ -416,21 +451,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
         sync(kDcRaw, l);
         // RoPE of the q and k heads (gpt_oss.py:44-54), v heads copied; CTA 0 stages the new K/V rows.
         {
-            const int half = hd / 2;
+            constexpr int half = HD / 2;
             for (int i = threadIdx.x; i < (H + 2 * KV) * half; i += blockDim.x) {
                 const int h = i / half, j = i % half;
-                const float lo = raw[h * hd + j], hi = raw[h * hd + j + half];
+                const float lo = raw[h * HD + j], hi = raw[h * HD + j + half];
                 float o1 = lo, o2 = hi;
                 if (h < H + KV) {
                     const float c = cs[2 * j], s = cs[2 * j + 1];
                     o1 = __fsub_rn(__fmul_rn(lo, c), __fmul_rn(hi, s));
                     o2 = __fadd_rn(__fmul_rn(hi, c), __fmul_rn(lo, s));
                 }
-                qkv[h * hd + j] = o1;
-                qkv[h * hd + j + half] = o2;
+                qkv[h * HD + j] = o1;
+                qkv[h * HD + j + half] = o2;
+                if (h >= H && nk > nkc) {  // the new token's K/V row is this CTA's key nkc
+                    float* row = (h < H + KV ? Ks + (l * a.kpc + nkc) * kvs + (h - H) * HD
+                                             : Vs + (l * a.kpc + nkc) * kvs + (h - H - KV) * HD);
+                    row[j] = o1;
+                    row[j + half] = o2;
+                }
                 if (rank == 0 && h >= H) {
-                    float* dst = h < H + KV ? a.new_k + size_t(l) * row_kv + (h - H) * hd
-                                            : a.new_v + size_t(l) * row_kv + (h - H - KV) * hd;
+                    float* dst = h < H + KV ? a.new_k + size_t(l) * row_kv + (h - H) * HD
+                                            : a.new_v + size_t(l) * row_kv + (h - H - KV) * HD;
                     dst[j] = o1;
                     dst[j + half] = o2;
                 }
@@ -443,29 +484,31 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
             const float* Vl = Vs + size_t(l) * a.kpc * kvs;
             const int window = a.windows[l];
             float* prow = dsm + lay.prow + warp * 32;
-            const int groups = 32 / hd, g = lane / hd, dd = lane % hd;
-            const int chunks = ps / 4;
+            constexpr int groups = 32 / HD;
+            const int g = lane / HD, dd = lane % HD;
+            constexpr int chunks = ps / 4;
             for (int hq = warp; hq < H; hq += kWarps) {
                 const int kvh = hq / dm.G;
-                const float* qv = qkv + hq * hd;
+                float q[HD];
+#pragma unroll
+                for (int e = 0; e < HD; e += 4) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(qkv + hq * HD + e);
+                    q[e] = q4.x; q[e + 1] = q4.y; q[e + 2] = q4.z; q[e + 3] = q4.w;
+                }
                 float s = -INFINITY;
                 if (lane < nk) {
-                    const int j = j0 + lane;
-                    const float* kr = j < a.ctx ? Kl + lane * kvs + kvh * hd : qkv + (H + kvh) * hd;
-                    float dot = 0.f;
-                    for (int e = 0; e < hd; e += 4) {
+                    const float* kr = Kl + lane * kvs + kvh * HD;
+                    float kv[HD];
+#pragma unroll
+                    for (int e = 0; e < HD; e += 4) {
                         const float4 k4 = *reinterpret_cast<const float4*>(kr + e);
-                        const float4 q4 = *reinterpret_cast<const float4*>(qv + e);
-                        dot = fmaf(q4.x, k4.x, dot);
-                        dot = fmaf(q4.y, k4.y, dot);
-                        dot = fmaf(q4.z, k4.z, dot);
-                        dot = fmaf(q4.w, k4.w, dot);
+                        kv[e] = k4.x; kv[e + 1] = k4.y; kv[e + 2] = k4.z; kv[e + 3] = k4.w;
                     }
+                    float dot = 0.f;
+#pragma unroll
+                    for (int e = 0; e < HD; ++e) dot = fmaf(q[e], kv[e], dot);
                     s = __fmul_rn(dot, dm.sm_scale);
-                    const int64_t t_j = j < a.ctx ? kst[lane] : t_i;
-                    const bool valid = j >= a.ctx || t_j >= 0;
-                    const bool visible = valid && t_j <= t_i && (window <= 0 || t_j > t_i - window);
-                    if (!visible) s = -INFINITY;
+                    if (!key_valid || (window > 0 && key_age >= window)) s = -INFINITY;
                 }
                 const float mx = warp_max(s);
                 const float p = (lane < nk && mx != -INFINITY) ? expf(s - mx) : 0.f;
@@ -474,30 +517,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
                 __syncwarp();
                 float acc = 0.f;
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {  // keys g, g + groups, ... (at most 32 / groups of them)
+                for (int i = 0; i < 32 / groups; ++i) {  // keys g, g + groups, ...
                     const int jj = g + groups * i;
-                    if (i * groups < 32 && jj < nk) {
-                        const int j = j0 + jj;
-                        const float* vr = j < a.ctx ? Vl + jj * kvs + kvh * hd : qkv + (H + KV + kvh) * hd;
-                        acc = fmaf(prow[jj], vr[dd], acc);
-                    }
+                    if (jj < nk) acc = fmaf(prow[jj], Vl[jj * kvs + kvh * HD + dd], acc);
                 }
-                for (int o = hd; o < 32; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-                // Partial = (max, sum, o[0..hd)) padded to ps floats; value i lives on lane i; pushed as float4s.
+#pragma unroll
+                for (int o = HD; o < 32; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                // Partial = (max, sum, o[0..HD)) padded to ps floats; value i lives on lane i; pushed as float4s.
                 const float ov = __shfl_sync(0xffffffffu, acc, (lane + 30) & 31);  // lane i <- o[i - 2]
-                const float val = lane == 0 ? mx : (lane == 1 ? lsum : (lane < hd + 2 ? ov : 0.f));
+                const float val = lane == 0 ? mx : (lane == 1 ? lsum : (lane < HD + 2 ? ov : 0.f));
                 const uint32_t base = off(parts + (rank * H + hq) * ps);
+#pragma unroll
                 for (int t0 = 0; t0 < chunks * kDcC; t0 += 32) {
                     const int t = t0 + lane;
-                    const int q = t % chunks, r = t / chunks;
+                    const int q4i = t % chunks, r = t / chunks;
                     float4 v4;
-                    v4.x = __shfl_sync(0xffffffffu, val, (4 * q) & 31);
-                    v4.y = __shfl_sync(0xffffffffu, val, (4 * q + 1) & 31);
-                    v4.z = __shfl_sync(0xffffffffu, val, (4 * q + 2) & 31);
-                    v4.w = __shfl_sync(0xffffffffu, val, (4 * q + 3) & 31);
+                    v4.x = __shfl_sync(0xffffffffu, val, (4 * q4i) & 31);
+                    v4.y = __shfl_sync(0xffffffffu, val, (4 * q4i + 1) & 31);
+                    v4.z = __shfl_sync(0xffffffffu, val, (4 * q4i + 2) & 31);
+                    v4.w = __shfl_sync(0xffffffffu, val, (4 * q4i + 3) & 31);
                     const uint32_t rs = __shfl_sync(0xffffffffu, rsm, r & 31);
                     const uint32_t rb = __shfl_sync(0xffffffffu, rbar, r & 31);
-                    if (t < chunks * kDcC) st_async_v4(rs + base + 16u * unsigned(q), v4, rb + 8u * kDcParts);
+                    if (t < chunks * kDcC) st_async_v4(rs + base + 16u * unsigned(q4i), v4, rb + 8u * kDcParts);
                 }
                 __syncwarp();
             }
@@ -517,21 +558,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
 #pragma unroll
             for (int c = 0; c < kDcC; ++c) {
                 const float e = __shfl_sync(0xffffffffu, ec, c);
-                if (lane < hd) o = fmaf(ph[c * H * ps + 2 + lane], e, o);
+                if (lane < HD) o = fmaf(ph[c * H * ps + 2 + lane], e, o);
             }
-            if (lane < hd) att[hq * hd + lane] = o / Lsum;
+            if (lane < HD) att[hq * HD + lane] = o / Lsum;
         }
         __syncthreads();
-        // ---- P3: out-projection + bias + residual -> x2[]
-        if (gw < d) {
+        // ---- P3: out-projection + bias + residual -> x2[]; then the next layer's P1-P3 rows
+        {
             float av[NJ][4];
             dc_read<NJ>(av, att);
             dc_push(rsm, rbar, off(x2 + gw), kDcX2, __fadd_rn(xs[gw], __fadd_rn(dc_dot<NJ>(st.out, av), st.out_b)));
         }
+        if (l + 1 < a.L) dc_load_static_attn<NJ>(st, lws[l + 1], dm, gw);
         sync(kDcX2, l);
         // ---- P4: norm and gate rows (per CTA), top-k and softmax (per warp), one mlp1 pair of each selected expert
         float xn[NJ][4];
-        dc_norm<NJ>(xn, x2, d, dm.eps, st.mlp_norm);
+        dc_norm<NJ>(xn, x2, dm.eps, st.mlp_norm);
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             const int e = warp + kWarps * u;
@@ -540,14 +582,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
                 if (lane == 0) gl[e] = __fadd_rn(acc, st.gate_b[u]);
             }
         }
-        if (threadIdx.x == 0 && live) {  // this layer's staged expert rows
-            unsigned i = 0;
-            while (i < kMaxPolls && !mbar_try_wait(&bars[kDcExperts], unsigned(l & 1))) ++i;
-            if (i == kMaxPolls) {
-                atomicOr(a.err, kErrTimeout);
-                live = false;
-            }
-        }
+        if (l + 1 < a.L) dc_load_static_mlp<NJ>(st, lws[l + 1], dm);
+        if (STAGE && threadIdx.x == 0) wait_bar(kDcExperts, unsigned(l & 1), false);  // this layer's staged rows
         __syncthreads();
         int sidx[kDcMaxK];
         float sw[kDcMaxK];
@@ -557,16 +593,37 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
             for (int r = 0; r < kDcMaxK; ++r)
                 if (r == lane && r < dm.k) a.routes[size_t(l) * dm.k + r] = sidx[r];
         }
+        int ex[kDcMaxK];
+#pragma unroll
+        for (int u = 0; u < kDcMaxK; ++u) ex[u] = u < dm.k ? int(checked_row(sidx[u], dm.E, true, a.err)) : 0;
+        // Routed rows: warp gw's mlp1 pair gw and mlp2 row gw of each selected expert (+ biases).
+        float wg[kDcMaxK][NJ][4], wl[kDcMaxK][NJ][4], w2r[kDcMaxK][NJ][4], bg[kDcMaxK], bl[kDcMaxK], bd[kDcMaxK];
 #pragma unroll
         for (int u = 0; u < kDcMaxK; ++u) {
             if (u < dm.k) {
-                const int e = int(checked_row(sidx[u], dm.E, true, a.err));
-                float wg[NJ][4], wl[NJ][4];
-                const float* W1 = w1s + (size_t(e) * lay.r1c + 2 * warp) * d;
-                dc_read<NJ>(wg, W1);
-                dc_read<NJ>(wl, W1 + d);
-                const float hg = __fadd_rn(dc_dot<NJ>(wg, xn), b1s[e * lay.r1c + 2 * warp]);
-                const float hlin = __fadd_rn(dc_dot<NJ>(wl, xn), b1s[e * lay.r1c + 2 * warp + 1]);
+                const int e = ex[u];
+                if (STAGE) {
+                    const float* W1 = w1s + (size_t(e) * lay.r1c + 2 * warp) * d;
+                    dc_read<NJ>(wg[u], W1);
+                    dc_read<NJ>(wl[u], W1 + d);
+                    bg[u] = b1s[e * lay.r1c + 2 * warp];
+                    bl[u] = b1s[e * lay.r1c + 2 * warp + 1];
+                } else {
+                    const float* W1 = w.w1 + (size_t(e) * 2 * I + 2 * gw) * d;
+                    dc_load<NJ>(wg[u], W1);
+                    dc_load<NJ>(wl[u], W1 + d);
+                    bg[u] = w.b1[size_t(e) * 2 * I + 2 * gw];
+                    bl[u] = w.b1[size_t(e) * 2 * I + 2 * gw + 1];
+                    dc_load<NJ>(w2r[u], w.w2 + (size_t(e) * d + gw) * I);
+                    bd[u] = w.b2[size_t(e) * d + gw];
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kDcMaxK; ++u) {
+            if (u < dm.k) {
+                const float hg = __fadd_rn(dc_dot<NJ>(wg[u], xn), bg[u]);
+                const float hlin = __fadd_rn(dc_dot<NJ>(wl[u], xn), bl[u]);
                 // Clamped SwiGLU (gpt_oss.py:212-219), the arithmetic of k_moe_up.
                 const float glu = fminf(hg, dm.limit);
                 const float lin = fminf(fmaxf(hlin, -dm.limit), dm.limit);
@@ -578,22 +635,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
             }
         }
         sync(kDcAct, l);
-        // ---- P5: mlp2 columns, weighted combine in slot order, residual -> x[]; next layer's static rows
+        // ---- P5: mlp2 columns, weighted combine in slot order, residual -> x[]
         {
             float comb = 0.f;
 #pragma unroll
             for (int u = 0; u < kDcMaxK; ++u) {
                 if (u < dm.k) {
-                    const int e = int(checked_row(sidx[u], dm.E, true, a.err));
-                    float w2r[NJ][4], av[NJ][4];
-                    dc_read<NJ>(w2r, w2s + (size_t(e) * lay.r2c + warp) * I);
+                    const int e = ex[u];
+                    float av[NJ][4];
+                    if (STAGE) {
+                        dc_read<NJ>(w2r[u], w2s + (size_t(e) * lay.r2c + warp) * I);
+                        bd[u] = b2s[e * lay.r2c + warp];
+                    }
                     dc_read<NJ>(av, act + u * I);
-                    comb = __fadd_rn(comb, __fmul_rn(__fadd_rn(dc_dot<NJ>(w2r, av), b2s[e * lay.r2c + warp]), sw[u]));
+                    comb = __fadd_rn(comb, __fmul_rn(__fadd_rn(dc_dot<NJ>(w2r[u], av), bd[u]), sw[u]));
                 }
             }
             dc_push(rsm, rbar, off(xs + gw), kDcXs, __fadd_rn(x2[gw], comb));
         }
-        if (l + 1 < a.L) dc_load_static<NJ>(st, lws[l + 1], dm, gw);
     }
     sync(kDcXs, a.L - 1);
 
@@ -602,7 +661,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
         if (a.rows && lane == 0) checked_row(a.rows[0], 1, true, a.err);
         float fw[NJ][4], out[NJ][4];
         dc_load<NJ>(fw, a.final_norm);
-        dc_norm<NJ>(out, xs, d, dm.eps, fw);
+        dc_norm<NJ>(out, xs, dm.eps, fw);
 #pragma unroll
         for (int j = 0; j < NJ; ++j)
             *reinterpret_cast<float4*>(a.tf + lane * 4 + 128 * j) = make_float4(out[j][0], out[j][1], out[j][2], out[j][3]);

@@ -992,6 +992,7 @@ struct GptExec {
     bool cluster_decode = false;
     int dc_kpc = 0;
     size_t dc_smem = 0;
+    void (*dc_kernel)(DecodeClusterArgs) = nullptr;
     DevBuf dc_layers, dc_windows;
 
     GptExec() = default;
@@ -1082,9 +1083,8 @@ struct GptExec {
 
     // The cluster path takes a single new token of a cached fp32 program whose widths fit its fixed work split
     // (d = H*hd = I = 128: one row of 128 per warp and lane-float4, one mlp1 pair and one mlp2 row of each expert
-    // per warp; QKV rows <= 2 per warp; k <= 4; E <= 16 gate rows; head_dim dividing 32 with room for the
-    // (max, sum) pair; ctx + 1 keys over 16 CTAs of at most 32 keys) and whose shared memory (every expert's rows
-    // of the CTA included) fits. CHROMA_B200_DECODE_CLUSTER=0 keeps the per-layer kernels.
+    // per warp; QKV rows <= 2 per warp; k <= 4; E <= 16 gate rows; head_dim 16; ctx + 1 keys over 16 CTAs of at
+    // most 32 keys) and whose shared memory fits. CHROMA_B200_DECODE_CLUSTER=0 keeps the per-layer kernels.
     void init_cluster_decode() {
         const Dims& d = m->dm;
         const int L = m->desc.layers;
@@ -1095,15 +1095,20 @@ struct GptExec {
         if (d.d != 128 || d.H * d.hd != 128 || d.I != 128) return;
         if ((d.H + 2 * d.KV) * d.hd > kDcRows1 * kDcWarps || d.k > kDcMaxK) return;
         if (reinterpret_cast<uintptr_t>(m->weights->ptr) % 16 != 0) return;  // bulk copies of the expert rows
-        if (d.E > kDcMaxE || d.E < d.k || d.hd % 4 != 0 || 32 % d.hd != 0 || d.hd + 2 > 32) return;
+        if (d.E > kDcMaxE || d.E < d.k || d.hd != 16) return;
         const int kpc = (ctx + 1 + kDcC - 1) / kDcC;
         if (kpc > 32) return;
-        const DcLayout lay(d, L, kpc);
+        // Staging every expert's rows of the CTA in shared memory (bulk copies behind P1-P3) against loading the
+        // routed rows into registers after the routing: CHROMA_B200_DECODE_STAGE=1 selects the former.
+        const char* stage_env = std::getenv("CHROMA_B200_DECODE_STAGE");
+        const bool stage = stage_env && stage_env[0] == '1';
+        const DcLayout lay(d, L, kpc, stage);
         const size_t smem = size_t(lay.total) * 4;
         if (smem + 1024 > 227 * 1024) return;
-        ClusterLaunch cl(nullptr, dim3(kDcC), dim3(kThreads), smem, kDcC, k_decode_cluster<1>);
+        dc_kernel = stage ? k_decode_cluster<1, 16, true> : k_decode_cluster<1, 16, false>;
+        ClusterLaunch cl(nullptr, dim3(kDcC), dim3(kThreads), smem, kDcC, dc_kernel);
         int clusters = 0;
-        if (cudaOccupancyMaxActiveClusters(&clusters, k_decode_cluster<1>, &cl.cfg) != cudaSuccess || clusters < 1) {
+        if (cudaOccupancyMaxActiveClusters(&clusters, dc_kernel, &cl.cfg) != cudaSuccess || clusters < 1) {
             cudaGetLastError();
             return;
         }
@@ -1117,9 +1122,19 @@ struct GptExec {
         dc_windows = DevBuf(win.size() * sizeof(int));
         check(cudaMemcpy(dc_layers.p, lw.data(), dc_layers.bytes, cudaMemcpyHostToDevice), "cluster layer table");
         check(cudaMemcpy(dc_windows.p, win.data(), dc_windows.bytes, cudaMemcpyHostToDevice), "cluster window table");
+        for (int l = 0; l + 1 < L; ++l)  // the per-layer L2 prefetch relies on each layer's tensors being contiguous
+            if (m->offsets.at(size_t(3 + 13 * (l + 1))) < m->offsets.at(size_t(3 + 13 * l))) return;
         dc_kpc = kpc;
         dc_smem = smem;
         cluster_decode = true;
+        // Beside the (L2-prefetching) cluster kernel, the side stream pulls the vocab matrix into L2 for the vocab GEMV.
+        if (!side) {
+            check(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking), "prefetch stream");
+            check(cudaEventCreateWithFlags(&fork_ev, cudaEventDisableTiming), "prefetch event");
+            check(cudaEventCreateWithFlags(&join_ev, cudaEventDisableTiming), "prefetch event");
+        }
+        prefetch_base = m->at(2);
+        prefetch_bytes = (size_t(d.V) * d.d * 4) & ~size_t(15);
     }
 
     // Kernels of this repository one enqueue() launches (the side-stream prefetch included).
@@ -1153,8 +1168,8 @@ struct GptExec {
         a.tf = tf;
         a.keys = io.keys;
         a.err = err;
-        ClusterLaunch cl(s, dim3(kDcC), dim3(kThreads), dc_smem, kDcC, k_decode_cluster<1>);
-        check(cudaLaunchKernelEx(&cl.cfg, k_decode_cluster<1>, a), "cluster decode launch");
+        ClusterLaunch cl(s, dim3(kDcC), dim3(kThreads), dc_smem, kDcC, dc_kernel);
+        check(cudaLaunchKernelEx(&cl.cfg, dc_kernel, a), "cluster decode launch");
     }
 
     template <typename T> void enqueue_t(cudaStream_t s) {
@@ -1165,7 +1180,8 @@ struct GptExec {
         if (side) {  // fork: the prefetch runs beside the whole step and joins at its end
             check(cudaEventRecord(fork_ev, s), "prefetch fork");
             check(cudaStreamWaitEvent(side, fork_ev, 0), "prefetch fork");
-            k_prefetch_l2<<<64, 256, 0, side>>>(prefetch_base, prefetch_bytes);
+            if (cluster_decode) k_prefetch_l2_bulk<<<8, 256, 0, side>>>(prefetch_base, prefetch_bytes);
+            else k_prefetch_l2<<<64, 256, 0, side>>>(prefetch_base, prefetch_bytes);
             check(cudaGetLastError(), "prefetch launch");
             check(cudaEventRecord(join_ev, side), "prefetch join");
             ++launches;
