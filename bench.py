@@ -47,6 +47,7 @@ CONTEXT = 256
 PREFILL = 8
 # DRAM bytes of one k_vocab launch of this workload, from an ncu capture (102.98 MB read + 3.87 MB written).
 VOCAB_NCU_TRAFFIC = 106_851_584
+CLUSTER_NCU_TRAFFIC = 30_900_789  # profiles/k_decode_cluster_dev_decode.md
 
 
 def parse() -> argparse.Namespace:
@@ -184,6 +185,19 @@ def prefill_flops(cfg, batch: int, n: int) -> float:  # type: ignore[no-untyped-
     gemm = 2 * N * ((H + 2 * KV) * hd * d + d * H * hd + E * d + k * (2 * I * d + d * I))
     attention = batch * H * (n * (n + 1) / 2) * hd * 2 * 2
     return cfg.num_hidden_layers * (gemm + attention) + 2 * batch * cfg.vocab_size * d
+
+
+def decode_layer_bytes(cfg, context: int) -> int:
+    """Algorithmic bytes of the layers of one batch-1 fp32 decode step: every weight the step reads (norms, sinks,
+    QKV, out-projection, router, the k routed experts' mlp1/mlp2 rows with biases), the K/V cache rows, the new
+    K/V rows written, the embedding row and the final-norm row."""
+    d, hd, H, KV, E, k, I = (cfg.hidden_size, cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads,
+                             cfg.num_experts, cfg.experts_per_token, cfg.intermediate_size)
+    qkv = (H + 2 * KV) * hd
+    static = d + H + qkv * d + qkv + d * H * hd + d + d + E * d + E
+    experts = k * (2 * I * d + 2 * I + d * I + d)
+    cache = 2 * context * KV * hd + 2 * KV * hd
+    return 4 * (cfg.num_hidden_layers * (static + experts + cache) + 3 * d)
 
 
 def decode_flops_per_token(cfg, ctx: int) -> float:  # type: ignore[no-untyped-def]
@@ -490,6 +504,21 @@ def main() -> None:
     vocab_t = statistics.mean(vocab_ms) / 1e3
     pk = peaks()
     achieved = vocab_bytes / vocab_t / 1e9
+
+    # ---- roofline of the dominant kernel: the layers (one cluster launch for batch-1 fp32), L2 flushed first
+    layer_ms = []
+    for i in range(args.warmup + reps):
+        flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        bd1._native.launch_layers(stream.cuda_stream)
+        e1.record(stream)
+        if i >= args.warmup:
+            layer_ms.append((e0, e1))
+    torch.cuda.synchronize()
+    layer_t = statistics.mean(a.elapsed_time(b) for a, b in layer_ms) / 1e3
+    layer_bytes = decode_layer_bytes(models.dev, CONTEXT)
+    layer_gbs = layer_bytes / layer_t / 1e9
     bd1.close()
 
     # ---- e2e batch 1 through the public Decoder API
@@ -630,13 +659,26 @@ def main() -> None:
                 "api": "chroma_b200.Decoder.append([token]) -> logits [1, 201088] on the host"},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {
+            "kernel": "k_decode_cluster (every layer of one decode step in a 16-CTA cluster; 60 dependent phases)",
+            "bound": "hbm", "achieved": layer_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": layer_gbs / pk["hbm_gbs"], "traffic": CLUSTER_NCU_TRAFFIC,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_decode_cluster launch of this "
+                              "workload, caches flushed (profiles/k_decode_cluster_dev_decode.md)",
+            "algorithmic_bytes": layer_bytes, "launch_us": layer_t * 1e6,
+            "peak_source": f"{pk['source']} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
+            "timing": f"launched alone after an L2 flush, CUDA events, mean of {reps}",
+            "note": "latency-bound: the weights touched per step are 12 MB; the kernel's time is its chain of "
+                    "dependent phases, not bytes",
+        },
+        "roofline_vocab": {
             "kernel": "k_vocab (unembedding GEMV, 201088 x 128 fp32, 1 row)", "bound": "hbm", "achieved": achieved,
             "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": VOCAB_NCU_TRAFFIC,
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_vocab<float, 1> launch of "
                               "this workload (profiles/k_vocab_dev_decode_step.md)",
             "algorithmic_bytes": vocab_bytes, "launch_us": vocab_t * 1e6,
             "peak_source": f"{pk['source']} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
-            "timing": f"launched alone after an L2 flush, CUDA events, mean of {reps}",
+            "timing": f"launched alone after an L2 flush, CUDA events, mean of {reps} (inside a step the vocab "
+                      "matrix is prefetched into L2 beside the layers and this kernel reads it from L2)",
         },
         "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "clocks": clocks.summary(),

@@ -128,6 +128,9 @@ class NativeDecoder:
     def launch_vocab(self, stream: int = 0) -> None:
         nat.call("chroma_b200_decoder_launch_vocab", self.handle, nat._VP(stream))
 
+    def launch_layers(self, stream: int = 0) -> None:
+        nat.call("chroma_b200_decoder_launch_layers", self.handle, nat._VP(stream))
+
     @property
     def step_launches(self) -> int:
         return int(nat.lib().chroma_b200_decoder_step_launches(self.handle))

@@ -89,6 +89,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "chroma_b200_decoder_advance": (ctypes.c_int, [_VP, _I64P, _I64P, _I32, _VP, _I64P, _CP, _SZ]),
     "chroma_b200_decoder_step_launches": (ctypes.c_int32, [_VP]),
     "chroma_b200_decoder_launch_vocab": (ctypes.c_int, [_VP, _VP, _CP, _SZ]),
+    "chroma_b200_decoder_launch_layers": (ctypes.c_int, [_VP, _VP, _CP, _SZ]),
     "chroma_b200_decoder_write": (ctypes.c_int, [_VP, _I32, _I32, _VP, _VP, _I64P, _CP, _SZ]),
     "chroma_b200_ep_create": (ctypes.c_int, [_I32, _I32, ctypes.c_int64, _I32, _I32, _I32, _I32, ctypes.POINTER(_VP),
                                              _CP, _SZ]),

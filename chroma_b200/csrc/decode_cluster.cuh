@@ -283,6 +283,7 @@ __device__ __forceinline__ void dc_prefetch_layer(const LayerW<float>* lws, int 
     const char* beg = reinterpret_cast<const char*>(lws[l].attn_norm);
     const char* end = l + 1 < L ? reinterpret_cast<const char*>(lws[l + 1].attn_norm)
                                 : reinterpret_cast<const char*>(lws[l].b2 + size_t(dm.E) * dm.d);
+    if (end <= beg) return;  // (the host admits only layer-major packed weights)
     const size_t share = ((size_t(end - beg) + kDcC - 1) / kDcC + 15) & ~size_t(15);
     const size_t off = share * size_t(rank);
     if (off >= size_t(end - beg)) return;

@@ -993,6 +993,7 @@ struct GptExec {
     int dc_kpc = 0;
     size_t dc_smem = 0;
     void (*dc_kernel)(DecodeClusterArgs) = nullptr;
+    bool skip_vocab = false;  // set while enqueue_layers runs the per-layer chain
     DevBuf dc_layers, dc_windows;
 
     GptExec() = default;
@@ -1251,9 +1252,36 @@ struct GptExec {
         const int nrows = io.rows ? B : N;
         launch(s, dim3(nrows), dim3(256), 0, k_final_norm<T>, x, nrows, io.rows, n,
                reinterpret_cast<const float*>(m->at(1)), dm, tf, io.keys, err);
-        enqueue_vocab_t<T>(s);
+        if (!skip_vocab) enqueue_vocab_t<T>(s);
         launches += 2;
         if (side) check(cudaStreamWaitEvent(s, join_ev, 0), "prefetch join");
+    }
+
+    // The layers alone, up to the final norm (reads the inputs left by the last run; no L2 prefetch beside them).
+    template <typename T> void enqueue_layers_t(cudaStream_t s) {
+        if constexpr (std::is_same_v<T, float>) {
+            if (cluster_decode) {
+                enqueue_cluster_decode(s);
+                return;
+            }
+        }
+        cudaStream_t keep = side;
+        side = nullptr;  // enqueue_t without its prefetch fork, then without the vocab kernel
+        skip_vocab = true;
+        try {
+            enqueue_t<T>(s);
+        } catch (...) {
+            side = keep;
+            skip_vocab = false;
+            throw;
+        }
+        side = keep;
+        skip_vocab = false;
+    }
+    void enqueue_layers(cudaStream_t s) {
+        if (large_path) throw ValueError("layer-only launches are for the dev-width programs");
+        if (m->desc.storage == CHROMA_B200_BF16) enqueue_layers_t<__nv_bfloat16>(s);
+        else enqueue_layers_t<float>(s);
     }
 
     // The vocab projection alone (reads the final-norm rows left by the last run).
@@ -2066,6 +2094,14 @@ int chroma_b200_decoder_advance(chroma_b200_decoder* d, const int64_t* tokens, c
 int32_t chroma_b200_decoder_step_launches(const chroma_b200_decoder* d) {
     // positions + decode program (with its L2 prefetch) + commit + advance
     return d ? 1 + d->ex[1].planned_launches() + 2 : 0;
+}
+
+int chroma_b200_decoder_launch_layers(chroma_b200_decoder* d, void* stream, char* err, size_t err_len) {
+    return guarded(err, err_len, [&] {
+        if (!d) throw ValueError("null decoder");
+        DeviceGuard guard(d->device);
+        d->ex[1].enqueue_layers(stream ? static_cast<cudaStream_t>(stream) : d->stream);
+    });
 }
 
 int chroma_b200_decoder_launch_vocab(chroma_b200_decoder* d, void* stream, char* err, size_t err_len) {

@@ -158,6 +158,9 @@ int chroma_b200_decoder_advance(chroma_b200_decoder* decoder, const int64_t* tok
                                 int32_t steps, void* stream, int64_t* ids, char* err, size_t err_len);
 /* Kernels launched by one `advance` step (launch accounting). */
 int32_t chroma_b200_decoder_step_launches(const chroma_b200_decoder* decoder);
+/* Queues the decode program's layers alone (embedding through the final norm: the one-launch cluster kernel for
+ * batch-1 fp32 programs) on `stream`, for per-kernel event timing. */
+int chroma_b200_decoder_launch_layers(chroma_b200_decoder* decoder, void* stream, char* err, size_t err_len);
 /* Queues the decode program's vocab-projection kernel alone on `stream` (for per-kernel event timing). */
 int chroma_b200_decoder_launch_vocab(chroma_b200_decoder* decoder, void* stream, char* err, size_t err_len);
 /* Empties every sequence's cache. */
