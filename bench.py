@@ -61,6 +61,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--c4-only", action="store_true", help="run only the GPT-OSS-20B-shaped prefill measurement")
     ap.add_argument("--c4-layers", type=int, default=0, help="layers of the C4 model (0: all 24; fewer for profiling)")
     ap.add_argument("--decode-only", action="store_true", help="only the headline decode measurement (profiling)")
+    ap.add_argument("--decode-batch", type=int, default=1, help="sequences of the --decode-only measurement")
     ap.add_argument("--skip-c5", action="store_true", help="skip the GPT-OSS-120B-shaped decode (multi-GPU runs)")
     ap.add_argument("--c5-only", action="store_true", help="run only the GPT-OSS-120B-shaped decode (needs >= 2 GPUs)")
     ap.add_argument("--c5-layers", type=int, default=0, help="layers of the C5 model (0: all 36)")
@@ -466,8 +467,9 @@ def main() -> None:
         return [a.elapsed_time(b) for a, b in times]
 
     # ---- headline: batch-1 device-resident greedy decode
-    bd1 = chroma_b200.BatchDecoder(prefill, decode, 1)
-    first = bd1.append(prompt[None, :], argmax=True)
+    nb = args.decode_batch if args.decode_only else 1
+    bd1 = chroma_b200.BatchDecoder(prefill, decode, nb)
+    first = bd1.append(np.repeat(prompt[None, :], nb, axis=0), argmax=True)
     bd1.generate(first, 1)
     timed_device(bd1, args.warmup)
     barrier()
@@ -480,7 +482,8 @@ def main() -> None:
     value = world * args.steps / t_max
     if args.decode_only:
         if rank == 0:
-            print(json.dumps({"decode_only": {"value": value, "ms_per_step": 1e3 * t_max / args.steps}}), flush=True)
+            print(json.dumps({"decode_only": {"batch": nb, "value": value * nb, "ms_per_step": 1e3 * t_max / args.steps}}),
+                  flush=True)
         bd1.close()
         if dist is not None:
             dist.destroy_process_group()

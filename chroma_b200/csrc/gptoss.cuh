@@ -909,4 +909,114 @@ __global__ void __launch_bounds__(kThreads + 32) k_vocab_tma(const float* __rest
     }
 }
 
+// Vocab projection of many rows (fp32, d = 128): one pass over the vocab matrix for up to kVtRows activation rows.
+// Each CTA keeps the rows in shared memory and walks 128-row vocab tiles (cp.async double buffer, 132-float padded
+// rows: conflict-free 16-byte reads); thread (ty, tx) computes kVtRows/16 rows x 8 vocab rows (tx + 16j), each dot
+// product one sequential FMA chain over the 128 features. The greedy argmax is kept per thread across tiles and
+// merged with one 64-bit atomicMax per (CTA, row). Compute-bound: 2 * rows * V * 128 FLOP, weights read once.
+constexpr int kVtRows = 64;
+constexpr int kVtVocab = 128;
+constexpr int kVtD = 128;
+constexpr int kVtPad = kVtD + 4;
+constexpr size_t kVtSmemBytes = (size_t(kVtRows) + 2 * kVtVocab) * kVtPad * 4;
+
+__global__ void __launch_bounds__(kThreads, 1) k_vocab_tiled(const float* __restrict__ xin, int nrows, int V,
+                                                             const float* __restrict__ W, float* __restrict__ logits,
+                                                             unsigned long long* __restrict__ keys) {
+    extern __shared__ __align__(16) float vt[];
+    float* xs = vt;                          // [kVtRows][kVtPad]
+    float* ws = vt + kVtRows * kVtPad;       // [2][kVtVocab][kVtPad]
+    constexpr int RPT = kVtRows / 16;        // rows per thread
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int tiles = (V + kVtVocab - 1) / kVtVocab;
+    auto load_tile = [&](int tile, int buf) {
+        float* dst = ws + buf * kVtVocab * kVtPad;
+        for (int i = threadIdx.x; i < kVtVocab * (kVtD / 4); i += blockDim.x) {
+            const int r = i / (kVtD / 4), c = (i % (kVtD / 4)) * 4;
+            const int v = tile * kVtVocab + r;
+            if (v < V) cp_async16(dst + r * kVtPad + c, W + size_t(v) * kVtD + c);
+        }
+        cp_async_commit();
+    };
+    int tile = blockIdx.x;
+    if (tile < tiles) load_tile(tile, 0);  // weights: before the PDL wait
+    pdl_wait();
+    pdl_trigger();
+    for (int r0 = 0; r0 < nrows; r0 += kVtRows) {
+        const int rr = min(kVtRows, nrows - r0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < kVtRows * (kVtD / 4); i += blockDim.x) {
+            const int r = i / (kVtD / 4), c = (i % (kVtD / 4)) * 4;
+            const float4 v = r < rr ? *reinterpret_cast<const float4*>(xin + size_t(r0 + r) * kVtD + c)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(xs + r * kVtPad + c) = v;
+        }
+        unsigned long long best[RPT];
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) best[i] = 0ull;
+        if (r0 > 0) {
+            tile = blockIdx.x;
+            if (tile < tiles) load_tile(tile, 0);
+        }
+        for (int it = 0; tile < tiles; ++it, tile += gridDim.x) {
+            const int buf = it & 1;
+            const int next = tile + gridDim.x;
+            if (next < tiles) {
+                load_tile(next, buf ^ 1);
+                cp_async_wait<1>();
+            } else {
+                cp_async_wait<0>();
+            }
+            __syncthreads();
+            const float* wt = ws + buf * kVtVocab * kVtPad;
+            float acc[RPT][8];
+#pragma unroll
+            for (int i = 0; i < RPT; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+#pragma unroll 4
+            for (int k = 0; k < kVtD; k += 4) {
+                float4 x[RPT], w[8];
+#pragma unroll
+                for (int i = 0; i < RPT; ++i) x[i] = *reinterpret_cast<const float4*>(xs + (ty * RPT + i) * kVtPad + k);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) w[j] = *reinterpret_cast<const float4*>(wt + (tx + 16 * j) * kVtPad + k);
+#pragma unroll
+                for (int i = 0; i < RPT; ++i)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        acc[i][j] = fmaf(x[i].x, w[j].x, acc[i][j]);
+                        acc[i][j] = fmaf(x[i].y, w[j].y, acc[i][j]);
+                        acc[i][j] = fmaf(x[i].z, w[j].z, acc[i][j]);
+                        acc[i][j] = fmaf(x[i].w, w[j].w, acc[i][j]);
+                    }
+            }
+#pragma unroll
+            for (int i = 0; i < RPT; ++i) {
+                const int row = ty * RPT + i;
+                if (row >= rr) continue;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int v = tile * kVtVocab + tx + 16 * j;
+                    if (v < V) {
+                        if (logits) logits[size_t(r0 + row) * V + v] = acc[i][j];
+                        best[i] = max(best[i], argmax_key(acc[i][j], v));
+                    }
+                }
+            }
+            __syncthreads();  // the buffer is refilled two tiles later
+        }
+        if (keys) {
+#pragma unroll
+            for (int i = 0; i < RPT; ++i) {
+                unsigned long long b = best[i];
+#pragma unroll
+                for (int o = 8; o; o >>= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
+                const int row = ty * RPT + i;
+                if (tx == 0 && row < rr && b) atomicMax(keys + r0 + row, b);
+            }
+        }
+    }
+}
+
 }  // namespace cb200

@@ -387,6 +387,14 @@ static void launch_vocab(cudaStream_t s, const Dims& dm, int sms, const float* x
         else launch_vocab_tma<T, kVocabRows>(s, dm, sms, x, rows, W, logits, keys, err);
         return;
     }
+    if constexpr (std::is_same_v<T, float>) {
+        if (rows > kVocabRows && dm.d == kVtD) {  // many rows: one pass over the vocab matrix per 64 rows
+            const int tiles = (dm.V + kVtVocab - 1) / kVtVocab;
+            launch(s, dim3(std::min(tiles, sms)), dim3(kThreads), kVtSmemBytes, k_vocab_tiled, x, rows, dm.V, W, logits,
+                   keys);
+            return;
+        }
+    }
     if (rows == 1) launch_vocab_r<T, 1>(s, dm, sms, x, rows, W, logits, keys);
     else if (rows <= 2) launch_vocab_r<T, 2>(s, dm, sms, x, rows, W, logits, keys);
     else if (rows <= 4) launch_vocab_r<T, 4>(s, dm, sms, x, rows, W, logits, keys);
@@ -1037,9 +1045,10 @@ struct GptExec {
             }
         }
         key_chunk = d.hd <= 32 ? 512 : 256;
-        // Few (row, kv head) pairs (small-batch fp32 decode): split the keys finer so more CTAs share the latency.
-        // bf16 programs keep whole chunks: a single chunk rounds the probabilities where the reference does.
-        if (model.desc.storage == CHROMA_B200_FP32 && N * size_t(d.KV) <= 8) key_chunk = 64;
+        // fp32 programs split the keys into 64-key chunks merged by the last CTA, so decode batches fill the GPU
+        // (batch 64: 320 CTAs instead of 64 whole-ring ones). bf16 programs keep whole chunks: a single chunk
+        // rounds the probabilities where the reference does.
+        if (model.desc.storage == CHROMA_B200_FP32) key_chunk = 64;
         chunks = (ctx + n + key_chunk - 1) / key_chunk;
         auto round = [](size_t b) { return (b + 255) / 256 * 256; };
         std::vector<Alloc> a = {
