@@ -469,7 +469,7 @@ def main() -> None:
     # ---- headline: batch-1 device-resident greedy decode
     nb = args.decode_batch if args.decode_only else 1
     bd1 = chroma_b200.BatchDecoder(prefill, decode, nb)
-    first = bd1.append(np.repeat(prompt[None, :], nb, axis=0), argmax=True)
+    first = bd1.append(prompt[None, :] if nb == 1 else rng.integers(0, V, (nb, PREFILL)), argmax=True)
     bd1.generate(first, 1)
     timed_device(bd1, args.warmup)
     barrier()

@@ -909,6 +909,212 @@ __global__ void __launch_bounds__(kThreads + 32) k_vocab_tma(const float* __rest
     }
 }
 
+// ------------------------------------------------------------------------------------------------------
+// Expert-grouped MoE for many tokens (d = I = 128). k_moe_up / k_moe_down give every (token, slot) its own CTAs,
+// which re-run the router per CTA and re-read each expert's rows once per token; with 64+ tokens per launch that
+// is ~30 MB of L2 reads per layer. Here the router runs once per token and appends (token * k + slot) to its
+// expert's list; then each CTA owns a block of one expert's rows, held in registers, and walks that expert's list.
+// Arithmetic, rounding points and summation orders are those of k_moe_up / k_moe_down: results are bit-identical.
+constexpr int kGroupRows = 16;  // (token, slot) rows per CTA pass of a grouped kernel (the list's split over grid.z)
+constexpr int kGroupTile = 4;   // rows computed together (independent reductions in flight)
+
+// grid = ntok, block = 128. RMSNorm + gate + top-k + softmax of one token (the router of k_moe_up); the normalised
+// row goes to xn_out for the grouped up-projection.
+template <typename T>
+__global__ void __launch_bounds__(128) k_route_rows(const float* __restrict__ x2, int ntok, Dims dm, LayerW<T> w,
+                                                    float* __restrict__ xn_out, int* __restrict__ ridx,
+                                                    float* __restrict__ rw, int* __restrict__ routes,
+                                                    int* __restrict__ lists, int* __restrict__ counts, unsigned* err) {
+    extern __shared__ float sm[];
+    const int d = dm.d;
+    float* xs = sm;            // [d]
+    float* gl = xs + d;        // [E]
+    float* misc = gl + dm.E;   // [1 + 8 + 8]: inv, indices, weights
+    int* sidx = reinterpret_cast<int*>(misc + 1);
+    float* sw = misc + 9;
+    const int t = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    pdl_wait();
+    pdl_trigger();
+    for (int c = threadIdx.x; c < d; c += blockDim.x) xs[c] = x2[size_t(t) * d + c];
+    __syncthreads();
+    rows_rmsnorm<T>(xs, 1, d, dm.eps, w.mlp_norm, misc);
+    for (int c = threadIdx.x; c < d; c += blockDim.x) xn_out[size_t(t) * d + c] = xs[c];
+    for (int e0 = warp * 2; e0 < dm.E; e0 += warps * 2) {
+        const T* rows[2] = {w.gate_w + size_t(e0) * d, w.gate_w + size_t(min(e0 + 1, dm.E - 1)) * d};
+        const int nr = min(2, dm.E - e0);
+        Frag<2> f;
+        frag_load<T, 2>(f, rows, nr, d, 0);
+        float acc[2][1];
+        warp_gemv<T, 2, 1>(f, rows, nr, xs, d, 1, acc);
+        if (lane == 0) {
+            gl[e0] = Store<T>::round(__fadd_rn(acc[0][0], Store<T>::load(w.gate_b + e0)));
+            if (nr > 1) gl[e0 + 1] = Store<T>::round(__fadd_rn(acc[1][0], Store<T>::load(w.gate_b + e0 + 1)));
+        }
+    }
+    __syncthreads();
+    if (warp == 0) warp_topk_softmax<T>(gl, dm.E, dm.k, sidx, sw);
+    __syncthreads();
+    if (threadIdx.x < dm.k) {
+        const int slot = threadIdx.x;
+        ridx[size_t(t) * dm.k + slot] = sidx[slot];
+        rw[size_t(t) * dm.k + slot] = sw[slot];
+        if (routes) routes[size_t(t) * dm.k + slot] = sidx[slot];
+        const int e = int(checked_row(sidx[slot], dm.E, true, err));
+        const int at = atomicAdd(counts + e, 1);
+        lists[size_t(e) * ntok + at] = t * dm.k + slot;
+    }
+}
+
+// grid = (E, ceil(I / kPairsPerCta), ceil(ntok / kGroupRows)), block = kThreads. Warp w holds mlp1 pairs p, p+1
+// (4 rows) of expert blockIdx.x; for every (token, slot) routed there (blockIdx.z's share of the list), the SwiGLU
+// of k_moe_up.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) k_moe_up_grouped(const float* __restrict__ xn, int ntok, Dims dm, LayerW<T> w,
+                                                             const int* __restrict__ lists,
+                                                             const int* __restrict__ counts, float* __restrict__ act) {
+    extern __shared__ float xg[];  // [kGroupRows][d]
+    __shared__ int tl[kGroupRows];  // the staged rows' (token * k + slot)
+    const int e = blockIdx.x, d = dm.d;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const T* W = w.w1 + size_t(e) * 2 * dm.I * d;
+    const T* B = w.b1 + size_t(e) * 2 * dm.I;
+    const int p = blockIdx.y * kPairsPerCta + warp * 2;
+    const int np = max(0, min(2, dm.I - p));
+    const int p1 = min(p + 1, dm.I - 1);
+    const int p0 = min(p, dm.I - 1);
+    const T* rows[4] = {W + size_t(2 * p0) * d, W + size_t(2 * p0 + 1) * d, W + size_t(2 * p1) * d,
+                        W + size_t(2 * p1 + 1) * d};
+    Frag<4> f;
+    frag_load<T, 4>(f, rows, 2 * np, d, 0);
+    float bias[4] = {0.f, 0.f, 0.f, 0.f};
+    if (np > 0) {
+        bias[0] = Store<T>::load(B + 2 * p0);
+        bias[1] = Store<T>::load(B + 2 * p0 + 1);
+        bias[2] = Store<T>::load(B + 2 * p1);
+        bias[3] = Store<T>::load(B + 2 * p1 + 1);
+    }
+    pdl_wait();
+    pdl_trigger();
+    const int n = counts[e];
+    for (int i0 = blockIdx.z * kGroupRows; i0 < n; i0 += gridDim.z * kGroupRows) {
+        const int rows_here = min(kGroupRows, n - i0);
+        __syncthreads();
+        for (int r = threadIdx.x; r < rows_here; r += blockDim.x) tl[r] = lists[size_t(e) * ntok + i0 + r];
+        __syncthreads();
+        for (int i = threadIdx.x; i < rows_here * (d / 4); i += blockDim.x) {
+            const int r = i / (d / 4), c = (i % (d / 4)) * 4;
+            const int tok = tl[r] / dm.k;
+            *reinterpret_cast<float4*>(xg + r * d + c) = *reinterpret_cast<const float4*>(xn + size_t(tok) * d + c);
+        }
+        __syncthreads();
+        if (np == 0) continue;
+        for (int r0 = 0; r0 < rows_here; r0 += kGroupTile) {
+            const int tt = min(kGroupTile, rows_here - r0);
+            float acc[4][kGroupTile];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int t = 0; t < kGroupTile; ++t) acc[u][t] = 0.f;
+            frag_fma<4, kGroupTile>(f, xg + r0 * d, d, tt, 0, acc);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int t = 0; t < kGroupTile; ++t) acc[u][t] = warp_sum(acc[u][t]);
+            // Lane q < 2 * tt handles row r0 + q / 2, pair p + q % 2.
+            const int q = lane;
+            if (q < 2 * tt && q % 2 < np) {
+                const int t = q / 2, h = q % 2;
+                float ag = 0.f, al = 0.f;
+#pragma unroll
+                for (int tq = 0; tq < kGroupTile; ++tq)
+                    if (tq == t) {
+                        ag = h == 0 ? acc[0][tq] : acc[2][tq];
+                        al = h == 0 ? acc[1][tq] : acc[3][tq];
+                    }
+                const float bg = h == 0 ? bias[0] : bias[2];
+                const float bl = h == 0 ? bias[1] : bias[3];
+                const float hg = Store<T>::round(__fadd_rn(Store<T>::round(ag), bg));
+                const float hl = Store<T>::round(__fadd_rn(Store<T>::round(al), bl));
+                const float glu = fminf(hg, dm.limit);
+                const float lin = fminf(fmaxf(hl, -dm.limit), dm.limit);
+                const float z = Store<T>::round(__fmul_rn(glu, dm.alpha));
+                const float sg = Store<T>::round(1.0f / (1.0f + expf(-z)));
+                const float og = Store<T>::round(__fmul_rn(glu, sg));
+                const float l1 = Store<T>::round(__fadd_rn(lin, 1.0f));
+                act[size_t(tl[r0 + t]) * dm.I + p + h] = Store<T>::round(__fmul_rn(og, l1));
+            }
+        }
+    }
+}
+
+// grid = (E, ceil(d / kWarps), ceil(ntok / kGroupRows)), block = kThreads. Warp w holds mlp2 row (e, c) of expert
+// blockIdx.x; for every (token, slot) routed there (blockIdx.z's share), y = mlp2 . act + bias (the per-slot term of
+// k_moe_down) into ys.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) k_moe_down_grouped(const float* __restrict__ act, int ntok, Dims dm,
+                                                               const T* __restrict__ w2, const T* __restrict__ b2,
+                                                               const int* __restrict__ lists,
+                                                               const int* __restrict__ counts, float* __restrict__ ys) {
+    extern __shared__ float ag[];  // [kGroupRows][I]
+    __shared__ int tl[kGroupRows];  // the staged rows' (token * k + slot)
+    const int e = blockIdx.x, I = dm.I;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.y * kWarps + warp;
+    const int cc = min(c, dm.d - 1);
+    const T* rows[1] = {w2 + (size_t(e) * dm.d + cc) * I};
+    Frag<1> f;
+    frag_load<T, 1>(f, rows, c < dm.d ? 1 : 0, I, 0);
+    const float bias = Store<T>::load(b2 + size_t(e) * dm.d + cc);
+    pdl_wait();
+    pdl_trigger();
+    const int n = counts[e];
+    for (int i0 = blockIdx.z * kGroupRows; i0 < n; i0 += gridDim.z * kGroupRows) {
+        const int rows_here = min(kGroupRows, n - i0);
+        __syncthreads();
+        for (int r = threadIdx.x; r < rows_here; r += blockDim.x) tl[r] = lists[size_t(e) * ntok + i0 + r];
+        __syncthreads();
+        for (int i = threadIdx.x; i < rows_here * (I / 4); i += blockDim.x) {
+            const int r = i / (I / 4), q = (i % (I / 4)) * 4;
+            *reinterpret_cast<float4*>(ag + r * I + q) = *reinterpret_cast<const float4*>(act + size_t(tl[r]) * I + q);
+        }
+        __syncthreads();
+        if (c >= dm.d) continue;
+        for (int r0 = 0; r0 < rows_here; r0 += kGroupTile) {
+            const int tt = min(kGroupTile, rows_here - r0);
+            float acc[1][kGroupTile];
+#pragma unroll
+            for (int t = 0; t < kGroupTile; ++t) acc[0][t] = 0.f;
+            frag_fma<1, kGroupTile>(f, ag + r0 * I, I, tt, 0, acc);
+#pragma unroll
+            for (int t = 0; t < kGroupTile; ++t) acc[0][t] = warp_sum(acc[0][t]);
+            if (lane < tt) {
+                float part = acc[0][0];
+#pragma unroll
+                for (int t = 1; t < kGroupTile; ++t)
+                    if (t == lane) part = acc[0][t];
+                ys[size_t(tl[r0 + lane]) * dm.d + c] = Store<T>::round(__fadd_rn(Store<T>::round(part), bias));
+            }
+        }
+    }
+}
+
+// grid = ntok, block = d (<= 1024). x = x2 + the routing-weighted sum of the slots' ys in slot order (the combine of
+// k_moe_down); CTA 0 also clears the per-expert counts for the next layer's router.
+template <typename T>
+__global__ void k_moe_combine_rows(const float* __restrict__ ys, const float* __restrict__ x2, int ntok, Dims dm,
+                                   const float* __restrict__ rw, float* __restrict__ x_out, int* __restrict__ counts) {
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.x, c = threadIdx.x;
+    if (t == 0 && c < dm.E) counts[c] = 0;
+    if (c >= dm.d) return;
+    float comb = 0.f;
+    for (int u = 0; u < dm.k; ++u)
+        comb = __fadd_rn(comb, __fmul_rn(ys[(size_t(t) * dm.k + u) * dm.d + c], rw[size_t(t) * dm.k + u]));
+    x_out[size_t(t) * dm.d + c] = Store<T>::round(__fadd_rn(x2[size_t(t) * dm.d + c], Store<T>::round(comb)));
+}
+
 // Vocab projection of many rows (fp32, d = 128): one pass over the vocab matrix for up to kVtRows activation rows.
 // Each CTA keeps the rows in shared memory and walks 128-row vocab tiles (cp.async double buffer, 132-float padded
 // rows: conflict-free 16-byte reads); thread (ty, tx) computes kVtRows/16 rows x 8 vocab rows (tx + 16j), each dot

@@ -1001,6 +1001,10 @@ struct GptExec {
     int dc_kpc = 0;
     size_t dc_smem = 0;
     void (*dc_kernel)(DecodeClusterArgs) = nullptr;
+    // Expert-grouped MoE for 16+ tokens of d = I = 128 programs (gptoss.cuh k_route_rows ... k_moe_combine_rows;
+    // CHROMA_B200_PER_SLOT_MOE keeps k_moe_up / k_moe_down, whose results are the same bits).
+    bool grouped_moe = false;
+    DevBuf g_xn, g_lists, g_counts, g_ys;
     bool skip_vocab = false;  // set while enqueue_layers runs the per-layer chain
     DevBuf dc_layers, dc_windows;
 
@@ -1088,6 +1092,14 @@ struct GptExec {
         }
         counters = DevBuf(N * d.KV * sizeof(unsigned));
         check(cudaMemset(counters.p, 0, counters.bytes), "attention counters");
+        if (N >= 16 && d.d == 128 && d.I == 128 && std::getenv("CHROMA_B200_PER_SLOT_MOE") == nullptr) {
+            grouped_moe = true;
+            g_xn = DevBuf(N * d.d * 4);
+            g_lists = DevBuf(size_t(d.E) * N * 4);
+            g_counts = DevBuf(size_t(d.E) * 4);
+            check(cudaMemset(g_counts.p, 0, g_counts.bytes), "expert counts");
+            g_ys = DevBuf(N * d.k * d.d * 4);
+        }
         init_cluster_decode();
     }
 
@@ -1151,7 +1163,7 @@ struct GptExec {
     int planned_launches() const {
         if (large_path) return large.launches;
         const int pre = side ? 1 : 0;
-        return cluster_decode ? pre + 2 : pre + 1 + 5 * m->desc.layers + 2;
+        return cluster_decode ? pre + 2 : pre + 1 + (grouped_moe ? 7 : 5) * m->desc.layers + 2;
     }
 
     void enqueue_cluster_decode(cudaStream_t s) {
@@ -1252,6 +1264,23 @@ struct GptExec {
                    static_cast<const T*>(nk), static_cast<const T*>(nv), bias, w.sinks, attn);
             launch(s, dim3((dm.d + 2 * kWarps - 1) / (2 * kWarps), tiles), dim3(kThreads), smem_out, k_out<T>, attn, x, N,
                    dm, w.out_w, w.out_b, x2);
+            if (grouped_moe) {
+                int* counts = g_counts.as<int>();
+                const unsigned zs = unsigned((N + kGroupRows - 1) / kGroupRows);  // a fully skewed routing still spreads
+                launch(s, dim3(N), dim3(128), smem_up, k_route_rows<T>, x2, N, dm, w, g_xn.as<float>(), ridx, rw,
+                       io.routes ? io.routes + size_t(l) * N * dm.k : nullptr, g_lists.as<int>(), counts, err);
+                launch(s, dim3(dm.E, (dm.I + kPairsPerCta - 1) / kPairsPerCta, zs), dim3(kThreads),
+                       size_t(kGroupRows) * dm.d * 4, k_moe_up_grouped<T>, static_cast<const float*>(g_xn.as<float>()), N,
+                       dm, w, static_cast<const int*>(g_lists.as<int>()), static_cast<const int*>(counts), act);
+                launch(s, dim3(dm.E, (dm.d + kWarps - 1) / kWarps, zs), dim3(kThreads), size_t(kGroupRows) * dm.I * 4,
+                       k_moe_down_grouped<T>, static_cast<const float*>(act), N, dm, w.w2, w.b2,
+                       static_cast<const int*>(g_lists.as<int>()), static_cast<const int*>(counts), g_ys.as<float>());
+                launch(s, dim3(N), dim3(std::max(dm.d, dm.E)), 0, k_moe_combine_rows<T>,
+                       static_cast<const float*>(g_ys.as<float>()), static_cast<const float*>(x2), N, dm,
+                       static_cast<const float*>(rw), x, counts);
+                launches += 7;
+                continue;
+            }
             launch(s, dim3(N * dm.k, (dm.I + kPairsPerCta - 1) / kPairsPerCta), dim3(kThreads), smem_up, k_moe_up<T>, x2,
                    N, dm, w, ridx, rw, io.routes ? io.routes + size_t(l) * N * dm.k : nullptr, act, err);
             launch(s, dim3(N, (dm.d + kWarps - 1) / kWarps), dim3(kThreads), size_t(dm.k) * dm.I * 4, k_moe_down<T>, act,

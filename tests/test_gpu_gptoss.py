@@ -177,6 +177,29 @@ def test_decoder_logits_are_independent_page_locked_arrays(gpu: None) -> None:
         np.testing.assert_allclose(c, want, **FP32)
 
 
+def test_grouped_moe_matches_per_slot_kernels(gpu: None) -> None:
+    """The expert-grouped MoE kernels (16+ tokens per launch) against the per-(token, slot) kernels
+    (CHROMA_B200_PER_SLOT_MOE=1, in a subprocess): the same arithmetic in the same order, so identical bits; and the
+    routing record of every layer."""
+    path = _TMP / "dev_fwd48"
+    tokens = np.random.default_rng(48).integers(0, models.dev.vocab_size, 48)
+    with chroma_b200.compile(torch.export.export(helpers.dev_model(), (torch.arange(48),)), path) as program:
+        got = np.asarray(program(tokens))
+    np.save(_TMP / "fwd48_tokens.npy", tokens)
+    code = (
+        "import sys, numpy as np\n"
+        "from chroma_b200 import Program\n"
+        "with Program(sys.argv[1]) as p:\n"
+        "    np.save(sys.argv[3], p(np.load(sys.argv[2])))\n"
+    )
+    env = dict(os.environ, CHROMA_B200_PER_SLOT_MOE="1", PYTHONPATH=str(ROOT))
+    subprocess.run([sys.executable, "-c", code, str(path), str(_TMP / "fwd48_tokens.npy"), str(_TMP / "fwd48_ref.npy")],
+                   check=True, env=env)
+    want = np.load(_TMP / "fwd48_ref.npy")
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    np.testing.assert_allclose(got, og.forward(*helpers.dev_oracle(), tokens), **FP32)
+
+
 def test_c2_batch_decoder_matches_reference(gpu: None) -> None:
     g = golden("c2_decode")
     prefill, decode = dev_pair()
