@@ -232,6 +232,7 @@ class Native:
                  ep: Any = None) -> None:
         self.plan = plan
         self._keep: list[Any] = []
+        self.pinned = PinnedPool()  # results of calls without `out` live in page-locked memory
         desc = self._desc(plan)
         handle = _VP()
         if ep is not None:
@@ -325,6 +326,9 @@ class Native:
         handle, self.handle = getattr(self, "handle", None), None
         if handle:
             lib().chroma_b200_destroy(handle)
+        pinned = getattr(self, "pinned", None)
+        if pinned is not None:
+            pinned.close()
 
     def __del__(self) -> None:
         try:

@@ -129,7 +129,13 @@ class Program:
         if out is None:
             from chroma_b200._src.native import dtype_of
 
-            res: list[np.ndarray] = [np.empty(spec["shape"], dtype=dtype_of(spec["dtype"])) for spec in self._outputs]
+            # Results of the native runtime go to page-locked blocks (one DMA per output, no staging copy).
+            pool = getattr(getattr(self._model, "native", None), "pinned", None)
+            res: list[np.ndarray] = [
+                pool.array(tuple(spec["shape"]), dtype_of(spec["dtype"])) if pool is not None
+                else np.empty(spec["shape"], dtype=dtype_of(spec["dtype"]))
+                for spec in self._outputs
+            ]
         else:
             res = [out] if isinstance(out, np.ndarray) else list(out)
         with self._lock:

@@ -63,7 +63,6 @@ struct DecodeClusterArgs {
     const float* final_norm;          // [d]
     const float* inv_freq;            // [hd/2]
     const int64_t* tokens;            // [1]
-    const float* positions;           // [1]
     const int64_t* pos0;              // [1] absolute position of the new token
     const int64_t* slots;             // [ctx] absolute position held by each cache row (-1 empty)
     const float* cache_k;             // [L][ctx][KV][hd]
@@ -75,6 +74,11 @@ struct DecodeClusterArgs {
     float* tf;                        // [d] final-norm output for the vocab kernel
     unsigned long long* keys;         // [1] argmax key cleared for the vocab kernel, or null
     unsigned* err;
+    // Device-resident decoding commits in place: the new K/V rows also go to ring slot pos0 % ctx of these caches
+    // and the slot records pos0 (the commit kernel's job otherwise). Null: staging only.
+    float* commit_k;
+    float* commit_v;
+    int64_t* commit_slots;
 };
 
 __host__ __device__ inline int dc_up4(int v) { return (v + 3) & ~3; }
@@ -380,6 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
     DcStatic<NJ> st;
     dc_load_static_attn<NJ>(st, a.layers[0], dm, gw);
     dc_load_static_mlp<NJ>(st, a.layers[0], dm);
+    float fnorm[NJ][4];  // the final norm's weights, for CTA 0's last step
+    dc_load<NJ>(fnorm, a.final_norm);
     if (threadIdx.x == 0) {
         for (int b = 0; b < kDcBars; ++b) mbar_init(&bars[b], 1);
         fence_barrier_init();
@@ -406,12 +412,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
         }
         cp_async_commit();
     }
-    {
-        const int64_t row = checked_row(a.tokens[0], dm.V, false, a.err);
-        for (int c = threadIdx.x; c < d; c += blockDim.x) xs[c] = a.emb[size_t(row) * d + c];
-    }
-    const float pos = a.positions[0];
     const int64_t t_i = a.pos0[0];
+    const float pos = float(t_i);  // the position k_positions would store for the single row
+    const int64_t tok_row = checked_row(a.tokens[0], dm.V, false, a.err);
     // Lane jj's key of this CTA: how far before the new token it lies (the new token itself: 0) and whether its cache
     // row holds a position at all (slots -1 = empty).
     int key_age = 0;
@@ -428,9 +431,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
         cs[2 * j] = __fmul_rn(c, dm.conc);
         cs[2 * j + 1] = __fmul_rn(s, dm.conc);
     }
-    cp_async_wait<0>();
+    for (int c = threadIdx.x; c < d; c += blockDim.x) xs[c] = a.emb[size_t(tok_row) * d + c];
     __syncthreads();
     cluster_sync_all();  // every CTA runs and has armed its mbarriers before the first remote store
+    // In-place commit: every CTA has consumed its slot positions (the barrier above releases those reads), and the
+    // ring slot being overwritten is masked for every reader (its old position lies ctx back, or it is empty).
+    const int commit_slot = int(t_i % a.ctx);
+    if (a.commit_slots && rank == 0 && threadIdx.x == 0) a.commit_slots[commit_slot] = t_i;
 
     for (int l = 0; l < a.L; ++l) {
         const LayerW<float>& w = lws[l];
@@ -475,9 +482,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
                                             : a.new_v + size_t(l) * row_kv + (h - H - KV) * HD;
                     dst[j] = o1;
                     dst[j + half] = o2;
+                    if (a.commit_k) {
+                        const size_t row = (size_t(l) * a.ctx + commit_slot) * row_kv;
+                        float* cdst = h < H + KV ? a.commit_k + row + (h - H) * HD : a.commit_v + row + (h - H - KV) * HD;
+                        cdst[j] = o1;
+                        cdst[j + half] = o2;
+                    }
                 }
             }
         }
+        if (l == 0) cp_async_wait<0>();  // the cache slices of every layer (issued in the prologue) have landed
         __syncthreads();
         // ---- P2: attention partials over this CTA's keys, one warp per query head
         {
@@ -660,9 +674,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
     // Final RMSNorm of the token's row (gpt_oss.py:309) for the vocab kernel; clears the argmax key.
     if (rank == 0 && warp == 0) {
         if (a.rows && lane == 0) checked_row(a.rows[0], 1, true, a.err);
-        float fw[NJ][4], out[NJ][4];
-        dc_load<NJ>(fw, a.final_norm);
-        dc_norm<NJ>(out, xs, dm.eps, fw);
+        float out[NJ][4];
+        dc_norm<NJ>(out, xs, dm.eps, fnorm);
 #pragma unroll
         for (int j = 0; j < NJ; ++j)
             *reinterpret_cast<float4*>(a.tf + lane * 4 + 128 * j) = make_float4(out[j][0], out[j][1], out[j][2], out[j][3]);

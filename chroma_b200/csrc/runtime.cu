@@ -579,6 +579,9 @@ struct GptIO {
     void* logits = nullptr;
     unsigned long long* keys = nullptr;  // [rows] optional fused-argmax keys
     int* routes = nullptr;          // [L][B*n][k] optional record of the routing
+    void* commit_k = nullptr;       // in-place commit of the new rows (device-resident decoding, cluster path)
+    void* commit_v = nullptr;
+    int64_t* commit_slots = nullptr;
 };
 
 // The large-width bf16 path (hidden >= 1024, head_dim 64): tensor-core GEMMs, flash attention for prefill chunks,
@@ -1178,7 +1181,6 @@ struct GptExec {
         a.final_norm = reinterpret_cast<const float*>(m->at(1));
         a.inv_freq = m->inv_freq.as<const float>();
         a.tokens = io.tokens;
-        a.positions = io.positions;
         a.pos0 = io.pos0;
         a.slots = io.slots;
         a.cache_k = static_cast<const float*>(io.cache_k);
@@ -1186,10 +1188,13 @@ struct GptExec {
         a.new_k = static_cast<float*>(io.new_k);
         a.new_v = static_cast<float*>(io.new_v);
         a.routes = io.routes;
-        a.rows = io.rows;
+        a.rows = io.commit_k ? nullptr : io.rows;  // device-resident steps always take their single new row
         a.tf = tf;
         a.keys = io.keys;
         a.err = err;
+        a.commit_k = static_cast<float*>(io.commit_k);
+        a.commit_v = static_cast<float*>(io.commit_v);
+        a.commit_slots = io.commit_slots;
         ClusterLaunch cl(s, dim3(kDcC), dim3(kThreads), dc_smem, kDcC, dc_kernel);
         check(cudaLaunchKernelEx(&cl.cfg, dc_kernel, a), "cluster decode launch");
     }
@@ -2098,9 +2103,22 @@ int chroma_b200_decoder_advance(chroma_b200_decoder* d, const int64_t* tokens, c
         GptExec& e = d->ex[1];
         for (int i = 0; i < steps; ++i) {
             d->advance_graph.run(s, [&](cudaStream_t st) {
+                e.io.keys = d->keys.as<unsigned long long>();
+                if (e.cluster_decode) {
+                    // One cluster launch computes the positions itself and commits its rows in place.
+                    e.io.commit_k = d->cache_k.p;
+                    e.io.commit_v = d->cache_v.p;
+                    e.io.commit_slots = d->slots.as<int64_t>();
+                    e.enqueue(st);
+                    e.io.commit_k = e.io.commit_v = nullptr;
+                    e.io.commit_slots = nullptr;
+                    launch(st, dim3(1), dim3(std::min(1024, ((d->B + 31) / 32) * 32)), 0, k_advance,
+                           d->keys.as<const unsigned long long>(), d->B, d->tokens, d->pos0, d->record.as<int64_t>(),
+                           d->counter.as<int>(), d->capacity);
+                    return;
+                }
                 launch(st, dim3((d->B + 255) / 256), dim3(256), 0, k_positions, static_cast<const int64_t*>(d->pos0), d->B,
                        1, d->positions.as<float>(), d->last.as<int64_t>(), 1, static_cast<unsigned*>(nullptr));
-                e.io.keys = d->keys.as<unsigned long long>();
                 e.enqueue(st);
                 const dim3 grid(unsigned(d->L * d->B));
                 const int threads = std::min(256, ((d->row + 31) / 32) * 32);
@@ -2130,8 +2148,10 @@ int chroma_b200_decoder_advance(chroma_b200_decoder* d, const int64_t* tokens, c
 }
 
 int32_t chroma_b200_decoder_step_launches(const chroma_b200_decoder* d) {
-    // positions + decode program (with its L2 prefetch) + commit + advance
-    return d ? 1 + d->ex[1].planned_launches() + 2 : 0;
+    // positions + decode program (with its L2 prefetch) + commit + advance; the cluster path commits in place and
+    // derives the position itself
+    if (!d) return 0;
+    return d->ex[1].cluster_decode ? d->ex[1].planned_launches() + 1 : 1 + d->ex[1].planned_launches() + 2;
 }
 
 int chroma_b200_decoder_launch_layers(chroma_b200_decoder* d, void* stream, char* err, size_t err_len) {

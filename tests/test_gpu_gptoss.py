@@ -200,6 +200,27 @@ def test_grouped_moe_matches_per_slot_kernels(gpu: None) -> None:
     np.testing.assert_allclose(got, og.forward(*helpers.dev_oracle(), tokens), **FP32)
 
 
+def test_c2_device_generation_matches_host_steps(gpu: None) -> None:
+    """Device-resident greedy generation of one sequence (the cluster kernel commits its rows in place and derives
+    the position itself) against host steps through Decoder.append, across a ring wrap: the same token ids, and
+    after it the same committed cache."""
+    prefill, decode = dev_pair()
+    prompt = golden("c2_decode")["prompt"]
+    with chroma_b200.BatchDecoder(chroma_b200.Program(prefill), chroma_b200.Program(decode), 1) as bd:
+        first = bd.append(prompt[None, :], argmax=True)
+        ids = bd.generate(first, 260)[0]
+        cache = bd._native.read()
+    with dev_decoder() as dec:
+        want = [int(np.argmax(dec.append(prompt)))]
+        for _ in range(260):
+            want.append(int(np.argmax(dec.append([want[-1]]))))
+        dec._flush()  # commit the last host step's rows, as every device step does
+        ref = dec._native.read()
+    assert [int(first[0])] + ids.tolist() == want
+    for got_part, ref_part in zip(cache, ref):
+        np.testing.assert_array_equal(np.asarray(got_part).reshape(-1), np.asarray(ref_part).reshape(-1))
+
+
 def test_c2_batch_decoder_matches_reference(gpu: None) -> None:
     g = golden("c2_decode")
     prefill, decode = dev_pair()
