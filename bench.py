@@ -672,6 +672,12 @@ def main() -> None:
             "note": "latency-bound: the weights touched per step are 12 MB; the kernel's time is its chain of "
                     "dependent phases, not bytes",
         },
+        "roofline_step": {
+            "what": "the whole decode step (layers + vocab GEMV): the per-step bytes of the workload table",
+            "bound": "hbm", "algorithmic_bytes": layer_bytes + vocab_bytes,
+            "achieved": (layer_bytes + vocab_bytes) / (ms_per_step / 1e3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": (layer_bytes + vocab_bytes) / (ms_per_step / 1e3) / 1e9 / pk["hbm_gbs"],
+        },
         "roofline_vocab": {
             "kernel": "k_vocab (unembedding GEMV, 201088 x 128 fp32, 1 row)", "bound": "hbm", "achieved": achieved,
             "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": VOCAB_NCU_TRAFFIC,
