@@ -25,7 +25,7 @@ import ctypes
 
 import threading
 from collections.abc import Sequence
-from dataclasses import dataclass, replace
+from dataclasses import dataclass
 from types import TracebackType
 from typing import Any
 
@@ -104,6 +104,14 @@ class NativeDecoder:
         self.logit_dtype = nat.dtype_of(decode.outputs[0]["dtype"])
         self.vocab = decode.outputs[0]["shape"][1]
         self.pinned = nat.PinnedPool()  # returned logits live in page-locked memory
+        # Argument buffers and entry points of the per-token calls, made once (ndarray.ctypes conversions and
+        # symbol lookups cost more than a decode step's host work otherwise).
+        self._tok = (nat.ctypes.c_int64 * (batch * max(self.steps)))()
+        self._pos = (nat.ctypes.c_int64 * batch)()
+        self._err = nat.ctypes.create_string_buffer(1024)
+        lib = nat.lib()
+        self._step_fn = lib.chroma_b200_decoder_step
+        self._commit_fn = lib.chroma_b200_decoder_commit
 
     def step(self, which: int, tokens: np.ndarray, count: int, positions: np.ndarray,
              logits: np.ndarray | None, argmax: np.ndarray | None) -> None:
@@ -115,6 +123,24 @@ class NativeDecoder:
             positions.ctypes.data_as(i64), nat._VP(logits.ctypes.data if logits is not None else None),
             argmax.ctypes.data_as(i64) if argmax is not None else None,
         )
+
+    def _check(self, status: int) -> None:
+        if status != nat.OK:
+            raise nat._ERRORS.get(status, RuntimeError)(self._err.value.decode(errors="replace") or "decoder step")
+
+    def step_one(self, which: int, ids: np.ndarray, position: int, logits_ptr: int) -> None:
+        """Batch-1 step of `ids` (at most the program's rows) from `position`, logits to `logits_ptr`."""
+        steps = self.steps[which]
+        count = len(ids)
+        for i in range(steps):
+            self._tok[i] = int(ids[i]) if i < count else 0
+        self._pos[0] = position
+        self._check(self._step_fn(self.handle, which, self._tok, count, self._pos, nat._VP(logits_ptr), None,
+                                  self._err, len(self._err)))
+
+    def commit_one(self, which: int, count: int, first: int) -> None:
+        self._pos[0] = first
+        self._check(self._commit_fn(self.handle, which, count, self._pos, self._err, len(self._err)))
 
     def advance(self, tokens: np.ndarray | None, positions: np.ndarray | None, steps: int, stream: int = 0,
                 ids: np.ndarray | None = None) -> None:
@@ -218,8 +244,8 @@ class Decoder:
         state = self._state
         if state.staged is not None and self._native is not None:
             which, count, first = state.staged
-            self._native.commit(which, count, np.array([first], np.int64))
-            state = replace(state, staged=None)
+            self._native.commit_one(which, count, first)
+            state = CacheState(state.keys, state.values, state.slots, state.position)
             self._commit(state)
         return state
 
@@ -278,15 +304,15 @@ class Decoder:
             steps = self._native.steps[index]
             count = min(steps, remaining)
             state = self._flush()
-            chunk = np.zeros(steps, dtype=np.int64)
-            chunk[:count] = ids[offset : offset + count]
-            logits = self._native.pinned.array((1, self.vocab_size), self._logit_dtype)
-            self._native.step(index, chunk, count, np.array([state.position], np.int64), logits, None)
-            rows = (state.position + np.arange(count)) % self.context
+            logits, ptr = self._native.pinned.array_ptr((1, self.vocab_size), self._logit_dtype)
+            pos = state.position
+            self._native.step_one(index, ids[offset : offset + count], pos, ptr)
             slots = state.slots.copy()
-            slots[rows] = state.position + np.arange(count)
-            self._commit(replace(state, slots=slots, position=state.position + count,
-                                 staged=(index, count, state.position)))
+            if count == 1:
+                slots[pos % self.context] = pos
+            else:
+                slots[(pos + np.arange(count)) % self.context] = pos + np.arange(count)
+            self._commit(CacheState(state.keys, state.values, slots, pos + count, (index, count, pos)))
             offset += count
         return logits
 

@@ -173,8 +173,14 @@ class PinnedPool:
         self._lock = threading.Lock()
 
     def array(self, shape: tuple[int, ...], dtype: Any) -> np.ndarray:
+        return self.array_ptr(shape, dtype)[0]
+
+    def array_ptr(self, shape: tuple[int, ...], dtype: Any) -> tuple[np.ndarray, int]:
+        """A page-locked array and its address."""
         dtype = np.dtype(dtype)
-        count = int(np.prod(shape))
+        count = 1
+        for n in shape:
+            count *= int(n)
         nbytes = max(1, count * dtype.itemsize)
         with self._lock:
             free = self._free.get(nbytes)
@@ -183,7 +189,7 @@ class PinnedPool:
             out = _VP()
             call("chroma_b200_host_alloc", _SZ(nbytes), ctypes.byref(out))
             ptr = int(out.value)
-        return np.frombuffer(_PinnedBlock(self, ptr, nbytes), dtype, count=count).reshape(shape)
+        return np.frombuffer(_PinnedBlock(self, ptr, nbytes), dtype, count=count).reshape(shape), ptr
 
     def give_back(self, ptr: int, nbytes: int) -> None:
         with self._lock:

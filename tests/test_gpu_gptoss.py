@@ -273,16 +273,16 @@ def test_decoder_errors_keep_state_and_recover(gpu: None) -> None:
             dec.append([])
         # KeyboardInterrupt after the native call returns: nothing is committed (tests/test_decoder.py:122-131).
         state = dec._state
-        step = dec._native.step
+        step = dec._native.step_one
 
         def interrupted(*args, **kwargs):  # type: ignore[no-untyped-def]
             step(*args, **kwargs)
             raise KeyboardInterrupt
 
-        dec._native.step = interrupted
+        dec._native.step_one = interrupted
         with pytest.raises(KeyboardInterrupt):
             dec.append([4])
-        dec._native.step = step
+        dec._native.step_one = step
         assert dec._state is state and dec.position == 3
         a = dec.append([4])
     with dev_decoder() as ref:
