@@ -22,10 +22,9 @@
 //       expert per warp -> clamped SwiGLU                                        -> act[]
 //   P5  mlp2 column (1 per warp) of each selected expert + bias, weighted combine in slot order + residual -> x[]
 //
-// The routed expert rows are not known before P4, so at the start of every layer each CTA bulk-copies (TMA) the
-// rows its warps would use of EVERY expert (mlp1 rows 2*gw, 2*gw+1 and mlp2 row gw of each expert, with their
-// biases: 145 KB for the dev model) into shared memory behind P1-P3; P4 and P5 then read them at shared-memory
-// latency instead of waiting on L2 after the routing.
+// The routed expert rows are known only in P4; each warp loads its rows of the 4 selected experts into registers
+// right after the routing (bulk-copying every expert's rows into shared memory behind P1-P3 instead was measured
+// slower: 145 KB per CTA per layer crowd the SM's inbound path and delay the exchanges).
 //
 // Buffer reuse is safe without barriers: a CTA reads each exchanged buffer only before it pushes its next phase's
 // outputs, and a sender can only reach the same phase of the next layer after receiving those outputs.
@@ -52,7 +51,7 @@ constexpr int kDcRows1 = 2;              // QKV rows per warp
 constexpr int kDcMaxK = 4;               // experts per token
 constexpr int kDcMaxE = 2 * kWarps;      // gate rows (2 per warp), also <= 32 for the one-slot warp top-k
 
-enum DcBar : int { kDcRaw = 0, kDcParts, kDcX2, kDcAct, kDcXs, kDcExperts, kDcBars };
+enum DcBar : int { kDcRaw = 0, kDcParts, kDcX2, kDcAct, kDcXs, kDcBars };
 
 struct DecodeClusterArgs {
     Dims dm;
@@ -83,18 +82,14 @@ struct DecodeClusterArgs {
 
 __host__ __device__ inline int dc_up4(int v) { return (v + 3) & ~3; }
 
-// Shared-memory carve-up (in floats), identical on host and device. The host admits d = H*hd = I = kDcWarps, so
-// warp gw owns pair gw of every expert's mlp1 (rows 2gw, 2gw+1) and row gw of every expert's mlp2.
+// Shared-memory carve-up (in floats), identical on host and device.
 struct DcLayout {
     int ps, kvs;  // floats per (CTA, head) partial; per cached key row (padded: conflict-free 16-byte reads)
-    int r1c, r2c; // mlp1 / mlp2 rows per CTA and expert
-    int lw, xs, raw, qkv, cs, parts, att, x2, gl, act, prow, w1s, w2s, b1s, b2s, ks, vs, total;
-    __host__ __device__ DcLayout(const Dims& dm, int L, int kpc, bool stage) {
+    int lw, xs, raw, qkv, cs, parts, att, x2, gl, act, prow, ks, vs, total;
+    __host__ __device__ DcLayout(const Dims& dm, int L, int kpc) {
         const int r1 = (dm.H + 2 * dm.KV) * dm.hd;
         ps = dc_up4(dm.hd + 2);
         kvs = dm.KV * dm.hd + 4;
-        r1c = 2 * kWarps;
-        r2c = kWarps;
         int o = 0;
         lw = o; o += dc_up4(L * int(sizeof(LayerW<float>) / 4));
         xs = o; o += dc_up4(dm.d);
@@ -107,11 +102,6 @@ struct DcLayout {
         gl = o; o += dc_up4(dm.E);
         act = o; o += dc_up4(dm.k * dm.I);
         prow = o; o += kWarps * 32;
-        const int se = stage ? dm.E : 0;  // staged experts
-        w1s = o; o += se * r1c * dm.d;
-        w2s = o; o += se * r2c * dm.I;
-        b1s = o; o += se * r1c;
-        b2s = o; o += se * r2c;
         ks = o; o += L * kpc * kvs;
         vs = o; o += L * kpc * kvs;
         total = o;
@@ -122,8 +112,7 @@ struct DcLayout {
             case kDcParts: return unsigned(kDcC * dm.H * ps) * 4u;
             case kDcX2: return unsigned(dm.d) * 4u;
             case kDcAct: return unsigned(dm.k * dm.I) * 4u;
-            case kDcXs: return unsigned(dm.d) * 4u;
-            default: return unsigned(dm.E * (r1c * dm.d + r2c * dm.I + r1c + r2c)) * 4u;
+            default: return unsigned(dm.d) * 4u;
         }
     }
 };
@@ -295,33 +284,13 @@ __device__ __forceinline__ void dc_prefetch_layer(const LayerW<float>* lws, int 
     for (size_t o = 0; o < n; o += 32768) bulk_prefetch_l2(beg + off + o, unsigned(n - o < 32768 ? n - o : 32768));
 }
 
-// Bulk-copies layer `w`'s expert rows of this CTA (every expert's mlp1 rows [2*kWarps*rank, +2*kWarps), mlp2 rows
-// [kWarps*rank, +kWarps) and their biases) into shared memory, completing on `bar`. Issued by one warp, one expert
-// per lane; all global addresses are 16-byte aligned (256-byte aligned tensors, 16-byte multiples of rows).
-__device__ __forceinline__ void dc_stage_experts(const LayerW<float>& w, const Dims& dm, const DcLayout& lay, float* dsm,
-                                                 int rank, uint64_t* bar) {
-    const int lane = threadIdx.x & 31;
-    if (lane == 0) mbar_arrive_expect_tx(bar, lay.bytes(kDcExperts, dm));
-    __syncwarp();
-    for (int e = lane; e < dm.E; e += 32) {
-        bulk_load(dsm + lay.w1s + size_t(e) * lay.r1c * dm.d, w.w1 + (size_t(e) * 2 * dm.I + size_t(lay.r1c) * rank) * dm.d,
-                  unsigned(lay.r1c * dm.d * 4), bar);
-        bulk_load(dsm + lay.w2s + size_t(e) * lay.r2c * dm.I, w.w2 + (size_t(e) * dm.d + size_t(lay.r2c) * rank) * dm.I,
-                  unsigned(lay.r2c * dm.I * 4), bar);
-        bulk_load(dsm + lay.b1s + e * lay.r1c, w.b1 + size_t(e) * 2 * dm.I + lay.r1c * rank, unsigned(lay.r1c * 4), bar);
-        bulk_load(dsm + lay.b2s + e * lay.r2c, w.b2 + size_t(e) * dm.d + lay.r2c * rank, unsigned(lay.r2c * 4), bar);
-    }
-}
-
-// NJ = d / 128 = H*hd / 128 = I / 128 (the host admits only d = H*hd = I = 128); HD = head_dim. STAGE: the expert
-// rows of every expert are bulk-copied into shared memory at the start of each layer (false: the routed rows are
-// loaded into registers right after the routing).
-template <int NJ, int HD, bool STAGE>
+// NJ = d / 128 = H*hd / 128 = I / 128 (the host admits only d = H*hd = I = 128); HD = head_dim.
+template <int NJ, int HD>
 __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArgs a) {
     extern __shared__ __align__(128) float dsm[];
     __shared__ uint64_t bars[kDcBars];
     const Dims dm = a.dm;
-    const DcLayout lay(dm, a.L, a.kpc, STAGE);
+    const DcLayout lay(dm, a.L, a.kpc);
     const LayerW<float>* lws = reinterpret_cast<const LayerW<float>*>(dsm + lay.lw);
     float* xs = dsm + lay.xs;
     float* raw = dsm + lay.raw;
@@ -332,10 +301,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
     float* x2 = dsm + lay.x2;
     float* gl = dsm + lay.gl;
     float* act = dsm + lay.act;
-    const float* w1s = dsm + lay.w1s;
-    const float* w2s = dsm + lay.w2s;
-    const float* b1s = dsm + lay.b1s;
-    const float* b2s = dsm + lay.b2s;
     float* Ks = dsm + lay.ks;
     float* Vs = dsm + lay.vs;
 
@@ -356,21 +321,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
     auto off = [&](const float* p) { return uint32_t(p - dsm) * 4u; };
     bool live = true;  // false after a timed-out wait (thread 0)
 
-    auto wait_bar = [&](int bar, unsigned parity, bool cluster_scope) {
-        if (!live) return;
-        unsigned i = 0;
-        while (i < kMaxPolls && !(cluster_scope ? mbar_try_wait_cluster(&bars[bar], parity)
-                                                : mbar_try_wait(&bars[bar], parity)))
-            ++i;
-        if (i == kMaxPolls) {
-            atomicOr(a.err, kErrTimeout);
-            live = false;
-        }
-    };
-    // Thread 0 waits for the buffer's phase of layer l and re-arms it for layer l + 1; then the block proceeds.
+    // Thread 0 waits (bounded) for the buffer's phase of layer l and re-arms it for layer l + 1; then the block
+    // proceeds.
     auto sync = [&](int bar, int l) {
         if (threadIdx.x == 0) {
-            wait_bar(bar, unsigned(l & 1), true);
+            if (live) {
+                unsigned i = 0;
+                while (i < kMaxPolls && !mbar_try_wait_cluster(&bars[bar], unsigned(l & 1))) ++i;
+                if (i == kMaxPolls) {
+                    atomicOr(a.err, kErrTimeout);
+                    live = false;
+                }
+            }
             if (l + 1 < a.L) mbar_arrive_expect_tx(&bars[bar], lay.bytes(bar, dm));
         }
         __syncthreads();
@@ -389,14 +351,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
     if (threadIdx.x == 0) {
         for (int b = 0; b < kDcBars; ++b) mbar_init(&bars[b], 1);
         fence_barrier_init();
-        for (int b = 0; b < kDcExperts; ++b) mbar_arrive_expect_tx(&bars[b], lay.bytes(b, dm));
+        for (int b = 0; b < kDcBars; ++b) mbar_arrive_expect_tx(&bars[b], lay.bytes(b, dm));
     }
     __syncthreads();
     if (threadIdx.x == 32) {  // layers 0 and 1 into L2 (later layers: one ahead, at the start of each layer)
         dc_prefetch_layer(lws, 0, a.L, dm, rank);
         if (a.L > 1) dc_prefetch_layer(lws, 1, a.L, dm, rank);
     }
-    if (STAGE && warp == kWarps - 1) dc_stage_experts(a.layers[0], dm, lay, dsm, rank, &bars[kDcExperts]);
     pdl_wait();
     pdl_trigger();
 
@@ -442,8 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
     for (int l = 0; l < a.L; ++l) {
         const LayerW<float>& w = lws[l];
         if (l > 0) {
-            sync(kDcXs, l - 1);  // also: every warp finished reading the previous layer's staged expert rows
-            if (STAGE && warp == kWarps - 1) dc_stage_experts(w, dm, lay, dsm, rank, &bars[kDcExperts]);
+            sync(kDcXs, l - 1);
             if (threadIdx.x == 32 && l + 1 < a.L) dc_prefetch_layer(lws, l + 1, a.L, dm, rank);
         }
         // ---- P1: norm, QKV rows, bias -> raw[] of every CTA
@@ -598,7 +558,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
             }
         }
         if (l + 1 < a.L) dc_load_static_mlp<NJ>(st, lws[l + 1], dm);
-        if (STAGE && threadIdx.x == 0) wait_bar(kDcExperts, unsigned(l & 1), false);  // this layer's staged rows
         __syncthreads();
         int sidx[kDcMaxK];
         float sw[kDcMaxK];
@@ -617,21 +576,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
         for (int u = 0; u < kDcMaxK; ++u) {
             if (u < dm.k) {
                 const int e = ex[u];
-                if (STAGE) {
-                    const float* W1 = w1s + (size_t(e) * lay.r1c + 2 * warp) * d;
-                    dc_read<NJ>(wg[u], W1);
-                    dc_read<NJ>(wl[u], W1 + d);
-                    bg[u] = b1s[e * lay.r1c + 2 * warp];
-                    bl[u] = b1s[e * lay.r1c + 2 * warp + 1];
-                } else {
-                    const float* W1 = w.w1 + (size_t(e) * 2 * I + 2 * gw) * d;
-                    dc_load<NJ>(wg[u], W1);
-                    dc_load<NJ>(wl[u], W1 + d);
-                    bg[u] = w.b1[size_t(e) * 2 * I + 2 * gw];
-                    bl[u] = w.b1[size_t(e) * 2 * I + 2 * gw + 1];
-                    dc_load<NJ>(w2r[u], w.w2 + (size_t(e) * d + gw) * I);
-                    bd[u] = w.b2[size_t(e) * d + gw];
-                }
+                const float* W1 = w.w1 + (size_t(e) * 2 * I + 2 * gw) * d;
+                dc_load<NJ>(wg[u], W1);
+                dc_load<NJ>(wl[u], W1 + d);
+                bg[u] = w.b1[size_t(e) * 2 * I + 2 * gw];
+                bl[u] = w.b1[size_t(e) * 2 * I + 2 * gw + 1];
+                dc_load<NJ>(w2r[u], w.w2 + (size_t(e) * d + gw) * I);
+                bd[u] = w.b2[size_t(e) * d + gw];
             }
         }
 #pragma unroll
@@ -656,12 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
 #pragma unroll
             for (int u = 0; u < kDcMaxK; ++u) {
                 if (u < dm.k) {
-                    const int e = ex[u];
                     float av[NJ][4];
-                    if (STAGE) {
-                        dc_read<NJ>(w2r[u], w2s + (size_t(e) * lay.r2c + warp) * I);
-                        bd[u] = b2s[e * lay.r2c + warp];
-                    }
                     dc_read<NJ>(av, act + u * I);
                     comb = __fadd_rn(comb, __fmul_rn(__fadd_rn(dc_dot<NJ>(w2r[u], av), bd[u]), sw[u]));
                 }

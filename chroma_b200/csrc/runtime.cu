@@ -1119,18 +1119,14 @@ struct GptExec {
         if (mask_mode != kMaskSlots || B * n != 1) return;
         if (d.d != 128 || d.H * d.hd != 128 || d.I != 128) return;
         if ((d.H + 2 * d.KV) * d.hd > kDcRows1 * kDcWarps || d.k > kDcMaxK) return;
-        if (reinterpret_cast<uintptr_t>(m->weights->ptr) % 16 != 0) return;  // bulk copies of the expert rows
+        if (reinterpret_cast<uintptr_t>(m->weights->ptr) % 16 != 0) return;  // bulk L2 prefetch of each layer
         if (d.E > kDcMaxE || d.E < d.k || d.hd != 16) return;
         const int kpc = (ctx + 1 + kDcC - 1) / kDcC;
         if (kpc > 32) return;
-        // Staging every expert's rows of the CTA in shared memory (bulk copies behind P1-P3) against loading the
-        // routed rows into registers after the routing: CHROMA_B200_DECODE_STAGE=1 selects the former.
-        const char* stage_env = std::getenv("CHROMA_B200_DECODE_STAGE");
-        const bool stage = stage_env && stage_env[0] == '1';
-        const DcLayout lay(d, L, kpc, stage);
+        const DcLayout lay(d, L, kpc);
         const size_t smem = size_t(lay.total) * 4;
         if (smem + 1024 > 227 * 1024) return;
-        dc_kernel = stage ? k_decode_cluster<1, 16, true> : k_decode_cluster<1, 16, false>;
+        dc_kernel = k_decode_cluster<1, 16>;
         ClusterLaunch cl(nullptr, dim3(kDcC), dim3(kThreads), smem, kDcC, dc_kernel);
         int clusters = 0;
         if (cudaOccupancyMaxActiveClusters(&clusters, dc_kernel, &cl.cfg) != cudaSuccess || clusters < 1) {
