@@ -12,7 +12,7 @@
 //
 //   P1  RMSNorm (per warp) -> QKV rows (2 per warp) -> +bias                     -> raw[]
 //       RoPE on the gathered row (per CTA, cos/sin of the step's position computed once); CTA 0 stages the new
-//       K/V rows for the commit kernel
+//       K/V rows for the commit kernel (device-resident steps: writes them into the ring slot as well)
 //   P2  attention over this CTA's ceil((ctx+1)/kDcC) keys (the K/V slices of every layer are copied into shared
 //       memory by cp.async at the start; the CTA holding the new token's key appends its row after RoPE), one warp
 //       per query head: (max, sum, P.V) partials -> parts[]
@@ -39,7 +39,6 @@
 // the kernel runs to its end, where one cluster barrier keeps every CTA resident until no store can target it.
 #pragma once
 
-#include "flash.cuh"
 #include "gptoss.cuh"
 #include "tcgen05.cuh"
 
