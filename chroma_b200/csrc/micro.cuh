@@ -76,21 +76,18 @@ __global__ void __launch_bounds__(512) k_micro(const __nv_bfloat16* __restrict__
         __nv_bfloat162* po = reinterpret_cast<__nv_bfloat162*>(&ov);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
+            // Two elements at a time. A product of two bf16 values is exact in fp32, so the packed bf16
+            // multiplies (one rounding of the exact product) give the bits of "fp32 multiply, round to bf16";
+            // 1/v through the correctly rounded reciprocal equals the IEEE division 1.0f / v.
             const float2 fx = __bfloat1622float2(px[i]);
-            const float2 fg = __bfloat1622float2(pg[i]);
-            const float2 fu = __bfloat1622float2(pu[i]);
-            float r[2];
-            const float xs[2] = {fx.x, fx.y}, gs[2] = {fg.x, fg.y}, us[2] = {fu.x, fu.y};
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const float y = bf16_round(__fmul_rn(__fmul_rn(xs[h], inv), wv[2 * i + h]));
-                const float z = bf16_round(__fmul_rn(y, gs[h]));
-                const float sg = bf16_round(1.0f / (1.0f + expf(-z)));
-                const float a = bf16_round(__fmul_rn(z, sg));
-                const float b = bf16_round(__fmul_rn(a, us[h]));
-                r[h] = __fadd_rn(b, xs[h]);
-            }
-            po[i] = __floats2bfloat162_rn(r[0], r[1]);
+            const __nv_bfloat162 y = __floats2bfloat162_rn(__fmul_rn(__fmul_rn(fx.x, inv), wv[2 * i]),
+                                                           __fmul_rn(__fmul_rn(fx.y, inv), wv[2 * i + 1]));
+            const __nv_bfloat162 z = __hmul2(y, pg[i]);
+            const float2 fz = __bfloat1622float2(z);
+            const __nv_bfloat162 sg = __floats2bfloat162_rn(__frcp_rn(__fadd_rn(1.0f, expf(-fz.x))),
+                                                            __frcp_rn(__fadd_rn(1.0f, expf(-fz.y))));
+            const float2 fb = __bfloat1622float2(__hmul2(__hmul2(z, sg), pu[i]));
+            po[i] = __floats2bfloat162_rn(__fadd_rn(fb.x, fx.x), __fadd_rn(fb.y, fx.y));
         }
         __stcs(reinterpret_cast<uint4*>(out + base + col), ov);
     }
