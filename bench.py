@@ -47,7 +47,7 @@ CONTEXT = 256
 PREFILL = 8
 # DRAM bytes of one k_vocab launch of this workload, from an ncu capture (102.98 MB read + 3.87 MB written).
 VOCAB_NCU_TRAFFIC = 106_851_584
-CLUSTER_NCU_TRAFFIC = 30_900_789  # profiles/k_decode_cluster_dev_decode.md
+CLUSTER_NCU_TRAFFIC = 30_900_789  # one k_decode_cluster launch of this workload, caches flushed (ncu)
 
 
 def parse() -> argparse.Namespace:
@@ -66,7 +66,53 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--c5-only", action="store_true", help="run only the GPT-OSS-120B-shaped decode (needs >= 2 GPUs)")
     ap.add_argument("--c5-layers", type=int, default=0, help="layers of the C5 model (0: all 36)")
     ap.add_argument("--c5-sequences", type=int, default=256, help="sequences of the C5 decode over all GPUs")
+    ap.add_argument("--gemm", nargs="*", choices=sorted(GEMM_SHAPES), default=None,
+                    help="only the tensor-core GEMM at GPT-OSS-20B shapes (all shapes when none is named): one JSON "
+                         "line per shape, CUDA events, L2 flushed before each launch, median of --steps launches")
     return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------------------------------------
+# The tensor-core GEMM (chroma_b200_gemm_bf16) alone at the C4 shapes: (M, N, K, epilogue, expert groups).
+GEMM_SHAPES = {
+    "qkv": (8192, 5120, 2880, 0, 1),
+    "out": (8192, 2880, 4096, 0, 1),
+    "moe_up": (32768, 5760, 2880, 2, 32),
+    "moe_down": (32768, 2880, 2880, 3, 32),
+}
+
+
+def bench_gemm(name: str, reps: int, warmup: int) -> dict:
+    import torch
+
+    from chroma_b200._src import native as nat
+
+    m, n, k, epi, groups = GEMM_SHAPES[name]
+    stream = torch.cuda.current_stream()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    b = (torch.randn(groups * n, k, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    bias = torch.zeros(groups, n, dtype=torch.bfloat16, device="cuda")
+    c = torch.empty(m, n // 2 if epi == 2 else n, dtype=torch.bfloat16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    offsets = torch.arange(groups + 1, dtype=torch.int32, device="cuda") * (m // groups) if groups > 1 else None
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    ptr = lambda t: nat._VP(t.data_ptr()) if t is not None else None  # noqa: E731
+    times = []
+    for i in range(warmup + reps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        nat.call("chroma_b200_gemm_bf16", ptr(a), ptr(b), ptr(bias), None, ptr(c), m, n, k, epi, 1.702, 7.0, groups,
+                 ptr(offsets), None, ptr(err), nat._VP(stream.cuda_stream))
+        e1.record(stream)
+        if i >= warmup:
+            times.append((e0, e1))
+    torch.cuda.synchronize()
+    if int(err.item()):
+        raise RuntimeError(f"GEMM error word {int(err.item())}")
+    ms = statistics.median(x.elapsed_time(y) for x, y in times)
+    return {"gemm": name, "m": m, "n": n, "k": k, "groups": groups, "ms": ms, "tflops": 2.0 * m * n * k / ms / 1e9}
 
 
 # ---------------------------------------------------------------------------------------------------------
@@ -422,6 +468,14 @@ def main() -> None:
     # streams) and the CUDA events below bracket exactly the queued work.
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
+    if args.gemm is not None:
+        for name in args.gemm or sorted(GEMM_SHAPES):
+            res = bench_gemm(name, max(1, args.steps), max(1, args.warmup))
+            if rank == 0:
+                print(json.dumps(res), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
     if args.c5_only:
         c5 = bench_c5(args, max_over_ranks, barrier, rank, world)
         if rank == 0:
@@ -665,7 +719,7 @@ def main() -> None:
             "bound": "hbm", "achieved": layer_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
             "frac": layer_gbs / pk["hbm_gbs"], "traffic": CLUSTER_NCU_TRAFFIC,
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_decode_cluster launch of this "
-                              "workload, caches flushed (profiles/k_decode_cluster_dev_decode.md)",
+                              "workload, caches flushed",
             "algorithmic_bytes": layer_bytes, "launch_us": layer_t * 1e6,
             "peak_source": f"{pk['source']} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
             "timing": f"launched alone after an L2 flush, CUDA events, mean of {reps}",
@@ -682,7 +736,7 @@ def main() -> None:
             "kernel": "k_vocab (unembedding GEMV, 201088 x 128 fp32, 1 row)", "bound": "hbm", "achieved": achieved,
             "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": VOCAB_NCU_TRAFFIC,
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_vocab<float, 1> launch of "
-                              "this workload (profiles/k_vocab_dev_decode_step.md)",
+                              "this workload",
             "algorithmic_bytes": vocab_bytes, "launch_us": vocab_t * 1e6,
             "peak_source": f"{pk['source']} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
             "timing": f"launched alone after an L2 flush, CUDA events, mean of {reps} (inside a step the vocab "

@@ -2,7 +2,7 @@
 // of kDcC CTAs on kDcC SMs exchanging activations through distributed shared memory. It replaces the per-layer
 // chain k_attn_in -> k_attention -> k_out -> k_moe_up -> k_moe_down (5 dependent launches per layer, each a few
 // microseconds of launch and drain latency around well under a microsecond of work) for the batch-1 decode program
-// (chroma/_src/decoding/cached.py:22-60 per step; the block of gpt_oss.py:189-265).
+// (chroma/models/cached.py:16-51 per step; the block of gpt_oss.py:189-265).
 //
 // Every CTA keeps its own copy of the small activations (residual x, x2, the QKV row, the attention partials, the
 // expert activations) in shared memory. A phase's outputs are split over the cluster's kDcC*kWarps warps and each

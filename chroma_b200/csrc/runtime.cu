@@ -376,11 +376,12 @@ static bool vocab_tma_ok(const Dims& dm, size_t es) {
 
 template <typename T>
 static void launch_vocab(cudaStream_t s, const Dims& dm, int sms, const float* x, int rows, const T* W, T* logits,
-                         unsigned long long* keys, unsigned* err) {
+                         unsigned long long* keys, unsigned* err, bool allow_tma = true) {
     // The TMA ring measured slower than the register-fragment kernel for the dev vocab (26.7 vs 21.6 us per launch,
-    // same 103 MB of DRAM reads), so it is only selected when CHROMA_B200_VOCAB_TMA is set.
+    // same 103 MB of DRAM reads), so it is only selected when CHROMA_B200_VOCAB_TMA is set. Callers that never read
+    // the program's error word (where the TMA ring reports a timed-out wait) pass allow_tma = false.
     static const bool use_tma = std::getenv("CHROMA_B200_VOCAB_TMA") != nullptr;
-    if (use_tma && vocab_tma_ok(dm, sizeof(T)) && rows <= kVocabRows) {
+    if (allow_tma && use_tma && vocab_tma_ok(dm, sizeof(T)) && rows <= kVocabRows) {
         if (rows == 1) launch_vocab_tma<T, 1>(s, dm, sms, x, rows, W, logits, keys, err);
         else if (rows <= 2) launch_vocab_tma<T, 2>(s, dm, sms, x, rows, W, logits, keys, err);
         else if (rows <= 4) launch_vocab_tma<T, 4>(s, dm, sms, x, rows, W, logits, keys, err);
@@ -1878,6 +1879,9 @@ int chroma_b200_vocab_argmax_static(const chroma_b200_program* p, const float* x
         if (!p || !x || !ids) throw ValueError("null argument");
         const auto& d = p->model.desc;
         if (d.kind == CHROMA_B200_MICRO) throw ValueError("not a GPT-OSS program");
+        // A vocab-sharded expert-parallel program holds only its rank's unembedding rows.
+        if (p->model.ep && p->model.ep->vrows_max > 0)
+            throw ValueError("vocab-sharded program: it holds only its rank's unembedding rows");
         if (rows < 1 || rows > kStaticArgmaxRows)
             throw ValueError("rows must be in [1, " + std::to_string(kStaticArgmaxRows) +
                              "]: the static argmax scratch holds that many rows");
@@ -1889,10 +1893,10 @@ int chroma_b200_vocab_argmax_static(const chroma_b200_program* p, const float* x
         if (d.storage == CHROMA_B200_BF16)
             launch_vocab<__nv_bfloat16>(s, dm, p->exec.sms, x, int(rows),
                                         reinterpret_cast<const __nv_bfloat16*>(p->model.at(2)),
-                                        static_cast<__nv_bfloat16*>(logits), keys, p->err.as<unsigned>());
+                                        static_cast<__nv_bfloat16*>(logits), keys, p->err.as<unsigned>(), false);
         else
             launch_vocab<float>(s, dm, p->exec.sms, x, int(rows), reinterpret_cast<const float*>(p->model.at(2)),
-                                static_cast<float*>(logits), keys, p->err.as<unsigned>());
+                                static_cast<float*>(logits), keys, p->err.as<unsigned>(), false);
         launch(s, dim3(1), dim3(256), 0, k_keys_to_ids, keys, int(rows), ids);
     });
 }

@@ -108,8 +108,9 @@ int chroma_b200_routes(chroma_b200_program* program, int32_t* out, int64_t count
  * storage type, or NULL) are caller-owned device buffers; the program supplies the unembedding weights it already
  * holds. Scratch is a static device array of 256 rows (2 KiB) held by every GPU that loads the library: rows > 256
  * is a CHROMA_B200_VALUE error. The first call on a device looks up that array's device address, so make it before
- * any stream capture. Calls share the array: calls that overlap on the GPU race. Queued on `stream` (a cudaStream_t;
- * 0 is the legacy default stream), not synchronised. */
+ * any stream capture. Calls share the array: calls that overlap on the GPU race. A vocab-sharded expert-parallel
+ * program (it holds only its rank's unembedding rows) is a CHROMA_B200_VALUE error. Queued on `stream` (a
+ * cudaStream_t; 0 is the legacy default stream), not synchronised. */
 int chroma_b200_vocab_argmax_static(const chroma_b200_program* program, const float* x, int32_t rows, void* logits,
                                     int64_t* ids, void* stream, char* err, size_t err_len);
 /* GEMM epilogues of chroma_b200_gemm_bf16. */
@@ -179,7 +180,7 @@ void chroma_b200_decoder_destroy(chroma_b200_decoder* decoder);
 
 /* Page-locked host memory for results the caller keeps (the decoders' returned logits): device-to-host copies
  * into it run at full link speed without a driver staging copy. The reference returns fresh numpy arrays
- * (chroma/_src/decoding/decoder.py:115-130); the Python layer returns numpy arrays over these blocks. */
+ * (chroma/_src/decoder.py:130-138); the Python layer returns numpy arrays over these blocks. */
 int chroma_b200_host_alloc(size_t bytes, void** out, char* err, size_t err_len);
 void chroma_b200_host_free(void* p);
 

@@ -27,7 +27,8 @@ import re
 import sys
 from pathlib import Path
 
-REFERENCE = Path(os.environ.get("CHROMA_REFERENCE", "/root/reference"))
+# The reference checkout: $CHROMA_REFERENCE, else a directory named ``reference`` beside this repository.
+REFERENCE = Path(os.environ.get("CHROMA_REFERENCE") or Path(__file__).resolve().parents[2] / "reference")
 _PACKAGES = ("chroma", "scripts")
 _EXCEPT = re.compile(r"^(\s*)except ([A-Za-z_][\w.]*(?:\s*,\s*[A-Za-z_][\w.]*)+):", re.M)
 
