@@ -100,15 +100,19 @@ def softmax(x: np.ndarray, axis: int = -1) -> np.ndarray:
 
 
 def topk(x: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
-    """Largest-k along the last axis, sorted descending; NaN ranks highest, ties keep the lowest index."""
-    key = np.where(np.isnan(x), np.inf, x).astype(np.float64)
-    # lexsort sorts by the last key first: primary descending value, secondary ascending index.
+    """Largest-k along the last axis, sorted descending; NaN ranks highest (above +inf), ties keep the lowest index
+    (the comparator of chroma/_src/codegen/cpu/kernels.h:158-164 with the GPU backend's lowest-index tie order,
+    chroma/_src/codegen/gpu.py:300-311)."""
+    nan = np.isnan(x)
+    key = np.where(nan, 0.0, x).astype(np.float64)
+    # lexsort sorts by the last key first: NaN before numbers, then descending value, then ascending index.
     idx = np.arange(x.shape[-1])
     order = np.empty(x.shape[:-1] + (k,), dtype=np.int64)
     flat_x = key.reshape(-1, x.shape[-1])
+    flat_n = nan.reshape(-1, x.shape[-1])
     flat_o = order.reshape(-1, k)
     for row in range(flat_x.shape[0]):
-        flat_o[row] = np.lexsort((idx, -flat_x[row]))[:k]
+        flat_o[row] = np.lexsort((idx, -flat_x[row], ~flat_n[row]))[:k]
     values = np.take_along_axis(x, order, axis=-1)
     return values, order
 

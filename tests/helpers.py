@@ -130,3 +130,55 @@ def assert_greedy_token(got: np.ndarray, want: np.ndarray, rel: float = 1e-2) ->
         a, b = int(np.argmax(g)), int(np.argmax(w))
         if a != b:
             assert w[a] >= w[b] - rel * np.max(np.abs(w)), f"greedy token {a} (ref {w[a]:.5g}) vs {b} (ref {w[b]:.5g})"
+
+
+def assert_top_and_rowsum(got: np.ndarray, top_idx: np.ndarray, top_val: np.ndarray, rowsum: np.ndarray, *,
+                          rtol: float = 1e-4, atol: float = 1e-5) -> None:
+    """Full-row checks against a golden summary of the reference's logits (tests/golden/make_golden.py ``summary``):
+    the reference's 16 largest logits (``top_idx`` / ``top_val``) within the fp32 bar; our 16 largest in the same
+    order, except where two neighbours are within that bar of each other (a near-tie swap); and the float64 row sum
+    of all V logits within the bar summed over the row (rtol * sum |logit| + atol * V)."""
+    got = np.asarray(got, np.float32).reshape(-1, np.asarray(got).shape[-1])
+    top_idx, top_val = np.asarray(top_idx).reshape(got.shape[0], -1), np.asarray(top_val).reshape(got.shape[0], -1)
+    rowsum = np.asarray(rowsum).reshape(-1)
+    for r, row in enumerate(got):
+        np.testing.assert_allclose(row[top_idx[r]], top_val[r], rtol=rtol, atol=atol)
+        mine = np.argsort(-row, kind="stable")[: top_idx.shape[1]]
+        for j in np.nonzero(mine != top_idx[r])[0]:
+            a, b = float(row[mine[j]]), float(row[top_idx[r][j]])
+            assert abs(a - b) <= atol + rtol * abs(float(top_val[r][j])), (r, j, int(mine[j]), int(top_idx[r][j]))
+        total = float(row.astype(np.float64).sum())
+        bound = rtol * float(np.abs(row).astype(np.float64).sum()) + atol * row.size
+        assert abs(total - float(rowsum[r])) <= bound, (r, total, float(rowsum[r]), bound)
+
+
+def route_agreement(ours: np.ndarray, ref: np.ndarray, gates: np.ndarray, k: int, rel: float = 1 / 64) -> dict:
+    """Layer-by-layer routing comparison of [layers, tokens, k] routes against the oracle's, with the oracle's gate
+    logits [layers, tokens, E]. A token is compared in a layer only while every earlier layer routed it identically
+    (after a different choice its hidden state legitimately differs from the oracle's). Every compared (layer,
+    token) whose oracle margin between the k-th and (k+1)-th gate logit exceeds ``rel`` (relative) must be routed
+    identically; the others may differ among the experts near the boundary. Returns the counts and the margins at
+    the mismatches for reporting."""
+    layers, tokens = ours.shape[0], ours.shape[1]
+    alive = np.ones(tokens, bool)
+    compared = mismatched = 0
+    margins: list[float] = []
+    for layer in range(layers):
+        g = np.sort(np.asarray(gates[layer], np.float64), axis=-1)[:, ::-1]
+        margin = (g[:, k - 1] - g[:, k]) / np.maximum(np.maximum(np.abs(g[:, k - 1]), np.abs(g[:, k])), 1e-6)
+        same = np.array([set(a.tolist()) == set(b.tolist()) for a, b in zip(ours[layer], ref[layer])])
+        for t in np.nonzero(alive)[0]:
+            compared += 1
+            if same[t]:
+                # The same experts: any difference in their order must be between near-equal gate logits.
+                gt = np.asarray(gates[layer][t], np.float64)
+                for a, b in zip(ours[layer][t], ref[layer][t]):
+                    assert abs(gt[a] - gt[b]) <= rel * max(abs(gt[a]), abs(gt[b]), 1e-6), (layer, t, a, b)
+                continue
+            mismatched += 1
+            margins.append(float(margin[t]))
+            assert margin[t] <= rel, f"layer {layer} token {t}: routes differ with oracle margin {margin[t]:.3g}"
+            ok = routes_match_near(ours[layer][t : t + 1], ref[layer][t : t + 1], gates[layer][t : t + 1], k, rel)
+            assert ok.all(), f"layer {layer} token {t}: routes differ away from the top-k boundary"
+        alive &= same
+    return {"compared": compared, "mismatched": mismatched, "margins": margins, "identical_tokens": alive}

@@ -1,7 +1,9 @@
 """GPU parity of the GPT-OSS kernels against the reference's golden vectors and the oracle.
 
 Bars (from the backend's contract): argmax token ids and routing indices identical; fp32 logits within 1e-4
-relative (atol 1e-5 for near-zero logits); bf16 logits within 2e-2 relative (atol 1e-2).
+relative (atol 1e-5 for near-zero logits); bf16 logits within 2e-2 relative (atol 1e-2). Against the golden
+summaries of the reference's full logits rows: a fixed sample of 4,096 columns, the 16 largest logits (index and
+value) and the float64 row sum (helpers.assert_top_and_rowsum).
 """
 
 from __future__ import annotations
@@ -56,6 +58,7 @@ def test_c1_forward_matches_reference(gpu: None) -> None:
         logits = program(tokens)
         np.testing.assert_array_equal(np.argmax(logits, -1), g["argmax"][s])
         np.testing.assert_allclose(logits[:, g["sample_cols"]], g["sample"][s], **FP32)
+        helpers.assert_top_and_rowsum(logits, g["top_idx"][s], g["top_val"][s], g["rowsum"][s], **FP32)
         routes = program.native.routes()
         np.testing.assert_array_equal(routes, g["routes"][s])
 
@@ -111,6 +114,7 @@ def test_c2_decoder_matches_reference(gpu: None) -> None:
         assert out.shape == (1, models.dev.vocab_size)
         assert int(np.argmax(out)) == int(g["step_argmax"][i][0])
         np.testing.assert_allclose(out[:, g["sample_cols"]], g["step_sample"][i], **FP32)
+        helpers.assert_top_and_rowsum(out, g["step_top_idx"][i], g["step_top_val"][i], g["step_rowsum"][i], **FP32)
 
 
 def test_c2_decoder_ring_wrap(gpu: None) -> None:
@@ -125,8 +129,9 @@ def test_c2_decoder_ring_wrap(gpu: None) -> None:
             if i >= len(tokens) - 8 - 4:
                 tail.append(out)
     np.testing.assert_array_equal(ids, g["long_argmax"])
-    for out, want in zip(tail, g["tail_sample"]):
+    for i, (out, want) in enumerate(zip(tail, g["tail_sample"])):
         np.testing.assert_allclose(out[:, g["sample_cols"]], want, **FP32)
+        helpers.assert_top_and_rowsum(out, g["tail_top_idx"][i], g["tail_top_val"][i], g["tail_rowsum"][i], **FP32)
 
 
 def _decode_sequence(prefill: str, decode: str, tokens: np.ndarray) -> tuple[np.ndarray, int]:
@@ -233,6 +238,8 @@ def test_c2_batch_decoder_matches_reference(gpu: None) -> None:
         np.testing.assert_array_equal(np.argmax(out, -1), g["batch_argmax"][:, step, 0])
         np.testing.assert_array_equal(am, g["batch_argmax"][:, step, 0])
         np.testing.assert_allclose(out[:, g["sample_cols"]], g["batch_sample"][:, step, 0], **FP32)
+        helpers.assert_top_and_rowsum(out, g["batch_top_idx"][:, step, 0], g["batch_top_val"][:, step, 0],
+                                      g["batch_rowsum"][:, step, 0], **FP32)
 
 
 def test_c2_program_with_host_masks_matches_device_path(gpu: None) -> None:
