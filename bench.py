@@ -45,6 +45,7 @@ REF_CPU_GFLOPS = 22.5 / 10.59
 A100_FWD8_MS = 4.25  # reference, docs/benchmarks.md:23
 CONTEXT = 256
 PREFILL = 8
+DATA = "synthetic (seeded dev-model weights as scripts/export.py:16-29, seeded token ids)"
 # DRAM bytes of one k_vocab launch of this workload, from an ncu capture (102.98 MB read + 3.87 MB written).
 VOCAB_NCU_TRAFFIC = 106_851_584
 CLUSTER_NCU_TRAFFIC = 30_900_789  # one k_decode_cluster launch of this workload, caches flushed (ncu)
@@ -66,6 +67,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--c5-only", action="store_true", help="run only the GPT-OSS-120B-shaped decode (needs >= 2 GPUs)")
     ap.add_argument("--c5-layers", type=int, default=0, help="layers of the C5 model (0: all 36)")
     ap.add_argument("--c5-sequences", type=int, default=256, help="sequences of the C5 decode over all GPUs")
+    ap.add_argument("--skip-parity", action="store_true", help="skip the expert-parallel bit-identity check")
     ap.add_argument("--gemm", nargs="*", choices=sorted(GEMM_SHAPES), default=None,
                     help="only the tensor-core GEMM at GPT-OSS-20B shapes (all shapes when none is named): one JSON "
                          "line per shape, CUDA events, L2 flushed before each launch, median of --steps launches")
@@ -166,22 +168,23 @@ def peaks() -> dict:
 
 # ---------------------------------------------------------------------------------------------------------
 def cpu_reference_decode(seconds: float, steps: int | None = None) -> dict:
-    """The reference's compiled CPU decode step (oracle/_ref/c2_*), driven by the reference Decoder's host algorithm
-    (per-step masks, full-cache inputs, cache copy on commit). Falls back to the NumPy oracle port if the reference
-    programs were not built."""
-    from chroma_b200._src.decoder import Decoder
-
+    """The reference's compiled CPU decode step (oracle/_ref/c2_*) driven by the reference's own ``chroma.Decoder``
+    and ``chroma.Program`` (the stock host path: per-step masks, full-cache inputs, cache copy on commit), from the
+    patched copy of its package staged under oracle/_ref. Falls back to the NumPy oracle port if the reference
+    programs or package were not built."""
     tokens = np.random.default_rng(7).integers(0, 201088, 4096)
     try:
-        from oracle.refprogram import RefProgram, available
+        from oracle import refimport
+        from oracle.refprogram import ROOT as REF_ROOT, available
 
         if not (available("c2_prefill8") and available("c2_decode")):
             raise FileNotFoundError("oracle/_ref/c2_* not built")
-        dec = Decoder(RefProgram("c2_prefill8"), RefProgram("c2_decode"))
+        chroma = refimport.runtime()
+        dec = chroma.Decoder(chroma.Program(REF_ROOT / "c2_prefill8"), chroma.Program(REF_ROOT / "c2_decode"))
         kind = "reference"
         step = lambda t: dec.append([int(t)])  # noqa: E731
         dec.append(tokens[:PREFILL])
-    except (FileNotFoundError, ImportError, OSError) as exc:
+    except (FileNotFoundError, ModuleNotFoundError, ImportError, OSError) as exc:
         from oracle import gpt_oss as og
         from tests.helpers import dev_oracle
 
@@ -200,8 +203,18 @@ def cpu_reference_decode(seconds: float, steps: int | None = None) -> dict:
             break
     return {"value": n / elapsed, "unit": "tokens/s", "cores": 1, "kind": kind.split(" ")[0],
             "ms_per_step": 1e3 * elapsed / n,
-            "sample": f"{n} cached decode steps (batch 1, 256-token cache, after an 8-token prefill), "
-                      f"single-threaded generated C++ (blas=False)" + ("" if kind == "reference" else f"; {kind}")}
+            "sample": f"{n} cached decode steps (batch 1, 256-token cache, after an 8-token prefill) through the "
+                      f"reference's chroma.Decoder over its compiled single-threaded C++ programs (blas=False)"
+                      + ("" if kind == "reference" else f"; {kind}")}
+
+
+def c2_config(world: int) -> dict:
+    """The headline workload's ``config``, printed identically by both arms."""
+    return {"workload": "C2: dev GPT-OSS (12 layers, d=128, 59.1M params) KV-cached greedy decode step, 256-token "
+                        "fp32 cache, 8-token prefill first, batch 1 per sequence",
+            "model": "gpt-oss dev", "global_batch": world, "seq_len": CONTEXT,
+            "parallelism": f"replicas x{world} (the dev model does not shard)",
+            "l2": "flushed before every timed step (256 MiB write, then 256 MiB read)"}
 
 
 def reference_arm(args: argparse.Namespace) -> None:
@@ -214,9 +227,9 @@ def reference_arm(args: argparse.Namespace) -> None:
         "impl": "reference", "metric": "dev decode tokens/s (KV cache 256, batch 1)", "value": res["value"],
         "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (seeded dev-model weights, seeded token ids)",
-        "config": {"workload": "C2 dev KV-cached decode, 256-token fp32 cache, batch 1", "model": "gpt-oss dev",
-                   "global_batch": 1, "seq_len": CONTEXT, "parallelism": "none (host CPU, 1 thread)"},
+        "dtype": "f32", "data": DATA,
+        "config": c2_config(args.gpus),
+        "execution": "rank 0 only: the reference's compiled CPU decode step on 1 host thread",
         "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -257,12 +270,13 @@ def decode_flops_per_token(cfg, ctx: int) -> float:  # type: ignore[no-untyped-d
 
 def bench_c4(args: argparse.Namespace, rng: np.random.Generator, max_over_ranks, barrier, rank: int = 0,
              world: int = 1) -> dict:  # type: ignore[no-untyped-def]
-    """GPT-OSS-20B-shaped prefill of 4 x 2048 tokens per GPU (config C4): bf16 weights N(0, 0.02) generated in
-    device memory, the batched prefill program through BatchDecoder (tokens in from the host, greedy ids out).
+    """GPT-OSS-20B-shaped prefill of 2048-token sequences (config C4): bf16 weights N(0, 0.02) generated in device
+    memory, the batched prefill program through BatchDecoder (tokens in from the host, greedy ids out).
 
     With several ranks (torchrun) the 32 experts are split over the GPUs (expert parallel, csrc/ep.cuh): each rank
-    holds E / world experts plus the replicated attention, router and embeddings, prefills its own 4 x 2048 tokens
-    (weak scaling), and exchanges routed rows with the other ranks every layer over NVLink peer memory."""
+    holds E / world experts plus the replicated attention, router and embeddings and exchanges routed rows with the
+    other ranks every layer over NVLink peer memory. Two measurements: ``weak`` (4 x 2048 tokens per GPU) and, where
+    4 sequences split evenly, ``strong`` (BASELINE's 4 x 2048 tokens in total, 4 / world sequences per GPU)."""
     import torch
 
     import chroma_b200
@@ -277,14 +291,7 @@ def bench_c4(args: argparse.Namespace, rng: np.random.Generator, max_over_ranks,
     plan_p, regions = synthetic_gptoss(cfg, steps=n, context=n, ep_world=world)
     plan_d, _ = synthetic_gptoss(cfg, steps=1, context=n, ep_world=world)
     wbuf = torch.empty(plan_p["desc"]["weight_bytes"], dtype=torch.uint8, device="cuda")
-    shared_gen = torch.Generator(device="cuda").manual_seed(20)  # replicated weights: the same on every rank
-    expert_gen = torch.Generator(device="cuda").manual_seed(1000 + rank)  # this rank's experts
-    for name, off, numel, is_norm in regions:
-        if is_norm:
-            wbuf[off : off + numel * 4].view(torch.float32).fill_(1.0)
-        else:
-            gen = expert_gen if ".mlp.mlp" in name else shared_gen
-            wbuf[off : off + numel * 2].view(torch.bfloat16).normal_(0.0, 0.02, generator=gen)
+    _fill_synthetic(regions, wbuf, 20, 1000 + rank)  # replicated weights identical on every rank; own experts
     torch.cuda.synchronize()
     group = None
     if world > 1:
@@ -292,25 +299,35 @@ def bench_c4(args: argparse.Namespace, rng: np.random.Generator, max_over_ranks,
                                         hidden=cfg.hidden_size, experts=cfg.num_experts)
     pre = chroma_b200.Program.from_native(Native(plan_p, device_weights=wbuf.data_ptr(), ep=group))
     dec = chroma_b200.Program.from_native(Native(plan_d, device_weights=wbuf.data_ptr(), ep=group))
-    bd = chroma_b200.BatchDecoder(pre, dec, batch)
-    tokens = rng.integers(0, cfg.vocab_size, (batch, n))
-    reps = max(2, min(5, args.steps // 40))
-    for _ in range(max(1, min(3, args.warmup))):
-        bd.reset()
-        barrier()
-        bd.append(tokens, argmax=True)
-    times = []
-    for _ in range(reps):
-        bd.reset()
-        barrier()
-        t0 = time.perf_counter()
-        ids = bd.append(tokens, argmax=True)
-        times.append(time.perf_counter() - t0)
-    t = max_over_ranks(statistics.median(times))
-    flops = prefill_flops(cfg, batch, n) * world
     peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops_sustained"] if (ROOT / "MEASURED_PEAKS.json").exists() else 1400.0
+
+    def timed(seqs: int) -> tuple[float, int, np.ndarray]:
+        bd = chroma_b200.BatchDecoder(pre, dec, seqs)
+        tokens = rng.integers(0, cfg.vocab_size, (seqs, n))
+        reps = max(2, min(5, args.steps // 40))
+        for _ in range(max(1, min(3, args.warmup))):
+            bd.reset()
+            barrier()
+            bd.append(tokens, argmax=True)
+        times = []
+        for _ in range(reps):
+            bd.reset()
+            barrier()
+            t0 = time.perf_counter()
+            ids = bd.append(tokens, argmax=True)
+            times.append(time.perf_counter() - t0)
+        bd.close()
+        return max_over_ranks(statistics.median(times)), reps, ids
+
+    t, reps, ids = timed(batch)
+    flops = prefill_flops(cfg, batch, n) * world
+    strong = None
+    if world > 1 and batch % world == 0:
+        ts, _, _ = timed(batch // world)
+        sflops = prefill_flops(cfg, batch // world, n) * world
+        strong = {"tokens_per_s": batch * n / ts, "ms": ts * 1e3, "sequences_per_gpu": batch // world,
+                  "frac_of_bf16_sustained": sflops / ts / 1e12 / (peak * world)}
     barrier()
-    bd.close()
     del pre, dec
     if group is not None:
         group.close()
@@ -323,6 +340,7 @@ def bench_c4(args: argparse.Namespace, rng: np.random.Generator, max_over_ranks,
                                                                "per GPU, NVLink peer-memory dispatch/return)"),
         "tokens_per_s": world * batch * n / t, "ms": t * 1e3, "reps": reps, "n_gpus": world,
         "scaling": "weak",
+        "strong": strong,
         "e2e": {"api": "BatchDecoder.append(tokens[4, 2048], argmax=True) on every rank",
                 "h2d_bytes": batch * n * 8 + batch * 16, "d2h_bytes": batch * 8 + 4},
         "algorithmic_tflop": flops / 1e12, "achieved_tflops": flops / t / 1e12,
@@ -334,6 +352,119 @@ def bench_c4(args: argparse.Namespace, rng: np.random.Generator, max_over_ranks,
                          "sample": "reference compiled CPU program for one C4-width layer, 16 tokens (10.59 s in the "
                                    "build container, 2.12 GFLOP/s), extrapolated by FLOPs to this prefill"},
     }
+
+
+def _fill_synthetic(regions, wbuf, shared_seed: int, expert_seed: int | None = None) -> None:  # type: ignore[no-untyped-def]
+    """bf16 N(0, 0.02) weights (norm scales 1) written in device memory; the expert tensors from their own generator
+    when ``expert_seed`` is given."""
+    import torch
+
+    shared_gen = torch.Generator(device="cuda").manual_seed(shared_seed)
+    expert_gen = None if expert_seed is None else torch.Generator(device="cuda").manual_seed(expert_seed)
+    for name, off, numel, is_norm in regions:
+        if is_norm:
+            wbuf[off : off + numel * 4].view(torch.float32).fill_(1.0)
+        else:
+            gen = expert_gen if (expert_gen is not None and ".mlp.mlp" in name) else shared_gen
+            wbuf[off : off + numel * 2].view(torch.bfloat16).normal_(0.0, 0.02, generator=gen)
+
+
+def _rank_slice(full_regions, rank_regions, full, out, rank: int, world: int, hidden: int,  # type: ignore[no-untyped-def]
+                vocab: range | None) -> None:
+    """Copy the all-local weights ``full`` into this rank's expert-parallel layout ``out``: replicated tensors whole,
+    the expert tensors' rows of this rank's experts, and (vocab shard) this rank's unembedding rows."""
+    src = {name: (off, numel) for name, off, numel, _ in full_regions}
+    for name, off, numel, is_norm in rank_regions:
+        soff, snumel = src[name]
+        es = 4 if is_norm else 2
+        start = 0
+        if ".mlp.mlp" in name:
+            start = rank * (snumel // world) * es
+        elif name == "unembedding.weight" and vocab is not None:
+            start = vocab.start * hidden * es
+        out[off : off + numel * es].copy_(full[soff + start : soff + start + numel * es])
+
+
+def ep_parity(rank: int, world: int, barrier) -> dict:  # type: ignore[no-untyped-def]
+    """Bit-identity of the expert-parallel programs with the all-local program on the same tokens, on every rank,
+    before any timing (the reference has no multi-GPU path, so the all-local program is the bar).
+
+    * ``c4``: a 2-layer model at GPT-OSS-20B widths (32 experts, top-4), a 64-token forward per rank, experts split
+      over the ranks: logits, routes and greedy ids bit for bit.
+    * ``c5``: a 2-layer model at GPT-OSS-120B widths (128 experts) with the vocab projection column-sharded as well,
+      16 sequences per rank through the batched decoder (16-token prefill, 3 greedy steps): greedy ids identical;
+      prefill logits within the bf16 rounding of the last bit (the vocab GEMM over a shard tiles the sums
+      differently from the whole-vocabulary GEMM).
+    Semantics: chroma/models/gpt_oss.py:243-265 (MLPBlock.forward) on every rank's tokens."""
+    import torch
+
+    import chroma_b200
+    from chroma_b200 import models
+    from chroma_b200._src.compiler import synthetic_gptoss
+    from chroma_b200._src.experts import vocab_shard
+    from chroma_b200._src.native import Native
+
+    out: dict = {"ranks": world}
+    exchange = None if world > 1 else (lambda h: [h])
+    # ---- C4 widths, forward
+    cfg = dataclasses.replace(models.gpt_oss_20b, num_hidden_layers=2)
+    n = 64
+    fplan, fregions = synthetic_gptoss(cfg, steps=n)
+    eplan, eregions = synthetic_gptoss(cfg, steps=n, ep_world=world)
+    full = torch.empty(fplan["desc"]["weight_bytes"], dtype=torch.uint8, device="cuda")
+    _fill_synthetic(fregions, full, 31)
+    part = torch.empty(eplan["desc"]["weight_bytes"], dtype=torch.uint8, device="cuda")
+    _rank_slice(fregions, eregions, full, part, rank, world, cfg.hidden_size, None)
+    group = chroma_b200.ExpertGroup(rank, world, max_pairs=n * cfg.experts_per_token, hidden=cfg.hidden_size,
+                                    experts=cfg.num_experts, exchange=exchange)
+    tokens = np.random.default_rng(300 + rank).integers(0, cfg.vocab_size, n)
+    local = chroma_b200.Program.from_native(Native(fplan, device_weights=full.data_ptr()))
+    shared = chroma_b200.Program.from_native(Native(eplan, device_weights=part.data_ptr(), ep=group))
+    want, want_routes = np.asarray(local(tokens)), local.native.routes()
+    barrier()
+    got = [np.asarray(shared(tokens)) for _ in range(2)]
+    got_routes = shared.native.routes()
+    out["c4"] = bool(all(np.array_equal(g.view(np.uint16), want.view(np.uint16)) for g in got)
+                     and np.array_equal(got_routes, want_routes))
+    barrier()
+    local.close()
+    shared.close()
+    group.close()
+    del full, part
+    torch.cuda.empty_cache()
+    # ---- C5 widths, vocab shard, batched decode
+    cfg = dataclasses.replace(models.gpt_oss_120b, num_hidden_layers=2)
+    B, pre_n, ctx = 16, 16, 64
+    vocab = vocab_shard(rank, world, cfg.vocab_size)
+    plans = [synthetic_gptoss(cfg, steps=s, context=ctx) for s in (pre_n, 1)]
+    eplans = [synthetic_gptoss(cfg, steps=s, context=ctx, ep_world=world, vocab_rows=len(vocab)) for s in (pre_n, 1)]
+    full = torch.empty(plans[0][0]["desc"]["weight_bytes"], dtype=torch.uint8, device="cuda")
+    _fill_synthetic(plans[0][1], full, 51)
+    part = torch.empty(eplans[0][0]["desc"]["weight_bytes"], dtype=torch.uint8, device="cuda")
+    _rank_slice(plans[0][1], eplans[0][1], full, part, rank, world, cfg.hidden_size, vocab)
+    group = chroma_b200.ExpertGroup(rank, world, max_pairs=B * pre_n * cfg.experts_per_token, hidden=cfg.hidden_size,
+                                    experts=cfg.num_experts, vocab_rows=B, vocab=cfg.vocab_size, exchange=exchange)
+    rng = np.random.default_rng(500 + rank)
+    prompts = rng.integers(0, cfg.vocab_size, (B, pre_n))
+    results = []
+    for weights, pl, grp in ((full, plans, None), (part, eplans, group)):
+        pre = chroma_b200.Program.from_native(Native(pl[0][0], device_weights=weights.data_ptr(), ep=grp))
+        dec = chroma_b200.Program.from_native(Native(pl[1][0], device_weights=weights.data_ptr(), ep=grp))
+        with chroma_b200.BatchDecoder(pre, dec, B) as bd:
+            if grp is not None:
+                barrier()
+            logits = np.asarray(bd.append(prompts)).astype(np.float32)
+            ids = bd.append(prompts[:, -1:], argmax=True)
+            results.append((logits, ids, bd.generate(ids, 3)))
+    (la, ia, ga), (lb, ib, gb) = results
+    scale = np.max(np.abs(la), axis=-1, keepdims=True)
+    out["c5"] = bool(np.array_equal(ia, ib) and np.array_equal(ga, gb)
+                     and float(np.max(np.abs(la - lb) / scale)) <= 1e-2)
+    barrier()
+    group.close()
+    del full, part
+    torch.cuda.empty_cache()
+    return out
 
 
 def bench_c5(args: argparse.Namespace, max_over_ranks, barrier, rank: int, world: int) -> dict:  # type: ignore[no-untyped-def]
@@ -398,6 +529,14 @@ def bench_c5(args: argparse.Namespace, max_over_ranks, barrier, rank: int, world
     torch.cuda.synchronize()
     t = max_over_ranks(e0.elapsed_time(e1) / 1e3)
     ids = bd.generate(np.asarray(tokens), 1)[:, 0]
+    # e2e: greedy steps through the public API, host token ids in and host greedy ids out every step.
+    e2e_steps = max(5, min(20, args.steps))
+    cur = np.asarray(bd.append(ids[:, None], argmax=True))  # warm-up
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        cur = np.asarray(bd.append(cur[:, None], argmax=True))
+    e2e_t = max_over_ranks((time.perf_counter() - t0) / e2e_steps)
     barrier()
     d, I, E, k_ = cfg.hidden_size, cfg.intermediate_size, cfg.num_experts, cfg.experts_per_token
     expert_bytes = (2 * I * d + d * I + 2 * I + d) * 2
@@ -421,7 +560,9 @@ def bench_c5(args: argparse.Namespace, max_over_ranks, barrier, rank: int, world
         "roofline_frac": per_rank / (t / steps) / 1e9 / pk,
         "roofline_note": "all experts of the rank assumed touched (B x top-4 routes over E / world experts); "
                          "measured copy peak of one GPU",
-        "e2e": None,
+        "e2e": {"value": total / e2e_t, "unit": "tokens/s", "ms_per_step": e2e_t * 1e3,
+                "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8,
+                "api": f"BatchDecoder.append(ids[{B}, 1], argmax=True) on every rank, host ids fed back"},
         "argmax_head": [int(v) for v in ids[:2]],
         "cpu_baseline": {"value": 1.0 / (decode_flops_per_token(cfg, ctx) / 1e9 / REF_CPU_GFLOPS), "unit": "tokens/s",
                          "cores": 1, "kind": "reference (extrapolated)",
@@ -490,6 +631,13 @@ def main() -> None:
         if dist is not None:
             dist.destroy_process_group()
         return
+    parity = None
+    if not args.skip_parity:
+        parity = ep_parity(rank, world, barrier)
+        flags = torch.tensor([int(parity["c4"]), int(parity["c5"])], device="cuda", dtype=torch.int32)
+        if dist is not None:
+            dist.all_reduce(flags, op=dist.ReduceOp.MIN)  # true only when every rank matched
+        parity.update(c4=bool(flags[0].item()), c5=bool(flags[1].item()))
     flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     flush_read = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
 
@@ -703,14 +851,8 @@ def main() -> None:
         "scaling": "weak",
         "vs_baseline": value / world / (1e3 / A100_DECODE_STEP_MS),
         "dtype": "f32",
-        "data": "synthetic (seeded dev-model weights as scripts/export.py:16-29, seeded token ids)",
-        "config": {
-            "workload": "C2: dev GPT-OSS (12 layers, d=128, 59.1M params) KV-cached greedy decode step, "
-                        "256-token fp32 cache, 8-token prefill first, batch 1 per GPU",
-            "model": "gpt-oss dev", "global_batch": world, "seq_len": CONTEXT,
-            "parallelism": f"replicas x{world} (the dev model does not shard)",
-            "l2": "flushed before every timed step (256 MiB write, then 256 MiB read)",
-        },
+        "data": DATA,
+        "config": c2_config(world),
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": d2h,
                 "api": "chroma_b200.Decoder.append([token]) -> logits [1, 201088] on the host"},
         "gpu_launches": launches_per_step * args.steps,
@@ -754,6 +896,19 @@ def main() -> None:
         "c5_decode": c5,
         "fwd8": {"device_ms": fwd_dev_ms, "e2e_ms": fwd_e2e_ms, "vs_a100_e2e": A100_FWD8_MS / fwd_e2e_ms,
                  "h2d_bytes": 64, "d2h_bytes": 8 * V * 4, "api": "Program(tokens[8]) -> logits [8, 201088]"},
+    }
+    # Last and compact, so a reader that keeps only the end of the line still sees the multi-GPU results.
+    line["multi_gpu"] = {
+        "n": world,
+        "ep_parity": parity,
+        "c4_weak": None if not c4 else {"tok_s": round(c4["tokens_per_s"]), "ms": round(c4["ms"], 2),
+                                        "frac_bf16": round(c4["frac_of_bf16_sustained"], 3)},
+        "c4_strong": None if not c4 or not c4.get("strong") else {
+            "tok_s": round(c4["strong"]["tokens_per_s"]), "ms": round(c4["strong"]["ms"], 2),
+            "frac_bf16": round(c4["strong"]["frac_of_bf16_sustained"], 3)},
+        "c5": None if not c5 or "unavailable" in c5 else {
+            "tok_s": round(c5["tokens_per_s"]), "ms_step": round(c5["ms_per_step"], 3),
+            "frac_hbm": round(c5["roofline_frac"], 3), "e2e_tok_s": round(c5["e2e"]["value"])},
     }
     print(json.dumps(line), flush=True)
 

@@ -5,15 +5,12 @@ new token ids and returns the ``[1, vocab]`` logits after the last one; a single
 anything longer runs prefill in chunks; the cache is a ring of ``context`` rows whose positions keep advancing;
 an ``append`` that fails or is interrupted leaves the committed state unchanged; ``reset()``/``close()``.
 
-Two execution paths:
-
-* **device-resident** (both programs are B200 programs): the cache lives in device memory inside a native
-  ``chroma_b200_decoder``; masks are built on the device from ring-slot positions; a step uploads only token ids
-  and positions. New K/V rows are staged on the device and written into the ring lazily: the committed
-  ``CacheState`` records which staged rows are pending, and the next call applies them first. The only commit
-  point is the swap of ``self._state``, exactly as in the reference (decoder.py:72-76).
-* **host** (any other ``Program``-like objects, e.g. mocks in tests): the reference's own algorithm, with the
-  cache, masks and positions built on the host and passed as the seven inputs (decoder.py:96-139).
+The cache lives in device memory inside a native ``chroma_b200_decoder``; masks are built on the device from
+ring-slot positions; a step uploads only token ids and positions. New K/V rows are staged on the device and
+written into the ring lazily: the committed ``CacheState`` records which staged rows are pending, and the next call
+applies them first. The only commit point is the swap of ``self._state``, as in the reference (decoder.py:72-76).
+Both programs must be chroma_b200 programs; the reference's own ``chroma.Decoder`` drives any other ``Program``
+(and a chroma_b200 artefact too, through its seven-input protocol, decoder.py:96-139).
 
 ``BatchDecoder`` runs ``batch`` independent sequences through the same device path in one launch per step and can
 return greedy argmax ids instead of logits (the ids are computed on the device).
@@ -215,29 +212,22 @@ class Decoder:
         self._lock = threading.Lock()
         self._closed = False
         natives = _natives(prefill, decode)
-        self._native = NativeDecoder(*natives, sliding_window, 1) if natives else None
-        self._buffers = [
-            (
-                [np.empty(spec["shape"], dtype=nat.dtype_of(spec["dtype"])) for spec in model.inputs],
-                [np.empty(spec["shape"], dtype=nat.dtype_of(spec["dtype"])) for spec in model.outputs[1:]],
-            )
-            for model in self._models
-        ] if self._native is None else []
+        if natives is None:
+            # The cache lives in device memory next to the programs; programs of another backend are driven by the
+            # reference's own host-side Decoder (chroma.Decoder), which takes any Program.
+            raise TypeError("chroma_b200.Decoder drives chroma_b200 programs; use chroma.Decoder for other Programs")
+        self._native: NativeDecoder | None = NativeDecoder(*natives, sliding_window, 1)
         self._commit(self._empty())
 
     # -- state ---------------------------------------------------------------------------------------------
     def _empty(self) -> CacheState:
+        assert self._native is not None
         slots = np.full(self.context, -1, dtype=np.int64)
-        if self._native is not None:
-            return CacheState(_DeviceCache(self._native, 0), _DeviceCache(self._native, 1), slots, 0)
-        keys = np.zeros(self._shape, dtype=self._cache_dtype)
-        return CacheState(keys, np.zeros_like(keys), slots, 0)
+        return CacheState(_DeviceCache(self._native, 0), _DeviceCache(self._native, 1), slots, 0)
 
     def _commit(self, state: CacheState) -> None:
         # Swapping in a whole new state is the single commit point, so an interrupt cannot half-apply a step.
         self._state = state
-        for args, _ in self._buffers:
-            args[2:4] = state.keys, state.values
 
     def _flush(self) -> CacheState:
         """Apply rows a previous successful step staged on the device (idempotent)."""
@@ -272,11 +262,11 @@ class Decoder:
     def cache(self) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
         """Committed (keys, values, slots) as host arrays."""
         with self._lock:
-            state = self._flush()
-            if self._native is not None:
-                keys, values, slots = self._native.read()
-                return keys, values, slots[0]
-            return state.keys, state.values, state.slots
+            self._flush()
+            if self._native is None:
+                raise RuntimeError("Decoder is closed")
+            keys, values, slots = self._native.read()
+            return keys, values, slots[0]
 
     # -- stepping ------------------------------------------------------------------------------------------
     def append(self, tokens: Sequence[int] | np.ndarray) -> np.ndarray:
@@ -288,11 +278,9 @@ class Decoder:
             raise TypeError(f"Token IDs must be integers, got {ids.dtype}")
         ids = ids.astype(np.int64)
         with self._lock:
-            if self._closed:
+            if self._closed or self._native is None:
                 raise RuntimeError("Decoder is closed")
-            if self._native is not None:
-                return self._append_device(ids)
-            return self._append_host(ids)
+            return self._append_device(ids)
 
     def _append_device(self, ids: np.ndarray) -> np.ndarray:
         assert self._native is not None
@@ -316,39 +304,6 @@ class Decoder:
             offset += count
         return logits
 
-    def _append_host(self, ids: np.ndarray) -> np.ndarray:
-        offset = 0
-        logits = np.empty((1, self.vocab_size), dtype=self._logit_dtype)
-        while offset < len(ids):
-            remaining = len(ids) - offset
-            index = 1 if remaining == 1 else 0
-            args, updates = self._buffers[index]
-            steps = len(args[0])
-            count = min(steps, remaining)
-            state = self._state
-            times = state.position + np.arange(steps, dtype=np.int64)
-            key_times = np.concatenate((state.slots, times))
-            valid = np.concatenate((state.slots >= 0, np.ones(steps, dtype=bool)))
-            causal = valid[None, :] & (key_times[None, :] <= times[:, None])
-            token_ids, positions, _, _, full_mask, window_mask, logit_index = args
-            token_ids.fill(0)
-            token_ids[:count] = ids[offset : offset + count]
-            positions[:] = times
-            for mask, window in ((full_mask, self.context), (window_mask, self._window)):
-                mask.fill(-np.inf)
-                mask[causal & (key_times[None, :] > times[:, None] - window)] = 0
-            logit_index[0] = count - 1
-            logits = np.empty((1, self.vocab_size), dtype=self._logit_dtype)
-            self._models[index](*args, out=[logits, *updates])
-            rows = times[:count] % self.context
-            keys, values, slots = state.keys.copy(), state.values.copy(), state.slots.copy()
-            keys[:, rows] = updates[0][:, :count]
-            values[:, rows] = updates[1][:, :count]
-            slots[rows] = times[:count]
-            self._commit(CacheState(keys, values, slots, state.position + count))
-            offset += count
-        return logits
-
     def close(self) -> None:
         with self._lock:
             if self._native is not None:
@@ -356,7 +311,6 @@ class Decoder:
             for model in self._models:
                 model.close()
             self._closed = True
-            self._buffers.clear()
 
     def __enter__(self) -> "Decoder":
         return self

@@ -247,18 +247,40 @@ def dedupe() -> None:
     """Keep one copy of identical weight files (the prefill/decode pair of one model share theirs).
 
     The reference names weight files by content hash (chroma/_src/build.py:61), so equal names mean equal bytes.
-    A program whose file was removed records the directory that holds it in ``shared_weights.json``;
-    ``oracle/refprogram.py`` follows that record.
+    A program whose file is a duplicate gets a relative symbolic link to the first copy in its place, so the
+    reference's own ``Program`` (which reads ``weights`` from the artefact directory) loads it unchanged.
     """
     seen: dict[str, Path] = {}
     for directory in sorted(p for p in ROOT.iterdir() if (p / "model.json").exists()):
         weights = json.loads((directory / "model.json").read_text())["weights"]
+        file = directory / weights
         if weights in seen:
-            if (directory / weights).exists():
-                (directory / weights).unlink()
-            (directory / "shared_weights.json").write_text(json.dumps({"directory": seen[weights].name}) + "\n")
-        elif (directory / weights).exists():
+            if file.is_symlink() and file.exists():
+                continue
+            if file.exists() or file.is_symlink():
+                file.unlink()
+            file.symlink_to(Path("..") / seen[weights].name / weights)
+            (directory / "shared_weights.json").unlink(missing_ok=True)
+        elif file.exists() and not file.is_symlink():
             seen[weights] = directory
+
+
+def stage_package() -> Path:
+    """A patched copy of the reference's Python package (``chroma``) under oracle/_ref/pkg, for machines without the
+    reference sources (the GPU hosts): the same mechanical Python 3.12 patches ``oracle/refimport.py`` applies in
+    memory, written out once. Only the ``.py`` modules are staged (enough for ``chroma.Program`` and
+    ``chroma.Decoder``; compiling needs the source tree). Test infrastructure, never committed."""
+    from oracle import refimport
+
+    source = refimport.REFERENCE / "chroma"
+    target = refimport.STAGED / "chroma"
+    for path in sorted(source.rglob("*.py")):
+        out = target / path.relative_to(source)
+        out.parent.mkdir(parents=True, exist_ok=True)
+        text = refimport._patch(path.read_text())
+        if not out.exists() or out.read_text() != text:
+            out.write_text(text)
+    return refimport.STAGED
 
 
 def names() -> list[str]:

@@ -26,9 +26,13 @@ import os
 import re
 import sys
 from pathlib import Path
+from typing import Any
 
 # The reference checkout: $CHROMA_REFERENCE, else a directory named ``reference`` beside this repository.
 REFERENCE = Path(os.environ.get("CHROMA_REFERENCE") or Path(__file__).resolve().parents[2] / "reference")
+# The patched copy of the reference's ``chroma`` package that oracle/build_ref.py stages for machines without the
+# reference sources (git-ignored; travels with the other reference programs under oracle/_ref).
+STAGED = Path(__file__).resolve().parent / "_ref" / "pkg"
 _PACKAGES = ("chroma", "scripts")
 _EXCEPT = re.compile(r"^(\s*)except ([A-Za-z_][\w.]*(?:\s*,\s*[A-Za-z_][\w.]*)+):", re.M)
 
@@ -99,3 +103,20 @@ def install() -> None:
     sys.dont_write_bytecode = True
     if not any(isinstance(f, _Finder) for f in sys.meta_path):
         sys.meta_path.insert(0, _Finder())
+
+
+def runtime() -> Any:
+    """The reference's ``chroma`` package for loading and running programs: from the source tree when it is here,
+    else from the staged copy (oracle/build_ref.py ``stage_package``). Raises ModuleNotFoundError when neither
+    exists."""
+    import importlib
+
+    if REFERENCE.exists():
+        install()
+    elif (STAGED / "chroma" / "__init__.py").exists():
+        sys.dont_write_bytecode = True
+        if str(STAGED) not in sys.path:
+            sys.path.insert(0, str(STAGED))
+    else:
+        raise ModuleNotFoundError("neither the reference sources nor the staged copy of its chroma package is here")
+    return importlib.import_module("chroma")

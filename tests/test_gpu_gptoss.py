@@ -242,27 +242,6 @@ def test_c2_batch_decoder_matches_reference(gpu: None) -> None:
                                       g["batch_rowsum"][:, step, 0], **FP32)
 
 
-def test_c2_program_with_host_masks_matches_device_path(gpu: None) -> None:
-    # The decode Program run directly on host buffers (the reference's seven-input protocol, masks built on the
-    # host) agrees with the device-resident decoder.
-    g = golden("c2_decode")
-    prefill, decode = dev_pair()
-    host = chroma_b200.Decoder(chroma_b200.Program(prefill), chroma_b200.Program(decode))
-    host._native.close()
-    host._native = None
-    host._buffers = [
-        ([np.empty(s["shape"], dtype=chroma_b200._src.native.dtype_of(s["dtype"])) for s in m.inputs],
-         [np.empty(s["shape"], dtype=chroma_b200._src.native.dtype_of(s["dtype"])) for s in m.outputs[1:]])
-        for m in host._models
-    ]
-    host._commit(host._empty())
-    with host:
-        outs = [host.append(g["prompt"])] + [host.append([int(t)]) for t in g["forced"][:4]]
-    for i, out in enumerate(outs):
-        assert int(np.argmax(out)) == int(g["step_argmax"][i][0])
-        np.testing.assert_allclose(out[:, g["sample_cols"]], g["step_sample"][i], **FP32)
-
-
 def test_decoder_errors_keep_state_and_recover(gpu: None) -> None:
     # A failed append leaves the committed state as it was (decoder.py:130-137). A failing call may first apply
     # the previous step's staged rows, which replaces the state object but not its content.
