@@ -13,7 +13,9 @@ kernels (``libchroma_b200.so``) and compiles a graph into a small *launch plan* 
      qualified names, scalars (eps, top-k, attention scale, SwiGLU clamp and slope, RoPE frequencies and
      concentration, per-layer window) from the graph nodes that use them;
    * the fused RMSNorm + gated-SiLU + residual row program (the benchmark micrograph).
-   Anything else raises ``NotImplementedError`` at compile time (generic graphs are not part of this backend).
+   Any other graph goes to the generic path (``chroma_b200/_src/graph.py``): a plan of steps over strided views for
+   the precompiled generic kernels (``csrc/graph.cu``); operators outside the reference's table raise
+   ``NotImplementedError`` at compile time, as the reference does.
 3. ``write_artifact``: pack the weights in the kernels' layout and write the manifest-v2 directory: ``model.json``
    (version 2, Python ABI, library, weights, inputs, outputs, stats; build.py:91-100), ``weights-<sha>.bin`` and
    the library module ``_chroma_<uuid>.py`` exposing ``signature`` and ``Model`` (the native object protocol of
@@ -531,17 +533,18 @@ def lower_model(model: Any, *, steps: int, context: int | None = None, last: boo
 
 
 def lower(program: Any) -> Lowered:
-    """prepare + recognise. Raises NotImplementedError for graphs outside the supported families."""
-    g = _Graph(prepare(program))
+    """prepare + recognise: a GPT-OSS program, the fused row program, or else a generic graph plan."""
+    prepared = prepare(program)
+    g = _Graph(prepared)
     if any(n.endswith("unembedding.weight") for n in g.params):
         return _lower_gptoss(g)
     try:
         return _lower_micro(g)
-    except (NotImplementedError, StopIteration, ValueError, TypeError, AttributeError) as exc:
-        raise NotImplementedError(
-            "backend='cuda' (chroma_b200) compiles GPT-OSS-style transformer programs and fused RMSNorm/"
-            f"gated-SiLU row programs; this graph is neither ({exc})"
-        ) from None
+    except Exception:  # noqa: BLE001 - not the fused row program: any other graph goes to the generic path
+        pass
+    from chroma_b200._src.graph import lower_graph
+
+    return lower_graph(prepared)
 
 
 # ---------------------------------------------------------------------------------------------------------

@@ -99,6 +99,11 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "chroma_b200_create_ep": (ctypes.c_int, [ctypes.POINTER(Desc), _CP, _VP, _VP, ctypes.POINTER(_VP), _CP, _SZ]),
     "chroma_b200_host_alloc": (ctypes.c_int, [_SZ, ctypes.POINTER(_VP), _CP, _SZ]),
     "chroma_b200_host_free": (None, [_VP]),
+    "chroma_b200_graph_create": (ctypes.c_int, [_I64P, _SZ, _CP, ctypes.POINTER(_VP), _CP, _SZ]),
+    "chroma_b200_graph_run": (ctypes.c_int, [_VP, ctypes.POINTER(_VP), ctypes.POINTER(_VP), _CP, _SZ]),
+    "chroma_b200_graph_device": (ctypes.c_char_p, [_VP]),
+    "chroma_b200_graph_launches": (ctypes.c_int32, [_VP]),
+    "chroma_b200_graph_destroy": (None, [_VP]),
 }
 
 EP_HANDLE_BYTES = 64  # CHROMA_B200_EP_HANDLE_BYTES
@@ -343,6 +348,67 @@ class Native:
             pass
 
 
+class GraphNative:
+    """Owns one ``chroma_b200_graph``: a generic exported graph run from its plan (chroma_b200/_src/graph.py)."""
+
+    def __init__(self, plan: dict[str, Any], weights_path: str | None) -> None:
+        self.plan = plan
+        self.pinned = PinnedPool()
+        words = np.asarray(plan["graph"], dtype=np.int64)
+        self._words = words
+        handle = _VP()
+        path = str(weights_path).encode() if plan["desc"]["weight_bytes"] else None
+        call("chroma_b200_graph_create", words.ctypes.data_as(_I64P), words.size, path, ctypes.byref(handle))
+        self.handle = handle
+        self.inputs = plan["inputs"]
+        self.outputs = plan["outputs"]
+        self.in_types = [dtype_of(s["dtype"]) for s in self.inputs]
+        self.out_types = [dtype_of(s["dtype"]) for s in self.outputs]
+
+    @property
+    def device(self) -> str:
+        return (lib().chroma_b200_graph_device(self.handle) or b"").decode()
+
+    @property
+    def launches(self) -> int:
+        return int(lib().chroma_b200_graph_launches(self.handle))
+
+    def run(self, inputs: list[Any], outputs: list[Any]) -> None:
+        if not isinstance(inputs, list) or not isinstance(outputs, list):
+            raise TypeError("inputs and outputs must be lists")
+        if len(inputs) != len(self.inputs) or len(outputs) != len(self.outputs):
+            raise ValueError("wrong number of arrays")
+        regions: list[tuple[int, int]] = []
+        in_ptrs = (_VP * max(1, len(inputs)))()
+        out_ptrs = (_VP * len(outputs))()
+        for i, (value, spec, dtype) in enumerate(zip(inputs, self.inputs, self.in_types)):
+            array = checked(value, spec["shape"], dtype, False)
+            in_ptrs[i] = array.ctypes.data
+            regions.append((array.ctypes.data, array.ctypes.data + array.nbytes))
+        for i, (value, spec, dtype) in enumerate(zip(outputs, self.outputs, self.out_types)):
+            array = checked(value, spec["shape"], dtype, True)
+            begin, end = array.ctypes.data, array.ctypes.data + array.nbytes
+            if any(begin < last and first < end for first, last in regions):
+                raise ValueError("output overlap")
+            out_ptrs[i] = begin
+            regions.append((begin, end))
+        call("chroma_b200_graph_run", self.handle, in_ptrs, out_ptrs)
+
+    def close(self) -> None:
+        handle, self.handle = getattr(self, "handle", None), None
+        if handle:
+            lib().chroma_b200_graph_destroy(handle)
+        pinned = getattr(self, "pinned", None)
+        if pinned is not None:
+            pinned.close()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def model_class(plan: dict[str, Any]) -> type:
     """The ``Model`` class a compiled artefact's library module exports (native object protocol)."""
 
@@ -351,7 +417,7 @@ def model_class(plan: dict[str, Any]) -> type:
             if plan.get("expert_parallel"):
                 raise ValueError("This artefact holds one rank's experts of an expert-parallel group; load it with "
                                  "chroma_b200.compile_model(..., experts=group) on every rank")
-            self._native = Native(plan, weights_path)
+            self._native = GraphNative(plan, weights_path) if "graph" in plan else Native(plan, weights_path)
 
         @property
         def device(self) -> str:
@@ -361,7 +427,7 @@ def model_class(plan: dict[str, Any]) -> type:
             self._native.run(inputs, outputs)
 
         @property
-        def native(self) -> Native:
+        def native(self) -> Any:
             return self._native
 
     return Model

@@ -14,7 +14,7 @@ from pathlib import Path
 
 PACKAGE = Path(__file__).resolve().parent
 ROOT = PACKAGE.parent
-SOURCES = [PACKAGE / "csrc" / "runtime.cu"]
+SOURCES = [PACKAGE / "csrc" / "runtime.cu", PACKAGE / "csrc" / "graph.cu"]
 DEPENDS = sorted((PACKAGE / "csrc").glob("*.cu*")) + [ROOT / "include" / "chroma_b200.h"]
 TARGET = PACKAGE / "libchroma_b200.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -113,6 +113,23 @@ int chroma_b200_routes(chroma_b200_program* program, int32_t* out, int64_t count
  * cudaStream_t; 0 is the legacy default stream), not synchronised. */
 int chroma_b200_vocab_argmax_static(const chroma_b200_program* program, const float* x, int32_t rows, void* logits,
                                     int64_t* ids, void* stream, char* err, size_t err_len);
+/* ---- Generic exported graphs -------------------------------------------------------------------------------------
+ * Graphs over the reference's operator table (chroma/_src/lowering.py:34-86) other than the recognised GPT-OSS
+ * programs. Replaces the per-graph generated kernels and their build (chroma/_src/codegen/gpu.py:63-435,
+ * chroma/_src/codegen/cuda/codegen.py:44-168, chroma/_src/build.py:22-30) with precompiled kernels driven by a plan:
+ * `plan` is `words` int64 values written by chroma_b200/_src/graph.py (buffers, strided views, elementwise bytecode,
+ * steps); `weights_path` holds the graph's parameters and folded constants (NULL when it has none). Created on the
+ * current device. `run` has the contract of chroma_b200_run (host buffers in manifest order, synchronises; an index
+ * out of range is CHROMA_B200_INDEX with the program still usable, as Runner::run, runtime.h:147-173). */
+typedef struct chroma_b200_graph chroma_b200_graph;
+int chroma_b200_graph_create(const int64_t* plan, size_t words, const char* weights_path, chroma_b200_graph** out,
+                             char* err, size_t err_len);
+int chroma_b200_graph_run(chroma_b200_graph* graph, const void* const* inputs, void* const* outputs, char* err,
+                          size_t err_len);
+const char* chroma_b200_graph_device(const chroma_b200_graph* graph);
+int32_t chroma_b200_graph_launches(const chroma_b200_graph* graph);
+void chroma_b200_graph_destroy(chroma_b200_graph* graph);
+
 /* GEMM epilogues of chroma_b200_gemm_bf16. */
 #define CHROMA_B200_EPI_STORE 0    /* C = bf16(A.B^T + bias) (nn.Linear, chroma/_src/codegen/cpu/kernels.h:63-74) */
 #define CHROMA_B200_EPI_RESIDUAL 1 /* C = bf16(R + bf16(A.B^T + bias)): linear + residual (gpt_oss.py:209) */

@@ -89,3 +89,19 @@ def test_reference_program_is_torch_free(gpu: None) -> None:
     )
     env = dict(os.environ, PYTHONPATH=str(ROOT))
     subprocess.run([sys.executable, "-c", code, str(tg._TMP / "dev_fwd8")], check=True, env=env, cwd=str(ROOT))
+
+
+def test_reference_program_loads_generic_b200_artifact(gpu: None, tmp_path) -> None:  # type: ignore[no-untyped-def]
+    """A generic graph compiled by this backend, loaded and run by the reference's unmodified Program."""
+    import torch
+
+    from tests import generic_cases as gc
+
+    chroma = reference_chroma()
+    case = gc.by_name()["reductions_f32"]
+    inputs = case.inputs()
+    chroma_b200.compile(torch.export.export(case.module(), inputs), tmp_path / "g").close()
+    arrays = [gc.to_numpy(t) for t in inputs]
+    with chroma.Program(tmp_path / "g") as ref_loaded, chroma_b200.Program(tmp_path / "g") as ours:
+        for a, b in zip(ref_loaded(*arrays), ours(*arrays)):
+            np.testing.assert_array_equal(a, b)
