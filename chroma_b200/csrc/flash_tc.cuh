@@ -5,15 +5,17 @@
 // One CTA = 128 query rows of one head of one sequence, 6 warps:
 //   warp 0 (one thread)  TMA: the Q tile once, then K and V tiles of 64 keys into a 2-stage ring, plus each tile's
 //                        key positions (ring slots or chunk rows) written by the warp's lanes
-//   warp 1 (one thread)  allocates 128 TMEM columns (S at [0, 64), O at [64, 128)) and issues, per key tile,
-//                        S = Q.K^T (M=128, N=64, K=64) then, once the softmax has written P, O += P.V (M=128, N=64,
-//                        K=64 keys, V read MN-major straight from its [key][dim] tile)
+//   warp 1 (one thread)  allocates 256 TMEM columns (two S buffers at [0, 64) and [64, 128), O at [128, 192)) and
+//                        issues S(t+1) = Q.K^T (M=128, N=64, K=64) into the other S buffer as soon as its K tile has
+//                        landed, then, once the softmax has written P(t), O += P(t).V (M=128, N=64, K=64 keys, V read
+//                        MN-major straight from its [key][dim] tile): the tensor core computes the next tile's
+//                        scores while the softmax warps work on this one
 //   warps 2-5            the online softmax, one query row per thread (TMEM lane = row): load the S row, mask,
 //                        running max in the log2 domain, rescale the O row in TMEM when the max grows, P = 2^(s - m)
 //                        as bf16 into shared memory (the 128-byte-swizzled layout the MMA reads), running sum; at the
 //                        end O / (sum + sink term), stored as bf16
 // Tiles with no visible key are never loaded (ring tiles screened against the slot positions, own tiles from the
-// window's edge), as in k_flash_prefill. 3 CTAs fit an SM (66 KB shared memory, 128 TMEM columns each). All waits
+// window's edge), as in k_flash_prefill. 2 CTAs fit an SM (66 KB shared memory, 256 TMEM columns each). All waits
 // are bounded (tma.cuh).
 #pragma once
 
@@ -85,7 +87,7 @@ __device__ __forceinline__ void tmem_store32(uint32_t taddr, const float (&v)[32
 }
 
 // grid = (ceil(n / 128), H, B); block = kFtThreads; dynamic shared memory kFtSmemBytes.
-__global__ void __launch_bounds__(kFtThreads, 3) k_flash_prefill_tc(const __grid_constant__ FlashMaps maps, FlashArgs a,
+__global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid_constant__ FlashMaps maps, FlashArgs a,
                                                                     const __nv_bfloat16* __restrict__ sinks,
                                                                     __nv_bfloat16* __restrict__ out, unsigned* err) {
     extern __shared__ uint8_t ft_raw[];
@@ -96,7 +98,7 @@ __global__ void __launch_bounds__(kFtThreads, 3) k_flash_prefill_tc(const __grid
     int64_t* tpos = reinterpret_cast<int64_t*>(Ps + kFtRows * kFtKeys * 2);  // [2][64] key positions
     uint16_t* live_list = reinterpret_cast<uint16_t*>(tpos + 2 * kFtKeys);
     uint32_t* live_bits = reinterpret_cast<uint32_t*>(live_list + kFtMaxCacheTiles);
-    __shared__ uint64_t q_full, kv_full[2], kv_empty[2], s_full, p_full, pv_done;
+    __shared__ uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], p_full, pv_done;
     __shared__ uint32_t tmem_base;
     __shared__ int s_nlive;
     __shared__ volatile int abort_flag;
@@ -115,7 +117,8 @@ __global__ void __launch_bounds__(kFtThreads, 3) k_flash_prefill_tc(const __grid
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        mbar_init(&s_full, 1);
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
         mbar_init(&p_full, 4);  // the 4 softmax warps
         mbar_init(&pv_done, 1);
         abort_flag = 0;
@@ -130,7 +133,7 @@ __global__ void __launch_bounds__(kFtThreads, 3) k_flash_prefill_tc(const __grid
     }
     for (int w = threadIdx.x; w < (cache_tiles + 31) / 32; w += blockDim.x) live_bits[w] = 0;
     if (warp == 1) {
-        tmem_alloc(&tmem_base, 128);
+        tmem_alloc(&tmem_base, 256);
         tmem_relinquish();
     }
     pdl_wait();
@@ -211,18 +214,28 @@ __global__ void __launch_bounds__(kFtThreads, 3) k_flash_prefill_tc(const __grid
         if (lane == 0) {
             constexpr uint32_t idesc_s = umma_idesc_bf16(kFtRows, kFtKeys);
             constexpr uint32_t idesc_o = umma_idesc_bf16(kFtRows, kFaDim) | (1u << 16);  // B (V) MN-major
-            const uint32_t tS = tmem, tO = tmem + kFtKeys;
+            const uint32_t tO = tmem + 2 * kFtKeys;
             if (!mbar_wait(&q_full, 0, err)) abort_flag = 1;
             tc_fence_after();
             const uint64_t dq = umma_desc_sw128(Qs);
+            // S(u) into S buffer u & 1, once tile u's K has landed.
+            auto issue_s = [&](int u) -> bool {
+                const int su = u & 1;
+                if (!mbar_wait(&kv_full[su], unsigned((u >> 1) & 1), err)) return false;
+                tc_fence_after();
+                const uint64_t dk = umma_desc_sw128(KV + size_t(2 * su) * kFtTile);
+#pragma unroll
+                for (int k = 0; k < kFaDim / 16; ++k)
+                    umma_bf16(tmem + uint32_t(su * kFtKeys), dq + 2 * k, dk + 2 * k, idesc_s, k > 0);
+                umma_commit(&s_full[su]);
+                return true;
+            };
+            if (tiles > 0 && !abort_flag && !issue_s(0)) abort_flag = 1;
             for (int t = 0; t < tiles && !abort_flag; ++t) {
                 const int s = t & 1;
-                if (!mbar_wait(&kv_full[s], unsigned((t >> 1) & 1), err)) { abort_flag = 1; break; }
-                tc_fence_after();
-                const uint64_t dk = umma_desc_sw128(KV + size_t(2 * s) * kFtTile);
-#pragma unroll
-                for (int k = 0; k < kFaDim / 16; ++k) umma_bf16(tS, dq + 2 * k, dk + 2 * k, idesc_s, k > 0);
-                umma_commit(&s_full);
+                // The S buffer of tile t + 1 last held tile t - 1, whose softmax finished (p_full, waited below in
+                // iteration t - 1) before this point.
+                if (t + 1 < tiles && !issue_s(t + 1)) { abort_flag = 1; break; }
                 if (!mbar_wait(&p_full, unsigned(t & 1), err)) { abort_flag = 1; break; }
                 tc_fence_after();
                 const uint64_t dp = umma_desc_sw128(Ps);
@@ -242,17 +255,19 @@ __global__ void __launch_bounds__(kFtThreads, 3) k_flash_prefill_tc(const __grid
         const int64_t ti = p0 + i;
         const bool row_ok = i < a.n;
         const uint32_t lane_base = uint32_t(q * 32) << 16;
-        const uint32_t tS = tmem + lane_base, tO = tmem + kFtKeys + lane_base;
+        const uint32_t tO = tmem + 2 * kFtKeys + lane_base;
         float m_run = -INFINITY, l_run = 0.f;
         for (int t = 0; t < tiles && !abort_flag; ++t) {
             const int s = t & 1;
             bool cached;
             const int j0 = tile_key0(t, cached);
-            if (!mbar_wait(&kv_full[s], unsigned((t >> 1) & 1), err) || !mbar_wait(&s_full, unsigned(t & 1), err)) {
+            if (!mbar_wait(&kv_full[s], unsigned((t >> 1) & 1), err) ||
+                !mbar_wait(&s_full[s], unsigned((t >> 1) & 1), err)) {
                 abort_flag = 1;
                 break;
             }
             tc_fence_after();
+            const uint32_t tS = tmem + uint32_t(s * kFtKeys) + lane_base;
             const bool masked = cached || j0 + kFtKeys - 1 > i0 || (a.window > 0 && j0 <= i_last - a.window);
             // Two passes over the S row (32 columns at a time keeps the registers low): the max, then P.
             float mx = -INFINITY;
@@ -356,7 +371,7 @@ __global__ void __launch_bounds__(kFtThreads, 3) k_flash_prefill_tc(const __grid
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 128);
+        tmem_dealloc(tmem, 256);
     }
 }
 
