@@ -875,7 +875,7 @@ def main() -> None:
             "frac": (layer_bytes + vocab_bytes) / (ms_per_step / 1e3) / 1e9 / pk["hbm_gbs"],
         },
         "roofline_vocab": {
-            "kernel": "k_vocab (unembedding GEMV, 201088 x 128 fp32, 1 row)", "bound": "hbm", "achieved": achieved,
+            "kernel": "k_vocab_row (unembedding GEMV, 201088 x 128 fp32, 1 row)", "bound": "hbm", "achieved": achieved,
             "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": VOCAB_NCU_TRAFFIC,
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_vocab<float, 1> launch of "
                               "this workload",

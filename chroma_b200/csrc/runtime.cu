@@ -389,6 +389,17 @@ static void launch_vocab(cudaStream_t s, const Dims& dm, int sms, const float* x
         return;
     }
     if constexpr (std::is_same_v<T, float>) {
+        if (rows == 1 && dm.d == 128) {  // one decode row: balanced contiguous ranges (k_vocab_row)
+            static int per_sm = 0;
+            if (!per_sm) check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_vocab_row, kVrThreads, 0),
+                               "vocab occupancy");
+            const int grid = std::max(1, sms * std::max(1, per_sm) * 2);
+            const int step = 4 * kVrU;
+            const int rows_per_cta = ((dm.V + grid - 1) / grid + step - 1) / step * step;
+            launch(s, dim3((dm.V + rows_per_cta - 1) / rows_per_cta), dim3(kVrThreads), 0, k_vocab_row, x, dm.V, W,
+                   logits, keys, rows_per_cta);
+            return;
+        }
         if (rows > kVocabRows && dm.d == kVtD) {  // many rows: one pass over the vocab matrix per 64 rows
             const int tiles = (dm.V + kVtVocab - 1) / kVtVocab;
             launch(s, dim3(std::min(tiles, sms)), dim3(kThreads), kVtSmemBytes, k_vocab_tiled, x, rows, dm.V, W, logits,
