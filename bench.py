@@ -395,6 +395,9 @@ def ep_parity(rank: int, world: int, barrier) -> dict:  # type: ignore[no-untype
       16 sequences per rank through the batched decoder (16-token prefill, 3 greedy steps): greedy ids identical;
       prefill logits within the bf16 rounding of the last bit (the vocab GEMM over a shard tiles the sums
       differently from the whole-vocabulary GEMM).
+    * ``artifacts``: a 2-layer model at reduced widths compiled per rank to its own artefact directory
+      (``compile_model(..., experts=group)``: the rank's expert shard, the manifest recording rank and world): its
+      32-token forward bit for bit against the all-local program.
     Semantics: chroma/models/gpt_oss.py:243-265 (MLPBlock.forward) on every rank's tokens."""
     import torch
 
@@ -432,6 +435,30 @@ def ep_parity(rank: int, world: int, barrier) -> dict:  # type: ignore[no-untype
     group.close()
     del full, part
     torch.cuda.empty_cache()
+    # ---- per-rank artefacts: compile_model(..., experts=group) writes this rank's expert shard to its own
+    # artefact directory (manifest records rank and world); its forward must equal the all-local program's bits.
+    import tempfile as _tempfile
+
+    small = dataclasses.replace(models.gpt_oss_20b, num_hidden_layers=2, hidden_size=1024, intermediate_size=1024,
+                                num_attention_heads=16, num_key_value_heads=2, num_experts=8, experts_per_token=2,
+                                vocab_size=8192)
+    model = models.random_transformer(small, seed=61, std=0.02, dtype=torch.bfloat16)
+    toks = np.random.default_rng(600 + rank).integers(0, small.vocab_size, 32)
+    with _tempfile.TemporaryDirectory() as tmp:
+        sgroup = chroma_b200.ExpertGroup(rank, world, max_pairs=32 * small.experts_per_token, hidden=1024, experts=8,
+                                         exchange=exchange)
+        local = chroma_b200.compile_model(model, Path(tmp) / "all", steps=32)
+        shard = chroma_b200.compile_model(model, Path(tmp) / f"rank{rank}", steps=32, experts=sgroup)
+        manifest = json.loads((Path(tmp) / f"rank{rank}" / "model.json").read_text())
+        want = np.asarray(local(toks))
+        barrier()
+        got = np.asarray(shard(toks))
+        out["artifacts"] = bool(manifest["b200"].get("expert_parallel") == {"rank": rank, "world": world}
+                                and np.array_equal(got.view(np.uint16), want.view(np.uint16)))
+        barrier()
+        local.close()
+        shard.close()
+        sgroup.close()
     # ---- C5 widths, vocab shard, batched decode
     cfg = dataclasses.replace(models.gpt_oss_120b, num_hidden_layers=2)
     B, pre_n, ctx = 16, 16, 64
@@ -634,10 +661,11 @@ def main() -> None:
     parity = None
     if not args.skip_parity:
         parity = ep_parity(rank, world, barrier)
-        flags = torch.tensor([int(parity["c4"]), int(parity["c5"])], device="cuda", dtype=torch.int32)
+        flags = torch.tensor([int(parity["c4"]), int(parity["c5"]), int(parity["artifacts"])], device="cuda",
+                             dtype=torch.int32)
         if dist is not None:
             dist.all_reduce(flags, op=dist.ReduceOp.MIN)  # true only when every rank matched
-        parity.update(c4=bool(flags[0].item()), c5=bool(flags[1].item()))
+        parity.update(c4=bool(flags[0].item()), c5=bool(flags[1].item()), artifacts=bool(flags[2].item()))
     flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     flush_read = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
 
