@@ -2,21 +2,23 @@
 // as k_flash_prefill (chroma/models/gpt_oss.py:133-151, chroma/models/cached.py:36-47), with both products issued
 // as tcgen05.mma into TMEM instead of mma.sync into registers.
 //
-// One CTA = 128 query rows of one head of one sequence, 6 warps:
-//   warp 0 (one thread)  TMA: the Q tile once, then K and V tiles of 64 keys into a 2-stage ring, plus each tile's
+// One CTA = two tiles of 128 query rows (256 consecutive rows) of one head of one sequence, which share every K and
+// V tile; 10 warps:
+//   warp 0 (one thread)  TMA: both Q tiles once, then K and V tiles of 64 keys into a 2-stage ring, plus each tile's
 //                        key positions (ring slots or chunk rows) written by the warp's lanes
-//   warp 1 (one thread)  allocates 256 TMEM columns (two S buffers at [0, 64) and [64, 128), O at [128, 192)) and
-//                        issues S(t+1) = Q.K^T (M=128, N=64, K=64) into the other S buffer as soon as its K tile has
-//                        landed, then, once the softmax has written P(t), O += P(t).V (M=128, N=64, K=64 keys, V read
-//                        MN-major straight from its [key][dim] tile): the tensor core computes the next tile's
-//                        scores while the softmax warps work on this one
-//   warps 2-5            the online softmax, one query row per thread (TMEM lane = row): load the S row, mask,
-//                        running max in the log2 domain, rescale the O row in TMEM when the max grows, P = 2^(s - m)
-//                        as bf16 into shared memory (the 128-byte-swizzled layout the MMA reads), running sum; at the
-//                        end O / (sum + sink term), stored as bf16
-// Tiles with no visible key are never loaded (ring tiles screened against the slot positions, own tiles from the
-// window's edge), as in k_flash_prefill. 2 CTAs fit an SM (66 KB shared memory, 256 TMEM columns each). All waits
-// are bounded (tma.cuh).
+//   warp 1 (one thread)  allocates 256 TMEM columns (S of query tile k at [64k, 64k + 64), O of query tile k at
+//                        [128 + 64k, ...)) and issues, per key tile t, in ping-pong order:
+//                          O0 += P0(t).V(t), S0(t+1) = Q0.K(t+1), O1 += P1(t).V(t), S1(t+1) = Q1.K(t+1)
+//                        (M=128, N=64, K=64 each; V read MN-major straight from its [key][dim] tile), each product
+//                        as soon as the softmax of that query tile has written its P
+//   warps 2-5, 6-9       the online softmax of query tile 0 and 1, one query row per thread (TMEM lane = row): load
+//                        the S row, mask, running max in the log2 domain, rescale the O row in TMEM when the max
+//                        grows, P = 2^(s - m) as bf16 into shared memory (the 128-byte-swizzled layout the MMA reads),
+//                        running sum; at the end O / (sum + sink term), stored as bf16
+// While one warpgroup works on its softmax, the tensor core runs the other tile's products: the exponentials and the
+// MMAs overlap instead of alternating. Tiles with no visible key are never loaded (ring tiles screened against the
+// slot positions, own tiles from the window's edge), as in k_flash_prefill. 2 CTAs fit an SM (100 KB shared memory,
+// 256 TMEM columns each). All waits are bounded (tma.cuh).
 #pragma once
 
 #include "flash.cuh"
@@ -24,13 +26,14 @@
 
 namespace cb200 {
 
-constexpr int kFtRows = 128;  // query rows per CTA
+constexpr int kFtRows = 128;  // query rows per query tile
+constexpr int kFtQ = 2;       // query tiles per CTA
 constexpr int kFtKeys = 64;   // keys per tile
-constexpr int kFtThreads = 192;
+constexpr int kFtThreads = 320;
 constexpr int kFtMaxCacheTiles = 1024;
 constexpr int kFtTile = kFtKeys * kFaDim * 2;  // one K or V tile: 8 KB
-// Q 16 KB | K,V x 2 stages 32 KB | P 16 KB | key positions 1 KB | live cache tiles 2 KB + bits 128 B, + alignment
-constexpr size_t kFtSmemBytes = 1024 + kFtRows * kFaDim * 2 + 4 * size_t(kFtTile) + kFtRows * kFtKeys * 2 +
+// Q 2 x 16 KB | K,V x 2 stages 32 KB | P 2 x 16 KB | key positions 1 KB | live cache tiles 2 KB + bits 128 B, + alignment
+constexpr size_t kFtSmemBytes = 1024 + kFtQ * kFtRows * kFaDim * 2 + 4 * size_t(kFtTile) + kFtQ * kFtRows * kFtKeys * 2 +
                                 2 * kFtKeys * sizeof(int64_t) + kFtMaxCacheTiles * 2 + kFtMaxCacheTiles / 8;
 
 struct FlashMaps {
@@ -86,19 +89,19 @@ __device__ __forceinline__ void tmem_store32(uint32_t taddr, const float (&v)[32
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// grid = (ceil(n / 128), H, B); block = kFtThreads; dynamic shared memory kFtSmemBytes.
+// grid = (ceil(n / 256), H, B); block = kFtThreads; dynamic shared memory kFtSmemBytes.
 __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid_constant__ FlashMaps maps, FlashArgs a,
                                                                     const __nv_bfloat16* __restrict__ sinks,
                                                                     __nv_bfloat16* __restrict__ out, unsigned* err) {
     extern __shared__ uint8_t ft_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ft_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* Qs = sm;                                      // [128][64] SW128
-    uint8_t* KV = Qs + kFtRows * kFaDim * 2;               // stage s: K at KV + 2s*tile, V at KV + (2s+1)*tile
-    uint8_t* Ps = KV + 4 * kFtTile;                        // [128][64] SW128
-    int64_t* tpos = reinterpret_cast<int64_t*>(Ps + kFtRows * kFtKeys * 2);  // [2][64] key positions
+    uint8_t* Qs = sm;                                      // [2][128][64] SW128
+    uint8_t* KV = Qs + kFtQ * kFtRows * kFaDim * 2;        // stage s: K at KV + 2s*tile, V at KV + (2s+1)*tile
+    uint8_t* Ps = KV + 4 * kFtTile;                        // [2][128][64] SW128
+    int64_t* tpos = reinterpret_cast<int64_t*>(Ps + kFtQ * kFtRows * kFtKeys * 2);  // [2][64] key positions
     uint16_t* live_list = reinterpret_cast<uint16_t*>(tpos + 2 * kFtKeys);
     uint32_t* live_bits = reinterpret_cast<uint32_t*>(live_list + kFtMaxCacheTiles);
-    __shared__ uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], p_full, pv_done;
+    __shared__ uint64_t q_full, kv_full[2], kv_empty[2], s_full[kFtQ], p_full[kFtQ], pv_done[kFtQ];
     __shared__ uint32_t tmem_base;
     __shared__ int s_nlive;
     __shared__ volatile int abort_flag;
@@ -107,8 +110,8 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
     const int h = blockIdx.y, b = blockIdx.z;
     const int kvh = h / a.G;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int i0 = qb * kFtRows;
-    const int i_last = min(i0 + kFtRows, a.n) - 1;
+    const int i0 = qb * kFtQ * kFtRows;
+    const int i_last = min(i0 + kFtQ * kFtRows, a.n) - 1;
     const int cache_tiles = (a.ctx + kFtKeys - 1) / kFtKeys;
 
     if (threadIdx.x == 0) {
@@ -117,10 +120,11 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        mbar_init(&s_full[0], 1);
-        mbar_init(&s_full[1], 1);
-        mbar_init(&p_full, 4);  // the 4 softmax warps
-        mbar_init(&pv_done, 1);
+        for (int k = 0; k < kFtQ; ++k) {
+            mbar_init(&s_full[k], 1);
+            mbar_init(&p_full[k], 4);  // the 4 softmax warps of query tile k
+            mbar_init(&pv_done[k], 1);
+        }
         abort_flag = 0;
         fence_barrier_init();
         prefetch_tensormap(&maps.q);
@@ -174,10 +178,11 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
     };
 
     if (warp == 0) {
-        // ---- producer: Q once, then K/V tiles and their key positions
+        // ---- producer: both Q tiles once, then K/V tiles and their key positions
         if (lane == 0) {
-            mbar_arrive_expect_tx(&q_full, kFtRows * kFaDim * 2);
-            tma_load_3d(Qs, &maps.q, 0, h, b * a.n + i0, &q_full);
+            mbar_arrive_expect_tx(&q_full, kFtQ * kFtRows * kFaDim * 2);
+            for (int k = 0; k < kFtQ; ++k)
+                tma_load_3d(Qs + size_t(k) * kFtRows * kFaDim * 2, &maps.q, 0, h, b * a.n + i0 + k * kFtRows, &q_full);
         }
         for (int t = 0; t < tiles && !abort_flag; ++t) {
             const int s = t & 1;
@@ -210,65 +215,83 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
             }
         }
     } else if (warp == 1) {
-        // ---- MMA issue
+        // ---- MMA issue, ping-pong over the two query tiles
         if (lane == 0) {
             constexpr uint32_t idesc_s = umma_idesc_bf16(kFtRows, kFtKeys);
             constexpr uint32_t idesc_o = umma_idesc_bf16(kFtRows, kFaDim) | (1u << 16);  // B (V) MN-major
-            const uint32_t tO = tmem + 2 * kFtKeys;
             if (!mbar_wait(&q_full, 0, err)) abort_flag = 1;
             tc_fence_after();
-            const uint64_t dq = umma_desc_sw128(Qs);
-            // S(u) into S buffer u & 1, once tile u's K has landed.
-            auto issue_s = [&](int u) -> bool {
-                const int su = u & 1;
-                if (!mbar_wait(&kv_full[su], unsigned((u >> 1) & 1), err)) return false;
-                tc_fence_after();
-                const uint64_t dk = umma_desc_sw128(KV + size_t(2 * su) * kFtTile);
+            // S_k(u) = Q_k . K(u) into query tile k's S columns (K of tile u has landed: waited by the caller).
+            auto issue_s = [&](int k, int u) {
+                const uint64_t dq = umma_desc_sw128(Qs + size_t(k) * kFtRows * kFaDim * 2);
+                const uint64_t dk = umma_desc_sw128(KV + size_t(2 * (u & 1)) * kFtTile);
 #pragma unroll
-                for (int k = 0; k < kFaDim / 16; ++k)
-                    umma_bf16(tmem + uint32_t(su * kFtKeys), dq + 2 * k, dk + 2 * k, idesc_s, k > 0);
-                umma_commit(&s_full[su]);
+                for (int kk = 0; kk < kFaDim / 16; ++kk)
+                    umma_bf16(tmem + uint32_t(k * kFtKeys), dq + 2 * kk, dk + 2 * kk, idesc_s, kk > 0);
+                umma_commit(&s_full[k]);
+            };
+            auto wait_kv = [&](int u) {
+                if (!mbar_wait(&kv_full[u & 1], unsigned((u >> 1) & 1), err)) return false;
+                tc_fence_after();
                 return true;
             };
-            if (tiles > 0 && !abort_flag && !issue_s(0)) abort_flag = 1;
+            if (tiles > 0 && !abort_flag) {
+                if (wait_kv(0)) {
+                    issue_s(0, 0);
+                    issue_s(1, 0);
+                } else {
+                    abort_flag = 1;
+                }
+            }
             for (int t = 0; t < tiles && !abort_flag; ++t) {
                 const int s = t & 1;
-                // The S buffer of tile t + 1 last held tile t - 1, whose softmax finished (p_full, waited below in
-                // iteration t - 1) before this point.
-                if (t + 1 < tiles && !issue_s(t + 1)) { abort_flag = 1; break; }
-                if (!mbar_wait(&p_full, unsigned(t & 1), err)) { abort_flag = 1; break; }
-                tc_fence_after();
-                const uint64_t dp = umma_desc_sw128(Ps);
                 const uint64_t dv = umma_desc_sw128_mn(KV + size_t(2 * s + 1) * kFtTile);
+                bool next_ready = false;
+                for (int k = 0; k < kFtQ; ++k) {
+                    // Query tile k's softmax has written P_k(t) (and finished reading S_k(t)).
+                    if (!mbar_wait(&p_full[k], unsigned(t & 1), err)) { abort_flag = 1; break; }
+                    tc_fence_after();
+                    const uint64_t dp = umma_desc_sw128(Ps + size_t(k) * kFtRows * kFtKeys * 2);
+                    const uint32_t tO = tmem + uint32_t(2 * kFtKeys + k * kFaDim);
 #pragma unroll
-                for (int k = 0; k < kFtKeys / 16; ++k)  // 16 keys per step: +32 B along P's rows, +2 KB down V
-                    umma_bf16(tO, dp + 2 * k, dv + 128 * k, idesc_o, t > 0 || k > 0);
-                umma_commit(&pv_done);
-                umma_commit(&kv_empty[s]);
+                    for (int kk = 0; kk < kFtKeys / 16; ++kk)  // 16 keys per step: +32 B along P's rows, +2 KB down V
+                        umma_bf16(tO, dp + 2 * kk, dv + 128 * kk, idesc_o, t > 0 || kk > 0);
+                    umma_commit(&pv_done[k]);
+                    if (k == kFtQ - 1) umma_commit(&kv_empty[s]);
+                    if (t + 1 < tiles) {
+                        if (k == 0) {
+                            if (!wait_kv(t + 1)) { abort_flag = 1; break; }
+                            next_ready = true;
+                        }
+                        if (next_ready) issue_s(k, t + 1);
+                    }
+                }
             }
         }
     } else {
-        // ---- softmax: warp q (= warp % 4) owns TMEM lanes / tile rows [32q, 32q + 32)
+        // ---- softmax of query tile k: warp q (= warp % 4) owns TMEM lanes / tile rows [32q, 32q + 32)
+        const int k = (warp - 2) >> 2;
         const int q = warp & 3;
-        const int r = q * 32 + lane;  // this thread's query row within the block
-        const int i = i0 + r;
+        const int r = q * 32 + lane;  // this thread's query row within its tile
+        const int i = i0 + k * kFtRows + r;
+        const int ik0 = i0 + k * kFtRows, ik_last = min(ik0 + kFtRows, a.n) - 1;
         const int64_t ti = p0 + i;
         const bool row_ok = i < a.n;
         const uint32_t lane_base = uint32_t(q * 32) << 16;
-        const uint32_t tO = tmem + 2 * kFtKeys + lane_base;
+        const uint32_t tS = tmem + uint32_t(k * kFtKeys) + lane_base;
+        const uint32_t tO = tmem + uint32_t(2 * kFtKeys + k * kFaDim) + lane_base;
+        uint8_t* prow = Ps + size_t(k) * kFtRows * kFtKeys * 2 + size_t(r) * 128;
         float m_run = -INFINITY, l_run = 0.f;
         for (int t = 0; t < tiles && !abort_flag; ++t) {
             const int s = t & 1;
             bool cached;
             const int j0 = tile_key0(t, cached);
-            if (!mbar_wait(&kv_full[s], unsigned((t >> 1) & 1), err) ||
-                !mbar_wait(&s_full[s], unsigned((t >> 1) & 1), err)) {
+            if (!mbar_wait(&kv_full[s], unsigned((t >> 1) & 1), err) || !mbar_wait(&s_full[k], unsigned(t & 1), err)) {
                 abort_flag = 1;
                 break;
             }
             tc_fence_after();
-            const uint32_t tS = tmem + uint32_t(s * kFtKeys) + lane_base;
-            const bool masked = cached || j0 + kFtKeys - 1 > i0 || (a.window > 0 && j0 <= i_last - a.window);
+            const bool masked = cached || j0 + kFtKeys - 1 > ik0 || (a.window > 0 && j0 <= ik_last - a.window);
             // Two passes over the S row (32 columns at a time keeps the registers low): the max, then P.
             float mx = -INFINITY;
 #pragma unroll 1
@@ -292,9 +315,9 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
             const bool none = m_new == -INFINITY;
             const float corr = none ? 1.f : fast_exp2(m_run - m_new);
             const float neg = none ? 0.f : -m_new;
-            // The previous P.V must have finished before O is rescaled and P is overwritten.
+            // The previous P_k.V must have finished before O_k is rescaled and P_k is overwritten.
             if (t > 0) {
-                if (!mbar_wait(&pv_done, unsigned((t - 1) & 1), err)) { abort_flag = 1; break; }
+                if (!mbar_wait(&pv_done[k], unsigned((t - 1) & 1), err)) { abort_flag = 1; break; }
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll 1
@@ -308,7 +331,6 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
                 }
             }
             float rs = 0.f;
-            uint8_t* prow = Ps + size_t(r) * 128;
 #pragma unroll 1
             for (int c = 0; c < 2; ++c) {
                 float v[32];
@@ -340,10 +362,10 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full);
+            if (lane == 0) mbar_arrive(&p_full[k]);
         }
-        // Final: wait for the last P.V, then O / (l + sink term) for this row.
-        if (tiles > 0 && !abort_flag && mbar_wait(&pv_done, unsigned((tiles - 1) & 1), err)) {
+        // Final: wait for the last P_k.V, then O / (l + sink term) for this row.
+        if (tiles > 0 && !abort_flag && mbar_wait(&pv_done[k], unsigned((tiles - 1) & 1), err)) {
             tc_fence_after();
             float ov[2][32];
             tmem_load32(tO, ov[0]);

@@ -801,8 +801,8 @@ struct LargeExec {
                 fa.slots = mask_mode == kMaskSlots ? io.slots : nullptr;
                 fa.pos0 = mask_mode == kMaskSlots ? io.pos0 : nullptr;
                 if (mask_mode != kMaskSlots) fa.ctx = 0;
-                // CHROMA_B200_FLASH_TC=1 selects the tcgen05 flash kernel (correct, but slower than the mma.sync one
-                // until its softmax overlaps the tensor core: 1.05 vs 0.71 ms per C4 layer).
+                // CHROMA_B200_FLASH_TC=1 selects the tcgen05 flash kernel (two query tiles per CTA in ping-pong; correct,
+                // but still slower than the mma.sync one: the C4 prefill takes 79.5 vs 74.2 ms).
                 static const bool tc_flash = [] {
                     const char* e = std::getenv("CHROMA_B200_FLASH_TC");
                     return e && e[0] == '1';
@@ -834,7 +834,7 @@ struct LargeExec {
                         fm.kc = fm.kn;
                         fm.vc = fm.vn;
                     }
-                    launch(s, dim3((n + kFtRows - 1) / kFtRows, dm.H, B), dim3(kFtThreads), kFtSmemBytes,
+                    launch(s, dim3((n + kFtQ * kFtRows - 1) / (kFtQ * kFtRows), dm.H, B), dim3(kFtThreads), kFtSmemBytes,
                            k_flash_prefill_tc, fm, fa, w.sinks, attn, err);
                 } else
                 launch(s, dim3((n + kFaRows - 1) / kFaRows, dm.H, B), dim3(kFaThreads), kFaSmemBytes, k_flash_prefill, q, fa, ck, cv,
