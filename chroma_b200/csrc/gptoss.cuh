@@ -1031,6 +1031,85 @@ __global__ void __launch_bounds__(128) k_route_rows(const float* __restrict__ x2
     }
 }
 
+// The out-projection + bias + residual of k_out and the router of k_route_rows in one launch, one CTA per token, for
+// programs with d = H*hd = 128 (the grouped-MoE path). Warp w owns out rows 8w .. 8w+7, each lane the same four
+// elements of every row that k_out's fragments give it, so every dot product keeps k_out's order (per-lane FMA chain,
+// then the warp butterfly) and the x2 row is bit-identical; then the token's norm, gate, top-k and expert-list append
+// exactly as k_route_rows. Saves one dependent launch per layer.
+constexpr int kOrThreads = 512;
+
+template <typename T>
+__global__ void __launch_bounds__(kOrThreads) k_out_route(const float* __restrict__ attn, const float* __restrict__ x,
+                                                         int ntok, Dims dm, LayerW<T> w, float* __restrict__ x2,
+                                                         float* __restrict__ xn_out, int* __restrict__ ridx,
+                                                         float* __restrict__ rw, int* __restrict__ routes,
+                                                         int* __restrict__ lists, int* __restrict__ counts, unsigned* err) {
+    constexpr int d = 128, RPW = d / (kOrThreads / 32);
+    __shared__ __align__(16) float as[d];
+    __shared__ __align__(16) float xs[d];
+    __shared__ float gl[kWarps * 2];
+    __shared__ float misc[17];  // inv, indices, weights
+    int* sidx = reinterpret_cast<int*>(misc + 1);
+    float* sw = misc + 9;
+    const int t = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float wv[RPW][4], bv[RPW];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+        load4(w.out_w + size_t(warp * RPW + i) * d + lane * 4, wv[i]);
+        bv[i] = Store<T>::load(w.out_b + warp * RPW + i);
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x < d) as[threadIdx.x] = attn[size_t(t) * d + threadIdx.x];
+    __syncthreads();
+    const float4 av = *reinterpret_cast<const float4*>(as + lane * 4);
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+        float acc = 0.f;
+        acc = fmaf(wv[i][0], av.x, acc);
+        acc = fmaf(wv[i][1], av.y, acc);
+        acc = fmaf(wv[i][2], av.z, acc);
+        acc = fmaf(wv[i][3], av.w, acc);
+        acc = warp_sum(acc);
+        if (lane == 0) {
+            const int r = warp * RPW + i;
+            const size_t o = size_t(t) * d + r;
+            const float v = Store<T>::round(__fadd_rn(x[o], Store<T>::round(__fadd_rn(acc, bv[i]))));
+            x2[o] = v;
+            xs[r] = v;
+        }
+    }
+    __syncthreads();
+    // ---- the router of k_route_rows on the x2 row
+    rows_rmsnorm<T>(xs, 1, d, dm.eps, w.mlp_norm, misc);
+    if (threadIdx.x < d) xn_out[size_t(t) * d + threadIdx.x] = xs[threadIdx.x];
+    for (int e0 = warp * 2; e0 < dm.E; e0 += (kOrThreads / 32) * 2) {
+        const T* rows[2] = {w.gate_w + size_t(e0) * d, w.gate_w + size_t(min(e0 + 1, dm.E - 1)) * d};
+        const int nr = min(2, dm.E - e0);
+        Frag<2> f;
+        frag_load<T, 2>(f, rows, nr, d, 0);
+        float acc[2][1];
+        warp_gemv<T, 2, 1>(f, rows, nr, xs, d, 1, acc);
+        if (lane == 0) {
+            gl[e0] = Store<T>::round(__fadd_rn(acc[0][0], Store<T>::load(w.gate_b + e0)));
+            if (nr > 1) gl[e0 + 1] = Store<T>::round(__fadd_rn(acc[1][0], Store<T>::load(w.gate_b + e0 + 1)));
+        }
+    }
+    __syncthreads();
+    if (warp == 0) warp_topk_softmax<T>(gl, dm.E, dm.k, sidx, sw);
+    __syncthreads();
+    if (threadIdx.x < dm.k) {
+        const int slot = threadIdx.x;
+        ridx[size_t(t) * dm.k + slot] = sidx[slot];
+        rw[size_t(t) * dm.k + slot] = sw[slot];
+        if (routes) routes[size_t(t) * dm.k + slot] = sidx[slot];
+        const int e = int(checked_row(sidx[slot], dm.E, true, err));
+        const int at = atomicAdd(counts + e, 1);
+        lists[size_t(e) * ntok + at] = t * dm.k + slot;
+    }
+}
+
 // grid = (E, ceil(I / kPairsPerCta), ceil(ntok / kGroupRows)), block = kThreads. Warp w holds mlp1 pairs p, p+1
 // (4 rows) of expert blockIdx.x; for every (token, slot) routed there (blockIdx.z's share of the list), the SwiGLU
 // of k_moe_up.

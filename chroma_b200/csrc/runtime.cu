@@ -1176,7 +1176,8 @@ struct GptExec {
     int planned_launches() const {
         if (large_path) return large.launches;
         const int pre = side ? 1 : 0;
-        return cluster_decode ? pre + 2 : pre + 1 + (grouped_moe ? 7 : 5) * m->desc.layers + 2;
+        const bool fused_or = grouped_moe && m->dm.H * m->dm.hd == 128 && m->dm.E <= 2 * kWarps;
+        return cluster_decode ? pre + 2 : pre + 1 + (grouped_moe ? (fused_or ? 6 : 7) : 5) * m->desc.layers + 2;
     }
 
     void enqueue_cluster_decode(cudaStream_t s) {
@@ -1277,13 +1278,21 @@ struct GptExec {
             const T* bias = static_cast<const T*>(windowed ? io.window_mask : io.mask);
             launch(s, dim3(n, dm.KV, B * chunks), dim3(kThreads), smem_attn, k_attention<T>, q, dm, a, ck, cv,
                    static_cast<const T*>(nk), static_cast<const T*>(nv), bias, w.sinks, attn);
-            launch(s, dim3((dm.d + 2 * kWarps - 1) / (2 * kWarps), tiles), dim3(kThreads), smem_out, k_out<T>, attn, x, N,
-                   dm, w.out_w, w.out_b, x2);
+            // The grouped-MoE path's out-projection and router run as one kernel when the widths allow it.
+            const bool fused_or = grouped_moe && dm.H * dm.hd == 128 && dm.E <= 2 * kWarps;
+            if (!fused_or)
+                launch(s, dim3((dm.d + 2 * kWarps - 1) / (2 * kWarps), tiles), dim3(kThreads), smem_out, k_out<T>, attn,
+                       x, N, dm, w.out_w, w.out_b, x2);
             if (grouped_moe) {
                 int* counts = g_counts.as<int>();
                 const unsigned zs = unsigned((N + kGroupRows - 1) / kGroupRows);  // a fully skewed routing still spreads
-                launch(s, dim3(N), dim3(128), smem_up, k_route_rows<T>, x2, N, dm, w, g_xn.as<float>(), ridx, rw,
-                       io.routes ? io.routes + size_t(l) * N * dm.k : nullptr, g_lists.as<int>(), counts, err);
+                if (fused_or)
+                    launch(s, dim3(N), dim3(kOrThreads), 0, k_out_route<T>, static_cast<const float*>(attn),
+                           static_cast<const float*>(x), N, dm, w, x2, g_xn.as<float>(), ridx, rw,
+                           io.routes ? io.routes + size_t(l) * N * dm.k : nullptr, g_lists.as<int>(), counts, err);
+                else
+                    launch(s, dim3(N), dim3(128), smem_up, k_route_rows<T>, x2, N, dm, w, g_xn.as<float>(), ridx, rw,
+                           io.routes ? io.routes + size_t(l) * N * dm.k : nullptr, g_lists.as<int>(), counts, err);
                 launch(s, dim3(dm.E, (dm.I + kPairsPerCta - 1) / kPairsPerCta, zs), dim3(kThreads),
                        size_t(kGroupRows) * dm.d * 4, k_moe_up_grouped<T>, static_cast<const float*>(g_xn.as<float>()), N,
                        dm, w, static_cast<const int*>(g_lists.as<int>()), static_cast<const int*>(counts), act);
@@ -1293,7 +1302,7 @@ struct GptExec {
                 launch(s, dim3(N), dim3(std::max(dm.d, dm.E)), 0, k_moe_combine_rows<T>,
                        static_cast<const float*>(g_ys.as<float>()), static_cast<const float*>(x2), N, dm,
                        static_cast<const float*>(rw), x, counts);
-                launches += 7;
+                launches += fused_or ? 6 : 7;
                 continue;
             }
             launch(s, dim3(N * dm.k, (dm.I + kPairsPerCta - 1) / kPairsPerCta), dim3(kThreads), smem_up, k_moe_up<T>, x2,
