@@ -4,21 +4,27 @@
 //
 // One CTA = two tiles of 128 query rows (256 consecutive rows) of one head of one sequence, which share every K and
 // V tile; 10 warps:
-//   warp 0 (one thread)  TMA: both Q tiles once, then K and V tiles of 64 keys into a 2-stage ring, plus each tile's
-//                        key positions (ring slots or chunk rows) written by the warp's lanes
+//   warp 0 (one thread)  TMA: both Q tiles once, then K and V tiles of 64 keys into a kFtStages-deep ring, plus each
+//                        tile's key positions (ring slots or chunk rows) written by the warp's lanes
 //   warp 1 (one thread)  allocates 256 TMEM columns (S of query tile k at [64k, 64k + 64), O of query tile k at
 //                        [128 + 64k, ...)) and issues, per key tile t, in ping-pong order:
 //                          O0 += P0(t).V(t), S0(t+1) = Q0.K(t+1), O1 += P1(t).V(t), S1(t+1) = Q1.K(t+1)
-//                        (M=128, N=64, K=64 each; V read MN-major straight from its [key][dim] tile), each product
-//                        as soon as the softmax of that query tile has written its P
-//   warps 2-5, 6-9       the online softmax of query tile 0 and 1, one query row per thread (TMEM lane = row): load
-//                        the S row, mask, running max in the log2 domain, rescale the O row in TMEM when the max
-//                        grows, P = 2^(s - m) as bf16 into shared memory (the 128-byte-swizzled layout the MMA reads),
-//                        running sum; at the end O / (sum + sink term), stored as bf16
-// While one warpgroup works on its softmax, the tensor core runs the other tile's products: the exponentials and the
-// MMAs overlap instead of alternating. Tiles with no visible key are never loaded (ring tiles screened against the
-// slot positions, own tiles from the window's edge), as in k_flash_prefill. 2 CTAs fit an SM (100 KB shared memory,
-// 256 TMEM columns each). All waits are bounded (tma.cuh).
+//                        (M=128, N=64, K=64 each). P.V takes P straight from TMEM (the A operand of the
+//                        tensor-memory form of tcgen05.mma) and V MN-major from its [key][dim] tile in shared memory.
+//   warps 2-5, 6-9       the online softmax of query tile k = 0, 1, one query row per thread (TMEM lane = row):
+//                        load the S row once (64 columns), mask, running max in the log2 domain, P = 2^(s - m)
+//                        packed as bf16 pairs and stored over the first 32 columns of the same S (the columns this
+//                        thread has already read), running sum; when the max grows, rescale the O row in TMEM; at the
+//                        end O / (sum + sink term), stored as bf16
+// P overwrites S in place, and the tensor core executes the MMAs of one issuing thread in order, so S_k(t+1) (written
+// into the same columns) never lands before O_k += P_k(t).V(t) has read P_k(t); the commit that signals S_k(t+1) also
+// covers that P.V, so the softmax may rescale O_k as soon as it sees S_k(t+1).
+// While one warpgroup works on its softmax, the tensor core runs the other tile's products. The masking test is
+// hoisted out of the per-element code (a 64-bit visibility word per row, applied only on tiles that need it): left
+// inside the unrolled element loops it was predicated into every tile and took most of the ALU pipe. Tiles with no
+// visible key are never loaded (ring tiles screened against the slot positions, own tiles from the window's edge),
+// as in k_flash_prefill. 2 CTAs fit an SM (about 86 KB of shared memory and 256 TMEM columns each). All waits are
+// bounded (tma.cuh).
 #pragma once
 
 #include "flash.cuh"
@@ -26,15 +32,19 @@
 
 namespace cb200 {
 
-constexpr int kFtRows = 128;  // query rows per query tile
-constexpr int kFtQ = 2;       // query tiles per CTA
-constexpr int kFtKeys = 64;   // keys per tile
+constexpr int kFtRows = 128;   // query rows per query tile
+constexpr int kFtQ = 2;        // query tiles per CTA
+constexpr int kFtKeys = 64;    // keys per tile
+constexpr int kFtStages = 3;   // K/V ring depth
 constexpr int kFtThreads = 320;
 constexpr int kFtMaxCacheTiles = 1024;
 constexpr int kFtTile = kFtKeys * kFaDim * 2;  // one K or V tile: 8 KB
-// Q 2 x 16 KB | K,V x 2 stages 32 KB | P 2 x 16 KB | key positions 1 KB | live cache tiles 2 KB + bits 128 B, + alignment
-constexpr size_t kFtSmemBytes = 1024 + kFtQ * kFtRows * kFaDim * 2 + 4 * size_t(kFtTile) + kFtQ * kFtRows * kFtKeys * 2 +
-                                2 * kFtKeys * sizeof(int64_t) + kFtMaxCacheTiles * 2 + kFtMaxCacheTiles / 8;
+// Of each group of 4 (s, s') pairs of a row, the pairs with index kFtPolyFrom..3 take 2^x from exp2_poly (4: none; the
+// special-function unit is not the limit at 2 CTAs per SM, and the polynomial costs issue slots).
+constexpr int kFtPolyFrom = 4;
+// Q 2 x 16 KB | K,V x kFtStages 16 KB | key positions 512 B per stage | live cache tiles 2 KB + bits 128 B, + alignment
+constexpr size_t kFtSmemBytes = 1024 + kFtQ * kFtRows * kFaDim * 2 + 2 * kFtStages * size_t(kFtTile) +
+                                kFtStages * kFtKeys * sizeof(int64_t) + kFtMaxCacheTiles * 2 + kFtMaxCacheTiles / 8;
 
 struct FlashMaps {
     CUtensorMap q;       // [B*n][H][64]: box {64, 1, 128}
@@ -57,8 +67,6 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
         : "memory");
 }
-// Generic-proxy shared-memory writes (P) made visible to the tensor cores' async proxy.
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Shared-memory descriptor of a 128-byte-swizzled tile read MN-major (rows of 64 elements along N, 8-row atoms of
 // 1024 bytes along K): the V tile [key][dim] as the B operand of P.V.
@@ -73,20 +81,112 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(const void* smem_tile) {
     return d;
 }
 
-__device__ __forceinline__ void tmem_store32(uint32_t taddr, const float (&v)[32]) {
+// D[tmem] (+)= A[tmem] * B[smem]: A (M rows on TMEM lanes, K-major, two bf16 per 32-bit column) read from tensor
+// memory. Issued by a single thread.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(uint32_t(accumulate))
+        : "memory");
+}
+
+// 32 lanes x 32 columns from TMEM without waiting (tmem_wait_ld() before the registers are read).
+__device__ __forceinline__ void tmem_load32_async(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 columns of 32-bit words into TMEM; waits for the store to complete.
+__device__ __forceinline__ void tmem_store32u(uint32_t taddr, const uint32_t* w) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
         "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
-        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
-        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
-        "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
-        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
-        "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7]), "r"(w[8]), "r"(w[9]),
+        "r"(w[10]), "r"(w[11]), "r"(w[12]), "r"(w[13]), "r"(w[14]), "r"(w[15]), "r"(w[16]), "r"(w[17]), "r"(w[18]),
+        "r"(w[19]), "r"(w[20]), "r"(w[21]), "r"(w[22]), "r"(w[23]), "r"(w[24]), "r"(w[25]), "r"(w[26]), "r"(w[27]),
+        "r"(w[28]), "r"(w[29]), "r"(w[30]), "r"(w[31])
         : "memory");
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_store32(uint32_t taddr, const float (&v)[32]) {
+    uint32_t w[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(v[i]);
+    tmem_store32u(taddr, w);
+}
+
+// 2^x on the FMA pipe, for x <= 8 (the softmax's exponents): x = j + f with j = round(x) and f in [-1/2, 1/2] (the
+// rounding by adding and subtracting 1.5 * 2^23), 2^f from a cubic with constant term 1 fitted here for the least
+// maximum relative error on [-1/2, 1/2] (1.0e-4, far below the half unit of the bf16 that P is rounded to), and
+// 2^j added to the exponent field. x below -126 gives 2^-126 or less (the caller's sums do not see it); -inf gives 0.
+__device__ __forceinline__ float exp2_poly(float x) {
+    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+    const float xc = fmaxf(x, -126.0f);
+    const float t = xc + kRound;
+    const float f = xc - (t - kRound);
+    float p = fmaf(0.05500858277082443f, f, 0.24221037328243256f);
+    p = fmaf(p, f, 0.6932829022407532f);
+    p = fmaf(p, f, 1.0f);
+    const float y = __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+    return x == -INFINITY ? 0.0f : y;
+}
+
+// Packed pairs of fp32 (the f32x2 instructions of sm_100): lo in the low word.
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f32x2_split(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// exp2_poly on a packed pair, the arithmetic in f32x2 (same rounding per element as exp2_poly).
+__device__ __forceinline__ void exp2_poly2(uint64_t x2, float& ya, float& yb) {
+    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+    float xa, xb;
+    f32x2_split(x2, xa, xb);
+    const uint64_t xc = f32x2(fmaxf(xa, -126.0f), fmaxf(xb, -126.0f));
+    const uint64_t t = fadd2(xc, f32x2(kRound, kRound));
+    const uint64_t f = fsub2(xc, fsub2(t, f32x2(kRound, kRound)));
+    uint64_t p = ffma2(f32x2(0.05500858277082443f, 0.05500858277082443f), f,
+                       f32x2(0.24221037328243256f, 0.24221037328243256f));
+    p = ffma2(p, f, f32x2(0.6932829022407532f, 0.6932829022407532f));
+    p = ffma2(p, f, f32x2(1.0f, 1.0f));
+    float pa, pb, ta, tb;
+    f32x2_split(p, pa, pb);
+    f32x2_split(t, ta, tb);
+    ya = xa == -INFINITY ? 0.0f : __uint_as_float(__float_as_uint(pa) + (__float_as_uint(ta) << 23));
+    yb = xb == -INFINITY ? 0.0f : __uint_as_float(__float_as_uint(pb) + (__float_as_uint(tb) << 23));
 }
 
 // grid = (ceil(n / 256), H, B); block = kFtThreads; dynamic shared memory kFtSmemBytes.
@@ -97,11 +197,10 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ft_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* Qs = sm;                                      // [2][128][64] SW128
     uint8_t* KV = Qs + kFtQ * kFtRows * kFaDim * 2;        // stage s: K at KV + 2s*tile, V at KV + (2s+1)*tile
-    uint8_t* Ps = KV + 4 * kFtTile;                        // [2][128][64] SW128
-    int64_t* tpos = reinterpret_cast<int64_t*>(Ps + kFtQ * kFtRows * kFtKeys * 2);  // [2][64] key positions
-    uint16_t* live_list = reinterpret_cast<uint16_t*>(tpos + 2 * kFtKeys);
+    int64_t* tpos = reinterpret_cast<int64_t*>(KV + 2 * kFtStages * kFtTile);  // [kFtStages][64] key positions
+    uint16_t* live_list = reinterpret_cast<uint16_t*>(tpos + kFtStages * kFtKeys);
     uint32_t* live_bits = reinterpret_cast<uint32_t*>(live_list + kFtMaxCacheTiles);
-    __shared__ uint64_t q_full, kv_full[2], kv_empty[2], s_full[kFtQ], p_full[kFtQ], pv_done[kFtQ];
+    __shared__ uint64_t q_full, kv_full[kFtStages], kv_empty[kFtStages], s_full[kFtQ], p_full[kFtQ], pv_done[kFtQ];
     __shared__ uint32_t tmem_base;
     __shared__ int s_nlive;
     __shared__ volatile int abort_flag;
@@ -116,7 +215,7 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
 
     if (threadIdx.x == 0) {
         mbar_init(&q_full, 1);
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < kFtStages; ++s) {
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
@@ -185,9 +284,9 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
                 tma_load_3d(Qs + size_t(k) * kFtRows * kFaDim * 2, &maps.q, 0, h, b * a.n + i0 + k * kFtRows, &q_full);
         }
         for (int t = 0; t < tiles && !abort_flag; ++t) {
-            const int s = t & 1;
+            const int s = t % kFtStages;
             bool ok = true;
-            if (lane == 0) ok = mbar_wait(&kv_empty[s], unsigned(((t >> 1) & 1) ^ 1), err);
+            if (lane == 0) ok = mbar_wait(&kv_empty[s], unsigned(((t / kFtStages) & 1) ^ 1), err);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) {
                 if (lane == 0) abort_flag = 1;
@@ -224,14 +323,14 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
             // S_k(u) = Q_k . K(u) into query tile k's S columns (K of tile u has landed: waited by the caller).
             auto issue_s = [&](int k, int u) {
                 const uint64_t dq = umma_desc_sw128(Qs + size_t(k) * kFtRows * kFaDim * 2);
-                const uint64_t dk = umma_desc_sw128(KV + size_t(2 * (u & 1)) * kFtTile);
+                const uint64_t dk = umma_desc_sw128(KV + size_t(2 * (u % kFtStages)) * kFtTile);
 #pragma unroll
                 for (int kk = 0; kk < kFaDim / 16; ++kk)
                     umma_bf16(tmem + uint32_t(k * kFtKeys), dq + 2 * kk, dk + 2 * kk, idesc_s, kk > 0);
                 umma_commit(&s_full[k]);
             };
             auto wait_kv = [&](int u) {
-                if (!mbar_wait(&kv_full[u & 1], unsigned((u >> 1) & 1), err)) return false;
+                if (!mbar_wait(&kv_full[u % kFtStages], unsigned((u / kFtStages) & 1), err)) return false;
                 tc_fence_after();
                 return true;
             };
@@ -244,19 +343,19 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
                 }
             }
             for (int t = 0; t < tiles && !abort_flag; ++t) {
-                const int s = t & 1;
+                const int s = t % kFtStages;
                 const uint64_t dv = umma_desc_sw128_mn(KV + size_t(2 * s + 1) * kFtTile);
                 bool next_ready = false;
                 for (int k = 0; k < kFtQ; ++k) {
-                    // Query tile k's softmax has written P_k(t) (and finished reading S_k(t)).
+                    // Query tile k's softmax has stored P_k(t) over S_k(t).
                     if (!mbar_wait(&p_full[k], unsigned(t & 1), err)) { abort_flag = 1; break; }
                     tc_fence_after();
-                    const uint64_t dp = umma_desc_sw128(Ps + size_t(k) * kFtRows * kFtKeys * 2);
+                    const uint32_t tP = tmem + uint32_t(k * kFtKeys);
                     const uint32_t tO = tmem + uint32_t(2 * kFtKeys + k * kFaDim);
 #pragma unroll
-                    for (int kk = 0; kk < kFtKeys / 16; ++kk)  // 16 keys per step: +32 B along P's rows, +2 KB down V
-                        umma_bf16(tO, dp + 2 * kk, dv + 128 * kk, idesc_o, t > 0 || kk > 0);
-                    umma_commit(&pv_done[k]);
+                    for (int kk = 0; kk < kFtKeys / 16; ++kk)  // 16 keys per step: 8 columns of P, +2 KB down V
+                        umma_bf16_ts(tO, tP + 8 * kk, dv + 128 * kk, idesc_o, t > 0 || kk > 0);
+                    if (t == tiles - 1) umma_commit(&pv_done[k]);
                     if (k == kFtQ - 1) umma_commit(&kv_empty[s]);
                     if (t + 1 < tiles) {
                         if (k == 0) {
@@ -280,33 +379,54 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
         const uint32_t lane_base = uint32_t(q * 32) << 16;
         const uint32_t tS = tmem + uint32_t(k * kFtKeys) + lane_base;
         const uint32_t tO = tmem + uint32_t(2 * kFtKeys + k * kFaDim) + lane_base;
-        uint8_t* prow = Ps + size_t(k) * kFtRows * kFtKeys * 2 + size_t(r) * 128;
         float m_run = -INFINITY, l_run = 0.f;
         for (int t = 0; t < tiles && !abort_flag; ++t) {
-            const int s = t & 1;
+            const int s = t % kFtStages;
             bool cached;
             const int j0 = tile_key0(t, cached);
-            if (!mbar_wait(&kv_full[s], unsigned((t >> 1) & 1), err) || !mbar_wait(&s_full[k], unsigned(t & 1), err)) {
+            const bool masked = cached || j0 + kFtKeys - 1 > ik0 || (a.window > 0 && j0 <= ik_last - a.window);
+            // S_k(t) has landed (and with it every earlier MMA, the last P_k.V included); the key positions of a
+            // masked tile come with its K/V stage.
+            if (!mbar_wait(&s_full[k], unsigned(t & 1), err) ||
+                (masked && !mbar_wait(&kv_full[s], unsigned((t / kFtStages) & 1), err))) {
                 abort_flag = 1;
                 break;
             }
             tc_fence_after();
-            const bool masked = cached || j0 + kFtKeys - 1 > ik0 || (a.window > 0 && j0 <= ik_last - a.window);
-            // Two passes over the S row (32 columns at a time keeps the registers low): the max, then P.
-            float mx = -INFINITY;
-#pragma unroll 1
-            for (int c = 0; c < 2; ++c) {
-                float v[32];
-                tmem_load32(tS + c * 32, v);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    if (masked) {
-                        const int64_t tj = tpos[s * kFtKeys + c * 32 + e];
-                        if (!(row_ok && tj >= 0 && tj <= ti && (a.window <= 0 || tj > ti - a.window))) v[e] = -INFINITY;
+            uint32_t sv[64];
+            tmem_load32_async(tS, sv);
+            tmem_load32_async(tS + 32, sv + 32);
+            tmem_wait_ld();
+            // Masked keys get s = -inf (so max ignores them and 2^-inf = 0). The test is hoisted out of the
+            // element loops: ring tiles compare slot positions, chunk tiles an index range.
+            if (masked) {
+                uint64_t vis = 0;  // bit e: key j0 + e visible to this row
+                if (cached) {
+#pragma unroll 4
+                    for (int e = 0; e < kFtKeys; ++e) {
+                        const int64_t tj = tpos[s * kFtKeys + e];
+                        if (row_ok && tj >= 0 && tj <= ti && (a.window <= 0 || tj > ti - a.window))
+                            vis |= 1ull << e;
                     }
-                    mx = fmaxf(mx, v[e]);
+                } else {
+                    // chunk key j0 + e is visible to row i iff i - window < j0 + e <= i: bits [lo, hi]
+                    const int hi = min(i - j0, kFtKeys - 1);
+                    const int lo = a.window > 0 ? max(i - a.window + 1 - j0, 0) : 0;
+                    vis = hi < lo ? 0ull : ((~0ull >> (63 - hi)) & (~0ull << lo));
                 }
+#pragma unroll
+                for (int e = 0; e < kFtKeys; ++e)
+                    if (!((vis >> e) & 1)) sv[e] = __float_as_uint(-INFINITY);
             }
+            float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int e = 0; e < kFtKeys; e += 8) {
+                mq[0] = fmax3(mq[0], __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
+                mq[1] = fmax3(mq[1], __uint_as_float(sv[e + 2]), __uint_as_float(sv[e + 3]));
+                mq[2] = fmax3(mq[2], __uint_as_float(sv[e + 4]), __uint_as_float(sv[e + 5]));
+                mq[3] = fmax3(mq[3], __uint_as_float(sv[e + 6]), __uint_as_float(sv[e + 7]));
+            }
+            const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
             // Lazy rescaling: the reference max moves only when the tile's max exceeds it by more than 8 (log2
             // domain), so P stays below 2^8 and most tiles leave O untouched; the sum uses the same reference, so the
             // result is unchanged.
@@ -315,57 +435,39 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
             const bool none = m_new == -INFINITY;
             const float corr = none ? 1.f : fast_exp2(m_run - m_new);
             const float neg = none ? 0.f : -m_new;
-            // The previous P_k.V must have finished before O_k is rescaled and P_k is overwritten.
-            if (t > 0) {
-                if (!mbar_wait(&pv_done[k], unsigned((t - 1) & 1), err)) { abort_flag = 1; break; }
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, corr != 1.f)) {
-#pragma unroll 1
-                    for (int c = 0; c < 2; ++c) {
-                        float ov[32];
-                        tmem_load32(tO + c * 32, ov);
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) ov[e] *= corr;
-                        tmem_store32(tO + c * 32, ov);
-                    }
-                }
-            }
+            // P = 2^(s * scale - m) (masked keys: 2^-inf = 0), as bf16 pairs over S's first 32 columns; the exponent
+            // arguments and the row sum in packed pairs (f32x2), four partial sums.
             float rs = 0.f;
+            uint32_t pw[32];
+#pragma unroll
+            for (int u = 0; u < kFtKeys / 2; ++u) {
+                const float xa = fmaf(__uint_as_float(sv[2 * u]), a.scale_log2, neg);
+                const float xb = fmaf(__uint_as_float(sv[2 * u + 1]), a.scale_log2, neg);
+                const bool poly = (u & 3) >= kFtPolyFrom;
+                const float pa = poly ? exp2_poly(xa) : fast_exp2(xa);
+                const float pb = poly ? exp2_poly(xb) : fast_exp2(xb);
+                rs += pa + pb;
+                pw[u] = pack_bf16(pa, pb);
+            }
+            tmem_store32u(tS, pw);
+            if (t > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll 1
-            for (int c = 0; c < 2; ++c) {
-                float v[32];
-                tmem_load32(tS + c * 32, v);
+                for (int c = 0; c < 2; ++c) {
+                    float ov[32];
+                    tmem_load32(tO + c * 32, ov);
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {  // 16-byte chunk ch = 4c + cc of the row (keys 8ch..8ch+7), swizzled
-                    uint32_t w4[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int e = cc * 8 + 2 * u;
-                        float pa = 0.f, pb = 0.f;
-                        bool va = true, vb = true;
-                        if (masked) {
-                            const int64_t ta = tpos[s * kFtKeys + c * 32 + e], tb = tpos[s * kFtKeys + c * 32 + e + 1];
-                            va = row_ok && ta >= 0 && ta <= ti && (a.window <= 0 || ta > ti - a.window);
-                            vb = row_ok && tb >= 0 && tb <= ti && (a.window <= 0 || tb > ti - a.window);
-                        }
-                        if (va) pa = fast_exp2(fmaf(v[e], a.scale_log2, neg));
-                        if (vb) pb = fast_exp2(fmaf(v[e + 1], a.scale_log2, neg));
-                        rs += pa + pb;
-                        w4[u] = pack_bf16(pa, pb);
-                    }
-                    const int ch = 4 * c + cc;
-                    *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    for (int e = 0; e < 32; ++e) ov[e] *= corr;
+                    tmem_store32(tO + c * 32, ov);
                 }
             }
             l_run = l_run * corr + rs;
             m_run = m_new;
-            fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[k]);
         }
         // Final: wait for the last P_k.V, then O / (l + sink term) for this row.
-        if (tiles > 0 && !abort_flag && mbar_wait(&pv_done[k], unsigned((tiles - 1) & 1), err)) {
+        if (tiles > 0 && !abort_flag && mbar_wait(&pv_done[k], 0, err)) {
             tc_fence_after();
             float ov[2][32];
             tmem_load32(tO, ov[0]);
