@@ -803,11 +803,12 @@ struct LargeExec {
                 fa.slots = mask_mode == kMaskSlots ? io.slots : nullptr;
                 fa.pos0 = mask_mode == kMaskSlots ? io.pos0 : nullptr;
                 if (mask_mode != kMaskSlots) fa.ctx = 0;
-                // CHROMA_B200_FLASH_TC=1 selects the tcgen05 flash kernel (two query tiles per CTA in ping-pong; correct,
-                // but still slower than the mma.sync one: the C4 prefill takes 79.5 vs 74.2 ms).
+                // The tcgen05 flash kernel (TMA tiles, both products on the tensor cores, P in TMEM) by default: one
+                // C4 layer's attention takes 333 us against 705 us for the mma.sync kernel, which
+                // CHROMA_B200_FLASH_TC=0 selects instead (kept as the cross-check of the tensor-core path).
                 static const bool tc_flash = [] {
                     const char* e = std::getenv("CHROMA_B200_FLASH_TC");
-                    return e && e[0] == '1';
+                    return !(e && e[0] == '0');
                 }();
                 if (tc_flash) {
                     // tcgen05 flash attention: Q, K, V tiles through TMA tensor maps.

@@ -67,8 +67,8 @@ def test_c4_slice_prefill_and_decode_match_oracle(gpu: None) -> None:
 
 
 def test_flash_prefill_chunks_cache_and_window_match_oracle(gpu: None) -> None:
-    """Long prefill chunks through the flash kernel: several 128-row query blocks, own key tiles below the diagonal
-    (mask-free), a second chunk that reads live ring-cache tiles, a windowed layer (layer 0, window 160), decode
+    """Long prefill chunks through the flash kernel (the tcgen05 one by default): several 256-row query blocks, own key
+    tiles below the diagonal (mask-free), a second chunk that reads live ring-cache tiles, a windowed layer (layer 0, window 160), decode
     steps in between and the ring wrapping. Steps whose oracle routing has a near-tie at the top-k boundary in some
     layer for the row whose logits are returned (helpers.near_tie) are held to the greedy token only."""
     cfg = dataclasses.replace(models.gpt_oss_20b, num_hidden_layers=2, hidden_size=1024, intermediate_size=1024,
@@ -130,13 +130,13 @@ def test_128_expert_routing_matches_oracle(gpu: None, record_property) -> None: 
     np.testing.assert_array_equal(np.argmax(logits[exact], -1), np.argmax(want[exact], -1))
 
 
-def test_tcgen05_flash_kernel_matches_oracle(gpu: None) -> None:
-    """The tcgen05 flash-attention kernel (opt-in, CHROMA_B200_FLASH_TC=1) through the same long-chunk case, in a
-    subprocess so the switch is read fresh."""
+def test_mma_sync_flash_kernel_matches_oracle(gpu: None) -> None:
+    """The mma.sync flash-attention kernel (CHROMA_B200_FLASH_TC=0; the tcgen05 kernel is the default) through the
+    same long-chunk case, in a subprocess so the switch is read fresh."""
     import os
     import subprocess
     import sys
 
     code = "import tests.test_gpu_large as t; t.test_flash_prefill_chunks_cache_and_window_match_oracle(None)"
-    env = dict(os.environ, CHROMA_B200_FLASH_TC="1")
+    env = dict(os.environ, CHROMA_B200_FLASH_TC="0")
     subprocess.run([sys.executable, "-c", code], check=True, env=env, cwd=str(Path(__file__).resolve().parents[1]))
