@@ -499,4 +499,291 @@ __global__ void __launch_bounds__(kFtThreads, 2) k_flash_prefill_tc(const __grid
     }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Flash decoding with TMA staging: the attention of k_flash_decode (n * G <= 16 query rows of one KV head against
+// the ring cache, split over the keys, mma.sync on the packed GQA rows), with the K/V tiles brought in by one
+// producer warp through the tensor maps into a kFdtStages-deep ring of mbarrier-tracked stages. The consumer warps
+// release a stage with one arrival each instead of a CTA barrier per tile, and the bytes in flight per CTA are the
+// ring's depth, not the loads its threads can issue. The M = 16 rows leave the 128-row tcgen05 tile mostly empty;
+// the products are a small share of this kernel, which streams the cache.
+//
+// grid = (B, KV, splits); block = kFdtThreads (warps 0-3 consumers, warp 4 producer); dynamic shared memory
+// kFdtSmemBytes: 4 CTAs per SM with 3 stages each (at C5's shape 65 us per layer against 78 us for the cp.async
+// kernel; 6 stages at 2 CTAs per SM took 91 us: each CTA's tiles go through its 4 consumer warps one after another,
+// so the tiles in flight per SM, not the bytes, set the pace). Each 64-key tile is 16 KB; tiles past the ring's end
+// read the tensor map's zero fill, keys outside the split or the chunk are masked through their positions (-1).
+// All waits are bounded.
+constexpr int kFdtStages = 3;
+constexpr int kFdtThreads = 160;
+constexpr int kFdtTile = kFdKeys * kFaDim * 2;  // 8 KB: one K or V tile
+constexpr size_t kFdtSmemBytes = 1024 + 2 * size_t(kFdtStages) * kFdtTile + size_t(kFdRows) * kFaDim * 2 +
+                                 size_t(kFdtStages) * kFdKeys * sizeof(int64_t);
+
+__global__ void __launch_bounds__(kFdtThreads, 4) k_flash_decode_tma(const __grid_constant__ FlashMaps maps,
+                                                                  const __nv_bfloat16* __restrict__ q, DecodeArgs a,
+                                                                  const __nv_bfloat16* __restrict__ sinks,
+                                                                  __nv_bfloat16* __restrict__ out, unsigned* err) {
+    extern __shared__ uint8_t fdt_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fdt_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* ring = sm;  // stage s: K at 2s tiles, V at 2s + 1 (128-byte swizzle, fa_swz order)
+    __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(ring + 2 * size_t(kFdtStages) * kFdtTile);
+    int64_t* ts0 = reinterpret_cast<int64_t*>(Qs + kFdRows * kFaDim);
+    __shared__ uint64_t full[kFdtStages], empty[kFdtStages];
+    __shared__ bool s_last;
+    __shared__ volatile int abort_flag;
+
+    const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int rows = a.n * a.G;  // real query rows (<= 16)
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kFdtStages; ++st) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], 4);  // the 4 consumer warps
+        }
+        abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&maps.kc);
+        prefetch_tensormap(&maps.vc);
+        prefetch_tensormap(&maps.kn);
+        prefetch_tensormap(&maps.vn);
+    }
+    pdl_wait();
+    pdl_trigger();
+    const int64_t p0 = a.pos0[b];
+    // Q rows: row r = i * G + gh is query row i of head kvh * G + gh (rows >= n * G are zero).
+    for (int e = threadIdx.x; e < kFdRows * 8; e += blockDim.x) {
+        const int r = e >> 3, c = (e & 7) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < rows) {
+            const int i = r / a.G, h = kvh * a.G + r % a.G;
+            v = *reinterpret_cast<const uint4*>(q + ((size_t(b) * a.n + i) * a.H + h) * kFaDim + c);
+        }
+        *reinterpret_cast<uint4*>(Qs + fa_swz(r, c)) = v;
+    }
+    __syncthreads();
+    const int j_begin = split * a.split_keys, j_end = min(a.ctx, j_begin + a.split_keys);
+    const int cache_tiles = j_end > j_begin ? (j_end - j_begin + kFdKeys - 1) / kFdKeys : 0;
+    const bool own = split == a.splits - 1;
+    const int tiles = cache_tiles + (own ? 1 : 0);  // n <= 16 < 64: the own rows fit one tile
+
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+
+    if (warp == 4) {
+        // ---- producer: positions by the warp's lanes, the two tiles by lane 0
+        for (int t = 0; t < tiles && !abort_flag; ++t) {
+            const int st = t % kFdtStages;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&empty[st], unsigned(((t / kFdtStages) & 1) ^ 1), err);
+            if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) {
+                if (lane == 0) abort_flag = 1;
+                break;
+            }
+            const bool cached = t < cache_tiles;
+            const int j0 = cached ? j_begin + t * kFdKeys : 0;
+            const int limit = cached ? j_end : a.n;
+            for (int c = lane; c < kFdKeys; c += 32) {
+                const int j = j0 + c;
+                ts0[st * kFdKeys + c] = j < limit ? (cached ? a.slots[size_t(b) * a.ctx + j] : p0 + j) : -1;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                uint8_t* Kd = ring + size_t(2 * st) * kFdtTile;
+                uint8_t* Vd = Kd + kFdtTile;
+                mbar_arrive_expect_tx(&full[st], 2 * kFdtTile);
+                if (cached) {
+                    tma_load_4d(Kd, &maps.kc, 0, kvh, j0, b, &full[st]);
+                    tma_load_4d(Vd, &maps.vc, 0, kvh, j0, b, &full[st]);
+                } else {
+                    tma_load_3d(Kd, &maps.kn, 0, kvh, b * a.n, &full[st]);
+                    tma_load_3d(Vd, &maps.vn, 0, kvh, b * a.n, &full[st]);
+                }
+            }
+        }
+    } else {
+        // ---- consumers: warp w takes keys [16w, 16w + 16) of every tile with its own online softmax
+        int64_t t_row[2];  // this thread's rows g and g + 8: their positions (-1 marks a padding row)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            const int r = g + 8 * rr;
+            t_row[rr] = r < rows ? p0 + r / a.G : -1;
+        }
+        uint32_t qf[4][4];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
+            const int col = kk * 16 + 8 * (lane >> 4);
+            ldsm_x4(qf[kk], Qs + fa_swz(row, col));
+        }
+        const int kw = warp * 16;
+        for (int t = 0; t < tiles && !abort_flag; ++t) {
+            const int st = t % kFdtStages;
+            if (!mbar_wait(&full[st], unsigned((t / kFdtStages) & 1), err)) {
+                abort_flag = 1;
+                break;
+            }
+            const __nv_bfloat16* Kb = reinterpret_cast<const __nv_bfloat16*>(ring + size_t(2 * st) * kFdtTile);
+            const __nv_bfloat16* Vb = Kb + kFdKeys * kFaDim;
+            const int64_t* ts = ts0 + st * kFdKeys;
+            float sc[2][4];
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                uint32_t kf[4];
+                const int key = kw + (lane & 7) + 8 * (lane >> 4);
+                const int col = kk * 16 + 8 * ((lane >> 3) & 1);
+                ldsm_x4(kf, Kb + fa_swz(key, col));
+                mma_bf16(sc[0], qf[kk], kf[0], kf[1]);
+                mma_bf16(sc[1], qf[kk], kf[2], kf[3]);
+            }
+            float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int rr = e >> 1;
+                    const int64_t tj = ts[kw + nt * 8 + 2 * t4 + (e & 1)];
+                    const int64_t ti = t_row[rr];
+                    const bool vis = ti >= 0 && tj >= 0 && tj <= ti && (a.window <= 0 || tj > ti - a.window);
+                    // The reference stores q.k in bf16 before scaling (gpt_oss.py:133-151 in a bf16 graph).
+                    sc[nt][e] = vis ? bf16_round(sc[nt][e]) : -INFINITY;
+                    mx[rr] = fmaxf(mx[rr], sc[nt][e]);
+                }
+            }
+            float corr[2], neg[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 1));
+                mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 2));
+                const float m_new = fmaxf(m_run[rr], mx[rr] * a.scale_log2);
+                const bool none = m_new == -INFINITY;
+                corr[rr] = none ? 1.f : fast_exp2(m_run[rr] - m_new);
+                neg[rr] = none ? 0.f : -m_new;
+                m_run[rr] = m_new;
+            }
+            uint32_t af[4];
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                float pv[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    pv[e] = fast_exp2(fmaf(sc[nt][e], a.scale_log2, neg[e >> 1]));
+                    rs[e >> 1] += pv[e];
+                }
+                af[nt * 2 + 0] = pack_bf16(pv[0], pv[1]);
+                af[nt * 2 + 1] = pack_bf16(pv[2], pv[3]);
+            }
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) l_run[rr] = l_run[rr] * corr[rr] + rs[rr];
+#pragma unroll
+            for (int nd = 0; nd < 8; ++nd) {
+                o[nd][0] *= corr[0];
+                o[nd][1] *= corr[0];
+                o[nd][2] *= corr[1];
+                o[nd][3] *= corr[1];
+            }
+#pragma unroll
+            for (int nd = 0; nd < 8; nd += 2) {
+                uint32_t vf[4];
+                const int key = kw + (lane & 7) + 8 * ((lane >> 3) & 1);
+                const int col = nd * 8 + 8 * (lane >> 4);
+                ldsm_x4_t(vf, Vb + fa_swz(key, col));
+                mma_bf16(o[nd], af, vf[0], vf[1]);
+                mma_bf16(o[nd + 1], af, vf[2], vf[3]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
+        }
+    }
+
+    __syncthreads();  // every tile consumed: the ring is free for the merge
+
+    // Merge the 4 consumer warps (shared memory reused: [warp][16 rows][64] outputs, then max and sum per warp and row).
+    float* wo = reinterpret_cast<float*>(ring);  // 4 x 16 x 64 floats = 16 KB
+    float* wm = wo + 4 * kFdRows * kFaDim;      // 4 x 16
+    float* wl = wm + 4 * kFdRows;               // 4 x 16
+    if (warp < 4) {
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            l_run[rr] += __shfl_xor_sync(0xffffffffu, l_run[rr], 1);
+            l_run[rr] += __shfl_xor_sync(0xffffffffu, l_run[rr], 2);
+        }
+#pragma unroll
+        for (int nd = 0; nd < 8; ++nd) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int r = g + 8 * (e >> 1), c = nd * 8 + 2 * t4 + (e & 1);
+                wo[(warp * kFdRows + r) * kFaDim + c] = o[nd][e];
+            }
+        }
+        if (t4 == 0) {
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                wm[warp * kFdRows + g + 8 * rr] = m_run[rr];
+                wl[warp * kFdRows + g + 8 * rr] = l_run[rr];
+            }
+        }
+    }
+    __syncthreads();
+    float* pp = a.part + ((size_t(b) * a.KV + kvh) * a.splits + split) * kFdRows * (2 + kFaDim);
+    if (threadIdx.x < 128) {  // thread -> (row, 8 columns): 16 rows x 8 column groups
+        const int r = threadIdx.x >> 3, c0 = (threadIdx.x & 7) * 8;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w * kFdRows + r]);
+        float L = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float mw = wm[w * kFdRows + r];
+            const float f = mw == -INFINITY ? 0.f : fast_exp2(mw - M);
+            L += wl[w * kFdRows + r] * f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc[c] += wo[(w * kFdRows + r) * kFaDim + c0 + c] * f;
+        }
+        if (c0 == 0) {
+            pp[r * (2 + kFaDim) + 0] = M;
+            pp[r * (2 + kFaDim) + 1] = L;
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) pp[r * (2 + kFaDim) + 2 + c0 + c] = acc[c];
+    }
+    // The last split CTA of this (sequence, KV head) merges the splits with the sink.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned* counter = a.counters + size_t(b) * a.KV + kvh;
+        const unsigned prev = atomicAdd(counter, 1u);
+        s_last = prev == unsigned(a.splits - 1);
+        if (s_last) *counter = 0u;
+    }
+    __syncthreads();
+    if (!s_last || threadIdx.x >= 128) return;
+    __threadfence();
+    const float* base = a.part + (size_t(b) * a.KV + kvh) * a.splits * kFdRows * (2 + kFaDim);
+    const int r = threadIdx.x >> 3, c0 = (threadIdx.x & 7) * 8;
+    if (r >= rows) return;
+    float M = -INFINITY;
+    for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, __ldcg(base + (size_t(sp) * kFdRows + r) * (2 + kFaDim)));
+    const int h = kvh * a.G + r % a.G, i = r / a.G;
+    const float sink = __bfloat162float(sinks[h]) * 1.4426950408889634f;
+    const float mf = fmaxf(M, sink);
+    float L = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int sp = 0; sp < a.splits; ++sp) {
+        const float* row = base + (size_t(sp) * kFdRows + r) * (2 + kFaDim);
+        const float ms = __ldcg(row);
+        const float f = ms == -INFINITY ? 0.f : exp2f(ms - mf);
+        L += __ldcg(row + 1) * f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[c] += __ldcg(row + 2 + c0 + c) * f;
+    }
+    const float inv = 1.0f / (L + exp2f(sink - mf));
+    __nv_bfloat16* orow = out + ((size_t(b) * a.n + i) * a.H + h) * kFaDim + c0;
+    *reinterpret_cast<uint4*>(orow) = make_uint4(pack_bf16(acc[0] * inv, acc[1] * inv), pack_bf16(acc[2] * inv, acc[3] * inv),
+                                                 pack_bf16(acc[4] * inv, acc[5] * inv), pack_bf16(acc[6] * inv, acc[7] * inv));
+}
+
 }  // namespace cb200

@@ -603,6 +603,18 @@ static bool is_large(const chroma_b200_desc& d) {
            d.intermediate % 64 == 0 && d.experts <= kGemmMaxGroups;
 }
 
+// Attention kernels at the large shapes: the TMA-staged ones (k_flash_prefill_tc on the tensor cores,
+// k_flash_decode_tma) by default; CHROMA_B200_FLASH_TC=0 selects the cp.async / mma.sync pair (k_flash_prefill,
+// k_flash_decode), kept as the cross-check. One C4 layer's prefill attention: 333 us against 705 us; one C5 layer's
+// decode attention: 65 us against 78 us.
+static bool tma_attention() {
+    static const bool on = [] {
+        const char* e = std::getenv("CHROMA_B200_FLASH_TC");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 struct LargeExec {
     const Model* m = nullptr;
     int B = 1, n = 1, ctx = 0, mask_mode = kMaskBuffer, window = 0, sms = 148, chunks = 1, key_chunk = 256, rows = 1;
@@ -644,9 +656,11 @@ struct LargeExec {
         // Flash decoding splits: about two CTAs per SM, whole 64-key tiles per split (at C5's 32 sequences x 8 KV heads
         // per GPU, 2 splits take 85 us per layer against 91 us for 4 and 98 us for 8: fewer, longer splits stream
         // better and merge less).
+        // The TMA-staged decode kernel runs 4 CTAs per SM: at most that many CTAs, so one wave.
         if (ctx > 0) {
             const int tiles = (ctx + kFdKeys - 1) / kFdKeys;
-            const int want = std::max(1, (sms * 2 + B * d.KV - 1) / (B * d.KV));
+            const int want = tma_attention() ? std::max(1, sms * 4 / (B * d.KV))
+                                             : std::max(1, (sms * 2 + B * d.KV - 1) / (B * d.KV));
             fd_splits = std::min(tiles, want);
             fd_split_keys = (tiles + fd_splits - 1) / fd_splits * kFdKeys;
             fd_splits = (ctx + fd_split_keys - 1) / fd_split_keys;
@@ -803,14 +817,7 @@ struct LargeExec {
                 fa.slots = mask_mode == kMaskSlots ? io.slots : nullptr;
                 fa.pos0 = mask_mode == kMaskSlots ? io.pos0 : nullptr;
                 if (mask_mode != kMaskSlots) fa.ctx = 0;
-                // The tcgen05 flash kernel (TMA tiles, both products on the tensor cores, P in TMEM) by default: one
-                // C4 layer's attention takes 333 us against 705 us for the mma.sync kernel, which
-                // CHROMA_B200_FLASH_TC=0 selects instead (kept as the cross-check of the tensor-core path).
-                static const bool tc_flash = [] {
-                    const char* e = std::getenv("CHROMA_B200_FLASH_TC");
-                    return !(e && e[0] == '0');
-                }();
-                if (tc_flash) {
+                if (tma_attention()) {
                     // tcgen05 flash attention: Q, K, V tiles through TMA tensor maps.
                     FlashMaps fm;
                     const uint64_t KVb = uint64_t(dm.KV) * 128;
@@ -859,6 +866,27 @@ struct LargeExec {
                 a.pos0 = io.pos0;
                 a.part = fd_part;
                 a.counters = counters.as<unsigned>();
+                if (tma_attention()) {
+                    FlashMaps fm;
+                    const uint64_t KVb = uint64_t(dm.KV) * 128;
+                    {
+                        const uint64_t dims[3] = {64, uint64_t(dm.KV), uint64_t(N)};
+                        const uint64_t st[2] = {128, KVb};
+                        const uint32_t box[3] = {64, 1, kFdKeys};
+                        fm.kn = bf16_map_nd(nk, 3, dims, st, box);
+                        fm.vn = bf16_map_nd(nv, 3, dims, st, box);
+                    }
+                    {
+                        const uint64_t dims[4] = {64, uint64_t(dm.KV), uint64_t(ctx), uint64_t(B)};
+                        const uint64_t st[3] = {128, KVb, uint64_t(L) * ctx * KVb};
+                        const uint32_t box[4] = {64, 1, kFdKeys, 1};
+                        fm.kc = bf16_map_nd(ck, 4, dims, st, box);
+                        fm.vc = bf16_map_nd(cv, 4, dims, st, box);
+                    }
+                    fm.q = fm.kn;  // unused
+                    launch(s, dim3(B, dm.KV, fd_splits), dim3(kFdtThreads), kFdtSmemBytes, k_flash_decode_tma, fm, q, a,
+                           w.sinks, attn, err);
+                } else
                 launch(s, dim3(B, dm.KV, fd_splits), dim3(kFdThreads), kFdSmemBytes, k_flash_decode, q, a, ck, cv,
                        static_cast<const bf16*>(nk), static_cast<const bf16*>(nv), w.sinks, attn);
             } else {
