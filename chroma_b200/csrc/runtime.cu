@@ -14,6 +14,7 @@
 #include "flash.cuh"
 #include "flash_tc.cuh"
 #include "decode_cluster.cuh"
+#include "fwd_cluster.cuh"
 #include "ep.cuh"
 #include "gemm.cuh"
 #include "gptoss.cuh"
@@ -1047,6 +1048,10 @@ struct GptExec {
     int dc_kpc = 0;
     size_t dc_smem = 0;
     void (*dc_kernel)(DecodeClusterArgs) = nullptr;
+    // Forward of up to 8 tokens of dev-sized fp32 uncached programs: every layer in one cluster launch
+    // (fwd_cluster.cuh).
+    bool cluster_fwd = false;
+    size_t fc_smem = 0;
     // Expert-grouped MoE for 16+ tokens of d = I = 128 programs (gptoss.cuh k_route_rows ... k_moe_combine_rows;
     // CHROMA_B200_PER_SLOT_MOE keeps k_moe_up / k_moe_down, whose results are the same bits).
     bool grouped_moe = false;
@@ -1147,6 +1152,77 @@ struct GptExec {
             g_ys = DevBuf(N * d.k * d.d * 4);
         }
         init_cluster_decode();
+        init_cluster_fwd();
+    }
+
+    // The forward cluster takes the uncached fp32 programs of up to 8 tokens at batch 1 whose widths fit its fixed
+    // work split (d = H*hd = I = 128, head_dim 16, QKV rows <= 2 per warp, one warp per (row, head), k <= 4,
+    // E <= 16) and whose layers are packed layer-major. CHROMA_B200_FWD_CLUSTER=0 keeps the per-layer kernels.
+    void init_cluster_fwd() {
+        const Dims& d = m->dm;
+        const int L = m->desc.layers;
+        const char* env = std::getenv("CHROMA_B200_FWD_CLUSTER");
+        if (env && env[0] == '0') return;
+        if (m->desc.storage != CHROMA_B200_FP32) return;
+        if (m->desc.kind != CHROMA_B200_GPTOSS_FORWARD && m->desc.kind != CHROMA_B200_GPTOSS_LAST) return;
+        if (mask_mode != kMaskCausal || ctx != 0 || B != 1 || n < 1 || n > kFcTok) return;
+        if (d.d != 128 || d.H * d.hd != 128 || d.I != 128 || d.hd != 16) return;
+        if ((d.H + 2 * d.KV) * d.hd > kDcRows1 * kDcWarps || n * d.H > kDcWarps) return;
+        if ((d.H + 2 * d.KV) * d.hd % 8 != 0) return;  // each CTA's 8-row QKV blocks are whole
+        if (d.k > kDcMaxK || d.E > kDcMaxE || d.E < d.k) return;
+        if (reinterpret_cast<uintptr_t>(m->weights->ptr) % 16 != 0) return;  // bulk L2 prefetch of each layer
+        for (int l = 0; l + 1 < L; ++l)
+            if (m->offsets.at(size_t(3 + 13 * (l + 1))) < m->offsets.at(size_t(3 + 13 * l))) return;
+        const FcLayout lay(d, L);
+        const size_t smem = size_t(lay.total) * 4;
+        if (smem + 1024 > 227 * 1024) return;
+        ClusterLaunch cl(nullptr, dim3(kDcC), dim3(kThreads), smem, kDcC, k_fwd_cluster<16>);
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, k_fwd_cluster<16>, &cl.cfg) != cudaSuccess || clusters < 1) {
+            cudaGetLastError();
+            return;
+        }
+        std::vector<LayerW<float>> lw(static_cast<size_t>(L));
+        std::vector<int> win(static_cast<size_t>(L));
+        for (int l = 0; l < L; ++l) {
+            lw[size_t(l)] = m->layer<float>(l);
+            win[size_t(l)] = m->layer_window[size_t(l)] != 0 ? window : 0;
+        }
+        dc_layers = DevBuf(lw.size() * sizeof(LayerW<float>));
+        dc_windows = DevBuf(win.size() * sizeof(int));
+        check(cudaMemcpy(dc_layers.p, lw.data(), dc_layers.bytes, cudaMemcpyHostToDevice), "cluster layer table");
+        check(cudaMemcpy(dc_windows.p, win.data(), dc_windows.bytes, cudaMemcpyHostToDevice), "cluster window table");
+        fc_smem = smem;
+        cluster_fwd = true;
+        // Beside the (L2-prefetching) cluster kernel, the side stream pulls the vocab matrix into L2.
+        if (!side) {
+            check(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking), "prefetch stream");
+            check(cudaEventCreateWithFlags(&fork_ev, cudaEventDisableTiming), "prefetch event");
+            check(cudaEventCreateWithFlags(&join_ev, cudaEventDisableTiming), "prefetch event");
+        }
+        prefetch_base = m->at(2);
+        prefetch_bytes = (size_t(d.V) * d.d * 4) & ~size_t(15);
+    }
+
+    void enqueue_cluster_fwd(cudaStream_t s) {
+        FwdClusterArgs a;
+        a.dm = m->dm;
+        a.L = m->desc.layers;
+        a.n = n;
+        a.layers = dc_layers.as<const LayerW<float>>();
+        a.windows = dc_windows.as<const int>();
+        a.emb = reinterpret_cast<const float*>(m->at(0));
+        a.final_norm = reinterpret_cast<const float*>(m->at(1));
+        a.inv_freq = m->inv_freq.as<const float>();
+        a.positions = io.positions;
+        a.tokens = io.tokens;
+        a.rows = io.rows;
+        a.routes = io.routes;
+        a.tf = tf;
+        a.keys = io.keys;
+        a.err = err;
+        ClusterLaunch cl(s, dim3(kDcC), dim3(kThreads), fc_smem, kDcC, k_fwd_cluster<16>);
+        check(cudaLaunchKernelEx(&cl.cfg, k_fwd_cluster<16>, a), "cluster forward launch");
     }
 
     // The cluster path takes a single new token of a cached fp32 program whose widths fit its fixed work split
@@ -1206,7 +1282,8 @@ struct GptExec {
         if (large_path) return large.launches;
         const int pre = side ? 1 : 0;
         const bool fused_or = grouped_moe && m->dm.H * m->dm.hd == 128 && m->dm.E <= 2 * kWarps;
-        return cluster_decode ? pre + 2 : pre + 1 + (grouped_moe ? (fused_or ? 6 : 7) : 5) * m->desc.layers + 2;
+        return (cluster_decode || cluster_fwd) ? pre + 2
+                                               : pre + 1 + (grouped_moe ? (fused_or ? 6 : 7) : 5) * m->desc.layers + 2;
     }
 
     void enqueue_cluster_decode(cudaStream_t s) {
@@ -1247,15 +1324,16 @@ struct GptExec {
         if (side) {  // fork: the prefetch runs beside the whole step and joins at its end
             check(cudaEventRecord(fork_ev, s), "prefetch fork");
             check(cudaStreamWaitEvent(side, fork_ev, 0), "prefetch fork");
-            if (cluster_decode) k_prefetch_l2_bulk<<<8, 256, 0, side>>>(prefetch_base, prefetch_bytes);
+            if (cluster_decode || cluster_fwd) k_prefetch_l2_bulk<<<8, 256, 0, side>>>(prefetch_base, prefetch_bytes);
             else k_prefetch_l2<<<64, 256, 0, side>>>(prefetch_base, prefetch_bytes);
             check(cudaGetLastError(), "prefetch launch");
             check(cudaEventRecord(join_ev, side), "prefetch join");
             ++launches;
         }
         if constexpr (std::is_same_v<T, float>) {
-            if (cluster_decode) {
-                enqueue_cluster_decode(s);
+            if (cluster_decode || cluster_fwd) {
+                if (cluster_decode) enqueue_cluster_decode(s);
+                else enqueue_cluster_fwd(s);
                 enqueue_vocab_t<T>(s);
                 launches += 2;
                 if (side) check(cudaStreamWaitEvent(s, join_ev, 0), "prefetch join");
@@ -1353,6 +1431,10 @@ struct GptExec {
         if constexpr (std::is_same_v<T, float>) {
             if (cluster_decode) {
                 enqueue_cluster_decode(s);
+                return;
+            }
+            if (cluster_fwd) {
+                enqueue_cluster_fwd(s);
                 return;
             }
         }

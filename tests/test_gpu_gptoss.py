@@ -105,6 +105,49 @@ def test_c1_repeated_calls_out_reuse_and_index_errors(gpu: None) -> None:
     np.testing.assert_allclose(program(noncontiguous), og.forward(*helpers.dev_oracle(), noncontiguous), **FP32)
 
 
+def test_c1_cluster_forward_matches_per_layer_kernels(gpu: None) -> None:
+    """The one-launch cluster forward (up to 8 tokens, batch 1, fp32) against the per-layer kernel chain
+    (CHROMA_B200_FWD_CLUSTER=0, in a subprocess) at 8 and 5 tokens: the same additions in the same order, so
+    identical logits and routes, bit for bit; and the same index error for an out-of-range id."""
+    rng = np.random.default_rng(81)
+    cases = {}
+    for n in (8, 5):
+        path = _TMP / f"dev_fwd{n}_cluster"
+        with chroma_b200.compile(torch.export.export(helpers.dev_model(), (torch.arange(n),)), path) as program:
+            tokens = rng.integers(0, models.dev.vocab_size, (3, n))
+            got, routes = [], []
+            for t in tokens:
+                got.append(np.asarray(program(t)))
+                routes.append(program.native.routes())
+            got, routes = np.stack(got), np.stack(routes)
+            assert 0 < program.native.launches <= 3, program.native.launches  # prefetch, cluster, vocab
+            with pytest.raises(IndexError):
+                program(np.full(n, models.dev.vocab_size, dtype=np.int64))
+            np.testing.assert_array_equal(np.asarray(program(tokens[0])), got[0])
+        np.save(_TMP / f"fwd{n}_cluster_tokens.npy", tokens)
+        cases[n] = (path, got, routes)
+    code = (
+        "import sys, numpy as np\n"
+        "from chroma_b200 import Program\n"
+        "with Program(sys.argv[1]) as p:\n"
+        "    toks = np.load(sys.argv[2])\n"
+        "    logits, routes = [], []\n"
+        "    for t in toks:\n"
+        "        logits.append(np.asarray(p(t)))\n"
+        "        routes.append(p.native.routes())\n"
+        "    np.savez(sys.argv[3], logits=np.stack(logits), routes=np.stack(routes), launches=p.native.launches)\n"
+    )
+    env = dict(os.environ, CHROMA_B200_FWD_CLUSTER="0", PYTHONPATH=str(ROOT))
+    for n, (path, got, routes) in cases.items():
+        out = _TMP / f"fwd{n}_per_layer.npz"
+        subprocess.run([sys.executable, "-c", code, str(path), str(_TMP / f"fwd{n}_cluster_tokens.npy"), str(out)],
+                       check=True, env=env)
+        ref = np.load(out)
+        assert int(ref["launches"]) > 8
+        np.testing.assert_array_equal(got.view(np.uint32), ref["logits"].view(np.uint32))
+        np.testing.assert_array_equal(routes, ref["routes"])
+
+
 def test_c2_decoder_matches_reference(gpu: None) -> None:
     g = golden("c2_decode")
     with dev_decoder() as dec:
