@@ -291,9 +291,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_fwd_cluster(FwdClusterArgs a) {
     // This warp's expert rows of layer l (P4's mlp1 pair gw and P5's mlp2 row gw of every expert) into shared
     // memory and its biases onto lanes e < E, issued a whole layer ahead (after P5 of layer l - 1): whichever
     // experts the routing picks, P4 and P5 then read nothing from L2.
-    float bg_l = 0.f, bl_l = 0.f, bd_l = 0.f;
+    float bg_l = 0.f, bl_l = 0.f, bd_l = 0.f, sink_l = 0.f;  // lane e: expert e's biases; lane h: head h's sink
+    int window_l = 0;
     auto stage_experts = [&](int l) {
         const LayerW<float>& w = lws[l];
+        if (lane < H) sink_l = w.sinks[lane];
+        window_l = a.windows[l];
         for (int e = 0; e < E; ++e) {
             const float* W1 = w.w1 + (size_t(e) * 2 * I + 2 * gw) * d + lane * 4;
             cp_async16(w1s + (2 * e) * 128 + lane * 4, W1);
@@ -312,7 +315,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_fwd_cluster(FwdClusterArgs a) {
     cluster_sync_all();  // every CTA runs and has armed its mbarriers before the first remote store
 
     for (int l = 0; l < a.L; ++l) {
-        const LayerW<float>& w = lws[l];
         if (l > 0) {
             sync(kFcXs, l - 1);
             if (threadIdx.x == 32 && l + 1 < a.L) dc_prefetch_layer(lws, l + 1, a.L, dm, rank);
@@ -358,19 +360,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_fwd_cluster(FwdClusterArgs a) {
         // ---- P2: one warp per (query row, head): k_attention's single-chunk arithmetic, key jj on lane jj
         if (gw < n * H) {
             const int i = gw / H, hq = gw % H, kvh = hq / G;
-            const int window = a.windows[l];
+            const int window = window_l;
             const float* qr = qkv + i * r1p + hq * HD;
             float s = -INFINITY;
             if (lane < n) {
                 const float* kr = qkv + lane * r1p + (H + kvh) * HD;
+                float qv[HD], kv[HD];  // both rows loaded before the FMA chain
+#pragma unroll
+                for (int e = 0; e < HD; e += 4) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(qr + e);
+                    const float4 k4 = *reinterpret_cast<const float4*>(kr + e);
+                    qv[e] = q4.x; qv[e + 1] = q4.y; qv[e + 2] = q4.z; qv[e + 3] = q4.w;
+                    kv[e] = k4.x; kv[e + 1] = k4.y; kv[e + 2] = k4.z; kv[e + 3] = k4.w;
+                }
                 float dot = 0.f;
 #pragma unroll
-                for (int e = 0; e < HD; ++e) dot = fmaf(qr[e], kr[e], dot);
+                for (int e = 0; e < HD; ++e) dot = fmaf(qv[e], kv[e], dot);
                 s = __fmul_rn(dot, dm.sm_scale);
                 if (!(lane <= i && (window <= 0 || i - lane < window))) s = -INFINITY;
             }
             const float mx = warp_max(s);
-            const float sink = w.sinks[hq];
+            const float sink = __shfl_sync(0xffffffffu, sink_l, hq);
             const float ref = fmaxf(mx, sink);
             float p = (lane < n && ref != -INFINITY) ? expf(s - ref) : 0.f;
             float lsum = warp_sum(p);
@@ -455,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fwd_cluster(FwdClusterArgs a) {
             float my_act = 0.f;
             cp_async_wait<0>();
             __syncwarp();
-            // Two experts per pass, so the two reduction chains overlap.
+            // Three experts per pass, so their reduction chains overlap.
             auto swiglu = [&](int e, float ag, float al) {
                 const float bg = __shfl_sync(0xffffffffu, bg_l, e), bl = __shfl_sync(0xffffffffu, bl_l, e);
                 if (my_e == e) {
@@ -474,15 +484,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_fwd_cluster(FwdClusterArgs a) {
                 um &= um - 1;
                 const int e1 = um ? __ffs(int(um)) - 1 : e0;
                 if (um) um &= um - 1;
-                float wg0[1][4], wl0[1][4], wg1[1][4], wl1[1][4];
+                const int e2 = um ? __ffs(int(um)) - 1 : e0;
+                if (um) um &= um - 1;
+                float wg0[1][4], wl0[1][4], wg1[1][4], wl1[1][4], wg2[1][4], wl2[1][4];
                 dc_read<1>(wg0, w1s + (2 * e0) * 128);
                 dc_read<1>(wl0, w1s + (2 * e0 + 1) * 128);
                 dc_read<1>(wg1, w1s + (2 * e1) * 128);
                 dc_read<1>(wl1, w1s + (2 * e1 + 1) * 128);
+                dc_read<1>(wg2, w1s + (2 * e2) * 128);
+                dc_read<1>(wl2, w1s + (2 * e2 + 1) * 128);
                 const float ag0 = fc_dot8(wg0, xn), al0 = fc_dot8(wl0, xn);
                 const float ag1 = fc_dot8(wg1, xn), al1 = fc_dot8(wl1, xn);
+                const float ag2 = fc_dot8(wg2, xn), al2 = fc_dot8(wl2, xn);
                 swiglu(e0, ag0, al0);
                 if (e1 != e0) swiglu(e1, ag1, al1);
+                if (e2 != e0) swiglu(e2, ag2, al2);
             }
             if (my_e >= 0) stg[(tj * kDcMaxK + tm) * kWarps + warp] = my_act;
         }
