@@ -399,6 +399,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
     const int commit_slot = int(t_i % a.ctx);
     if (a.commit_slots && rank == 0 && threadIdx.x == 0) a.commit_slots[commit_slot] = t_i;
 
+    // Layer l's attention sinks (lane h: head h) and window, fetched a layer ahead: read from L2 inside the
+    // attention phases they sat on its critical path.
+    float sink_l = lane < H ? lws[0].sinks[lane] : 0.f;
+    int window_l = a.windows[0];
     for (int l = 0; l < a.L; ++l) {
         const LayerW<float>& w = lws[l];
         if (l > 0) {
@@ -456,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
         {
             const float* Kl = Ks + size_t(l) * a.kpc * kvs;
             const float* Vl = Vs + size_t(l) * a.kpc * kvs;
-            const int window = a.windows[l];
+            const int window = window_l;
             float* prow = dsm + lay.prow + warp * 32;
             constexpr int groups = 32 / HD;
             const int g = lane / HD, dd = lane % HD;
@@ -521,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
         // Merge the kDcC partials of every head with its sink (the split-KV merge of k_attention), lane c holding
         // partial c's rescale factor.
         for (int hq = warp; hq < H; hq += kWarps) {
-            const float sink = w.sinks[hq];
+            const float sink = __shfl_sync(0xffffffffu, sink_l, hq);
             const float* ph = parts + hq * ps;
             const float mc = lane < kDcC ? ph[lane * H * ps] : -INFINITY;
             const float M = fmaxf(sink, warp_max(mc));
@@ -535,6 +539,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_cluster(DecodeClusterArg
                 if (lane < HD) o = fmaf(ph[c * H * ps + 2 + lane], e, o);
             }
             if (lane < HD) att[hq * HD + lane] = o / Lsum;
+        }
+        if (l + 1 < a.L) {
+            sink_l = lane < H ? lws[l + 1].sinks[lane] : 0.f;
+            window_l = a.windows[l + 1];
         }
         __syncthreads();
         // ---- P3: out-projection + bias + residual -> x2[]; then the next layer's P1-P3 rows
