@@ -62,6 +62,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--c4-only", action="store_true", help="run only the GPT-OSS-20B-shaped prefill measurement")
     ap.add_argument("--c4-layers", type=int, default=0, help="layers of the C4 model (0: all 24; fewer for profiling)")
     ap.add_argument("--decode-only", action="store_true", help="only the headline decode measurement (profiling)")
+    ap.add_argument("--fwd8-only", action="store_true", help="only the 8-token forward (C1) measurement (profiling)")
     ap.add_argument("--decode-batch", type=int, default=1, help="sequences of the --decode-only measurement")
     ap.add_argument("--skip-c5", action="store_true", help="skip the GPT-OSS-120B-shaped decode (multi-GPU runs)")
     ap.add_argument("--c5-only", action="store_true", help="run only the GPT-OSS-120B-shaped decode (needs >= 2 GPUs)")
@@ -598,6 +599,40 @@ def bench_c5(args: argparse.Namespace, max_over_ranks, barrier, rank: int, world
     }
 
 
+def measure_fwd8(fwd8, rng, V, args, flush, stream, reps, max_over_ranks):  # type: ignore[no-untyped-def]
+    """C1: the 8-token forward `Program(tokens[8])`, device time of one run (CUDA events around the program's
+    launch on `stream`, L2 flushed before each) and end to end through the public call; medians, ms."""
+    import torch
+
+    native = fwd8.native
+    tokens8 = rng.integers(0, V, 8).astype(np.int64)
+    torch.cuda.synchronize()
+    fwd8(tokens8)
+    f_ms = []
+    for i in range(args.warmup + reps):
+        flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        native.run_device(stream.cuda_stream)
+        e1.record(stream)
+        if i >= args.warmup:
+            f_ms.append((e0, e1))
+    native.check(stream.cuda_stream)
+    f_ms = [a.elapsed_time(b) for a, b in f_ms]
+    fe2e = []
+    for i in range(args.warmup + reps):
+        flush()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        fwd8(tokens8)  # the default call: the result array is the runtime's (page-locked) allocation
+        if i >= args.warmup:
+            fe2e.append(time.perf_counter() - t0)
+    fwd_dev_ms = max_over_ranks(statistics.median(f_ms))
+    fwd_e2e_ms = max_over_ranks(1e3 * statistics.median(fe2e))
+
+    return fwd_dev_ms, fwd_e2e_ms
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
@@ -683,6 +718,13 @@ def main() -> None:
     fwd8 = chroma_b200.compile_model(model, tmp / "fwd8", steps=8)
     rng = np.random.default_rng(1234 + rank)
     prompt = rng.integers(0, V, PREFILL)
+    if args.fwd8_only:
+        dev_ms, e2e_ms = measure_fwd8(fwd8, rng, V, args, flush, stream, max(3, min(50, args.steps)), max_over_ranks)
+        if rank == 0:
+            print(json.dumps({"fwd8_only": {"device_ms": dev_ms, "e2e_ms": e2e_ms}}), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
 
     def timed_device(bd: "chroma_b200.BatchDecoder", steps: int) -> list[float]:
         times = []
@@ -799,33 +841,7 @@ def main() -> None:
     b_e2e = world * B * bsteps / max_over_ranks(sum(be2e))
     bd64.close()
 
-    # ---- C1: 8-token forward, device and e2e
-    native = fwd8.native
-    ins, _ = native.buffers()
-    tokens8 = rng.integers(0, V, 8).astype(np.int64)
-    torch.cuda.synchronize()
-    fwd8(tokens8)
-    f_ms = []
-    for i in range(args.warmup + reps):
-        flush()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        native.run_device(stream.cuda_stream)
-        e1.record(stream)
-        if i >= args.warmup:
-            f_ms.append((e0, e1))
-    native.check(stream.cuda_stream)
-    f_ms = [a.elapsed_time(b) for a, b in f_ms]
-    fe2e = []
-    for i in range(args.warmup + reps):
-        flush()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        out8 = fwd8(tokens8)  # the default call: the result array is the runtime's (page-locked) allocation
-        if i >= args.warmup:
-            fe2e.append(time.perf_counter() - t0)
-    fwd_dev_ms = max_over_ranks(statistics.median(f_ms))
-    fwd_e2e_ms = max_over_ranks(1e3 * statistics.median(fe2e))
+    fwd_dev_ms, fwd_e2e_ms = measure_fwd8(fwd8, rng, V, args, flush, stream, reps, max_over_ranks)
 
     # ---- C3: the fused norm/SiLU micrograph, bf16 [16384, 4096] (HBM bound), device-resident inputs
     from chroma_b200._src.compiler import lower_micro, write_artifact
