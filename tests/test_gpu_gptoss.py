@@ -148,6 +148,26 @@ def test_c1_cluster_forward_matches_per_layer_kernels(gpu: None) -> None:
         np.testing.assert_array_equal(routes, ref["routes"])
 
 
+def test_c1_last_row_program_matches_forward_row(gpu: None) -> None:
+    """The UncachedTransformer variant (tokens[8], position[1] -> logits[1, V]) against the full forward's row at
+    that position, bit for bit (both on the cluster forward); negative positions wrap, out-of-range ones raise
+    IndexError and leave the program usable."""
+    model = models.make_dev_model(0)
+    tokens = np.random.default_rng(17).integers(0, models.dev.vocab_size, 8)
+    with chroma_b200.compile_model(model, _TMP / "last8", steps=8, last=True) as last, \
+            chroma_b200.compile_model(model, _TMP / "fwd8_rows", steps=8) as fwd:
+        full = np.asarray(fwd(tokens))
+        for pos in (7, 0, 3, -1, -8):
+            row = np.asarray(last(tokens, np.array([pos], np.int64)))
+            assert row.shape == (1, models.dev.vocab_size)
+            np.testing.assert_array_equal(row.view(np.uint32), full[pos % 8][None].view(np.uint32))
+        for bad in (8, -9):
+            with pytest.raises(IndexError):
+                last(tokens, np.array([bad], np.int64))
+        np.testing.assert_array_equal(np.asarray(last(tokens, np.array([2], np.int64))).view(np.uint32),
+                                      full[2][None].view(np.uint32))
+
+
 def test_c2_decoder_matches_reference(gpu: None) -> None:
     g = golden("c2_decode")
     with dev_decoder() as dec:
