@@ -17,6 +17,19 @@ enum : unsigned int { kErrIndex = 1u, kErrTimeout = 2u };
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// sigmoid(z) = 1 / (1 + exp(-z)) for a z that is a bf16 value, on the special-function unit: __expf and the
+// approximate reciprocal (rcp.approx.f32, full range) instead of expf and the correctly rounded division (the C3
+// micrograph was issue-bound on those two sequences). The result is only ever rounded to bf16, and for every one of
+// the 65,536 bf16 inputs (NaNs included) this form gives the same bf16 bits as bf16(1.0f / (1.0f + expf(-z))) on
+// the B200, checked exhaustively (__fdividef(1, .) in its place differs on z = -87.5, -88, -88.5, where the divisor
+// exceeds 2^126 and it returns 0).
+__device__ __forceinline__ float fast_sigmoid_bf16in(float z) {
+    const float den = __fadd_rn(1.0f, __expf(-z));
+    float r;
+    asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(den));
+    return r;
+}
+
 // Storage precision policy: Round<float> is the identity, Round<bf16> rounds to bf16 and back.
 template <typename T> struct Store;
 template <> struct Store<float> {

@@ -80,7 +80,7 @@ __device__ __forceinline__ float swiglu_pair(float acc_g, float acc_l, float bg,
     const float glu = fminf(hg, limit);
     const float lin = fminf(fmaxf(hl, -limit), limit);
     const float z = round_bf16(glu * alpha);
-    const float sg = round_bf16(1.0f / (1.0f + expf(-z)));
+    const float sg = round_bf16(fast_sigmoid_bf16in(z));  // z is a bf16 value: same bits as 1 / (1 + expf(-z))
     const float og = round_bf16(glu * sg);
     const float l1 = round_bf16(lin + 1.0f);
     return og * l1;

@@ -77,15 +77,13 @@ __global__ void __launch_bounds__(512) k_micro(const __nv_bfloat16* __restrict__
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             // Two elements at a time. A product of two bf16 values is exact in fp32, so the packed bf16
-            // multiplies (one rounding of the exact product) give the bits of "fp32 multiply, round to bf16";
-            // 1/v through the correctly rounded reciprocal equals the IEEE division 1.0f / v.
+            // multiplies (one rounding of the exact product) give the bits of "fp32 multiply, round to bf16".
             const float2 fx = __bfloat1622float2(px[i]);
             const __nv_bfloat162 y = __floats2bfloat162_rn(__fmul_rn(__fmul_rn(fx.x, inv), wv[2 * i]),
                                                            __fmul_rn(__fmul_rn(fx.y, inv), wv[2 * i + 1]));
             const __nv_bfloat162 z = __hmul2(y, pg[i]);
             const float2 fz = __bfloat1622float2(z);
-            const __nv_bfloat162 sg = __floats2bfloat162_rn(__frcp_rn(__fadd_rn(1.0f, expf(-fz.x))),
-                                                            __frcp_rn(__fadd_rn(1.0f, expf(-fz.y))));
+            const __nv_bfloat162 sg = __floats2bfloat162_rn(fast_sigmoid_bf16in(fz.x), fast_sigmoid_bf16in(fz.y));
             const float2 fb = __bfloat1622float2(__hmul2(__hmul2(z, sg), pu[i]));
             po[i] = __floats2bfloat162_rn(__fadd_rn(fb.x, fx.x), __fadd_rn(fb.y, fx.y));
         }
