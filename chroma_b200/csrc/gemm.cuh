@@ -55,6 +55,10 @@ struct GemmArgs {
     // argmax_key over each thread's columns of a tile; the caller zeroes the keys).
     unsigned long long* argmax_keys;
     int argmax_col_offset;  // added to the column index in the keys (a vocab shard's first global row)
+    // Narrow last column tile (single-CTA kernel): when the last column tile holds at most half of BN columns, its
+    // MMAs run at N = tail_n (those columns rounded up to 16) from a B tile of tail_n rows (the third tensor map), and
+    // these tiles are scheduled after every full-width tile so they even out the per-SM totals. 0: full width.
+    int tail_n;
     // Split-K (dense only): ksplit > 1 splits the K blocks over ksplit tiles whose raw fp32 sums go to
     // partial[ks][M][N]; k_gemm_splitk_epilogue then adds them in order and applies the epilogue.
     int ksplit;
@@ -205,7 +209,8 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& g, const flo
 
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_constant__ CUtensorMap map_a,
-                                                               const __grid_constant__ CUtensorMap map_b, GemmArgs g,
+                                                               const __grid_constant__ CUtensorMap map_b,
+                                                               const __grid_constant__ CUtensorMap map_bt, GemmArgs g,
                                                                unsigned* err) {
     constexpr int A_BYTES = kGemmBM * kGemmBK * 2;
     constexpr int B_BYTES = BN * kGemmBK * 2;
@@ -236,6 +241,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
         fence_barrier_init();
         prefetch_tensormap(&map_a);
         prefetch_tensormap(&map_b);
+        if (g.tail_n) prefetch_tensormap(&map_bt);
     }
     if (warp == 1) {
         tmem_alloc(&tmem_base, TMEM_COLS);
@@ -279,6 +285,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
     const int ksplit = g.ksplit > 1 ? g.ksplit : 1;
     const int mn_tiles = total_m * ntiles_n;
     const int total = mn_tiles * ksplit;
+    // Full-width tiles first (m-tile major), then one narrow tail tile per m-tile when g.tail_n is set.
+    const int nfull = g.tail_n ? ntiles_n - 1 : ntiles_n;
+    const int full_tiles = total_m * nfull;
+    auto is_tail = [&](int t) { return g.tail_n && t % mn_tiles >= full_tiles; };
     const int kb_per = (kblocks + ksplit - 1) / ksplit;
     const uint32_t tmem = tmem_base;
     // Split-K part of tile t: K blocks [kb_lo, kb_hi).
@@ -291,8 +301,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
     // Tile t -> (group, first row, row end, n0). Consecutive tiles share an m-tile (A reuse) and sweep the group's B.
     auto tile_of = [&](int t, int& grp, int& row0, int& row_end, int& n0) {
         t %= mn_tiles;
-        const int mt = t / ntiles_n;
-        n0 = (t % ntiles_n) * BN;
+        int mt;
+        if (t < full_tiles) {
+            mt = t / nfull;
+            n0 = (t % nfull) * BN;
+        } else {
+            mt = t - full_tiles;
+            n0 = nfull * BN;
+        }
         int lo = 0, hi = g.groups - 1;
         while (lo < hi) {  // last group with s_tiles[grp] <= mt
             const int mid = (lo + hi + 1) >> 1;
@@ -311,22 +327,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
                 int grp, row0, row_end, n0, kb_lo, kb_hi;
                 tile_of(t, grp, row0, row_end, n0);
                 k_range(t, kb_lo, kb_hi);
+                const bool tail = is_tail(t);
                 for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
                     const int s = it % kGemmStages;
                     if (!mbar_wait(&empty[s], unsigned(((it / kGemmStages) & 1) ^ 1), err)) { abort_flag = 1; break; }
                     uint8_t* sa = gsm + size_t(s) * STAGE;
-                    mbar_arrive_expect_tx(&full[s], STAGE);
+                    mbar_arrive_expect_tx(&full[s], tail ? A_BYTES + g.tail_n * kGemmBK * 2 : STAGE);
                     tma_load_2d(sa, &map_a, kb * kGemmBK, row0, &full[s]);
-                    tma_load_2d(sa + A_BYTES, &map_b, kb * kGemmBK, grp * g.N + n0, &full[s]);
+                    tma_load_2d(sa + A_BYTES, tail ? &map_bt : &map_b, kb * kGemmBK, grp * g.N + n0, &full[s]);
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_bf16(kGemmBM, BN);
+            constexpr uint32_t idesc_full = umma_idesc_bf16(kGemmBM, BN);
+            const uint32_t idesc_tail = umma_idesc_bf16(kGemmBM, g.tail_n);
             int it = 0, tile_it = 0;
             for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++tile_it) {
                 const int acc = tile_it & 1;
+                const uint32_t idesc = is_tail(t) ? idesc_tail : idesc_full;
                 if (!mbar_wait(&tmem_empty[acc], unsigned(((tile_it >> 1) & 1) ^ 1), err)) { abort_flag = 1; break; }
                 tc_fence_after();
                 const uint32_t d = tmem + uint32_t(acc * BN);
@@ -368,10 +387,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
             const int row = row0 + q * 32 + lane;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
+                const int col0 = n0 + c * 32;
+                if (col0 >= g.N) break;  // warp-uniform; a narrow tail tile wrote only its first tail_n columns
                 float v[32];
                 tmem_load32(taddr + uint32_t(c * 32), v);
-                const int col0 = n0 + c * 32;
-                if (col0 >= g.N) continue;
                 if (ksplit > 1) {  // raw partial sums; the split-K epilogue kernel finishes them
                     if (row < row_end) {
                         float* dst = g.partial + (size_t(t / mn_tiles) * g.M + row) * g.N + col0;

@@ -275,6 +275,12 @@ static void gemm_bf16(cudaStream_t s, const void* A, const void* B, GemmArgs g, 
     const CUtensorMap mb = bf16_tile_map(B, uint64_t(rows_b), uint64_t(g.K), narrow ? 32 : 256);
     (void)tile_scratch;  // tile prefix sums are computed in the kernel's prologue
     const int bn = narrow ? 32 : 256;
+    // A last column tile of at most 128 columns (N = 2,880: 64) runs as a narrow MMA after the full-width tiles
+    // (GemmArgs::tail_n). CHROMA_B200_GEMM_TAIL=0 keeps it at full width.
+    static const char* tail_env = std::getenv("CHROMA_B200_GEMM_TAIL");
+    const int ntiles_n = (g.N + bn - 1) / bn, tail_w = g.N - (ntiles_n - 1) * bn;
+    g.tail_n = !narrow && ntiles_n >= 2 && tail_w <= 128 && !(tail_env && tail_env[0] == '0') ? (tail_w + 15) / 16 * 16 : 0;
+    const CUtensorMap mbt = g.tail_n ? bf16_tile_map(B, uint64_t(rows_b), uint64_t(g.K), g.tail_n) : mb;
     int tiles = g.offsets ? sms : ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + bn - 1) / bn);
     g.ksplit = 1;
     if (!g.offsets && splitk_ws && (g.epi == kEpiStore || g.epi == kEpiResidual)) {
@@ -287,8 +293,8 @@ static void gemm_bf16(cudaStream_t s, const void* A, const void* B, GemmArgs g, 
     }
     const dim3 grid(unsigned(std::max(1, std::min(tiles, sms))));
     const size_t smem = size_t(kGemmStages) * (kGemmBM + bn) * kGemmBK * 2 + 4 * kGemmStageBytes + 1024;
-    if (narrow) launch(s, grid, dim3(kGemmThreads), smem, k_gemm_bf16<32>, ma, mb, g, err);
-    else launch(s, grid, dim3(kGemmThreads), smem, k_gemm_bf16<256>, ma, mb, g, err);
+    if (narrow) launch(s, grid, dim3(kGemmThreads), smem, k_gemm_bf16<32>, ma, mb, mbt, g, err);
+    else launch(s, grid, dim3(kGemmThreads), smem, k_gemm_bf16<256>, ma, mb, mbt, g, err);
     if (g.ksplit > 1)
         launch(s, dim3(unsigned((g.N + 511) / 512), unsigned(g.M)), dim3(256), 0, k_gemm_splitk_epilogue, g);
 }

@@ -160,3 +160,58 @@ def test_pair_kernel_grouped_ragged(gpu: None) -> None:
         if hi > lo:
             want2[lo:hi] = reference(got[lo:hi], w2[e * k : (e + 1) * k], b2[e], None, EXPERT)
     check(got2, want2)
+
+
+def test_narrow_tail_tiles_match_full_width(gpu: None, tmp_path: Path) -> None:
+    """A last column tile of at most 128 columns runs as a narrow MMA scheduled after the full-width tiles. The same
+    cases with that split (default) and without it (CHROMA_B200_GEMM_TAIL=0), each in a fresh process so the switch
+    is read anew: N = 2,880 (a 64-column tail), N = 300 (44 columns, MMA width 48), the grouped SwiGLU GEMM with
+    N = 5,760 (128) and the grouped expert GEMM with N = 2,880 over ragged groups. Both give the same bits, and the
+    split run matches the torch reference."""
+    import subprocess
+
+    root = str(Path(__file__).resolve().parents[1])
+    outs = {}
+    for mode in ("1", "0"):
+        path = tmp_path / f"tail{mode}.pt"
+        code = f"import tests.test_gpu_gemm as t; t._tail_body({str(path)!r})"
+        env = dict(os.environ, CHROMA_B200_GEMM_TAIL=mode)
+        subprocess.run([sys.executable, "-c", code], check=True, env=env, cwd=root)
+        outs[mode] = torch.load(path)
+    for name, (got, want) in outs["1"].items():
+        check(got.cuda(), want.cuda())
+        assert torch.equal(got, outs["0"][name][0]), f"{name}: narrow tail tiles differ from full-width ones"
+
+
+def _tail_body(path: str) -> None:
+    g = torch.Generator(device="cuda").manual_seed(9)
+    res: dict[str, tuple[torch.Tensor, torch.Tensor]] = {}
+    for m, n, k in [(1200, 2880, 2880), (333, 300, 4096)]:
+        a = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+        b = (torch.randn(n, k, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        bias = torch.randn(n, generator=g, device="cuda").to(torch.bfloat16)
+        r = torch.randn(m, n, generator=g, device="cuda").to(torch.bfloat16)
+        res[f"store{m}"] = (gemm(a, b, bias), reference(a, b, bias, None, STORE))
+        res[f"residual{m}"] = (gemm(a, b, bias, r, RESIDUAL), reference(a, b, bias, r, RESIDUAL))
+    E, k, i2 = 8, 2880, 5760
+    counts = [0, 130, 1, 257, 0, 64, 500, 7]
+    offsets = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    m = int(offsets[-1])
+    off = torch.from_numpy(offsets).cuda()
+    a = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    w1 = (torch.randn(E * i2, k, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    b1 = torch.randn(E, i2, generator=g, device="cuda").to(torch.bfloat16)
+    h = gemm(a, w1, b1, epi=SWIGLU, groups=E, offsets=off, n=i2)
+    w2 = (torch.randn(E * k, i2 // 2, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    b2 = torch.randn(E, k, generator=g, device="cuda").to(torch.bfloat16)
+    y = gemm(h, w2, b2, epi=EXPERT, groups=E, offsets=off, n=k)
+    want_h = torch.empty(m, i2 // 2, device="cuda")
+    want_y = torch.empty(m, k, device="cuda")
+    for e in range(E):
+        lo, hi = int(offsets[e]), int(offsets[e + 1])
+        if hi > lo:
+            want_h[lo:hi] = reference(a[lo:hi], w1[e * i2 : (e + 1) * i2], b1[e], None, SWIGLU)
+            want_y[lo:hi] = reference(h[lo:hi], w2[e * k : (e + 1) * k], b2[e], None, EXPERT)
+    res["swiglu"] = (h, want_h)
+    res["expert"] = (y, want_y)
+    torch.save({name: (got.cpu(), want.cpu()) for name, (got, want) in res.items()}, path)
