@@ -32,6 +32,7 @@ enum GemmEpi : int {
     kEpiResidual = 1, // C = round(R[row] + round(acc + bias))            (linear + residual, gpt_oss.py:209)
     kEpiSwiglu = 2,   // C[row, p] = swiglu(round(round(acc)+b) pairs)    (mlp1 + SwiGLU, gpt_oss.py:253-254)
     kEpiExpert = 3,   // C = round(round(acc) + bias[g])                   (mlp2 einsum + bias, gpt_oss.py:259-260)
+    kEpiRope = 4,     // QKV + RoPE: q heads (C) and new K rows rotated, new V rows copied (gpt_oss.py:44-54, 189-202)
 };
 
 struct GemmArgs {
@@ -59,6 +60,13 @@ struct GemmArgs {
     // MMAs run at N = tail_n (those columns rounded up to 16) from a B tile of tail_n rows (the third tensor map), and
     // these tiles are scheduled after every full-width tile so they even out the per-SM totals. 0: full width.
     int tail_n;
+    // kEpiRope (head_dim 64, single-CTA kernel): C is q [M][rope_H * 64]; output heads [rope_H, rope_H + rope_KV) go
+    // rotated to rope_k and the next rope_KV heads unrotated to rope_v (rows of rope_KV * 64); rope_cs[row * 32 + j]
+    // holds the rounded (cos, sin) of the row's position for frequency j.
+    const float2* rope_cs;
+    __nv_bfloat16* rope_k;
+    __nv_bfloat16* rope_v;
+    int rope_H, rope_KV;
     // Split-K (dense only): ksplit > 1 splits the K blocks over ksplit tiles whose raw fp32 sums go to
     // partial[ks][M][N]; k_gemm_splitk_epilogue then adds them in order and applies the epilogue.
     int ksplit;
@@ -93,8 +101,8 @@ __device__ __forceinline__ float swiglu_pair(float acc_g, float acc_l, float bg,
 // Row-per-thread packed bf16 words -> stage -> coalesced 16-byte stores of rows [row_base, row_end).
 // CHUNKS = 16-byte chunks per row (4 = 32 columns, 2 = 16 SwiGLU outputs).
 template <int CHUNKS>
-__device__ __forceinline__ void stage_store(const GemmArgs& g, const uint32_t (&w)[16], int row_base, int row_end,
-                                            int out_col, uint8_t* stage) {
+__device__ __forceinline__ void stage_store(__nv_bfloat16* C, int ldc, const uint32_t (&w)[16], int row_base,
+                                            int row_end, int out_col, uint8_t* stage) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int c = 0; c < CHUNKS; ++c)
@@ -104,10 +112,91 @@ __device__ __forceinline__ void stage_store(const GemmArgs& g, const uint32_t (&
     for (int pass = 0; pass < CHUNKS; ++pass) {
         const int r = pass * (32 / CHUNKS) + lane / CHUNKS, c = lane % CHUNKS;
         if (row_base + r < row_end)
-            *reinterpret_cast<uint4*>(g.C + size_t(row_base + r) * g.ldc + out_col + 8 * c) =
+            *reinterpret_cast<uint4*>(C + size_t(row_base + r) * ldc + out_col + 8 * c) =
                 *reinterpret_cast<const uint4*>(stage + stage_off(r, c));
     }
     __syncwarp();
+}
+
+template <int CHUNKS>
+__device__ __forceinline__ void stage_store(const GemmArgs& g, const uint32_t (&w)[16], int row_base, int row_end,
+                                            int out_col, uint8_t* stage) {
+    stage_store<CHUNKS>(g.C, g.ldc, w, row_base, row_end, out_col, stage);
+}
+
+// kEpiRope, one 64-wide head of an epilogue warp's 32 rows: `lo` and `hi` hold the accumulator columns [col0, col0 +
+// 32) and [col0 + 32, col0 + 64) of row (row_base + lane). The values are rounded with the bias as in kEpiStore (the
+// fused QKV linear), then q and K heads are rotated pairwise (lo[j], hi[j]) with the row's (cos, sin) of frequency j,
+// each product and the sum rounded to bf16 as in k_rope_split; V heads pass unrotated. Stores go through `stage`.
+__device__ __forceinline__ void gemm_rope_head(const GemmArgs& g, float (&lo)[32], float (&hi)[32],
+                                               const __nv_bfloat16* bias, int row_base, int row_end, int col0,
+                                               uint8_t* stage) {
+    const int lane = threadIdx.x & 31;
+    const int head = col0 >> 6;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        float bl[8], bh[8];
+        if (bias) {
+            const uint4 ul = __ldg(reinterpret_cast<const uint4*>(bias + col0) + c);
+            const uint4 uh = __ldg(reinterpret_cast<const uint4*>(bias + col0 + 32) + c);
+            const __nv_bfloat162* hl = reinterpret_cast<const __nv_bfloat162*>(&ul);
+            const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&uh);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 fl = __bfloat1622float2(hl[j]), fh = __bfloat1622float2(hh[j]);
+                bl[2 * j] = fl.x;
+                bl[2 * j + 1] = fl.y;
+                bh[2 * j] = fh.x;
+                bh[2 * j + 1] = fh.y;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) bl[j] = bh[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            lo[8 * c + j] = round_bf16(lo[8 * c + j] + bl[j]);
+            hi[8 * c + j] = round_bf16(hi[8 * c + j] + bh[j]);
+        }
+    }
+    if (head < g.rope_H + g.rope_KV) {
+        const int row = min(row_base + lane, row_end - 1);  // rows past the end read a valid row and store nothing
+        const float4* cs = reinterpret_cast<const float4*>(g.rope_cs + size_t(row) * 32);
+#pragma unroll
+        for (int p = 0; p < 16; ++p) {
+            const float4 v = __ldg(cs + p);  // (cos, sin) of frequencies 2p and 2p + 1
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int j = 2 * p + u;
+                const float c = u ? v.z : v.x, sn = u ? v.w : v.y;
+                const float l = lo[j], h = hi[j];
+                lo[j] = round_bf16(__fsub_rn(round_bf16(__fmul_rn(l, c)), round_bf16(__fmul_rn(h, sn))));
+                hi[j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(h, c)), round_bf16(__fmul_rn(l, sn))));
+            }
+        }
+    }
+    __nv_bfloat16* dst;
+    int ldc, col;
+    if (head < g.rope_H) {
+        dst = g.C;
+        ldc = g.ldc;
+        col = head * 64;
+    } else if (head < g.rope_H + g.rope_KV) {
+        dst = g.rope_k;
+        ldc = g.rope_KV * 64;
+        col = (head - g.rope_H) * 64;
+    } else {
+        dst = g.rope_v;
+        ldc = g.rope_KV * 64;
+        col = (head - g.rope_H - g.rope_KV) * 64;
+    }
+    uint32_t w[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(lo[2 * j], lo[2 * j + 1]);
+    stage_store<4>(dst, ldc, w, row_base, row_end, col, stage);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(hi[2 * j], hi[2 * j + 1]);
+    stage_store<4>(dst, ldc, w, row_base, row_end, col + 32, stage);
 }
 
 // One 32-row x 32-column accumulator chunk of an epilogue warp: `v` holds row (row_base + lane), columns
@@ -385,6 +474,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
             const uint32_t taddr = tmem + uint32_t(acc * BN) + (uint32_t(q * 32) << 16);
             unsigned long long best = 0ull;
             const int row = row0 + q * 32 + lane;
+            if constexpr (BN % 64 == 0) {
+                if (g.epi == kEpiRope) {  // whole heads: column chunk pairs
+#pragma unroll 1
+                    for (int c = 0; c < BN / 32; c += 2) {
+                        const int col0 = n0 + c * 32;
+                        if (col0 >= g.N) break;
+                        float lo[32], hi[32];
+                        tmem_load32(taddr + uint32_t(c * 32), lo);
+                        tmem_load32(taddr + uint32_t(c * 32 + 32), hi);
+                        gemm_rope_head(g, lo, hi, bias, row0 + q * 32, row_end, col0, stage);
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+                    continue;
+                }
+            }
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 const int col0 = n0 + c * 32;

@@ -4,7 +4,8 @@
 //
 //   k_embed_bf16    embedding rows -> residual stream x                       (gpt_oss.py:304-306)
 //   k_rms_bf16      x -> bf16(x * rsqrt(mean(x^2) + eps) * w)                 (gpt_oss.py:30-41)
-//   k_rope_split    fused QKV output -> q (RoPE), new K rows (RoPE), new V rows (gpt_oss.py:44-54, 189-202)
+//   k_rope_split    fused QKV output -> q (RoPE), new K rows (RoPE), new V rows (gpt_oss.py:44-54, 189-202); where
+//                   the QKV GEMM has no split-K, its kEpiRope epilogue does this instead from k_rope_table's pairs
 //   k_route_fused   norm -> gate logits -> top-k experts (sorted, lowest index on ties) + softmax weights, and the
 //                   per-expert counts (gpt_oss.py:243-247)
 //   k_route_offsets / k_route_scatter
@@ -105,6 +106,19 @@ __global__ void __launch_bounds__(256) k_rope_split(const bf16* __restrict__ qkv
         *reinterpret_cast<__nv_bfloat162*>(dst + j) = __floats2bfloat162_rn(o1[0], o1[1]);
         *reinterpret_cast<__nv_bfloat162*>(dst + j + half) = __floats2bfloat162_rn(o2[0], o2[1]);
     }
+}
+
+// (cos, sin) of every token's position for the QKV GEMM's RoPE epilogue (kEpiRope), once per forward: cs[t * half + j]
+// = the pair k_rope_split computes for token t and frequency j, rounded the same way.
+__global__ void k_rope_table(const float* __restrict__ positions, const float* __restrict__ inv_freq, float conc,
+                             int ntok, int half, float2* __restrict__ cs) {
+    pdl_wait();
+    pdl_trigger();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= ntok * half) return;
+    float sn, c;
+    sincosf(__fmul_rn(positions[i / half], inv_freq[i % half]), &sn, &c);
+    cs[i] = make_float2(bf16_round(__fmul_rn(c, conc)), bf16_round(__fmul_rn(sn, conc)));
 }
 
 // One warp per token: gate logits [N][E] (bf16, from the tensor-core gate GEMM) -> sorted top-k experts, softmax

@@ -255,6 +255,11 @@ static void gemm_bf16(cudaStream_t s, const void* A, const void* B, GemmArgs g, 
     if (g.K % 8) throw ValueError("GEMM K must be a multiple of 8");
     if (g.epi == kEpiSwiglu && g.N % 32) throw ValueError("SwiGLU epilogue needs N a multiple of 32");
     const bool narrow = g.N <= 32;
+    if (g.epi == kEpiRope && (narrow || g.N % 64 || g.ldc % 8 || g.rope_KV < 1 || g.offsets ||
+                              ((reinterpret_cast<uintptr_t>(g.C) | reinterpret_cast<uintptr_t>(g.rope_k) |
+                                reinterpret_cast<uintptr_t>(g.rope_v) | reinterpret_cast<uintptr_t>(g.bias) |
+                                reinterpret_cast<uintptr_t>(g.rope_cs)) & 15)))
+        throw ValueError("RoPE epilogue needs whole 64-wide heads, a dense GEMM and 16-byte aligned outputs");
     const CUtensorMap ma = bf16_tile_map(A, uint64_t(rows_a), uint64_t(g.K), kGemmBM);
     // The CTA-pair kernel (256 x 256 tiles over two SMs, two thirds of the operand bytes per SM) measured faster only
     // for the grouped SwiGLU GEMM of the prefill MoE (0.93 vs 0.99 ms at 32,768 x 5,760 x 2,880); the single-CTA
@@ -262,7 +267,7 @@ static void gemm_bf16(cudaStream_t s, const void* A, const void* B, GemmArgs g, 
     static const char* pair_env = std::getenv("CHROMA_B200_PAIR_GEMM");
     const bool pair_auto = g.offsets && g.epi == kEpiSwiglu && rows_a >= 8192;
     const bool pair_on = pair_env ? pair_env[0] == '1' : pair_auto;
-    if (pair_on && !narrow && sms >= 2) {
+    if (pair_on && !narrow && sms >= 2 && g.epi != kEpiRope) {
         const int pair_tiles = g.offsets ? sms : ((g.M + kPairBM - 1) / kPairBM) * ((g.N + kPairBN - 1) / kPairBN);
         if (g.offsets ? rows_a >= 8192 : (g.M >= 1024 && pair_tiles * 2 >= sms)) {
             const CUtensorMap mb2 = bf16_tile_map(B, uint64_t(rows_b), uint64_t(g.K), 128);
@@ -744,10 +749,25 @@ struct LargeExec {
     };
     static FlagWait ep_wait(const EpArgs& a, const unsigned* flags) { return {flags, a.world, a.epoch, a.timeout_ns}; }
 
+    // Outputs of the QKV GEMM's RoPE epilogue (kEpiRope): (cos, sin) table, new K and V rows, head counts.
+    struct RopeOut {
+        const float2* cs;
+        bf16* k;
+        bf16* v;
+        int H, KV;
+    };
+
     void gemm(cudaStream_t s, const bf16* A, int M, const bf16* W, int N, int K, int epi, const bf16* bias, bf16* C,
               int ldc, const bf16* residual, int groups, const int* offs, unsigned* err, const FlagWait* wait = nullptr,
-              unsigned long long* argmax_keys = nullptr, int argmax_col_offset = 0) {
+              unsigned long long* argmax_keys = nullptr, int argmax_col_offset = 0, const RopeOut* rope = nullptr) {
         GemmArgs g{};
+        if (rope) {
+            g.rope_cs = rope->cs;
+            g.rope_k = rope->k;
+            g.rope_v = rope->v;
+            g.rope_H = rope->H;
+            g.rope_KV = rope->KV;
+        }
         g.argmax_keys = argmax_keys;
         g.argmax_col_offset = argmax_col_offset;
         if (wait) {  // A arrives from the other ranks: wait for their flags in the prologue
@@ -770,7 +790,7 @@ struct LargeExec {
         g.groups = groups;
         g.offsets = offs;
         gemm_bf16(s, A, W, g, M, groups * N, tiles, sms, err, splitk_ws, splitk_bytes);
-        launches += offs == nullptr && splitk_choice(M, N, K, N <= 32 ? 32 : 256, sms) > 1 ? 2 : 1;
+        launches += offs == nullptr && epi != kEpiRope && splitk_choice(M, N, K, N <= 32 ? 32 : 256, sms) > 1 ? 2 : 1;
     }
 
     void enqueue(cudaStream_t s, const GptIO& io, unsigned* err) {
@@ -784,6 +804,18 @@ struct LargeExec {
         // CHROMA_B200_NO_FLASH selects the split-KV SIMT attention for every chunk (a cross-check of the two kernels).
         static const bool no_flash = std::getenv("CHROMA_B200_NO_FLASH") != nullptr;
         const bool flash = !no_flash && n >= 16 && mask_mode != kMaskBuffer && ctx <= kFaMaxCacheTiles * kFaKeys;
+        // RoPE in the QKV GEMM's epilogue (no k_rope_split launch, no re-read of the QKV output) where that GEMM runs
+        // without split-K; the (cos, sin) table of this forward's positions then lives in the unused QKV buffer.
+        // CHROMA_B200_ROPE_EPILOGUE=0 keeps the separate kernel.
+        static const char* rope_env = std::getenv("CHROMA_B200_ROPE_EPILOGUE");
+        const bool rope_fused = !(rope_env && rope_env[0] == '0') && dm.hd == 64 &&
+                                splitk_choice(N, heads, dm.d, 256, sms) == 1;
+        const float2* rope_cs = reinterpret_cast<const float2*>(qkv);
+        if (rope_fused) {
+            launch(s, dim3(unsigned((N * (dm.hd / 2) + 255) / 256)), dim3(256), 0, k_rope_table, io.positions,
+                   m->inv_freq.as<const float>(), dm.conc, N, dm.hd / 2, reinterpret_cast<float2*>(qkv));
+            ++launches;
+        }
         for (int l = 0; l < L; ++l) {
             const LayerW<bf16> w = m->layer<bf16>(l);
             bf16* nk;
@@ -805,9 +837,15 @@ struct LargeExec {
                 launch(s, dim3(N), dim3(256), 0, k_rms_bf16, x, dm.d, dm.eps, w.attn_norm, xn);
                 ++launches;
             }
-            gemm(s, xn, N, w.qkv_w, heads, dm.d, kEpiStore, w.qkv_b, qkv, heads, nullptr, 1, nullptr, err);
-            launch(s, dim3(N), dim3(256), 0, k_rope_split, qkv, dm.H, dm.KV, dm.hd, io.positions,
-                   m->inv_freq.as<const float>(), dm.conc, q, nk, nv);
+            if (rope_fused) {
+                const RopeOut ro{rope_cs, nk, nv, dm.H, dm.KV};
+                gemm(s, xn, N, w.qkv_w, heads, dm.d, kEpiRope, w.qkv_b, q, dm.H * dm.hd, nullptr, 1, nullptr, err,
+                     nullptr, nullptr, 0, &ro);
+            } else {
+                gemm(s, xn, N, w.qkv_w, heads, dm.d, kEpiStore, w.qkv_b, qkv, heads, nullptr, 1, nullptr, err);
+                launch(s, dim3(N), dim3(256), 0, k_rope_split, qkv, dm.H, dm.KV, dm.hd, io.positions,
+                       m->inv_freq.as<const float>(), dm.conc, q, nk, nv);
+            }
             const bool windowed = m->layer_window[size_t(l)] != 0;
             const int win = mask_mode == kMaskSlots ? (windowed ? window : ctx) : (windowed ? window : 0);
             if (flash) {
@@ -954,7 +992,7 @@ struct LargeExec {
                        static_cast<const float*>(rw), dm.k, dm.d, x, ex);
                 launches += 3;
             }
-            launches += 3;
+            launches += rope_fused ? 2 : 3;
         }
         launch(s, dim3(rows), dim3(256), 0, k_norm_rows, x, rows, io.rows, n, reinterpret_cast<const float*>(m->at(1)),
                dm.d, dm.eps, tf32, tf16, io.keys, err);

@@ -140,3 +140,52 @@ def test_mma_sync_flash_kernel_matches_oracle(gpu: None) -> None:
     code = "import tests.test_gpu_large as t; t.test_flash_prefill_chunks_cache_and_window_match_oracle(None)"
     env = dict(os.environ, CHROMA_B200_FLASH_TC="0")
     subprocess.run([sys.executable, "-c", code], check=True, env=env, cwd=str(Path(__file__).resolve().parents[1]))
+
+
+def _rope_case(fwd: str, pre: str, dec: str, tokens_path: str, out: str) -> None:
+    """Forward of 512 tokens (logits of every row, routes, launch count) and a 512-token prefill + 3 decode steps
+    through the programs at the given paths; results saved to `out`."""
+    tokens = np.load(tokens_path)
+    with chroma_b200.Program(fwd) as p:
+        logits = np.asarray(p(tokens[:512]), np.float32)
+        routes = p.native.routes()
+        launches = p.native.launches
+    with chroma_b200.Decoder(chroma_b200.Program(pre), chroma_b200.Program(dec)) as d:
+        steps = [np.asarray(d.append(tokens[:512]), np.float32)]
+        steps += [np.asarray(d.append([int(t)]), np.float32) for t in tokens[512:]]
+    np.savez(out, logits=logits, routes=routes, steps=np.concatenate(steps), launches=launches)
+
+
+def test_rope_epilogue_matches_separate_kernel(gpu: None) -> None:
+    """RoPE in the QKV GEMM's epilogue (the default where that GEMM has no split-K: here 512 tokens at C4's attention
+    widths, 64 / 8 heads of 64, d = 2,880) against the separate k_rope_split kernel (CHROMA_B200_ROPE_EPILOGUE=0, in
+    a subprocess so the switch is read fresh). The forward's logits of every row and its routes, and a cached prefill
+    (q, new K and V rows into the cache) followed by decode steps that read those rows, are bit-identical; the
+    forward launches one kernel less per layer after the first (one (cos, sin) table per forward)."""
+    import os
+    import subprocess
+    import sys
+
+    cfg = dataclasses.replace(models.gpt_oss_20b, num_hidden_layers=2, num_experts=8, intermediate_size=1024,
+                              vocab_size=8192)
+    model = models.random_transformer(cfg, seed=31, std=0.02, dtype=torch.bfloat16)
+    tokens = np.random.default_rng(32).integers(0, cfg.vocab_size, 515)
+    paths = [str(_TMP / name) for name in ("ropefwd", "ropepre", "ropedec")]
+    for path, kw in zip(paths, ({"steps": 512}, {"steps": 512, "context": 520}, {"steps": 1, "context": 520})):
+        with chroma_b200.compile_model(model, path, **kw) as p:
+            assert p.stats["tensor_core_path"]
+    np.save(_TMP / "rope_tokens.npy", tokens)
+    root = str(Path(__file__).resolve().parents[1])
+    results = {}
+    for mode in ("1", "0"):
+        out = str(_TMP / f"rope{mode}.npz")
+        code = "import sys, tests.test_gpu_large as t; t._rope_case(*sys.argv[1:])"
+        env = dict(os.environ, CHROMA_B200_ROPE_EPILOGUE=mode, PYTHONPATH=root)
+        subprocess.run([sys.executable, "-c", code, *paths, str(_TMP / "rope_tokens.npy"), out], check=True, env=env,
+                       cwd=root)
+        results[mode] = np.load(out)
+    fused, separate = results["1"], results["0"]
+    for key in ("logits", "steps"):
+        np.testing.assert_array_equal(fused[key].view(np.uint32), separate[key].view(np.uint32))
+    np.testing.assert_array_equal(fused["routes"], separate["routes"])
+    assert int(fused["launches"]) == int(separate["launches"]) - (cfg.num_hidden_layers - 1)
